@@ -1,0 +1,179 @@
+"""ctypes front end of the CPU restatement in ``ltxattn_oracle.c``.
+
+TEST INFRASTRUCTURE ONLY: imported by ``tests/``, by ``__graft_entry__.smoke()``
+as the checker, and by ``bench.py``'s CPU-baseline leg.  The product library
+(``libltxattn_cuda``) never loads it.
+
+Every function takes and returns numpy float32 arrays in contiguous
+``[B, H, T, D]`` layout (see the C file's header for the reference lines each
+one restates).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libltxattn_oracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+def build() -> str:
+    """Compile the oracle with the Makefile beside this file."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        src = os.path.join(_HERE, "ltxattn_oracle.c")
+        if (not os.path.exists(_LIB_PATH)
+                or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oracle_fill_normal.argtypes = [ctypes.c_uint64, ctypes.c_int64, _f32p]
+        L.oracle_round_bf16.argtypes = [_f32p, ctypes.c_int64]
+        L.oracle_rope.argtypes = [_f32p, _f32p, _f32p] + [ctypes.c_int] * 4 + [
+            ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
+        L.oracle_rope_bwd.argtypes = L.oracle_rope.argtypes
+        L.oracle_attn_fwd.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64] + [
+            ctypes.c_int] * 5 + [ctypes.c_double, _f32p, _f32p, ctypes.c_int]
+        L.oracle_attn_fwd_f32.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64] + [
+            ctypes.c_int] * 5 + [ctypes.c_float, _f32p, _f32p, ctypes.c_int]
+        L.oracle_attn_bwd.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64, _f32p] + [
+            ctypes.c_int] * 5 + [ctypes.c_double, _f32p, _f32p, _f32p, ctypes.c_int]
+        for f in ("oracle_rope", "oracle_rope_bwd", "oracle_attn_fwd",
+                  "oracle_attn_fwd_f32", "oracle_attn_bwd"):
+            getattr(L, f).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(_f32p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def fill_normal(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().oracle_fill_normal(ctypes.c_uint64(seed), n, _p(out))
+    return out
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    y = _f32(x).copy()
+    lib().oracle_round_bf16(_p(y), y.size)
+    return y
+
+
+def _table_strides(tab: np.ndarray, H: int):
+    """Tables are [Bt, Ht, T, D/2]; Bt, Ht in {1, B/H}.  Size-1 dims get stride 0."""
+    Bt, Ht, T, half = tab.shape
+    sb = 0 if Bt == 1 else Ht * T * half
+    sh = 0 if Ht == 1 else T * half
+    return sb, sh
+
+
+def rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, bf16: bool) -> np.ndarray:
+    y = _f32(x).copy()
+    B, H, T, D = y.shape
+    c, s = _f32(cos), _f32(sin)
+    sb, sh = _table_strides(c, H)
+    rc = lib().oracle_rope(_p(y), _p(c), _p(s), B, H, T, D, sb, sh, int(bf16))
+    assert rc == 0
+    return y
+
+
+def rope_bwd(dx: np.ndarray, cos: np.ndarray, sin: np.ndarray, bf16_tables: bool) -> np.ndarray:
+    y = _f32(dx).copy()
+    B, H, T, D = y.shape
+    c, s = _f32(cos), _f32(sin)
+    sb, sh = _table_strides(c, H)
+    rc = lib().oracle_rope_bwd(_p(y), _p(c), _p(s), B, H, T, D, sb, sh, int(bf16_tables))
+    assert rc == 0
+    return y
+
+
+def _mask_args(mask, B, Lk):
+    if mask is None:
+        return None, 0, None
+    m = np.ascontiguousarray(mask, dtype=np.uint8).reshape(B, Lk)
+    return m.ctypes.data_as(_u8p), Lk, m
+
+
+def attn_fwd(q, k, v, mask=None, scale=None, threads=0):
+    """fp64-accumulated forward; returns (out[B,H,Lq,D], lse[B,H,Lq])."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    out = np.empty((B, H, Lq, D), np.float32)
+    lse = np.empty((B, H, Lq), np.float32)
+    mp, ms, _keep = _mask_args(mask, B, Lk)
+    rc = lib().oracle_attn_fwd(_p(q), _p(k), _p(v), mp, ms, B, H, Lq, Lk, D,
+                               float(scale), _p(out), _p(lse), threads)
+    assert rc == 0
+    return out, lse
+
+
+def attn_fwd_f32(q, k, v, mask=None, scale=None, threads=0):
+    """fp32 explicit-path forward (the timed CPU baseline)."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    out = np.empty((B, H, Lq, D), np.float32)
+    lse = np.empty((B, H, Lq), np.float32)
+    mp, ms, _keep = _mask_args(mask, B, Lk)
+    rc = lib().oracle_attn_fwd_f32(_p(q), _p(k), _p(v), mp, ms, B, H, Lq, Lk, D,
+                                   float(scale), _p(out), _p(lse), threads)
+    assert rc == 0
+    return out, lse
+
+
+def attn_bwd(q, k, v, dout, mask=None, scale=None, threads=0):
+    """fp64-accumulated backward w.r.t. the (rotated) q, k and v."""
+    q, k, v, dout = _f32(q), _f32(k), _f32(v), _f32(dout)
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    dq = np.empty_like(q)
+    dk = np.empty_like(k)
+    dv = np.empty_like(v)
+    mp, ms, _keep = _mask_args(mask, B, Lk)
+    rc = lib().oracle_attn_bwd(_p(q), _p(k), _p(v), mp, ms, _p(dout), B, H, Lq, Lk, D,
+                               float(scale), _p(dq), _p(dk), _p(dv), threads)
+    assert rc == 0
+    return dq, dk, dv
+
+
+def attention_reference(q, k, v, mask=None, q_rot=None, k_rot=None, bf16=False, scale=None):
+    """Full reference composition: RoPE (:364-367) then SDPA (:369-382).
+
+    ``q_rot`` / ``k_rot`` are ``(cos, sin)`` pairs or None; ``k_rot`` None with
+    ``q_rot`` given means "use the query's table for the key", as
+    ``keyRotary ?? rotary`` does at DiTAttention.swift:366.
+    """
+    if q_rot is not None:
+        if k_rot is None:
+            k_rot = q_rot
+        q = rope(q, q_rot[0], q_rot[1], bf16)
+        k = rope(k, k_rot[0], k_rot[1], bf16)
+    return attn_fwd(q, k, v, mask=mask, scale=scale)
+
+
+if __name__ == "__main__":  # pragma: no cover
+    print(build())

@@ -1,0 +1,175 @@
+"""The CPU oracle against the golden vectors and the reference's known answers.
+
+Parity pins for the restatement in oracle/ltxattn_oracle.c:
+* MLXCapabilityTests.fusedAttention (Tests/LTXModulesTests/MLXCapabilityTests.swift:78-91)
+* fixtures from an independent float64 torch implementation (tests/golden/make_golden.py)
+* analytic known answers (uniform attention, one-hot keys, zero-angle RoPE, LSE)
+"""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from ltxattn import inputs
+
+
+def sha(*arrays) -> str:
+    """Same digest as tests/golden/make_golden.py records."""
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a, dtype=np.float32).tobytes())
+    return h.hexdigest()
+
+
+def load(golden_dir, name):
+    z = np.load(os.path.join(golden_dir, name + ".npz"))
+    meta = json.loads(str(z["meta"]))
+    return meta, z
+
+
+def regen(meta):
+    s, B, H, Lq, Lk, D = meta["seed"], meta["B"], meta["H"], meta["Lq"], meta["Lk"], meta["D"]
+    bf16, rms = meta["bf16"], meta["rmsnorm"]
+    q = inputs.seeded_tensor(s + 2, (B, H, Lq, D), rmsnorm=rms, bf16=bf16)
+    k = inputs.seeded_tensor(s + 3, (B, H, Lk, D), rmsnorm=rms, bf16=bf16)
+    v = inputs.seeded_tensor(s + 4, (B, H, Lk, D), bf16=bf16)
+    dout = inputs.seeded_tensor(s + 5, (B, H, Lq, D), bf16=bf16) if meta["grad"] else None
+    return q, k, v, dout
+
+
+def test_reference_known_answer_fused_attention():
+    # MLXCapabilityTests.swift:80-90: q = k = 1, v = 2, H=4, T=16, D=64 -> 2.0 within 1e-4
+    q = np.ones((1, 4, 16, 64), np.float32)
+    v = np.full((1, 4, 16, 64), 2.0, np.float32)
+    out, _ = oracle.attn_fwd(q, q, v)
+    assert out.shape == (1, 4, 16, 64)
+    assert abs(out[0, 0, 0, 0] - 2.0) < 1e-4
+    assert np.all(np.abs(out - 2.0) < 1e-6)
+
+
+@pytest.mark.parametrize("name", ["c1_fp32_256", "mask_cross_bf16", "mask_cross_fp32",
+                                  "rope_self_bf16_d128", "rope_cross_bf16_d64",
+                                  "grad_mask_fp32", "grad_rope_fp32"])
+def test_oracle_matches_golden(golden_dir, name):
+    meta, z = load(golden_dir, name)
+    q, k, v, dout = regen(meta)
+    assert sha(q, k, v, *([dout] if dout is not None else [])) == meta["input_sha256"]
+    mask = z["mask"] if "mask" in z.files else None
+    qt = (z["q_cos"], z["q_sin"]) if "q_cos" in z.files else None
+    kt = (z["k_cos"], z["k_sin"]) if "k_cos" in z.files else None
+    qr, kr = q, k
+    if qt is not None:
+        ktab = kt if kt is not None else qt
+        qr = oracle.rope(q, qt[0], qt[1], meta["bf16"])
+        kr = oracle.rope(k, ktab[0], ktab[1], meta["bf16"])
+        tol = 0.0 if meta["bf16"] else 1e-6
+        np.testing.assert_allclose(qr, z["q_rotated"], atol=tol, rtol=0)
+        np.testing.assert_allclose(kr, z["k_rotated"], atol=tol, rtol=0)
+    out, lse = oracle.attn_fwd(qr, kr, v, mask=mask)
+    np.testing.assert_allclose(out, z["out"], atol=1e-6, rtol=0)
+    np.testing.assert_allclose(lse, z["lse"], atol=1e-5, rtol=0)
+    if meta["grad"]:
+        dq, dk, dv = oracle.attn_bwd(qr, kr, v, dout, mask=mask)
+        if qt is not None:
+            ktab = kt if kt is not None else qt
+            dq = oracle.rope_bwd(dq, qt[0], qt[1], False)
+            dk = oracle.rope_bwd(dk, ktab[0], ktab[1], False)
+        np.testing.assert_allclose(dq, z["dq"], atol=1e-5, rtol=0)
+        np.testing.assert_allclose(dk, z["dk"], atol=1e-5, rtol=0)
+        np.testing.assert_allclose(dv, z["dv"], atol=1e-5, rtol=0)
+
+
+def test_generators_agree():
+    # the package's numpy stream and the oracle's C stream are the same function
+    a = inputs.normal(77, 100000)
+    b = oracle.fill_normal(77, 100000)
+    assert np.max(np.abs(a - b)) <= 1e-6 * np.max(np.abs(a))
+    assert np.array_equal(inputs.round_bf16(a), oracle.round_bf16(a))
+
+
+def test_uniform_attention_is_mean_of_v():
+    rng = np.random.default_rng(0)
+    q = np.zeros((1, 2, 5, 64), np.float32)
+    k = rng.standard_normal((1, 2, 9, 64)).astype(np.float32)
+    v = rng.standard_normal((1, 2, 9, 64)).astype(np.float32)
+    out, lse = oracle.attn_fwd(q, k, v)
+    np.testing.assert_allclose(out, np.broadcast_to(v.mean(axis=2, keepdims=True), out.shape), atol=1e-6)
+    np.testing.assert_allclose(lse, np.log(9.0), atol=1e-6)
+
+
+def test_one_hot_key_and_mask_all_but_one():
+    rng = np.random.default_rng(1)
+    q = np.ones((1, 1, 3, 64), np.float32)
+    k = np.zeros((1, 1, 7, 64), np.float32)
+    k[0, 0, 4] = 10.0  # logit 80 against 0
+    v = rng.standard_normal((1, 1, 7, 64)).astype(np.float32)
+    out, _ = oracle.attn_fwd(q, k, v)
+    np.testing.assert_allclose(out[0, 0], np.broadcast_to(v[0, 0, 4], (3, 64)), atol=1e-6)
+    m = np.zeros((1, 7), np.uint8)
+    m[0, 2] = 1
+    out, _ = oracle.attn_fwd(q, np.ones_like(k), v, mask=m)
+    np.testing.assert_allclose(out[0, 0], np.broadcast_to(v[0, 0, 2], (3, 64)), atol=1e-6)
+
+
+def test_fully_masked_rows_are_unmasked():
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((1, 2, 4, 64)).astype(np.float32)
+    k = rng.standard_normal((1, 2, 6, 64)).astype(np.float32)
+    v = rng.standard_normal((1, 2, 6, 64)).astype(np.float32)
+    a, la = oracle.attn_fwd(q, k, v, mask=np.zeros((1, 6), np.uint8))
+    b, lb = oracle.attn_fwd(q, k, v)
+    assert np.isfinite(a).all()
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(la, lb)
+
+
+def test_rope_zero_angle_is_identity_and_relative():
+    x = inputs.seeded_tensor(5, (1, 2, 8, 64), bf16=True)
+    cos, sin = inputs.rope1d(np.zeros(8), 64)
+    np.testing.assert_array_equal(oracle.rope(x, cos, sin, True), x)
+    # relative-position invariance of q.k under a 1-D table (fp32, no rounding)
+    c, s = inputs.rope1d(np.arange(8, dtype=np.float64), 64, bf16=False)
+    q = np.broadcast_to(x[:, :, :1], x.shape).copy()
+    qr = oracle.rope(q, c, s, False)
+    dots = np.einsum("bhid,bhjd->bhij", qr, qr)
+    for d in range(1, 4):
+        diag = np.array([dots[0, 0, i, i + d] for i in range(8 - d)])
+        np.testing.assert_allclose(diag, diag[0], rtol=1e-4, atol=1e-4)
+
+
+def test_f32_mode_matches_f64_mode():
+    q = inputs.seeded_tensor(11, (1, 2, 70, 64), bf16=False)
+    k = inputs.seeded_tensor(12, (1, 2, 90, 64), bf16=False)
+    v = inputs.seeded_tensor(13, (1, 2, 90, 64), bf16=False)
+    m = np.ones((1, 90), np.uint8)
+    m[0, 50:] = 0
+    a, la = oracle.attn_fwd(q, k, v, mask=m)
+    b, lb = oracle.attn_fwd_f32(q, k, v, mask=m)
+    np.testing.assert_allclose(a, b, atol=2e-6)
+    np.testing.assert_allclose(la, lb, atol=2e-5)
+
+
+def test_backward_matches_finite_differences():
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((1, 1, 5, 8)).astype(np.float32)
+    k = rng.standard_normal((1, 1, 6, 8)).astype(np.float32)
+    v = rng.standard_normal((1, 1, 6, 8)).astype(np.float32)
+    do = rng.standard_normal((1, 1, 5, 8)).astype(np.float32)
+    dq, dk, dv = oracle.attn_bwd(q, k, v, do, scale=0.5)
+
+    def loss(qq, kk, vv):
+        o, _ = oracle.attn_fwd(qq, kk, vv, scale=0.5)
+        return float(np.sum(o.astype(np.float64) * do))
+
+    eps = 1e-2
+    for arr, g in ((q, dq), (k, dk), (v, dv)):
+        for idx in [(0, 0, 1, 3), (0, 0, 4, 0)]:
+            p = arr.copy(); p[idx] += eps
+            m = arr.copy(); m[idx] -= eps
+            args_p = [p if arr is x else x for x in (q, k, v)]
+            args_m = [m if arr is x else x for x in (q, k, v)]
+            fd = (loss(*args_p) - loss(*args_m)) / (2 * eps)
+            assert abs(fd - g[idx]) < 2e-3, (idx, fd, g[idx])
