@@ -1,0 +1,374 @@
+"""Benchmark of the LTX 2.5 DiT fused attention on B200 (libltxattn_cuda).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3|c4a|c4b|c4c|c5]
+
+Default workload (the metric's configuration): video
+self-attention at the 640x384x97 render shape -- 3120 tokens, 32 heads, D=128,
+bf16, q/k/v seeded N(0,1) with per-head RMSNorm, 3D split-RoPE fused into the
+call, scale 1/sqrt(128), no mask.  One step = one ltxattn_fwd call.
+
+Multi-GPU (torchrun, one process per GPU): heads are the independent units.
+For c2..c4c each rank runs its own 32-head block of a (32*N)-head job (weak
+scaling, no collective on the data path).  --workload c5 is the 29760-token
+shape with its 32 heads sharded 32/N per rank (strong scaling).
+
+FLOPs: 4*B*H*Lq*Lk*D per forward (the reference's convention,
+Sources/ltx/BenchGEMM.swift:289).  Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ltx-2.5-swift_b200"))
+
+import numpy as np  # noqa: E402
+
+WORKLOADS = {
+    # name: (B, H, Lq, Lk, D, rope, mask_valid, description)
+    "c2": (1, 32, 3120, 3120, 128, "3d", None, "video self-attn 640x384x97, 3120 tok, H32 D128, 3D RoPE"),
+    "c3": (1, 32, 3120, 1024, 128, None, 94, "text cross-attn Q3120 x KV1024 (94 valid), H32 D128"),
+    "c4a": (1, 32, 126, 126, 64, "1d", None, "audio self-attn 126 tok, H32 D64, 1D RoPE"),
+    "c4b": (1, 32, 3120, 126, 64, "av", None, "video->audio cross Q3120 x KV126, H32 D64, time RoPE"),
+    "c4c": (1, 32, 126, 3120, 64, "va", None, "audio->video cross Q126 x KV3120, H32 D64, time RoPE"),
+    "c5": (1, 32, 29760, 29760, 128, None, None, "video self-attn 1280x768x241, 29760 tok, H32 D128"),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for ln in f:
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def make_inputs(wl, rank, Hc, B, Lq, Lk, D):
+    from ltxattn import inputs
+    seed = 1000 + 97 * rank
+    q = inputs.seeded_tensor(seed + 2, (B, Hc, Lq, D), rmsnorm=True, bf16=True)
+    k = inputs.seeded_tensor(seed + 3, (B, Hc, Lk, D), rmsnorm=True, bf16=True)
+    v = inputs.seeded_tensor(seed + 4, (B, Hc, Lk, D), bf16=True)
+    rope = WORKLOADS[wl][5]
+    tabs = None
+    if rope == "3d":
+        tabs = (inputs.rope3d_grid(13, 12, 20, D), None)
+    elif rope == "1d":
+        tabs = (inputs.rope1d(np.arange(Lq, dtype=np.float64), D), None)
+    elif rope == "av":
+        tabs = (inputs.rope1d(inputs.video_frame_seconds(13, 240), D),
+                inputs.rope1d(inputs.audio_token_seconds(Lk), D))
+    elif rope == "va":
+        tabs = (inputs.rope1d(inputs.audio_token_seconds(Lq), D),
+                inputs.rope1d(inputs.video_frame_seconds(13, 240), D))
+    mask = None
+    mv = WORKLOADS[wl][6]
+    if mv is not None:
+        mask = np.zeros((B, Lk), np.uint8)
+        mask[:, :mv] = 1
+    return q, k, v, tabs, mask
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from ltxattn import AttentionBackend, Rotary, device_status
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    wl = args.workload
+    B, H, Lq, Lk, D = WORKLOADS[wl][:5]
+    strong = wl == "c5"
+    if strong:
+        if H % ws:
+            raise SystemExit(f"{H} heads do not shard over {ws} ranks")
+        Hc = H // ws
+    else:
+        Hc = H
+    q, k, v, tabs, mask = make_inputs(wl, rank, Hc, B, Lq, Lk, D)
+    dt = torch.bfloat16
+    qd = torch.from_numpy(q).to("cuda", dt)
+    kd = torch.from_numpy(k).to("cuda", dt)
+    vd = torch.from_numpy(v).to("cuda", dt)
+    out = torch.empty_like(qd)
+    lse = torch.empty((B, Hc, Lq), device="cuda", dtype=torch.float32)
+    qrot = krot = None
+    if tabs is not None:
+        qrot = Rotary(torch.from_numpy(tabs[0][0]).to("cuda", dt), torch.from_numpy(tabs[0][1]).to("cuda", dt))
+        if tabs[1] is not None:
+            krot = Rotary(torch.from_numpy(tabs[1][0]).to("cuda", dt), torch.from_numpy(tabs[1][1]).to("cuda", dt))
+    md = torch.from_numpy(mask).cuda() if mask is not None else None
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(qq=qd, kk=kd, vv=vd, oo=out, qr=qrot, kr=krot):
+        AttentionBackend.attention(qq, kk, vv, key_mask=md, q_rotary=qr, k_rotary=kr, out=oo, lse=lse)
+
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    ctas = math.ceil(Lq / 128) * Hc * B
+    splits = ctas < sms and math.ceil(Lk / 128) > 1
+    launches_per_step = 1 + (2 if qrot is not None else 0) + (1 if splits else 0)
+    flops = 4.0 * B * Hc * Lq * Lk * D
+    if mask is not None:
+        eff_flops = 4.0 * B * Hc * Lq * WORKLOADS[wl][6] * D
+    else:
+        eff_flops = flops
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    total_ms = sum(step_ms)
+
+    # kernel-only timing of the attention kernel: the same call without tables is one
+    # launch of fwd_bf16_sm100_kernel (same shape, same FLOPs)
+    kern_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        kern_evs[i][0].record(stream)
+        AttentionBackend.attention(qd, kd, vd, key_mask=md, out=out, lse=lse)
+        kern_evs[i][1].record(stream)
+    barrier()
+    kern_ms = [a.elapsed_time(b) for a, b in kern_evs]
+
+    # end to end through the public API with host buffers
+    hq = torch.from_numpy(q).to(dt).pin_memory()
+    hk = torch.from_numpy(k).to(dt).pin_memory()
+    hv = torch.from_numpy(v).to(dt).pin_memory()
+    hout = torch.empty(out.shape, dtype=dt).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        qd.copy_(hq, non_blocking=True)
+        kd.copy_(hk, non_blocking=True)
+        vd.copy_(hv, non_blocking=True)
+        step()
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2
+    d2h = hout.numel() * 2
+    status = device_status(clear=True)
+
+    # max over ranks
+    vals = torch.tensor([total_ms, sum(kern_ms), e2e_ms], device="cuda", dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, kern_total, e2e_ms = vals.tolist()
+    ranks_flops = flops * ws
+    ms_per_step = total_ms / args.steps
+    value = ranks_flops / (ms_per_step * 1e-3) / 1e12
+    kern_avg_ms = kern_total / args.steps
+    burst, sustained, hbm, src = peaks()
+    achieved = flops / (kern_avg_ms * 1e-3) / 1e12  # per GPU, one launch of the dominant kernel
+    result = None
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(wl, budget_s=args.cpu_seconds)
+        result = {
+            "metric": "fused-attn TFLOP/s bf16 @3120-tok video self-attn (aggregate over GPUs)"
+            if wl == "c2" else f"fused-attn TFLOP/s bf16 ({wl})",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1), per-head RMSNorm, bf16)",
+            "config": {"workload": f"{wl}: {WORKLOADS[wl][7]}", "batch": B, "heads_per_gpu": Hc,
+                       "q_len": Lq, "kv_len": Lk, "head_dim": D, "rope": WORKLOADS[wl][5] or "none",
+                       "mask_valid_keys": WORKLOADS[wl][6], "parallelism": f"heads x{ws}",
+                       "l2": "flushed (256 MB write) before every timed step; flush outside the timed events",
+                       "flops_per_step_per_gpu": flops, "effective_flops_per_step_per_gpu": eff_flops},
+            "pct_of_datasheet_dense_bf16": round(100.0 * value / ws / 2250.0, 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst, "unit": "TFLOP/s",
+                         "frac": round(achieved / burst, 4), "peak_source": f"{src} bf16_tflops (burst)",
+                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5),
+                         "traffic": None},
+            "e2e": {"value": round(ranks_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "device_status": status,
+            "cpu_baseline": cpu,
+        }
+        if wl == "c3":
+            result["hbm_gbs_effective"] = None
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def cpu_baseline(wl, budget_s=12.0, threads=None):
+    """The oracle's fp32 explicit-path restatement on the host cores, over a
+    bounded sample of heads of the same workload; TFLOP/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # test/baseline infrastructure; never on the GPU path
+    B, H, Lq, Lk, D = WORKLOADS[wl][:5]
+    threads = threads or os.cpu_count() or 1
+    q, k, v, tabs, mask = make_inputs(wl, 0, 1, B, Lq, Lk, D)
+    if tabs is not None:
+        kt = tabs[1] if tabs[1] is not None else tabs[0]
+        q = oracle.rope(q, tabs[0][0], tabs[0][1], True)
+        k = oracle.rope(k, kt[0], kt[1], True)
+    oracle.attn_fwd_f32(q[:, :, :64], k, v, mask=mask, threads=threads)  # warm
+    t0 = time.perf_counter()
+    heads = 0
+    rows = min(Lq, 512) if wl == "c5" else Lq
+    while True:
+        oracle.attn_fwd_f32(q[:, :, :rows], k, v, mask=mask, threads=threads)
+        heads += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or heads >= H:
+            break
+    flops = 4.0 * B * heads * rows * Lk * D
+    return {"value": round(flops / el / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{heads} head(s) x {rows} query rows of {wl} ({el:.1f} s), fp32 explicit path "
+                      f"(oracle/ltxattn_oracle.c oracle_attn_fwd_f32, OpenMP)"}
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    wl = args.workload
+    B, H, Lq, Lk, D = WORKLOADS[wl][:5]
+    threads = os.cpu_count() or 1
+    per_step = max(1.0, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_baseline(wl, budget_s=per_step * 0.25, threads=threads)
+    samples = [cpu_baseline(wl, budget_s=per_step, threads=threads) for _ in range(args.steps)]
+    vals = [s["value"] for s in samples]
+    value = statistics.median(vals)
+    flops_step = 4.0 * B * H * Lq * Lk * D
+    return {
+        "impl": "reference",
+        "metric": "fused-attn TFLOP/s bf16 @3120-tok video self-attn (aggregate over GPUs)"
+        if wl == "c2" else f"fused-attn TFLOP/s bf16 ({wl})",
+        "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(flops_step / (value * 1e12) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if wl == "c5" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), per-head RMSNorm, bf16-rounded inputs)",
+        "config": {"workload": f"{wl}: {WORKLOADS[wl][7]}", "batch": B, "heads": H, "q_len": Lq, "kv_len": Lk,
+                   "head_dim": D},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": samples[0]["sample"] + "; MLX (the reference's CPU path) cannot run here: "
+                                   "no Swift toolchain and no MLX"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,224 @@
+/*
+ * ltxattn.h -- C ABI of libltxattn_cuda, the B200 (sm_100a) fused attention of
+ * the LTX 2.5 diffusion transformer.
+ *
+ * This is the drop-in boundary behind the reference's attention seam.  In
+ * loading-awesome/LTX-2.5-Swift the seam is `Sources/LTXAttention`
+ * (`AttentionBackend.swift:13-15`, an empty placeholder) and the attention
+ * core it stands in for is the SDPA switch of
+ * `Sources/LTXModules/DiTAttention.swift:369-382`, together with the split
+ * RoPE applied just before it (`:364-367`, `:206-234`).  A Swift caller binds
+ * this header through a module map.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Device pointers are CUDA device memory;
+ *    `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Tensors are [B, H, T, D] views with element strides for B, H and T; the
+ *    D stride is 1.  The reference's `split` (`DiTAttention.swift:346-348`)
+ *    is a transposed view of [B, T, H*D]: strides (T*H*D, D, H*D).  It is
+ *    accepted as is, with no copy.
+ *  - The caller owns every buffer, including outputs, the log-sum-exp and the
+ *    workspace.  The library allocates no device memory per call.
+ *  - Calls are asynchronous with respect to the host and ordered on `stream`.
+ *    They are re-entrant; distinct host threads may use distinct streams.
+ *  - No exception crosses the ABI.  Every entry returns an ltxattn_status;
+ *    ltxattn_last_error() gives this thread's message for the last failure.
+ *  - There is no CPU fallback.  A shape the kernels do not cover returns
+ *    LTXATTN_ERR_UNSUPPORTED (the reference's own warning against a silent
+ *    fallback is at `DiTAttention.swift:284-287`).
+ */
+#ifndef LTXATTN_H
+#define LTXATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LTXATTN_ABI_VERSION 1
+
+/* Entry points are the only symbols the library exports. */
+#if defined(__GNUC__)
+#define LTXATTN_API __attribute__((visibility("default")))
+#else
+#define LTXATTN_API
+#endif
+
+typedef enum ltxattn_status {
+  LTXATTN_OK = 0,
+  LTXATTN_ERR_SHAPE = 1,       /* sizes disagree; mirrors DiTAttention.Failure.shape (:109) */
+  LTXATTN_ERR_DTYPE = 2,       /* dtype not F32 / BF16 */
+  LTXATTN_ERR_ALIGN = 3,       /* pointer or stride not 16-byte aligned where TMA needs it */
+  LTXATTN_ERR_UNSUPPORTED = 4, /* head_dim or size outside what the kernels cover */
+  LTXATTN_ERR_CUDA = 5,        /* a CUDA runtime call failed */
+  LTXATTN_ERR_NCCL = 6,        /* an NCCL call failed or NCCL is not loadable */
+  LTXATTN_ERR_TIMEOUT = 7,     /* a device-side bounded wait gave up */
+  LTXATTN_ERR_WORKSPACE = 8,   /* workspace missing or smaller than required */
+  LTXATTN_ERR_ARG = 9          /* NULL where a pointer is required, bad enum, bad range */
+} ltxattn_status;
+
+typedef enum ltxattn_dtype {
+  LTXATTN_F32 = 0,  /* float32: the `.explicit` arm's arithmetic, parity gate */
+  LTXATTN_BF16 = 1  /* bfloat16 storage, fp32 accumulation: the render/training dtype */
+} ltxattn_dtype;
+
+/* A [B, H, T, D] view.  Strides are in elements; the D stride is 1. */
+typedef struct ltxattn_tensor {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+} ltxattn_tensor;
+
+/* One split-RoPE table pair, DiTAttention.Rotary (`DiTAttention.swift:98-105`):
+ * cos and sin are [B, H, T, D/2] in the activation dtype (the reference narrows
+ * them to x.dtype before use, `:231-232`).  A zero stride_b / stride_h shares
+ * the table across batch / heads.  `tokens` is how many rows the table holds.
+ * cos == NULL means "no rotary". */
+typedef struct ltxattn_rotary {
+  const void* cos;
+  const void* sin;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+  int32_t tokens;
+} ltxattn_rotary;
+
+/* Forward arguments: out = softmax(scale * rope(q) rope(k)^T + mask) v.
+ *
+ *  - heads [head_begin, head_begin + head_count) are computed (head_count 0 =
+ *    all heads); the views cover all `heads`.  This is how a rank of a
+ *    head-sharded job runs its block of a shared tensor.
+ *  - key_mask: [B, kv_len] uint8, nonzero = valid, or NULL.  Masked keys get
+ *    exactly zero weight; a batch row with no valid key attends to every key
+ *    unmasked, the rule of `GemmaTextEncoder.swift:306-319`.
+ *  - q_rotary rotates q; k_rotary rotates k; k_rotary.cos == NULL with
+ *    q_rotary given rotates k with the q table (`keyRotary ?? rotary`,
+ *    `DiTAttention.swift:366`).  k_rotary without q_rotary is ignored, as in
+ *    the reference (`:364`).
+ *  - lse: [B, H, q_len] float32, natural-log log-sum-exp of the scaled
+ *    logits, or NULL.  The backward needs it.
+ *  - workspace: device scratch of ltxattn_fwd_workspace() bytes (may be 0).
+ *  - num_splits: KV splits for short-query shapes (0 = choose). */
+typedef struct ltxattn_fwd_args {
+  int32_t dtype;
+  int32_t batch, heads, q_len, kv_len, head_dim;
+  int32_t head_begin, head_count;
+  ltxattn_tensor q, k, v, out;
+  float scale;
+  const uint8_t* key_mask;
+  int64_t key_mask_stride_b;
+  ltxattn_rotary q_rotary, k_rotary;
+  float* lse;
+  int64_t lse_stride_b, lse_stride_h;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t num_splits;
+} ltxattn_fwd_args;
+
+/* Backward arguments: gradients of sum(dout * out) with respect to q, k and v
+ * (the un-rotated inputs when rotaries are given; the bf16 roundings inside
+ * RoPE pass gradients straight through, as autodiff does).  P is recomputed
+ * from the forward's saved `lse`; no score matrix is stored.  This replaces
+ * MLX's VJP of the fused SDPA under gradient checkpointing
+ * (`LoRATrainingStep.swift:283-304`, `GradientCheckpoint.swift:48-67`). */
+typedef struct ltxattn_bwd_args {
+  int32_t dtype;
+  int32_t batch, heads, q_len, kv_len, head_dim;
+  int32_t head_begin, head_count;
+  ltxattn_tensor q, k, v, out, dout;
+  const float* lse;
+  int64_t lse_stride_b, lse_stride_h;
+  ltxattn_tensor dq, dk, dv;
+  float scale;
+  const uint8_t* key_mask;
+  int64_t key_mask_stride_b;
+  ltxattn_rotary q_rotary, k_rotary;
+  void* workspace;
+  size_t workspace_bytes;
+} ltxattn_bwd_args;
+
+/* Replaces `MLXFast.scaledDotProductAttention(queries:keys:values:scale:mask:)`
+ * and the `.explicit` arm (`DiTAttention.swift:373-382`), fused with the RoPE
+ * of `:364-367`. */
+LTXATTN_API int ltxattn_fwd(const ltxattn_fwd_args* args, void* stream);
+
+/* Device scratch bytes ltxattn_fwd needs for these arguments. */
+LTXATTN_API size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* args);
+
+/* Replaces the autodiff VJP of the SDPA core (LoRA training backward). */
+LTXATTN_API int ltxattn_bwd(const ltxattn_bwd_args* args, void* stream);
+
+/* Device scratch bytes ltxattn_bwd needs for these arguments. */
+LTXATTN_API size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* args);
+
+/* ---- head-parallel all-gather (NCCL over NVLink) ------------------------- */
+
+/* Opaque NCCL communicator owned by the library. */
+typedef struct ltxattn_comm ltxattn_comm;
+
+/* Fill 128 bytes with a fresh NCCL unique id (rank 0 calls this and shares
+ * the bytes with the other ranks out of band). */
+LTXATTN_API int ltxattn_comm_unique_id(uint8_t id[128]);
+
+/* Create the communicator for `rank` of `nranks` on CUDA device `device`. */
+LTXATTN_API int ltxattn_comm_init(ltxattn_comm** comm, int32_t nranks, int32_t rank, const uint8_t id[128],
+                      int32_t device);
+LTXATTN_API int ltxattn_comm_destroy(ltxattn_comm* comm);
+
+/* All-gather head blocks: rank r holds send = [B, heads_per_rank, T, D]
+ * (contiguous) for heads [r*heads_per_rank, (r+1)*heads_per_rank); every rank
+ * receives recv = [B, nranks*heads_per_rank, T, D] (contiguous).  The
+ * reference has no collective; this is only used where a caller needs every
+ * head (e.g. a non-sharded to_out, `DiTAttention.swift:402-404`). */
+typedef struct ltxattn_gather_args {
+  int32_t dtype;
+  int32_t batch, heads_per_rank, tokens, head_dim;
+  const void* send;
+  void* recv;
+} ltxattn_gather_args;
+
+LTXATTN_API int ltxattn_allgather_heads(const ltxattn_gather_args* args, ltxattn_comm* comm, void* stream);
+
+/* ---- device discovery ----------------------------------------------------- */
+
+/* Replaces `LTXHardware.Machine.detect` (`Machine.swift:31-36`) and the Metal
+ * library locator (`MetalLibrary.swift:25-128`) for a CUDA device. */
+typedef struct ltxattn_device_info {
+  char name[256];
+  int32_t device;
+  int32_t cc_major, cc_minor;
+  int32_t sm_count;
+  int64_t total_memory_bytes;
+  int64_t free_memory_bytes;
+  int32_t max_smem_per_block_optin;
+  int32_t l2_bytes;
+  int32_t sm_clock_khz;
+  int32_t mem_clock_khz;
+  int32_t mem_bus_width_bits;
+  int32_t supported; /* 1 when the kernels here run on it (sm_100) */
+} ltxattn_device_info;
+
+LTXATTN_API int ltxattn_device_count(int32_t* count);
+LTXATTN_API int ltxattn_device_query(int32_t device, ltxattn_device_info* info);
+
+/* ---- status --------------------------------------------------------------- */
+
+/* Message for this thread's most recent failure ("" if none). */
+LTXATTN_API const char* ltxattn_last_error(void);
+
+/* Read (and, when `clear` is nonzero, reset) the current device's kernel
+ * error word.  Synchronises the device.  Returns LTXATTN_ERR_TIMEOUT when a
+ * kernel's bounded wait gave up since the last clear; *site receives the
+ * encoded wait site (may be NULL). */
+LTXATTN_API int ltxattn_device_status(int32_t clear, int32_t* site);
+
+LTXATTN_API int ltxattn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTXATTN_H */

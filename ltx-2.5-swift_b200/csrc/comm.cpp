@@ -1,0 +1,149 @@
+// comm.cpp -- head-parallel all-gather over NCCL (NVLink / NVSwitch).
+//
+// The reference has no collective (a single device, SURVEY of
+// RenderEngine.swift:16-24).  Heads are independent, so a head-sharded job
+// needs communication only where a caller wants every head's output on every
+// rank; this file provides exactly that gather.
+//
+// NCCL is opened lazily with dlopen: a process that already loaded an NCCL
+// (PyTorch bundles one) reuses it, and the library itself has no link-time
+// NCCL dependency, so attention calls work where NCCL is absent.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ltxattn.h"
+
+namespace ltx {
+int set_error_message(int status, const char* msg);
+}
+
+struct ltxattn_comm {
+  ncclComm_t nccl;
+  int nranks;
+  int rank;
+  int device;
+};
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*GroupStart)();
+  ncclResult_t (*GroupEnd)();
+  const char* (*GetErrorString)(ncclResult_t);
+  bool ok;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api{};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+    api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+    api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
+    api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
+    api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GroupStart &&
+             api.GroupEnd && api.GetErrorString;
+  });
+  return api;
+}
+
+int nccl_fail(const char* what, ncclResult_t r) {
+  char buf[256];
+  snprintf(buf, sizeof buf, "%s: %s", what, nccl().GetErrorString ? nccl().GetErrorString(r) : "?");
+  return ltx::set_error_message(LTXATTN_ERR_NCCL, buf);
+}
+
+int need_nccl() {
+  if (!nccl().ok) return ltx::set_error_message(LTXATTN_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  return LTXATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltxattn_comm_unique_id(uint8_t id[128]) {
+  if (!id) return ltx::set_error_message(LTXATTN_ERR_ARG, "id is NULL");
+  if (int rc = need_nccl()) return rc;
+  ncclUniqueId u;
+  ncclResult_t r = nccl().GetUniqueId(&u);
+  if (r != ncclSuccess) return nccl_fail("ncclGetUniqueId", r);
+  memcpy(id, u.internal, 128);
+  return LTXATTN_OK;
+}
+
+int ltxattn_comm_init(ltxattn_comm** comm, int32_t nranks, int32_t rank, const uint8_t id[128], int32_t device) {
+  if (!comm || !id) return ltx::set_error_message(LTXATTN_ERR_ARG, "comm or id is NULL");
+  *comm = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return ltx::set_error_message(LTXATTN_ERR_ARG, "rank out of range");
+  if (int rc = need_nccl()) return rc;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  ncclUniqueId u;
+  memcpy(u.internal, id, 128);
+  ncclComm_t c = nullptr;
+  ncclResult_t r = nccl().CommInitRank(&c, nranks, u, rank);
+  if (r != ncclSuccess) return nccl_fail("ncclCommInitRank", r);
+  *comm = new ltxattn_comm{c, nranks, rank, device};
+  return LTXATTN_OK;
+}
+
+int ltxattn_comm_destroy(ltxattn_comm* comm) {
+  if (!comm) return LTXATTN_OK;
+  int rc = LTXATTN_OK;
+  if (nccl().ok && comm->nccl) {
+    ncclResult_t r = nccl().CommDestroy(comm->nccl);
+    if (r != ncclSuccess) rc = nccl_fail("ncclCommDestroy", r);
+  }
+  delete comm;
+  return rc;
+}
+
+int ltxattn_allgather_heads(const ltxattn_gather_args* a, ltxattn_comm* comm, void* stream) {
+  if (!a || !comm) return ltx::set_error_message(LTXATTN_ERR_ARG, "args or comm is NULL");
+  if (a->dtype != LTXATTN_F32 && a->dtype != LTXATTN_BF16)
+    return ltx::set_error_message(LTXATTN_ERR_DTYPE, "dtype must be LTXATTN_F32 or LTXATTN_BF16");
+  if (a->batch < 1 || a->heads_per_rank < 1 || a->tokens < 1 || a->head_dim < 1)
+    return ltx::set_error_message(LTXATTN_ERR_SHAPE, "gather sizes must be >= 1");
+  if (!a->send || !a->recv) return ltx::set_error_message(LTXATTN_ERR_ARG, "send or recv is NULL");
+  if (int rc = need_nccl()) return rc;
+  const size_t esize = a->dtype == LTXATTN_BF16 ? 2 : 4;
+  const ncclDataType_t t = a->dtype == LTXATTN_BF16 ? ncclBfloat16 : ncclFloat32;
+  const size_t count = (size_t)a->heads_per_rank * a->tokens * a->head_dim;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ncclResult_t r = nccl().GroupStart();
+  if (r != ncclSuccess) return nccl_fail("ncclGroupStart", r);
+  for (int b = 0; b < a->batch; ++b) {
+    const char* s = static_cast<const char*>(a->send) + (size_t)b * count * esize;
+    char* d = static_cast<char*>(a->recv) + (size_t)b * comm->nranks * count * esize;
+    r = nccl().AllGather(s, d, count, t, comm->nccl, st);
+    if (r != ncclSuccess) {
+      nccl().GroupEnd();
+      return nccl_fail("ncclAllGather", r);
+    }
+  }
+  r = nccl().GroupEnd();
+  if (r != ncclSuccess) return nccl_fail("ncclGroupEnd", r);
+  return LTXATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,474 @@
+// ltxattn_api.cu -- the C ABI of libltxattn_cuda (include/ltxattn.h).
+//
+// Validation mirrors the reference's up-front refusals
+// (DiTAttention.Failure, DiTAttention.swift:107-122): a wrong shape, dtype or
+// alignment is an error code with a message, never a silent fallback.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ltxattn.h"
+#include "ltxattn_internal.h"
+
+namespace ltx {
+
+__device__ int g_error_word;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(LTXATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda
+// link dependency).
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [D, T, H, B] bf16 view, box {64, 128, 1, 1}, 128-byte swizzle.  Strides of
+// size-1 dims are irrelevant to addressing; they are replaced by a packed
+// value so the encoder's alignment checks see a valid number.
+int make_tmap(CUtensorMap* map, const void* ptr, int D, int T, int H, int B, int64_t st, int64_t sh,
+              int64_t sb, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(LTXATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  int64_t s1 = st, s2 = sh, s3 = sb;
+  if (T == 1) s1 = D;
+  if (H == 1) s2 = s1 * T;
+  if (B == 1) s3 = s2 * H;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)s1 * 2, (cuuint64_t)s2 * 2, (cuuint64_t)s3 * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LTXATTN_ERR_ALIGN, "%s: cuTensorMapEncodeTiled rejected the view (CUresult %d)", name, (int)r);
+  return LTXATTN_OK;
+}
+
+int current_sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// shared validation of the forward / backward shape block
+
+struct Shape {
+  int dtype, B, H, Lq, Lk, D, h0, Hc;
+  size_t esize;
+};
+
+int check_tensor(const ltxattn_tensor& t, const char* name, const Shape& s, bool need_tma) {
+  if (t.data == nullptr) return fail(LTXATTN_ERR_ARG, "%s is NULL", name);
+  if (t.stride_b < 0 || t.stride_h < 0 || t.stride_t < 0)
+    return fail(LTXATTN_ERR_SHAPE, "%s has a negative stride", name);
+  if (need_tma) {
+    if (!aligned16(t.data)) return fail(LTXATTN_ERR_ALIGN, "%s is not 16-byte aligned", name);
+    const int64_t q = 16 / (int64_t)s.esize;
+    if ((s.B > 1 && t.stride_b % q) || (s.H > 1 && t.stride_h % q) || t.stride_t % q)
+      return fail(LTXATTN_ERR_ALIGN, "%s strides must be multiples of %lld elements (16 bytes)", name,
+                  (long long)q);
+  }
+  return LTXATTN_OK;
+}
+
+int check_shape(int dtype, int B, int H, int Lq, int Lk, int D, int head_begin, int head_count, Shape* s) {
+  if (dtype != LTXATTN_F32 && dtype != LTXATTN_BF16)
+    return fail(LTXATTN_ERR_DTYPE, "dtype %d is neither LTXATTN_F32 nor LTXATTN_BF16", dtype);
+  if (B < 1 || H < 1 || Lq < 1 || Lk < 1)
+    return fail(LTXATTN_ERR_SHAPE, "batch %d, heads %d, q_len %d, kv_len %d: all must be >= 1", B, H, Lq, Lk);
+  if (D != 64 && D != 128)
+    return fail(LTXATTN_ERR_UNSUPPORTED, "head_dim %d is not supported (64 and 128 are: the DiT's audio and video heads)",
+                D);
+  if (Lk > kMaxKvLen) return fail(LTXATTN_ERR_UNSUPPORTED, "kv_len %d exceeds %d", Lk, kMaxKvLen);
+  const int hc = head_count == 0 ? H - head_begin : head_count;
+  if (head_begin < 0 || hc < 1 || head_begin + hc > H)
+    return fail(LTXATTN_ERR_ARG, "head range [%d, %d) is outside [0, %d)", head_begin, head_begin + hc, H);
+  if ((int64_t)B * hc > 65535 * 65535LL) return fail(LTXATTN_ERR_SHAPE, "too many heads");
+  if (B > 65535 || hc > 65535) return fail(LTXATTN_ERR_UNSUPPORTED, "batch and head count must be <= 65535");
+  s->dtype = dtype;
+  s->B = B;
+  s->H = H;
+  s->Lq = Lq;
+  s->Lk = Lk;
+  s->D = D;
+  s->h0 = head_begin;
+  s->Hc = hc;
+  s->esize = dtype == LTXATTN_BF16 ? 2 : 4;
+  return LTXATTN_OK;
+}
+
+int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
+  if (r.cos == nullptr) return LTXATTN_OK;
+  if (r.sin == nullptr) return fail(LTXATTN_ERR_ARG, "%s has cos but no sin", name);
+  if (r.tokens < tokens_needed)
+    return fail(LTXATTN_ERR_SHAPE, "%s covers %d tokens, expected at least %d", name, r.tokens, tokens_needed);
+  if (r.stride_b < 0 || r.stride_h < 0 || r.stride_t < 0)
+    return fail(LTXATTN_ERR_SHAPE, "%s has a negative stride", name);
+  return LTXATTN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// forward plan: workspace layout and split count (identical for the
+// workspace query and the call)
+
+struct FwdPlan {
+  Shape s;
+  bool rope_q, rope_k;
+  const ltxattn_rotary* kr;  // table used for k
+  int q_tiles, kv_tiles, splits;
+  size_t off_q, off_k, off_po, off_pl, total;
+};
+
+int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
+  if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
+  int rc = check_shape(a->dtype, a->batch, a->heads, a->q_len, a->kv_len, a->head_dim, a->head_begin,
+                       a->head_count, &P->s);
+  if (rc) return rc;
+  const Shape& s = P->s;
+  P->rope_q = a->q_rotary.cos != nullptr;
+  P->kr = (a->k_rotary.cos != nullptr) ? &a->k_rotary : &a->q_rotary;
+  P->rope_k = P->rope_q;  // k_rotary without q_rotary is ignored (DiTAttention.swift:364)
+  if (P->rope_q) {
+    if ((rc = check_rotary(a->q_rotary, "q_rotary", s.Lq))) return rc;
+    if ((rc = check_rotary(*P->kr, a->k_rotary.cos ? "k_rotary" : "q_rotary (used for k)", s.Lk))) return rc;
+  }
+  P->q_tiles = (s.Lq + kTileM - 1) / kTileM;
+  P->kv_tiles = (s.Lk + kTileN - 1) / kTileN;
+  P->splits = 1;
+  if (s.dtype == LTXATTN_BF16) {
+    if (a->num_splits > 0) {
+      P->splits = std::min({a->num_splits, P->kv_tiles, kMaxSplits});
+    } else if (a->num_splits == 0) {
+      const int64_t ctas = (int64_t)P->q_tiles * s.Hc * s.B;
+      const int sms = current_sm_count();
+      if (ctas < sms && P->kv_tiles > 1) {
+        const int want = (int)((2 * (int64_t)sms + ctas - 1) / ctas);
+        P->splits = std::max(1, std::min({want, P->kv_tiles, kMaxSplits}));
+      }
+    } else {
+      return fail(LTXATTN_ERR_ARG, "num_splits %d is negative", a->num_splits);
+    }
+  }
+  size_t off = 0;
+  P->off_q = off;
+  if (P->rope_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
+  P->off_k = off;
+  if (P->rope_k) off += align256((size_t)s.B * s.Hc * s.Lk * s.D * s.esize);
+  P->off_po = off;
+  if (P->splits > 1) off += align256((size_t)P->splits * s.B * s.Hc * s.Lq * s.D * sizeof(float));
+  P->off_pl = off;
+  if (P->splits > 1) off += align256((size_t)P->splits * s.B * s.Hc * s.Lq * sizeof(float));
+  P->total = off;
+  return LTXATTN_OK;
+}
+
+RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const Shape& s, int T, void* y,
+                       int inverse) {
+  RopeParams p{};
+  p.x = x.data;
+  p.x_sb = x.stride_b;
+  p.x_sh = x.stride_h;
+  p.x_st = x.stride_t;
+  p.cos = r.cos;
+  p.sin = r.sin;
+  p.t_sb = r.stride_b;
+  p.t_sh = r.stride_h;
+  p.t_st = r.stride_t;
+  p.y = y;
+  p.B = s.B;
+  p.Hc = s.Hc;
+  p.T = T;
+  p.D = s.D;
+  p.head_begin = s.h0;
+  p.inverse = inverse;
+  return p;
+}
+
+}  // namespace
+
+int set_error_message(int status, const char* msg) {
+  t_last_error = msg;
+  return status;
+}
+
+int* device_error_word() {
+  int* p = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) != cudaSuccess) return nullptr;
+  return p;
+}
+
+}  // namespace ltx
+
+using namespace ltx;
+
+extern "C" {
+
+int ltxattn_abi_version(void) { return LTXATTN_ABI_VERSION; }
+
+const char* ltxattn_last_error(void) { return t_last_error.c_str(); }
+
+size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* a) {
+  FwdPlan P;
+  if (plan_fwd(a, &P) != LTXATTN_OK) return 0;
+  return P.total;
+}
+
+int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
+  FwdPlan P;
+  int rc = plan_fwd(a, &P);
+  if (rc) return rc;
+  const Shape& s = P.s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = s.dtype == LTXATTN_BF16;
+  if ((rc = check_tensor(a->q, "q", s, bf16 && !P.rope_q))) return rc;
+  if ((rc = check_tensor(a->k, "k", s, bf16 && !P.rope_k))) return rc;
+  if ((rc = check_tensor(a->v, "v", s, bf16))) return rc;
+  if ((rc = check_tensor(a->out, "out", s, bf16))) return rc;
+  if (P.total > 0) {
+    if (a->workspace == nullptr || a->workspace_bytes < P.total)
+      return fail(LTXATTN_ERR_WORKSPACE, "workspace of %zu bytes is needed, %zu given", P.total,
+                  a->workspace == nullptr ? (size_t)0 : a->workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(LTXATTN_ERR_ALIGN, "workspace must be 256-byte aligned");
+  }
+  int* err = device_error_word();
+  if (!err) return fail(LTXATTN_ERR_CUDA, "no device error word (is a CUDA device current?)");
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+
+  // inputs as the attention kernel sees them: rotated copies in the workspace
+  // (contiguous, local heads) or the caller's views
+  ltxattn_tensor q = a->q, k = a->k;
+  int q_head_off = s.h0, kv_head_off = s.h0;
+  cudaError_t e;
+  if (P.rope_q) {
+    RopeParams rp = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q, 0);
+    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope(q) launch");
+    q.data = ws + P.off_q;
+    q.stride_t = s.D;
+    q.stride_h = (int64_t)s.Lq * s.D;
+    q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
+    q_head_off = 0;
+  }
+  ltxattn_tensor v = a->v;
+  if (P.rope_k) {
+    RopeParams rp = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k, 0);
+    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope(k) launch");
+    k.data = ws + P.off_k;
+    k.stride_t = s.D;
+    k.stride_h = (int64_t)s.Lk * s.D;
+    k.stride_b = (int64_t)s.Hc * s.Lk * s.D;
+  }
+  const int k_head_off = P.rope_k ? 0 : s.h0;
+  const int v_head_off = s.h0;
+
+  if (!bf16) {
+    F32Params p{};
+    p.q = static_cast<const float*>(q.data);
+    p.k = static_cast<const float*>(k.data);
+    p.v = static_cast<const float*>(v.data);
+    p.q_sb = q.stride_b; p.q_sh = q.stride_h; p.q_st = q.stride_t;
+    p.k_sb = k.stride_b; p.k_sh = k.stride_h; p.k_st = k.stride_t;
+    p.v_sb = v.stride_b; p.v_sh = v.stride_h; p.v_st = v.stride_t;
+    p.q_head_off = q_head_off;
+    p.kv_head_off = 0;
+    // k and v may sit at different head offsets (k rotated into the workspace)
+    if (k_head_off != v_head_off) {
+      p.k = static_cast<const float*>(k.data);  // local heads
+      p.v = static_cast<const float*>(v.data) + (int64_t)v_head_off * v.stride_h;
+    } else {
+      p.kv_head_off = k_head_off;
+    }
+    p.out = static_cast<float*>(a->out.data);
+    p.o_sb = a->out.stride_b; p.o_sh = a->out.stride_h; p.o_st = a->out.stride_t;
+    p.lse = a->lse;
+    p.lse_sb = a->lse_stride_b; p.lse_sh = a->lse_stride_h;
+    p.mask = a->key_mask;
+    p.mask_sb = a->key_mask_stride_b;
+    p.Lq = s.Lq; p.Lk = s.Lk; p.head_begin = s.h0;
+    p.scale = a->scale;
+    e = launch_fwd_f32(p, s.D, s.Hc, s.B, st);
+    if (e != cudaSuccess) return cuda_fail(e, "fwd_f32 launch");
+    return LTXATTN_OK;
+  }
+
+  FwdParams p{};
+  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, P.rope_q ? s.Hc : s.H, s.B, q.stride_t, q.stride_h,
+                      q.stride_b, "q")))
+    return rc;
+  if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, P.rope_k ? s.Hc : s.H, s.B, k.stride_t, k.stride_h,
+                      k.stride_b, "k")))
+    return rc;
+  // v keeps the caller's head indexing; k may be local.  One kv_head_off
+  // serves both only when they agree, so v is re-based to local heads when
+  // k is a local copy.
+  const void* vptr = v.data;
+  int vH = s.H;
+  if (P.rope_k) {
+    vptr = static_cast<const __nv_bfloat16*>(v.data) + (int64_t)s.h0 * v.stride_h;
+    vH = s.Hc;
+    if (!aligned16(vptr)) return fail(LTXATTN_ERR_ALIGN, "v head block is not 16-byte aligned");
+  }
+  if ((rc = make_tmap(&p.tm_v, vptr, s.D, s.Lk, vH, s.B, v.stride_t, v.stride_h, v.stride_b, "v"))) return rc;
+  p.out = static_cast<__nv_bfloat16*>(a->out.data);
+  p.o_sb = a->out.stride_b;
+  p.o_sh = a->out.stride_h;
+  p.o_st = a->out.stride_t;
+  p.lse = a->lse;
+  p.lse_sb = a->lse_stride_b;
+  p.lse_sh = a->lse_stride_h;
+  p.mask = a->key_mask;
+  p.mask_sb = a->key_mask_stride_b;
+  p.Lq = s.Lq;
+  p.Lk = s.Lk;
+  p.head_begin = s.h0;
+  p.q_head_off = q_head_off;
+  p.kv_head_off = P.rope_k ? 0 : s.h0;
+  p.n_kv_tiles = P.kv_tiles;
+  p.num_splits = P.splits;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.part_o = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_po) : nullptr;
+  p.part_lse = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_pl) : nullptr;
+  p.err = err;
+  const size_t smem = fwd_bf16_smem_bytes(s.D, s.Lk, a->key_mask != nullptr);
+  e = launch_fwd_bf16(p, s.D, P.q_tiles, s.Hc, s.B, smem, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
+  if (P.splits > 1) {
+    CombineParams c{};
+    c.part_o = p.part_o;
+    c.part_lse = p.part_lse;
+    c.out = p.out;
+    c.o_sb = p.o_sb;
+    c.o_sh = p.o_sh;
+    c.o_st = p.o_st;
+    c.lse = a->lse;
+    c.lse_sb = a->lse_stride_b;
+    c.lse_sh = a->lse_stride_h;
+    c.B = s.B;
+    c.Hc = s.Hc;
+    c.Lq = s.Lq;
+    c.D = s.D;
+    c.num_splits = P.splits;
+    c.head_begin = s.h0;
+    e = launch_combine(c, st);
+    if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  }
+  return LTXATTN_OK;
+}
+
+size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* a) {
+  (void)a;
+  return 0;
+}
+
+int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
+  (void)a;
+  (void)stream;
+  return fail(LTXATTN_ERR_UNSUPPORTED, "backward is not built yet");
+}
+
+// ---------------------------------------------------------------------------
+// device discovery and status
+
+int ltxattn_device_count(int32_t* count) {
+  if (!count) return fail(LTXATTN_ERR_ARG, "count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return cuda_fail(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return LTXATTN_OK;
+}
+
+int ltxattn_device_query(int32_t device, ltxattn_device_info* info) {
+  if (!info) return fail(LTXATTN_ERR_ARG, "info is NULL");
+  memset(info, 0, sizeof *info);
+  cudaDeviceProp prop;
+  cudaError_t e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  snprintf(info->name, sizeof info->name, "%s", prop.name);
+  info->device = device;
+  info->cc_major = prop.major;
+  info->cc_minor = prop.minor;
+  info->sm_count = prop.multiProcessorCount;
+  info->total_memory_bytes = (int64_t)prop.totalGlobalMem;
+  info->max_smem_per_block_optin = (int32_t)prop.sharedMemPerBlockOptin;
+  info->l2_bytes = prop.l2CacheSize;
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrClockRate, device) == cudaSuccess) info->sm_clock_khz = v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMemoryClockRate, device) == cudaSuccess) info->mem_clock_khz = v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrGlobalMemoryBusWidth, device) == cudaSuccess)
+    info->mem_bus_width_bits = v;
+  int prev = 0;
+  if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(device) == cudaSuccess) {
+    size_t fr = 0, tot = 0;
+    if (cudaMemGetInfo(&fr, &tot) == cudaSuccess) info->free_memory_bytes = (int64_t)fr;
+    cudaSetDevice(prev);
+  }
+  info->supported = (prop.major == 10 && prop.minor == 0) ? 1 : 0;
+  return LTXATTN_OK;
+}
+
+int ltxattn_device_status(int32_t clear, int32_t* site) {
+  int* w = device_error_word();
+  if (!w) return fail(LTXATTN_ERR_CUDA, "no device error word");
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (clear && v != 0) {
+    const int z = 0;
+    e = cudaMemcpy(w, &z, sizeof z, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  if (site) *site = v >> 8;
+  if ((v & 0xff) == kErrTimeout)
+    return fail(LTXATTN_ERR_TIMEOUT, "a kernel wait gave up (site %d)", v >> 8);
+  return LTXATTN_OK;
+}
+
+}  // extern "C"

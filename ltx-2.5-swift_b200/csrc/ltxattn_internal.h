@@ -1,0 +1,100 @@
+// ltxattn_internal.h -- parameter blocks and launchers shared by the kernel
+// files and the C-ABI layer.  Not installed; the public surface is
+// include/ltxattn.h.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ltx {
+
+// Device error word encoding: (site << 8) | code.
+constexpr int kErrNone = 0;
+constexpr int kErrTimeout = 1;
+
+constexpr int kTileM = 128;            // query rows per CTA (UMMA M)
+constexpr int kTileN = 128;            // keys per KV tile (UMMA N of QK^T)
+constexpr int kMaxKvLen = 131072;      // 1024 KV tiles
+constexpr int kMaxKvTiles = kMaxKvLen / kTileN;
+constexpr int kMaxSplits = 32;
+
+// Forward, bf16 tcgen05 path.
+struct FwdParams {
+  CUtensorMap tm_q;  // [D, Lq, Hq, B] box {64, 128, 1, 1}, 128B swizzle
+  CUtensorMap tm_k;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
+  CUtensorMap tm_v;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_st;
+  float* lse;  // natural log, may be null
+  int64_t lse_sb, lse_sh;
+  const uint8_t* mask;  // [B, Lk] or null
+  int64_t mask_sb;
+  int Lq, Lk;
+  int head_begin;   // global index of local head 0 (out / lse / mask addressing)
+  int q_head_off;   // head coordinate of local head 0 in tm_q
+  int kv_head_off;  // head coordinate of local head 0 in tm_k / tm_v
+  int n_kv_tiles;
+  int num_splits;
+  float scale_log2;  // softmax scale * log2(e)
+  float* part_o;     // [splits][B][Hc][Lq][D] fp32 (num_splits > 1)
+  float* part_lse;   // [splits][B][Hc][Lq] log2 domain (num_splits > 1)
+  int* err;
+};
+
+// Forward, fp32 SIMT path (parity path for the float32 dtype).
+struct F32Params {
+  const float* q;
+  const float* k;
+  const float* v;
+  int64_t q_sb, q_sh, q_st;
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  int q_head_off, kv_head_off;  // head index of local head 0 in q / k,v
+  float* out;
+  int64_t o_sb, o_sh, o_st;
+  float* lse;
+  int64_t lse_sb, lse_sh;
+  const uint8_t* mask;
+  int64_t mask_sb;
+  int Lq, Lk, head_begin;
+  float scale;
+};
+
+// Split-RoPE pre-pass: y[b][hl][t][:] = rope(x[b][head_begin+hl][t][:]) into a
+// contiguous buffer.
+struct RopeParams {
+  const void* x;
+  int64_t x_sb, x_sh, x_st;
+  const void* cos;
+  const void* sin;
+  int64_t t_sb, t_sh, t_st;
+  void* y;  // contiguous [B][Hc][T][D]
+  int B, Hc, T, D, head_begin;
+  int inverse;  // 1: apply the transpose rotation (gradient path, no rounding)
+};
+
+struct CombineParams {
+  const float* part_o;
+  const float* part_lse;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_st;
+  float* lse;
+  int64_t lse_sb, lse_sh;
+  int B, Hc, Lq, D, num_splits, head_begin;
+};
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int B,
+                            size_t smem_bytes, cudaStream_t s);
+size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
+cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
+cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);
+cudaError_t launch_rope_bf16(const RopeParams& p, cudaStream_t s);
+cudaError_t launch_rope_f32(const RopeParams& p, cudaStream_t s);
+
+// Device error word of this module (one per device).
+int* device_error_word();
+
+}  // namespace ltx

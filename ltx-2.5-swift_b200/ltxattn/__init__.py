@@ -1,1 +1,11 @@
-"""Host side of libltxattn_cuda (filled in below)."""
+"""ltxattn -- host side of libltxattn_cuda, the B200 fused attention of the
+LTX 2.5 DiT (the path of DiTAttention.swift:364-382 in the reference).
+
+    from ltxattn import AttentionBackend, Rotary, scaled_dot_product_attention
+"""
+from . import _lib
+from .backend import (AttentionBackend, Failure, Rotary, Variant, device_info, device_status,
+                      scaled_dot_product_attention)
+
+__all__ = ["AttentionBackend", "Failure", "Rotary", "Variant", "scaled_dot_product_attention",
+           "device_info", "device_status", "_lib"]

@@ -1,0 +1,131 @@
+"""The C ABI without a GPU: the library loads, exports exactly what
+include/ltxattn.h declares, its structs have the layout the ctypes binding
+assumes, and argument validation refuses bad calls before touching a device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from ltxattn import _lib, backend
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ltxattn.h")
+
+
+def declared_entry_points():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if h.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", h)).read()
+            names |= set(re.findall(r"LTXATTN_API[^;(]*?\b(ltxattn_\w+)\s*\(", text))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.load()
+    declared = declared_entry_points()
+    assert declared, "no entry points parsed from include/"
+    assert set(_lib.EXPORTED) <= declared
+    for name in sorted(declared):
+        assert hasattr(L, name), f"{name} declared in include/ but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln and "ltxattn_" in ln}
+    assert exported == declared, f"exports differ from the header: {exported ^ declared}"
+    assert L.ltxattn_abi_version() == 1
+
+
+PROBE = r"""
+#include <stddef.h>
+#include <stdio.h>
+#include "ltxattn.h"
+#define P(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("ltxattn_tensor %zu\n", sizeof(ltxattn_tensor));
+  printf("ltxattn_rotary %zu\n", sizeof(ltxattn_rotary));
+  printf("ltxattn_fwd_args %zu\n", sizeof(ltxattn_fwd_args));
+  printf("ltxattn_bwd_args %zu\n", sizeof(ltxattn_bwd_args));
+  printf("ltxattn_gather_args %zu\n", sizeof(ltxattn_gather_args));
+  printf("ltxattn_device_info %zu\n", sizeof(ltxattn_device_info));
+  P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
+  P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
+  P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
+  P(ltxattn_bwd_args, dout) P(ltxattn_bwd_args, lse) P(ltxattn_bwd_args, dq) P(ltxattn_bwd_args, scale)
+  P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
+  P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
+  return 0;
+}
+"""
+
+
+def test_ctypes_layout_matches_the_header(tmp_path):
+    src = tmp_path / "probe.c"
+    src.write_text(PROBE)
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(ln.rsplit(" ", 1) for ln in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                         check=True).stdout.splitlines())
+    sizes = {"ltxattn_tensor": _lib.Tensor, "ltxattn_rotary": _lib.Rotary, "ltxattn_fwd_args": _lib.FwdArgs,
+             "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
+             "ltxattn_device_info": _lib.DeviceInfo}
+    for cname, py in sizes.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+    structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
+               "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo}
+    for key, val in got.items():
+        if "." in key:
+            s, f = key.split(".")
+            assert getattr(structs[s], f).offset == int(val), key
+
+
+def _args(**kw):
+    a = _lib.FwdArgs()
+    a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, 1, 2, 16, 16, 64
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(dtype=7), _lib.ERR_DTYPE),
+    (dict(head_dim=80), _lib.ERR_UNSUPPORTED),
+    (dict(head_dim=256), _lib.ERR_UNSUPPORTED),
+    (dict(batch=0), _lib.ERR_SHAPE),
+    (dict(kv_len=0), _lib.ERR_SHAPE),
+    (dict(head_begin=1, head_count=2), _lib.ERR_ARG),
+    (dict(kv_len=200000), _lib.ERR_UNSUPPORTED),
+])
+def test_validation_refuses_before_any_device_work(kw, status):
+    L = _lib.load()
+    rc = L.ltxattn_fwd(ctypes.byref(_args(**kw)), None)
+    assert rc == status, (_lib.last_error(), rc)
+    assert _lib.last_error() != ""
+    assert L.ltxattn_fwd_workspace(ctypes.byref(_args(**kw))) == 0
+
+
+def test_null_arguments():
+    L = _lib.load()
+    assert L.ltxattn_fwd(None, None) == _lib.ERR_ARG
+    assert L.ltxattn_device_count(None) == _lib.ERR_ARG
+    assert L.ltxattn_device_query(0, None) == _lib.ERR_ARG
+    assert L.ltxattn_allgather_heads(None, None, None) == _lib.ERR_ARG
+    assert L.ltxattn_comm_destroy(None) == _lib.OK
+
+
+def test_rotary_table_must_cover_the_tokens():
+    L = _lib.load()
+    a = _args()
+    a.q_rotary = _lib.Rotary(cos=1024, sin=2048, stride_b=0, stride_h=0, stride_t=32, tokens=8)
+    assert L.ltxattn_fwd(ctypes.byref(a), None) == _lib.ERR_SHAPE
+    assert "q_rotary covers 8 tokens" in _lib.last_error()
+
+
+def test_variant_rotary_rule_mirrors_the_reference():
+    # DiTAttention.swift:319-321: attn2 / audio_attn2 take no rotary embedding
+    assert not backend.Variant.video_cross.takes_rotary
+    assert not backend.Variant.audio_cross.takes_rotary
+    assert backend.Variant.audio_to_video.takes_rotary
+    e = backend.Failure.rotary_without_position(backend.Variant.video_cross)
+    assert e.kind == "rotaryWithoutPosition" and "attn2 takes no rotary" in str(e)
+    assert str(backend.Failure.shape("q", (1, 2), "[B, H, T, D]")) == "q is [1, 2], expected [B, H, T, D]"
