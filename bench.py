@@ -104,7 +104,7 @@ class Clocks:
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
                 "samples": len(rows)}
 
@@ -188,11 +188,17 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    clocks = Clocks(local)
+    clocks.start()
     for _ in range(args.warmup):
         step()
     barrier()
-    clocks = Clocks(local)
-    clocks.start()
+    # keep the GPU loaded for ~1.5 s so the clock sampler sees this workload under load
+    t_end = time.perf_counter() + 1.5
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     for i in range(args.steps):

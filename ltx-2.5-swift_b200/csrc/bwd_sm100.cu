@@ -1,0 +1,564 @@
+// bwd_sm100.cu -- bf16 attention backward on tcgen05 (sm_100a).
+//
+// The reference trains LoRA adapters through MLX's autodiff VJP of the fused
+// SDPA under per-block gradient checkpointing (LoRATrainingStep.swift:283-304,
+// GradientCheckpoint.swift:48-67, DiTForward.swift:1012-1049).  This is that
+// VJP in closed form, with P recomputed from the forward's saved per-row
+// log-sum-exp, so no score matrix is ever stored:
+//
+//   P  = exp(scale*QK^T - lse)          dV = P^T dO
+//   dP = dO V^T                         dS = P o (dP - Delta),  Delta = rowsum(dO o O)
+//   dQ = scale * dS K                   dK = scale * dS^T Q
+//
+// Three launches, all deterministic (no atomics, so a recomputed step is
+// bit-identical, as gradient checkpointing expects):
+//   bwd_prep_kernel   Delta and lse*log2(e) per query row, padded to 128 rows
+//   bwd_dq_kernel     Q-stationary: per 128-row Q tile, loop over KV tiles;
+//                     TMEM: S [0,128), dP [128,256), dQ [256,256+D)
+//   bwd_dkdv_kernel   KV-stationary: per 128-key tile, loop over Q tiles;
+//                     TMEM: S^T [0,128), dP^T [128,256), dV [256,..), dK [384,..)
+// In both, the softmax warps turn S/dP into bf16 P or dS in place (TMEM) and
+// the PV-style products read them straight from TMEM (tcgen05.mma A-from-TMEM).
+// When rotary tables are given, dQ and dK leave through the transpose
+// rotation: the gradient with respect to the un-rotated input.
+#include "ltxattn_internal.h"
+#include "sm100.cuh"
+
+namespace ltx {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr uint32_t kChunkBytes = 128u * 128u;
+
+// column validity of 32 keys starting at key0 (mask bits in smem, tail by length)
+__device__ __forceinline__ uint32_t key_bits(const uint32_t* mbits, bool use_mask, int key0, int Lk) {
+  uint32_t bits = use_mask ? mbits[key0 / 32] : 0xffffffffu;
+  const int lim = Lk - key0;
+  if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
+  return bits;
+}
+
+// Build mask bits for all KV tiles of batch b (zero-padded to whole tiles) and
+// report whether any key is valid.  Every thread of the CTA calls this.
+__device__ __forceinline__ int load_mask_bits(const BwdParams& p, int b, uint32_t* mbits) {
+  int local_any = 0;
+  if (p.mask != nullptr) {
+    const uint8_t* mrow = p.mask + (int64_t)b * p.mask_sb;
+    const int nwords = p.n_kv_tiles * (kTileN / 32);
+    for (int w = threadIdx.x; w < nwords; w += kThreads) {
+      uint32_t bits = 0;
+      const int k0 = w * 32;
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) {
+        const int key = k0 + i;
+        if (key < p.Lk && mrow[key] != 0) bits |= 1u << i;
+      }
+      mbits[w] = bits;
+      local_any |= (bits != 0);
+    }
+  }
+  return __syncthreads_or(local_any);
+}
+
+// ---------------------------------------------------------------------------
+// Delta = rowsum(dO o O) and lse2 = lse * log2(e); padded rows get Delta 0 and
+// lse2 = +inf, so their recomputed P is exactly 0.  One warp per row.
+
+template <int D>
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)p.B * p.Hc * p.Lq_pad;
+  if (gw >= rows) return;
+  const int row = (int)(gw % p.Lq_pad);
+  const int hl = (int)((gw / p.Lq_pad) % p.Hc);
+  const int b = (int)(gw / ((int64_t)p.Lq_pad * p.Hc));
+  float acc = 0.f;
+  if (row < p.Lq) {
+    const __nv_bfloat16* o = p.o + (int64_t)b * p.o_sb + (int64_t)hl * p.o_sh + (int64_t)row * p.o_st;
+    const __nv_bfloat16* g = p.dout + (int64_t)b * p.do_sb + (int64_t)hl * p.do_sh + (int64_t)row * p.do_st;
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) acc += __bfloat162float(o[lane + 32 * e]) * __bfloat162float(g[lane + 32 * e]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    p.delta[gw] = acc;
+    p.lse2[gw] = (row < p.Lq) ? p.lse[(int64_t)b * p.lse_sb + (int64_t)hl * p.lse_sh + row] * 1.4426950408889634f
+                              : INFINITY;
+  }
+}
+
+// Transpose rotation of one row held as D fp32 values in registers.
+template <int D>
+__device__ __forceinline__ void rope_inverse_row(float (&g)[D], const __nv_bfloat16* c, const __nv_bfloat16* s) {
+#pragma unroll
+  for (int i = 0; i < D / 2; ++i) {
+    const float cc = __bfloat162float(c[i]), ss = __bfloat162float(s[i]);
+    const float g1 = g[i], g2 = g[i + D / 2];
+    g[i] = __fadd_rn(__fmul_rn(g1, cc), __fmul_rn(g2, ss));
+    g[i + D / 2] = __fsub_rn(__fmul_rn(g2, cc), __fmul_rn(g1, ss));
+  }
+}
+
+// Load D fp32 columns of this thread's TMEM lane starting at taddr.
+template <int D>
+__device__ __forceinline__ void tmem_row(uint32_t taddr, float (&g)[D]) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) g[c * 32 + e] = __uint_as_float(r[e]);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&g)[D], float mul) {
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    uint4 v = make_uint4(pack_bf16x2(g[8 * c] * mul, g[8 * c + 1] * mul), pack_bf16x2(g[8 * c + 2] * mul, g[8 * c + 3] * mul),
+                         pack_bf16x2(g[8 * c + 4] * mul, g[8 * c + 5] * mul), pack_bf16x2(g[8 * c + 6] * mul, g[8 * c + 7] * mul));
+    reinterpret_cast<uint4*>(dst)[c] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ: Q-stationary
+
+template <int D>
+struct DqSmem {
+  static constexpr int kChunks = D / 64;
+  static constexpr uint32_t kTile = kChunks * kChunkBytes;
+  static constexpr uint32_t kOffQ = 0, kOffDO = kTile, kOffK0 = 2 * kTile, kOffV0 = 3 * kTile,
+                            kOffK1 = 4 * kTile, kOffV1 = 5 * kTile;
+  static constexpr uint32_t kOffBar = 6 * kTile;  // q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full
+  static constexpr uint32_t kOffCtl = kOffBar + 8 * 8;
+  static constexpr uint32_t kOffTiles = kOffCtl + 16;
+  static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+  using S = DqSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sQ = sm + S::kOffQ;
+  uint8_t* sDO = sm + S::kOffDO;
+  uint8_t* sK[2] = {sm + S::kOffK0, sm + S::kOffK1};
+  uint8_t* sV[2] = {sm + S::kOffV0, sm + S::kOffV1};
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* bar_kvf = bars + 1;  // [2]
+  uint64_t* bar_kve = bars + 3;  // [2]
+  uint64_t* bar_s = bars + 5;
+  uint64_t* bar_p = bars + 6;
+  uint64_t* bar_o = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+  int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
+  uint16_t* tiles = reinterpret_cast<uint16_t*>(sm + S::kOffTiles);
+  uint32_t* mbits = reinterpret_cast<uint32_t*>(sm + S::kOffBits);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * kTileM, hl = blockIdx.y, b = blockIdx.z;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(bars + i, i == 6 ? 128 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  const bool use_mask = p.mask != nullptr && load_mask_bits(p, b, mbits) != 0;
+  if (warp == 0) {
+    int count = 0;
+    for (int j0 = 0; j0 < p.n_kv_tiles; j0 += 32) {
+      const int j = j0 + lane;
+      bool act = j < p.n_kv_tiles;
+      if (act && use_mask) act = (mbits[4 * j] | mbits[4 * j + 1] | mbits[4 * j + 2] | mbits[4 * j + 3]) != 0u;
+      const unsigned bal = __ballot_sync(0xffffffffu, act);
+      if (act) tiles[count + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint16_t>(j);
+      count += __popc(bal);
+    }
+    if (lane == 0) *n_tiles_slot = count;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n = *n_tiles_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && n > 0) {
+      int issued = 0;
+      mbar_arrive_expect_tx(bar_q, 2 * S::kTile);
+#pragma unroll
+      for (int c = 0; c < S::kChunks; ++c) {
+        tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, hl, b);
+        tma_load_4d(&p.tm_do, bar_q, sDO + c * kChunkBytes, c * 64, q0, hl, b);
+      }
+      for (int i = 0; i < n; ++i) {
+        const int st = i & 1;
+        if (i >= 2 && !mbar_wait(bar_kve + st, ((i >> 1) - 1) & 1, abort_flag, p.err, 21)) break;
+        const int kv0 = (int)tiles[i] * kTileN;
+        mbar_arrive_expect_tx(bar_kvf + st, 2 * S::kTile);
+#pragma unroll
+        for (int c = 0; c < S::kChunks; ++c) {
+          tma_load_4d(&p.tm_k, bar_kvf + st, sK[st] + c * kChunkBytes, c * 64, kv0, hl, b);
+          tma_load_4d(&p.tm_v, bar_kvf + st, sV[st] + c * kChunkBytes, c * 64, kv0, hl, b);
+        }
+        ++issued;
+      }
+      drain_wait(bar_q, 0);
+      for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i) drain_wait(bar_kvf + (i & 1), (i >> 1) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0 && n > 0) {
+      const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idesc_dq = idesc_bf16_f32(128, D, 0, 1);
+      const uint32_t tS = tmem, tP = tmem + 128, tQ = tmem + 256;
+      const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      if (mbar_wait(bar_q, 0, abort_flag, p.err, 22)) {
+        for (int i = 0; i < n; ++i) {
+          const int st = i & 1;
+          if (!mbar_wait(bar_kvf + st, (i >> 1) & 1, abort_flag, p.err, 23)) break;
+          tc_fence_after();
+          const uint32_t aK = smem_u32(sK[st]), aV = smem_u32(sV[st]);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+            umma_ss(tS, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idesc_s, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+            umma_ss(tP, sdesc_sw128(aDO + off, 16, 1024), sdesc_sw128(aV + off, 16, 1024), idesc_s, kk > 0);
+          }
+          umma_commit(bar_s);
+          if (!mbar_wait(bar_p, i & 1, abort_flag, p.err, 24)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk)
+            umma_ts(tQ, tS + kk * 8, sdesc_sw128(aK + kk * 16 * 128, kChunkBytes, 1024), idesc_dq,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar_kve + st);
+        }
+      }
+      umma_commit(bar_o);
+      drain_wait(bar_o, 0);
+    }
+    __syncwarp();
+  } else {
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tP = tmem + 128 + lane_off, tQ = tmem + 256 + lane_off;
+    const int row = q0 + threadIdx.x;
+    const int64_t rix = ((int64_t)b * gridDim.y + hl) * p.Lq_pad + row;
+    const float lse2 = p.lse2[rix];
+    const float delta = p.delta[rix];
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      if (!warp_wait(bar_s, i & 1, abort_flag, p.err, 25)) { ok = false; break; }
+      tc_fence_after();
+      const int kv0 = (int)tiles[i] * kTileN;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tS + c * 32, rs);
+        tmem_ld32(tP + c * 32, rp);
+        tmem_wait_ld();
+        const uint32_t bits = key_bits(mbits, use_mask, kv0 + 32 * c, p.Lk);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ((bits >> (2 * e)) & 1u) ? fast_exp2(fmaf(__uint_as_float(rs[2 * e]), sl2, -lse2)) : 0.f;
+          const float p1 = ((bits >> (2 * e + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(rs[2 * e + 1]), sl2, -lse2)) : 0.f;
+          pk[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - delta), p1 * (__uint_as_float(rp[2 * e + 1]) - delta));
+        }
+        tmem_st16(tS + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p);
+    }
+    const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
+    tc_fence_after();
+    float g[D];
+    if (have) {
+      tmem_row<D>(tQ, g);
+    } else {
+#pragma unroll
+      for (int e = 0; e < D; ++e) g[e] = 0.f;
+    }
+    if (row < p.Lq) {
+#pragma unroll
+      for (int e = 0; e < D; ++e) g[e] *= p.scale;
+      if (p.qcos != nullptr)
+        rope_inverse_row<D>(g, p.qcos + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
+                            p.qsin + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
+      store_row_bf16<D>(p.dq + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dK, dV: KV-stationary
+
+template <int D>
+struct DkvSmem {
+  static constexpr int kChunks = D / 64;
+  static constexpr uint32_t kTile = kChunks * kChunkBytes;
+  static constexpr uint32_t kOffK = 0, kOffV = kTile, kOffQ0 = 2 * kTile, kOffDO0 = 3 * kTile,
+                            kOffQ1 = 4 * kTile, kOffDO1 = 5 * kTile;
+  static constexpr uint32_t kOffL = 6 * kTile;  // lse2[2][128], delta[2][128]
+  static constexpr uint32_t kOffBar = kOffL + 4 * 128 * 4;  // kv_full, q_full[2], q_empty[2], s_full, p_full, o_full
+  static constexpr uint32_t kOffCtl = kOffBar + 8 * 8;
+  static constexpr uint32_t kOffBits = kOffCtl + 16;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
+  using S = DkvSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sK = sm + S::kOffK;
+  uint8_t* sV = sm + S::kOffV;
+  uint8_t* sQ[2] = {sm + S::kOffQ0, sm + S::kOffQ1};
+  uint8_t* sDO[2] = {sm + S::kOffDO0, sm + S::kOffDO1};
+  float* sL = reinterpret_cast<float*>(sm + S::kOffL);  // lse2: sL[st*128 + q]; delta: sL[256 + st*128 + q]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* bar_kv = bars + 0;
+  uint64_t* bar_qf = bars + 1;  // [2]
+  uint64_t* bar_qe = bars + 3;  // [2]
+  uint64_t* bar_s = bars + 5;
+  uint64_t* bar_p = bars + 6;
+  uint64_t* bar_o = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+  uint32_t* mbits = reinterpret_cast<uint32_t*>(sm + S::kOffBits);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kv0 = blockIdx.x * kTileN, hl = blockIdx.y, b = blockIdx.z;
+  const int nq = p.n_q_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(bars + i, i == 6 ? 128 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  const bool use_mask = p.mask != nullptr && load_mask_bits(p, b, mbits) != 0;
+  uint32_t tile_bits = 0;
+  if (use_mask) {
+    const uint32_t* w4 = mbits + (kv0 / 32);
+    tile_bits = w4[0] | w4[1] | w4[2] | w4[3];
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // a KV tile whose keys are all masked gets zero gradients and no work
+  const int n = (use_mask && tile_bits == 0) ? 0 : nq;
+  const int64_t lrow = ((int64_t)b * gridDim.y + hl) * p.Lq_pad;
+
+  if (warp == 4) {
+    if (lane == 0 && n > 0) {
+      int issued = 0;
+      mbar_arrive_expect_tx(bar_kv, 2 * S::kTile);
+#pragma unroll
+      for (int c = 0; c < S::kChunks; ++c) {
+        tma_load_4d(&p.tm_k, bar_kv, sK + c * kChunkBytes, c * 64, kv0, hl, b);
+        tma_load_4d(&p.tm_v, bar_kv, sV + c * kChunkBytes, c * 64, kv0, hl, b);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(bar_qe + st, ((j >> 1) - 1) & 1, abort_flag, p.err, 31)) break;
+        const int q0 = j * kTileM;
+        mbar_arrive_expect_tx(bar_qf + st, 2 * S::kTile + 2 * 128 * 4);
+#pragma unroll
+        for (int c = 0; c < S::kChunks; ++c) {
+          tma_load_4d(&p.tm_q, bar_qf + st, sQ[st] + c * kChunkBytes, c * 64, q0, hl, b);
+          tma_load_4d(&p.tm_do, bar_qf + st, sDO[st] + c * kChunkBytes, c * 64, q0, hl, b);
+        }
+        bulk_load(sL + st * 128, p.lse2 + lrow + q0, 128 * 4, bar_qf + st);
+        bulk_load(sL + 256 + st * 128, p.delta + lrow + q0, 128 * 4, bar_qf + st);
+        ++issued;
+      }
+      drain_wait(bar_kv, 0);
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) drain_wait(bar_qf + (j & 1), (j >> 1) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0 && n > 0) {
+      const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idesc_g = idesc_bf16_f32(128, D, 0, 1);
+      const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 384;
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      if (mbar_wait(bar_kv, 0, abort_flag, p.err, 32)) {
+        for (int j = 0; j < n; ++j) {
+          const int st = j & 1;
+          if (!mbar_wait(bar_qf + st, (j >> 1) & 1, abort_flag, p.err, 33)) break;
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(sQ[st]), aDO = smem_u32(sDO[st]);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+            umma_ss(tS, sdesc_sw128(aK + off, 16, 1024), sdesc_sw128(aQ + off, 16, 1024), idesc_s, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+            umma_ss(tP, sdesc_sw128(aV + off, 16, 1024), sdesc_sw128(aDO + off, 16, 1024), idesc_s, kk > 0);
+          }
+          umma_commit(bar_s);
+          if (!mbar_wait(bar_p, j & 1, abort_flag, p.err, 34)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTileM / 16; ++kk)
+            umma_ts(tV, tS + kk * 8, sdesc_sw128(aDO + kk * 16 * 128, kChunkBytes, 1024), idesc_g,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kTileM / 16; ++kk)
+            umma_ts(tK, tP + kk * 8, sdesc_sw128(aQ + kk * 16 * 128, kChunkBytes, 1024), idesc_g,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar_qe + st);
+        }
+      }
+      umma_commit(bar_o);
+      drain_wait(bar_o, 0);
+    }
+    __syncwarp();
+  } else {
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tP = tmem + 128 + lane_off;
+    const uint32_t tV = tmem + 256 + lane_off, tK = tmem + 384 + lane_off;
+    const int key = kv0 + threadIdx.x;
+    bool kvalid = key < p.Lk;
+    if (use_mask && kvalid) kvalid = (mbits[key / 32] >> (key % 32)) & 1u;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int st = j & 1;
+      if (!warp_wait(bar_s, j & 1, abort_flag, p.err, 35)) { ok = false; break; }
+      // the lse / delta rows arrived with the Q tile
+      if (!warp_wait(bar_qf + st, (j >> 1) & 1, abort_flag, p.err, 36)) { ok = false; break; }
+      tc_fence_after();
+      const float* L2 = sL + st * 128;
+      const float* DL = sL + 256 + st * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tS + c * 32, rs);
+        tmem_ld32(tP + c * 32, rp);
+        tmem_wait_ld();
+        uint32_t pp[16], pd[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int q = c * 32 + 2 * e;
+          const float p0 = kvalid ? fast_exp2(fmaf(__uint_as_float(rs[2 * e]), sl2, -L2[q])) : 0.f;
+          const float p1 = kvalid ? fast_exp2(fmaf(__uint_as_float(rs[2 * e + 1]), sl2, -L2[q + 1])) : 0.f;
+          pp[e] = pack_bf16x2(p0, p1);
+          pd[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - DL[q]), p1 * (__uint_as_float(rp[2 * e + 1]) - DL[q + 1]));
+        }
+        tmem_st16(tS + c * 16, pp);
+        tmem_st16(tP + c * 16, pd);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p);
+    }
+    const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 37);
+    tc_fence_after();
+    float g[D];
+    if (have) {
+      tmem_row<D>(tV, g);
+    } else {
+#pragma unroll
+      for (int e = 0; e < D; ++e) g[e] = 0.f;
+    }
+    if (key < p.Lk)
+      store_row_bf16<D>(p.dv + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
+    if (have) {
+      tmem_row<D>(tK, g);
+    }
+    if (key < p.Lk) {
+#pragma unroll
+      for (int e = 0; e < D; ++e) g[e] *= p.scale;
+      if (p.kcos != nullptr)
+        rope_inverse_row<D>(g, p.kcos + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
+                            p.ksin + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
+      store_row_bf16<D>(p.dk + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <typename K>
+cudaError_t set_smem(K kernel, size_t smem) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+}  // namespace
+
+size_t bwd_dq_smem_bytes(int D, int Lk, bool has_mask) {
+  const int n_tiles = (Lk + kTileN - 1) / kTileN;
+  const size_t fixed = D == 128 ? DqSmem<128>::kOffBits : DqSmem<64>::kOffBits;
+  return 1024 + fixed + (has_mask ? (size_t)n_tiles * 16 : 0);
+}
+
+size_t bwd_dkdv_smem_bytes(int D, int Lk, bool has_mask) {
+  const int n_tiles = (Lk + kTileN - 1) / kTileN;
+  const size_t fixed = D == 128 ? DkvSmem<128>::kOffBits : DkvSmem<64>::kOffBits;
+  return 1024 + fixed + (has_mask ? (size_t)n_tiles * 16 : 0);
+}
+
+cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s) {
+  const int64_t threads = (int64_t)p.B * p.Hc * p.Lq_pad * 32;
+  const int blocks = (int)((threads + 255) / 256);
+  if (p.D == 128)
+    bwd_prep_kernel<128><<<blocks, 256, 0, s>>>(p);
+  else
+    bwd_prep_kernel<64><<<blocks, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_bf16(const BwdParams& p, int D, int Hc, int B, size_t smem_dq, size_t smem_dkdv,
+                            cudaStream_t s) {
+  dim3 gdq(p.n_q_tiles, Hc, B), gkv(p.n_kv_tiles, Hc, B);
+  cudaError_t e;
+  if (D == 128) {
+    if ((e = set_smem(bwd_dq_kernel<128>, smem_dq)) != cudaSuccess) return e;
+    if ((e = set_smem(bwd_dkdv_kernel<128>, smem_dkdv)) != cudaSuccess) return e;
+    bwd_dq_kernel<128><<<gdq, kThreads, smem_dq, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    bwd_dkdv_kernel<128><<<gkv, kThreads, smem_dkdv, s>>>(p);
+  } else {
+    if ((e = set_smem(bwd_dq_kernel<64>, smem_dq)) != cudaSuccess) return e;
+    if ((e = set_smem(bwd_dkdv_kernel<64>, smem_dkdv)) != cudaSuccess) return e;
+    bwd_dq_kernel<64><<<gdq, kThreads, smem_dq, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    bwd_dkdv_kernel<64><<<gkv, kThreads, smem_dkdv, s>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ltx

@@ -61,29 +61,6 @@ struct Smem {
   static constexpr uint32_t kFixed = kOffBits;
 };
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
-
-// Lane-0 waits, the warp learns the outcome; keeps .sync.aligned tcgen05 ops
-// warp-uniform even when a wait gives up.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int site) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err, site) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
-// Drain wait used only on the way out: bounded, ignores the abort flag.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) break;
-  }
-}
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __grid_constant__ FwdParams p) {
   using S = Smem<D>;

@@ -258,6 +258,42 @@ __device__ __forceinline__ void tmem_wait_st() {
 #undef LTX_W8
 
 // ---------------------------------------------------------------------------
+// CTA-level helpers shared by the attention kernels
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Lane-0 waits, the warp learns the outcome; keeps .sync.aligned tcgen05 ops
+// warp-uniform even when a wait gives up.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int site) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err, site) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// Drain wait used only on the way out: bounded, ignores the abort flag.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) break;
+  }
+}
+
+// 1D bulk copy global -> shared, completion counted on `bar` (16-byte aligned,
+// size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // small numeric helpers
 
 __device__ __forceinline__ float fast_exp2(float x) {
