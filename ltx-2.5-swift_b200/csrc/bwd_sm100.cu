@@ -30,6 +30,9 @@ namespace {
 constexpr int kThreads = 192;
 constexpr uint32_t kChunkBytes = 128u * 128u;
 
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
 // column validity of 32 keys starting at key0 (mask bits in smem, tail by length)
 __device__ __forceinline__ uint32_t key_bits(const uint32_t* mbits, bool use_mask, int key0, int Lk) {
   uint32_t bits = use_mask ? mbits[key0 / 32] : 0xffffffffu;
@@ -61,10 +64,11 @@ __device__ __forceinline__ int load_mask_bits(const BwdParams& p, int b, uint32_
 }
 
 // ---------------------------------------------------------------------------
-// Delta = rowsum(dO o O) and lse2 = lse * log2(e); padded rows get Delta 0 and
-// lse2 = +inf, so their recomputed P is exactly 0.  One warp per row.
+// Delta = rowsum(dO o O) and the row's lse (times log2(e) for the bf16
+// kernels); padded rows get Delta 0 and lse +inf, so their recomputed P is
+// exactly 0.  One warp per row.
 
-template <int D>
+template <int D, typename T>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -75,17 +79,17 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
   const int b = (int)(gw / ((int64_t)p.Lq_pad * p.Hc));
   float acc = 0.f;
   if (row < p.Lq) {
-    const __nv_bfloat16* o = p.o + (int64_t)b * p.o_sb + (int64_t)hl * p.o_sh + (int64_t)row * p.o_st;
-    const __nv_bfloat16* g = p.dout + (int64_t)b * p.do_sb + (int64_t)hl * p.do_sh + (int64_t)row * p.do_st;
+    const T* o = static_cast<const T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)hl * p.o_sh + (int64_t)row * p.o_st;
+    const T* g = static_cast<const T*>(p.dout) + (int64_t)b * p.do_sb + (int64_t)hl * p.do_sh + (int64_t)row * p.do_st;
 #pragma unroll
-    for (int e = 0; e < D / 32; ++e) acc += __bfloat162float(o[lane + 32 * e]) * __bfloat162float(g[lane + 32 * e]);
+    for (int e = 0; e < D / 32; ++e) acc += to_f32(o[lane + 32 * e]) * to_f32(g[lane + 32 * e]);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) {
     p.delta[gw] = acc;
-    p.lse2[gw] = (row < p.Lq) ? p.lse[(int64_t)b * p.lse_sb + (int64_t)hl * p.lse_sh + row] * 1.4426950408889634f
-                              : INFINITY;
+    const float l = (row < p.Lq) ? p.lse[(int64_t)b * p.lse_sb + (int64_t)hl * p.lse_sh + row] : INFINITY;
+    p.lse2[gw] = (p.log2_domain && row < p.Lq) ? l * 1.4426950408889634f : l;
   }
 }
 
@@ -299,9 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
 #pragma unroll
       for (int e = 0; e < D; ++e) g[e] *= p.scale;
       if (p.qcos != nullptr)
-        rope_inverse_row<D>(g, p.qcos + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
-                            p.qsin + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
-      store_row_bf16<D>(p.dq + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
+        rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.qcos) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
+                            static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
+      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
     }
   }
   tc_fence_before();
@@ -491,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       for (int e = 0; e < D; ++e) g[e] = 0.f;
     }
     if (key < p.Lk)
-      store_row_bf16<D>(p.dv + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
+      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
     if (have) {
       tmem_row<D>(tK, g);
     }
@@ -499,9 +503,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
 #pragma unroll
       for (int e = 0; e < D; ++e) g[e] *= p.scale;
       if (p.kcos != nullptr)
-        rope_inverse_row<D>(g, p.kcos + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
-                            p.ksin + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
-      store_row_bf16<D>(p.dk + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
+        rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.kcos) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
+                            static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
+      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
     }
   }
   tc_fence_before();
@@ -534,10 +538,17 @@ size_t bwd_dkdv_smem_bytes(int D, int Lk, bool has_mask) {
 cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s) {
   const int64_t threads = (int64_t)p.B * p.Hc * p.Lq_pad * 32;
   const int blocks = (int)((threads + 255) / 256);
-  if (p.D == 128)
-    bwd_prep_kernel<128><<<blocks, 256, 0, s>>>(p);
-  else
-    bwd_prep_kernel<64><<<blocks, 256, 0, s>>>(p);
+  if (p.f32) {
+    if (p.D == 128)
+      bwd_prep_kernel<128, float><<<blocks, 256, 0, s>>>(p);
+    else
+      bwd_prep_kernel<64, float><<<blocks, 256, 0, s>>>(p);
+  } else {
+    if (p.D == 128)
+      bwd_prep_kernel<128, __nv_bfloat16><<<blocks, 256, 0, s>>>(p);
+    else
+      bwd_prep_kernel<64, __nv_bfloat16><<<blocks, 256, 0, s>>>(p);
+  }
   return cudaGetLastError();
 }
 

@@ -204,6 +204,40 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   return LTXATTN_OK;
 }
 
+struct BwdPlan {
+  Shape s;
+  bool rope;
+  const ltxattn_rotary* kr;
+  int Lq_pad;
+  size_t off_q, off_k, off_l, off_d, total;
+};
+
+int plan_bwd(const ltxattn_bwd_args* a, BwdPlan* P) {
+  if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
+  int rc = check_shape(a->dtype, a->batch, a->heads, a->q_len, a->kv_len, a->head_dim, a->head_begin,
+                       a->head_count, &P->s);
+  if (rc) return rc;
+  const Shape& s = P->s;
+  P->rope = a->q_rotary.cos != nullptr;
+  P->kr = (a->k_rotary.cos != nullptr) ? &a->k_rotary : &a->q_rotary;
+  if (P->rope) {
+    if ((rc = check_rotary(a->q_rotary, "q_rotary", s.Lq))) return rc;
+    if ((rc = check_rotary(*P->kr, a->k_rotary.cos ? "k_rotary" : "q_rotary (used for k)", s.Lk))) return rc;
+  }
+  P->Lq_pad = (s.Lq + kTileM - 1) / kTileM * kTileM;
+  size_t off = 0;
+  P->off_q = off;
+  if (P->rope) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
+  P->off_k = off;
+  if (P->rope) off += align256((size_t)s.B * s.Hc * s.Lk * s.D * s.esize);
+  P->off_l = off;
+  off += align256((size_t)s.B * s.Hc * P->Lq_pad * sizeof(float));
+  P->off_d = off;
+  off += align256((size_t)s.B * s.Hc * P->Lq_pad * sizeof(float));
+  P->total = off;
+  return LTXATTN_OK;
+}
+
 RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const Shape& s, int T, void* y,
                        int inverse) {
   RopeParams p{};
@@ -400,14 +434,132 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
 }
 
 size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* a) {
-  (void)a;
-  return 0;
+  BwdPlan P;
+  if (plan_bwd(a, &P) != LTXATTN_OK) return 0;
+  return P.total;
 }
 
 int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
-  (void)a;
-  (void)stream;
-  return fail(LTXATTN_ERR_UNSUPPORTED, "backward is not built yet");
+  BwdPlan P;
+  int rc = plan_bwd(a, &P);
+  if (rc) return rc;
+  const Shape& s = P.s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = s.dtype == LTXATTN_BF16;
+  if ((rc = check_tensor(a->q, "q", s, bf16 && !P.rope))) return rc;
+  if ((rc = check_tensor(a->k, "k", s, bf16 && !P.rope))) return rc;
+  if ((rc = check_tensor(a->v, "v", s, bf16))) return rc;
+  if ((rc = check_tensor(a->out, "out", s, false))) return rc;
+  if ((rc = check_tensor(a->dout, "dout", s, bf16))) return rc;
+  if ((rc = check_tensor(a->dq, "dq", s, bf16))) return rc;
+  if ((rc = check_tensor(a->dk, "dk", s, bf16))) return rc;
+  if ((rc = check_tensor(a->dv, "dv", s, bf16))) return rc;
+  if (a->lse == nullptr) return fail(LTXATTN_ERR_ARG, "lse is NULL (the backward recomputes P from it)");
+  if (a->workspace == nullptr || a->workspace_bytes < P.total)
+    return fail(LTXATTN_ERR_WORKSPACE, "workspace of %zu bytes is needed, %zu given", P.total,
+                a->workspace == nullptr ? (size_t)0 : a->workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+    return fail(LTXATTN_ERR_ALIGN, "workspace must be 256-byte aligned");
+  int* err = device_error_word();
+  if (!err) return fail(LTXATTN_ERR_CUDA, "no device error word (is a CUDA device current?)");
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  const size_t es = s.esize;
+  const int64_t h0 = s.h0;
+  // every view below is based at local head 0
+  auto at = [&](const ltxattn_tensor& t) {
+    return static_cast<const void*>(static_cast<const uint8_t*>(t.data) + h0 * t.stride_h * (int64_t)es);
+  };
+  ltxattn_tensor q = a->q, k = a->k;
+  q.data = const_cast<void*>(at(a->q));
+  k.data = const_cast<void*>(at(a->k));
+  cudaError_t e;
+  if (P.rope) {
+    RopeParams rp = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q, 0);
+    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope(q) launch");
+    rp = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k, 0);
+    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope(k) launch");
+    q.data = ws + P.off_q;
+    q.stride_t = s.D;
+    q.stride_h = (int64_t)s.Lq * s.D;
+    q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
+    k.data = ws + P.off_k;
+    k.stride_t = s.D;
+    k.stride_h = (int64_t)s.Lk * s.D;
+    k.stride_b = (int64_t)s.Hc * s.Lk * s.D;
+  }
+  float* lse2 = reinterpret_cast<float*>(ws + P.off_l);
+  float* delta = reinterpret_cast<float*>(ws + P.off_d);
+  BwdPrepParams pp{};
+  pp.o = at(a->out);
+  pp.o_sb = a->out.stride_b; pp.o_sh = a->out.stride_h; pp.o_st = a->out.stride_t;
+  pp.dout = at(a->dout);
+  pp.do_sb = a->dout.stride_b; pp.do_sh = a->dout.stride_h; pp.do_st = a->dout.stride_t;
+  pp.lse = a->lse + h0 * a->lse_stride_h;
+  pp.lse_sb = a->lse_stride_b; pp.lse_sh = a->lse_stride_h;
+  pp.lse2 = lse2;
+  pp.delta = delta;
+  pp.B = s.B; pp.Hc = s.Hc; pp.Lq = s.Lq; pp.Lq_pad = P.Lq_pad; pp.D = s.D;
+  pp.log2_domain = bf16 ? 1 : 0;
+  pp.f32 = bf16 ? 0 : 1;
+  e = launch_bwd_prep(pp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "bwd prep launch");
+
+  BwdParams p{};
+  p.lse2 = lse2;
+  p.delta = delta;
+  p.Lq_pad = P.Lq_pad;
+  p.dq = const_cast<void*>(at(a->dq));
+  p.dq_sb = a->dq.stride_b; p.dq_sh = a->dq.stride_h; p.dq_st = a->dq.stride_t;
+  p.dk = const_cast<void*>(at(a->dk));
+  p.dk_sb = a->dk.stride_b; p.dk_sh = a->dk.stride_h; p.dk_st = a->dk.stride_t;
+  p.dv = const_cast<void*>(at(a->dv));
+  p.dv_sb = a->dv.stride_b; p.dv_sh = a->dv.stride_h; p.dv_st = a->dv.stride_t;
+  p.mask = a->key_mask;
+  p.mask_sb = a->key_mask_stride_b;
+  if (P.rope) {
+    const ltxattn_rotary& qr = a->q_rotary;
+    const ltxattn_rotary& kr = *P.kr;
+    p.qcos = static_cast<const uint8_t*>(qr.cos) + h0 * qr.stride_h * (int64_t)es;
+    p.qsin = static_cast<const uint8_t*>(qr.sin) + h0 * qr.stride_h * (int64_t)es;
+    p.qt_sb = qr.stride_b; p.qt_sh = qr.stride_h; p.qt_st = qr.stride_t;
+    p.kcos = static_cast<const uint8_t*>(kr.cos) + h0 * kr.stride_h * (int64_t)es;
+    p.ksin = static_cast<const uint8_t*>(kr.sin) + h0 * kr.stride_h * (int64_t)es;
+    p.kt_sb = kr.stride_b; p.kt_sh = kr.stride_h; p.kt_st = kr.stride_t;
+  }
+  p.Lq = s.Lq;
+  p.Lk = s.Lk;
+  p.n_q_tiles = P.Lq_pad / kTileM;
+  p.n_kv_tiles = (s.Lk + kTileN - 1) / kTileN;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.err = err;
+  if (!bf16) {
+    p.q = static_cast<const float*>(q.data);
+    p.q_sb = q.stride_b; p.q_sh = q.stride_h; p.q_st = q.stride_t;
+    p.k = static_cast<const float*>(k.data);
+    p.k_sb = k.stride_b; p.k_sh = k.stride_h; p.k_st = k.stride_t;
+    p.v = static_cast<const float*>(at(a->v));
+    p.v_sb = a->v.stride_b; p.v_sh = a->v.stride_h; p.v_st = a->v.stride_t;
+    p.dout = static_cast<const float*>(at(a->dout));
+    p.do_sb = a->dout.stride_b; p.do_sh = a->dout.stride_h; p.do_st = a->dout.stride_t;
+    e = launch_bwd_f32(p, s.D, s.Hc, s.B, st);
+    if (e != cudaSuccess) return cuda_fail(e, "bwd_f32 launch");
+    return LTXATTN_OK;
+  }
+  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, s.Hc, s.B, q.stride_t, q.stride_h, q.stride_b, "q"))) return rc;
+  if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, s.Hc, s.B, k.stride_t, k.stride_h, k.stride_b, "k"))) return rc;
+  if ((rc = make_tmap(&p.tm_v, at(a->v), s.D, s.Lk, s.Hc, s.B, a->v.stride_t, a->v.stride_h, a->v.stride_b, "v")))
+    return rc;
+  if ((rc = make_tmap(&p.tm_do, at(a->dout), s.D, s.Lq, s.Hc, s.B, a->dout.stride_t, a->dout.stride_h,
+                      a->dout.stride_b, "dout")))
+    return rc;
+  const bool has_mask = a->key_mask != nullptr;
+  e = launch_bwd_bf16(p, s.D, s.Hc, s.B, bwd_dq_smem_bytes(s.D, s.Lk, has_mask),
+                      bwd_dkdv_smem_bytes(s.D, s.Lk, has_mask), st);
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_bf16 launch");
+  return LTXATTN_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -85,6 +85,54 @@ struct CombineParams {
   int B, Hc, Lq, D, num_splits, head_begin;
 };
 
+// Backward.  Every pointer and tensor map is based at local head 0 (the
+// C-ABI layer offsets the caller's views by head_begin), so kernels index
+// heads by blockIdx.y directly.
+struct BwdParams {
+  CUtensorMap tm_q, tm_k, tm_v, tm_do;  // [D, T, Hc, B] box {64, 128, 1, 1}
+  const float* lse2;                    // [B][Hc][Lq_pad]: lse*log2(e) (bf16) or lse (f32); +inf pad
+  const float* delta;                   // [B][Hc][Lq_pad]: rowsum(dO o O); 0 pad
+  int Lq_pad;
+  void* dq;
+  int64_t dq_sb, dq_sh, dq_st;
+  void* dk;
+  int64_t dk_sb, dk_sh, dk_st;
+  void* dv;
+  int64_t dv_sb, dv_sh, dv_st;
+  const uint8_t* mask;
+  int64_t mask_sb;
+  const void* qcos;  // transpose rotation of dq (null = none), activation dtype
+  const void* qsin;
+  int64_t qt_sb, qt_sh, qt_st;
+  const void* kcos;  // transpose rotation of dk
+  const void* ksin;
+  int64_t kt_sb, kt_sh, kt_st;
+  // fp32 path: plain strided inputs (no tensor maps)
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* dout;
+  int64_t q_sb, q_sh, q_st, k_sb, k_sh, k_st, v_sb, v_sh, v_st, do_sb, do_sh, do_st;
+  int Lq, Lk;
+  int n_q_tiles, n_kv_tiles;
+  float scale, scale_log2;
+  int* err;
+};
+
+struct BwdPrepParams {
+  const void* o;
+  int64_t o_sb, o_sh, o_st;
+  const void* dout;
+  int64_t do_sb, do_sh, do_st;
+  const float* lse;
+  int64_t lse_sb, lse_sh;
+  float* lse2;
+  float* delta;
+  int B, Hc, Lq, Lq_pad, D;
+  int log2_domain;  // 1: lse2 = lse*log2(e) (bf16 kernels); 0: natural lse (fp32 kernels)
+  int f32;          // o / dout are float32
+};
+
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int B,
                             size_t smem_bytes, cudaStream_t s);
@@ -93,6 +141,12 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);
 cudaError_t launch_rope_bf16(const RopeParams& p, cudaStream_t s);
 cudaError_t launch_rope_f32(const RopeParams& p, cudaStream_t s);
+cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s);
+size_t bwd_dq_smem_bytes(int D, int Lk, bool has_mask);
+size_t bwd_dkdv_smem_bytes(int D, int Lk, bool has_mask);
+cudaError_t launch_bwd_bf16(const BwdParams& p, int D, int Hc, int B, size_t smem_dq, size_t smem_dkdv,
+                            cudaStream_t s);
+cudaError_t launch_bwd_f32(const BwdParams& p, int D, int Hc, int B, cudaStream_t s);
 
 // Device error word of this module (one per device).
 int* device_error_word();

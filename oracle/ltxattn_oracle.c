@@ -286,72 +286,89 @@ int oracle_attn_bwd(const float* q, const float* k, const float* v,
                     int B, int H, int Lq, int Lk, int D, double scale,
                     float* dq, float* dk, float* dv, int threads) {
     if (B <= 0 || H <= 0 || Lq < 0 || Lk <= 0 || D <= 0) return 1;
+    if (D > 256) return 3; /* per-row accumulators are sized for D <= 256 */
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
 #else
     (void)threads;
 #endif
-    int64_t bh_count = (int64_t)B * H;
-#pragma omp parallel
-    {
-        double* P = (double*)malloc(sizeof(double) * (size_t)Lq * Lk);
-        double* dS = (double*)malloc(sizeof(double) * (size_t)Lq * Lk);
-        double* accq = (double*)malloc(sizeof(double) * D);
-        unsigned char* allowed = (unsigned char*)malloc(Lk);
-#pragma omp for schedule(dynamic, 1)
-        for (int64_t bh = 0; bh < bh_count; ++bh) {
-            int b = (int)(bh / H);
-            allowed_keys(mask, mask_stride_b, b, Lk, allowed);
+    double* P = (double*)malloc(sizeof(double) * (size_t)Lq * Lk);
+    double* dS = (double*)malloc(sizeof(double) * (size_t)Lq * Lk);
+    unsigned char* allowed = (unsigned char*)malloc(Lk);
+    if (!P || !dS || !allowed) { free(P); free(dS); free(allowed); return 2; }
+    enum { KB = 16 };
+    for (int b = 0; b < B; ++b) {
+        allowed_keys(mask, mask_stride_b, b, Lk, allowed);
+        for (int h = 0; h < H; ++h) {
+            const int64_t bh = (int64_t)b * H + h;
             const float* qh = q + bh * Lq * D;
             const float* kh = k + bh * Lk * D;
             const float* vh = v + bh * Lk * D;
             const float* doh = dout + bh * Lq * D;
+            /* rows: P = softmax, dS = P o (dP - rowsum(P o dP)), dQ = scale dS K */
+#pragma omp parallel for schedule(static)
             for (int i = 0; i < Lq; ++i) {
-                double mx = -INFINITY;
                 double* pr = P + (int64_t)i * Lk;
+                double* dsr = dS + (int64_t)i * Lk;
+                const float* qi = qh + (int64_t)i * D;
+                const float* gi = doh + (int64_t)i * D;
+                double mx = -INFINITY;
                 for (int j = 0; j < Lk; ++j) {
                     if (!allowed[j]) { pr[j] = -INFINITY; continue; }
                     double s = 0.0;
-                    for (int d = 0; d < D; ++d) s += (double)qh[(int64_t)i * D + d] * kh[(int64_t)j * D + d];
+                    for (int d = 0; d < D; ++d) s += (double)qi[d] * kh[(int64_t)j * D + d];
                     pr[j] = s * scale;
                     if (pr[j] > mx) mx = pr[j];
                 }
                 double sum = 0.0;
                 for (int j = 0; j < Lk; ++j) { pr[j] = allowed[j] ? exp(pr[j] - mx) : 0.0; sum += pr[j]; }
-                for (int j = 0; j < Lk; ++j) pr[j] /= sum;
-                double* dsr = dS + (int64_t)i * Lk;
                 double delta = 0.0;
                 for (int j = 0; j < Lk; ++j) {
+                    pr[j] /= sum;
                     double dp = 0.0;
-                    for (int d = 0; d < D; ++d) dp += (double)doh[(int64_t)i * D + d] * vh[(int64_t)j * D + d];
+                    for (int d = 0; d < D; ++d) dp += (double)gi[d] * vh[(int64_t)j * D + d];
                     dsr[j] = dp;
                     delta += pr[j] * dp;
                 }
                 for (int j = 0; j < Lk; ++j) dsr[j] = pr[j] * (dsr[j] - delta);
-            }
-            for (int i = 0; i < Lq; ++i) {
-                for (int d = 0; d < D; ++d) accq[d] = 0.0;
+                double acc[256];
+                for (int d = 0; d < D; ++d) acc[d] = 0.0;
                 for (int j = 0; j < Lk; ++j) {
-                    double g = dS[(int64_t)i * Lk + j];
+                    const double g = dsr[j];
                     if (g == 0.0) continue;
-                    for (int d = 0; d < D; ++d) accq[d] += g * kh[(int64_t)j * D + d];
+                    for (int d = 0; d < D; ++d) acc[d] += g * kh[(int64_t)j * D + d];
                 }
-                for (int d = 0; d < D; ++d) dq[bh * Lq * D + (int64_t)i * D + d] = (float)(scale * accq[d]);
+                for (int d = 0; d < D; ++d) dq[bh * Lq * D + (int64_t)i * D + d] = (float)(scale * acc[d]);
             }
-            for (int j = 0; j < Lk; ++j) {
-                for (int d = 0; d < D; ++d) {
-                    double ak = 0.0, av = 0.0;
-                    for (int i = 0; i < Lq; ++i) {
-                        ak += dS[(int64_t)i * Lk + j] * qh[(int64_t)i * D + d];
-                        av += P[(int64_t)i * Lk + j] * doh[(int64_t)i * D + d];
+            /* key blocks: dK = scale dS^T Q, dV = P^T dO */
+            const int nkb = (Lk + KB - 1) / KB;
+#pragma omp parallel for schedule(dynamic, 1)
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int j0 = kb * KB, j1 = j0 + KB < Lk ? j0 + KB : Lk;
+                double ak[KB][256], av[KB][256];
+                for (int jj = 0; jj < j1 - j0; ++jj)
+                    for (int d = 0; d < D; ++d) ak[jj][d] = av[jj][d] = 0.0;
+                for (int i = 0; i < Lq; ++i) {
+                    const float* qi = qh + (int64_t)i * D;
+                    const float* gi = doh + (int64_t)i * D;
+                    for (int j = j0; j < j1; ++j) {
+                        const double g = dS[(int64_t)i * Lk + j], pj = P[(int64_t)i * Lk + j];
+                        if (g == 0.0 && pj == 0.0) continue;
+                        for (int d = 0; d < D; ++d) {
+                            ak[j - j0][d] += g * qi[d];
+                            av[j - j0][d] += pj * gi[d];
+                        }
                     }
-                    dk[bh * Lk * D + (int64_t)j * D + d] = (float)(scale * ak);
-                    dv[bh * Lk * D + (int64_t)j * D + d] = (float)av;
                 }
+                for (int j = j0; j < j1; ++j)
+                    for (int d = 0; d < D; ++d) {
+                        dk[bh * Lk * D + (int64_t)j * D + d] = (float)(scale * ak[j - j0][d]);
+                        dv[bh * Lk * D + (int64_t)j * D + d] = (float)av[j - j0][d];
+                    }
             }
         }
-        free(P); free(dS); free(accq); free(allowed);
     }
+    free(P); free(dS); free(allowed);
     return 0;
 }
 
