@@ -176,7 +176,7 @@ def run_ours(args):
     sms = torch.cuda.get_device_properties(local).multi_processor_count
     ctas = math.ceil(Lq / 128) * Hc * B
     splits = ctas < sms and math.ceil(Lk / 128) > 1
-    launches_per_step = 1 + (2 if qrot is not None else 0) + (1 if splits else 0)
+    launches_per_step = 1 + (1 if qrot is not None else 0) + (1 if splits else 0)
     flops = 4.0 * B * Hc * Lq * Lk * D
     if mask is not None:
         eff_flops = 4.0 * B * Hc * Lq * WORKLOADS[wl][6] * D

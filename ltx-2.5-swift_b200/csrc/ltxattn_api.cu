@@ -238,8 +238,7 @@ int plan_bwd(const ltxattn_bwd_args* a, BwdPlan* P) {
   return LTXATTN_OK;
 }
 
-RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const Shape& s, int T, void* y,
-                       int inverse) {
+RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const Shape& s, int T, void* y) {
   RopeParams p{};
   p.x = x.data;
   p.x_sb = x.stride_b;
@@ -256,7 +255,6 @@ RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const S
   p.T = T;
   p.D = s.D;
   p.head_begin = s.h0;
-  p.inverse = inverse;
   return p;
 }
 
@@ -317,9 +315,11 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   int q_head_off = s.h0, kv_head_off = s.h0;
   cudaError_t e;
   if (P.rope_q) {
-    RopeParams rp = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q, 0);
-    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rope(q) launch");
+    // k is always rotated with q (with its own table or q's)
+    const RopeParams rq = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
+    const RopeParams rk = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
+    e = launch_rope(&rq, &rk, bf16, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope launch");
     q.data = ws + P.off_q;
     q.stride_t = s.D;
     q.stride_h = (int64_t)s.Lq * s.D;
@@ -328,9 +328,6 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   }
   ltxattn_tensor v = a->v;
   if (P.rope_k) {
-    RopeParams rp = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k, 0);
-    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rope(k) launch");
     k.data = ws + P.off_k;
     k.stride_t = s.D;
     k.stride_h = (int64_t)s.Lk * s.D;
@@ -474,12 +471,10 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
   k.data = const_cast<void*>(at(a->k));
   cudaError_t e;
   if (P.rope) {
-    RopeParams rp = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q, 0);
-    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rope(q) launch");
-    rp = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k, 0);
-    e = bf16 ? launch_rope_bf16(rp, st) : launch_rope_f32(rp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rope(k) launch");
+    const RopeParams rq = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
+    const RopeParams rk = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
+    e = launch_rope(&rq, &rk, bf16, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope launch");
     q.data = ws + P.off_q;
     q.stride_t = s.D;
     q.stride_h = (int64_t)s.Lq * s.D;

@@ -72,7 +72,6 @@ struct RopeParams {
   int64_t t_sb, t_sh, t_st;
   void* y;  // contiguous [B][Hc][T][D]
   int B, Hc, T, D, head_begin;
-  int inverse;  // 1: apply the transpose rotation (gradient path, no rounding)
 };
 
 struct CombineParams {
@@ -139,8 +138,8 @@ cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int 
 size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);
-cudaError_t launch_rope_bf16(const RopeParams& p, cudaStream_t s);
-cudaError_t launch_rope_f32(const RopeParams& p, cudaStream_t s);
+// Rotate one tensor (b == nullptr) or two in one launch.
+cudaError_t launch_rope(const RopeParams* a, const RopeParams* b, bool bf16, cudaStream_t s);
 cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s);
 size_t bwd_dq_smem_bytes(int D, int Lk, bool has_mask);
 size_t bwd_dkdv_smem_bytes(int D, int Lk, bool has_mask);

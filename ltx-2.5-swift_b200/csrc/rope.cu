@@ -7,17 +7,84 @@
 // dtype first, :231-232).  Each op is evaluated in fp32 and rounded once, so
 // no product is fused into the following add.
 // fp32: the same four products and two sums in fp32, unfused.
-// inverse = 1 applies the transpose rotation (g1*c + g2*s, g2*c - g1*s) in
-// fp32 without rounding: the gradient w.r.t. the un-rotated input.
 //
 // Reads a strided [B, H, T, D] view, writes a contiguous [B, Hc, T, D] buffer
-// (the library's workspace), 8 rotary pairs per thread.
+// (the library's workspace).  One launch rotates q and k together (two jobs).
+// Each thread handles 8 rotary pairs; when every address of a job is 16-byte
+// aligned the pairs move as one 16-byte load/store per operand (bf16), else
+// element by element.
 #include "ltxattn_internal.h"
 
 namespace ltx {
 namespace {
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void rot(float x1, float x2, float c, float s, bool bf16, float& o1, float& o2) {
+  if (bf16) {
+    o1 = bf(__fsub_rn(bf(__fmul_rn(x1, c)), bf(__fmul_rn(x2, s))));
+    o2 = bf(__fadd_rn(bf(__fmul_rn(x2, c)), bf(__fmul_rn(x1, s))));
+  } else {
+    o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  }
+}
+
+struct Job {
+  const RopeParams* p;
+  int64_t count;  // groups of 8 pairs
+};
+
+__device__ __forceinline__ void locate(const RopeParams& p, int64_t gid, int& b, int& hl, int& t, int& g) {
+  const int groups = p.D / 16;
+  g = (int)(gid % groups);
+  t = (int)((gid / groups) % p.T);
+  hl = (int)((gid / ((int64_t)groups * p.T)) % p.Hc);
+  b = (int)(gid / ((int64_t)groups * p.T * p.Hc));
+}
+
+__global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2, int64_t na,
+                                                            int64_t nc) {
+  int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const RopeParams* pp = &a;
+  if (gid >= na) {
+    gid -= na;
+    pp = &c2;
+    if (gid >= nc) return;
+  }
+  const RopeParams& p = *pp;
+  int b, hl, t, g;
+  locate(p, gid, b, hl, t, g);
+  const int half = p.D / 2;
+  const int h = p.head_begin + hl;
+  const __nv_bfloat16* x =
+      static_cast<const __nv_bfloat16*>(p.x) + (int64_t)b * p.x_sb + (int64_t)h * p.x_sh + (int64_t)t * p.x_st + g * 8;
+  const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + g * 8;
+  const uint4 vx1 = *reinterpret_cast<const uint4*>(x);
+  const uint4 vx2 = *reinterpret_cast<const uint4*>(x + half);
+  const uint4 vc = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.cos) + toff);
+  const uint4 vs = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.sin) + toff);
+  const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&vx1);
+  const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&vx2);
+  const __nv_bfloat162* cc = reinterpret_cast<const __nv_bfloat162*>(&vc);
+  const __nv_bfloat162* ss = reinterpret_cast<const __nv_bfloat162*>(&vs);
+  uint4 o1v, o2v;
+  __nv_bfloat162* o1 = reinterpret_cast<__nv_bfloat162*>(&o1v);
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o2v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 a1 = __bfloat1622float2(x1[e]), a2 = __bfloat1622float2(x2[e]);
+    const float2 c = __bfloat1622float2(cc[e]), s = __bfloat1622float2(ss[e]);
+    float r1x, r2x, r1y, r2y;
+    rot(a1.x, a2.x, c.x, s.x, true, r1x, r2x);
+    rot(a1.y, a2.y, c.y, s.y, true, r1y, r2y);
+    o1[e] = __floats2bfloat162_rn(r1x, r1y);
+    o2[e] = __floats2bfloat162_rn(r2x, r2y);
+  }
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y) + (((int64_t)b * p.Hc + hl) * p.T + t) * p.D + g * 8;
+  *reinterpret_cast<uint4*>(y) = o1v;
+  *reinterpret_cast<uint4*>(y + half) = o2v;
+}
 
 template <typename T>
 __device__ __forceinline__ float ld(const T* p, int64_t i);
@@ -36,18 +103,22 @@ __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, int64_t i, f
   p[i] = __float2bfloat16_rn(v);
 }
 
-template <typename T, bool kBf16>
-__global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
+template <typename T>
+__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2, int64_t na,
+                                                          int64_t nc) {
+  int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const RopeParams* pp = &a;
+  if (gid >= na) {
+    gid -= na;
+    pp = &c2;
+    if (gid >= nc) return;
+  }
+  const RopeParams& p = *pp;
+  int b, hl, t, g;
+  locate(p, gid, b, hl, t, g);
   const int half = p.D / 2;
-  const int groups = half / 8;  // 8 pairs per thread
-  const int64_t total = (int64_t)p.B * p.Hc * p.T * groups;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= total) return;
-  const int g = (int)(gid % groups);
-  const int t = (int)((gid / groups) % p.T);
-  const int hl = (int)((gid / ((int64_t)groups * p.T)) % p.Hc);
-  const int b = (int)(gid / ((int64_t)groups * p.T * p.Hc));
   const int h = p.head_begin + hl;
+  const bool bf16 = sizeof(T) == 2;
   const T* x = static_cast<const T*>(p.x) + (int64_t)b * p.x_sb + (int64_t)h * p.x_sh + (int64_t)t * p.x_st;
   const T* c = static_cast<const T*>(p.cos) + (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st;
   const T* s = static_cast<const T*>(p.sin) + (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st;
@@ -55,35 +126,40 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int i = g * 8 + e;
-    const float x1 = ld(x, i), x2 = ld(x, i + half);
-    const float cc = ld(c, i), ss = ld(s, i);
     float o1, o2;
-    if (p.inverse) {
-      o1 = __fadd_rn(__fmul_rn(x1, cc), __fmul_rn(x2, ss));
-      o2 = __fsub_rn(__fmul_rn(x2, cc), __fmul_rn(x1, ss));
-    } else if (kBf16) {
-      o1 = bf(__fsub_rn(bf(__fmul_rn(x1, cc)), bf(__fmul_rn(x2, ss))));
-      o2 = bf(__fadd_rn(bf(__fmul_rn(x2, cc)), bf(__fmul_rn(x1, ss))));
-    } else {
-      o1 = __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, ss));
-      o2 = __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, ss));
-    }
+    rot(ld(x, i), ld(x, i + half), ld(c, i), ld(s, i), bf16, o1, o2);
     st(y, i, o1);
     st(y, i + half, o2);
   }
 }
 
-template <typename T, bool kBf16>
-cudaError_t launch(const RopeParams& p, cudaStream_t s) {
-  const int64_t total = (int64_t)p.B * p.Hc * p.T * (p.D / 16);
-  const int blocks = (int)((total + 255) / 256);
-  if (blocks > 0) rope_kernel<T, kBf16><<<blocks, 256, 0, s>>>(p);
-  return cudaGetLastError();
+bool vec_ok(const RopeParams& p) {
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  auto m8 = [](int64_t s) { return (s % 8) == 0; };
+  return al(p.x) && al(p.cos) && al(p.sin) && al(p.y) && m8(p.x_sb) && m8(p.x_sh) && m8(p.x_st) && m8(p.t_sb) &&
+         m8(p.t_sh) && m8(p.t_st);
 }
+
+int64_t groups(const RopeParams* p) { return p ? (int64_t)p->B * p->Hc * p->T * (p->D / 16) : 0; }
 
 }  // namespace
 
-cudaError_t launch_rope_bf16(const RopeParams& p, cudaStream_t s) { return launch<__nv_bfloat16, true>(p, s); }
-cudaError_t launch_rope_f32(const RopeParams& p, cudaStream_t s) { return launch<float, false>(p, s); }
+// Rotate one or two tensors (b may be null) in one launch.
+cudaError_t launch_rope(const RopeParams* a, const RopeParams* b, bool bf16, cudaStream_t s) {
+  const int64_t na = groups(a), nb = groups(b);
+  const RopeParams none{};
+  const RopeParams& pb = b ? *b : none;
+  const int blocks = (int)((na + nb + 255) / 256);
+  if (blocks == 0) return cudaSuccess;
+  if (bf16) {
+    if (vec_ok(*a) && (!b || vec_ok(*b)))
+      rope_bf16_vec_kernel<<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+    else
+      rope_scalar_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+  } else {
+    rope_scalar_kernel<float><<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+  }
+  return cudaGetLastError();
+}
 
 }  // namespace ltx

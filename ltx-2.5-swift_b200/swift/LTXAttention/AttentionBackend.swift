@@ -1,0 +1,88 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Drop-in body for Sources/LTXAttention/AttentionBackend.swift of
+// loading-awesome/LTX-2.5-Swift (today a placeholder, :13-15), binding the C
+// ABI of libltxattn_cuda.  Not compiled in this repository: no Swift
+// toolchain is available where it was written.  The arguments mirror the SDPA
+// switch of DiTAttention.swift:369-382 plus the RoPE of :364-367.
+//
+// Device buffers are passed as raw CUDA device addresses with [B, H, T, D]
+// element strides, so the transposed `split` views (DiTAttention.swift:346-348)
+// need no copy.  How an MLXArray exposes its device address depends on the MLX
+// backend in use; `DeviceTensor` is the seam for that.
+
+import CLTXAttnCUDA
+import Foundation
+
+public enum AttentionBackend {
+
+    /// One [B, H, T, D] device view: address plus element strides (D stride 1).
+    public struct DeviceTensor {
+        public var address: UnsafeMutableRawPointer
+        public var strides: (b: Int64, h: Int64, t: Int64)
+        public init(address: UnsafeMutableRawPointer, strides: (b: Int64, h: Int64, t: Int64)) {
+            self.address = address
+            self.strides = strides
+        }
+        var c: ltxattn_tensor {
+            ltxattn_tensor(data: address, stride_b: strides.b, stride_h: strides.h, stride_t: strides.t)
+        }
+    }
+
+    /// DiTAttention.Rotary on the device: cos and sin [B, H, T, D/2] in the activation dtype.
+    public struct DeviceRotary {
+        public var cos: UnsafeRawPointer
+        public var sin: UnsafeRawPointer
+        public var strides: (b: Int64, h: Int64, t: Int64)
+        public var tokens: Int32
+        var c: ltxattn_rotary {
+            ltxattn_rotary(cos: cos, sin: sin, stride_b: strides.b, stride_h: strides.h,
+                           stride_t: strides.t, tokens: tokens)
+        }
+    }
+
+    /// Mirrors DiTAttention.Failure (DiTAttention.swift:107-122) for library errors.
+    public struct Failure: Error, CustomStringConvertible {
+        public let status: Int32
+        public let message: String
+        public var description: String { "ltxattn status \(status): \(message)" }
+    }
+
+    static func check(_ rc: Int32) throws {
+        if rc != 0 { throw Failure(status: rc, message: String(cString: ltxattn_last_error())) }
+    }
+
+    /// The fused RoPE + SDPA the `.fused` and `.explicit` arms collapse into.
+    /// `keyRotary == nil` with `rotary` given rotates k with `rotary`
+    /// (`keyRotary ?? rotary`, DiTAttention.swift:366).
+    public static func attention(
+        bf16: Bool, batch: Int32, heads: Int32, queryTokens: Int32, keyTokens: Int32, headDim: Int32,
+        q: DeviceTensor, k: DeviceTensor, v: DeviceTensor, out: DeviceTensor, scale: Float,
+        keyMask: UnsafePointer<UInt8>? = nil, rotary: DeviceRotary? = nil, keyRotary: DeviceRotary? = nil,
+        lse: UnsafeMutablePointer<Float>? = nil, workspace: UnsafeMutableRawPointer?, workspaceBytes: Int,
+        stream: UnsafeMutableRawPointer?
+    ) throws {
+        var a = ltxattn_fwd_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.heads = heads; a.q_len = queryTokens; a.kv_len = keyTokens; a.head_dim = headDim
+        a.q = q.c; a.k = k.c; a.v = v.c; a.out = out.c
+        a.scale = scale
+        a.key_mask = keyMask
+        a.key_mask_stride_b = Int64(keyTokens)
+        if let rotary { a.q_rotary = rotary.c }
+        if let keyRotary { a.k_rotary = keyRotary.c }
+        if let lse {
+            a.lse = lse
+            a.lse_stride_b = Int64(heads) * Int64(queryTokens)
+            a.lse_stride_h = Int64(queryTokens)
+        }
+        a.workspace = workspace
+        a.workspace_bytes = workspaceBytes
+        try check(ltxattn_fwd(&a, stream))
+    }
+
+    /// Device scratch the same arguments need (call once per shape; the caller allocates).
+    public static func workspaceBytes(_ a: inout ltxattn_fwd_args) -> Int {
+        Int(ltxattn_fwd_workspace(&a))
+    }
+}
