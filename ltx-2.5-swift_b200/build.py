@@ -13,6 +13,7 @@ from __future__ import annotations
 import concurrent.futures as cf
 import glob
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -45,14 +46,41 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+# Kernels that re-split registers between warpgroups (setmaxnreg) must be
+# launched with exactly the per-thread count their split was sized for: a
+# setmaxnreg.inc that asks for more than the launch provided never returns.
+# ptxas' report is checked against the value the kernel source assumes.
+REGISTER_PINS = {"fwd_sm100.cu": ("fwd_bf16_sm100_kernel", 168)}
+
+
+def _check_register_pin(src: str, ptxas_log: str) -> None:
+    pin = REGISTER_PINS.get(os.path.basename(src))
+    if not pin:
+        return
+    kernel, regs = pin
+    lines = ptxas_log.splitlines()
+    found = 0
+    for i, ln in enumerate(lines):
+        if "Compiling entry function" in ln and kernel in ln:
+            for ln2 in lines[i + 1:i + 6]:
+                m = re.search(r"Used (\d+) registers", ln2)
+                if m:
+                    found += 1
+                    if int(m.group(1)) != regs:
+                        raise RuntimeError(f"{kernel}: ptxas used {m.group(1)} registers, the warpgroup "
+                                           f"register split assumes {regs}")
+                    break
+    if not found:
+        raise RuntimeError(f"{kernel}: no ptxas register report found")
+
+
 def _compile(src: str, obj: str, verbose: bool) -> str:
-    cmd = [nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
+    cmd = [nvcc()] + NVCC_FLAGS + ["-Xptxas=-v", "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
-    return r.stderr
+    _check_register_pin(src, r.stderr + r.stdout)
+    return r.stderr if verbose else ""
 
 
 def build(force: bool = False, verbose: bool = False) -> str:

@@ -1,36 +1,46 @@
 // fwd_sm100.cu -- bf16 fused attention forward on tcgen05 (sm_100a).
 //
-// Computes, per (batch, head, 128-row query tile):
+// Computes, per (batch, head, 256-row query block):
 //     O = softmax(scale * Q K^T + mask) V,   lse = log sum exp(scale * Q K^T + mask)
 // the function of DiTAttention.swift:369-382 (fused arm: MLXFast SDPA;
 // explicit arm: fp32 logits -> softmax -> PV), online-softmax style with O(N)
 // memory: no score matrix leaves the SM.
 //
-// CTA layout (192 threads, two CTAs per SM):
-//   warps 0-3  softmax + correction + epilogue; thread i owns query row i,
-//              which is TMEM lane i (warp w reads lane quadrant w)
-//   warp 4     TMA producer (lane 0): Q once, then K_j / V_j per KV tile
-//   warp 5     TMEM owner; lane 0 issues every tcgen05.mma
-// TMEM (256 columns): S = Q K_j^T in columns [0,128) (fp32); P_j (bf16,
-// packed two per column) overwrites S's first 64 columns and feeds the PV
-// MMA straight from TMEM; O in columns [128, 128+D).
-// Per KV tile j the MMA order is  QK_j -> (softmax j) -> PV_j -> QK_{j+1}:
-// tcgen05 ops of one thread run in issue order, so QK_{j+1} never overwrites
-// P_j before PV_j has read it, and the commit that publishes S_{j+1} also
-// proves PV_j finished (so the softmax may rescale O).  The second CTA on the
-// SM overlaps its softmax with this CTA's MMAs.
+// CTA layout (384 threads = 3 warpgroups, one CTA per SM, two 128-row Q
+// tiles sharing K/V):
+//   warps 0-3  softmax of Q tile 0 (thread i owns row i = TMEM lane i;
+//              warp w reads lane quadrant w % 4); also the lazy O rescale and
+//              the epilogue of tile 0
+//   warps 4-7  the same for Q tile 1
+//   warp 8     TMA producer (lane 0): Q0/Q1 once, K_j and V_j through two stages
+//   warp 9     TMEM owner; lane 0 issues every tcgen05.mma
+//   warps 10-11 idle (they complete the third warpgroup)
+// Registers: launched at kLaunchRegs per thread; the producer warpgroup gives
+// its share to the softmax warpgroups (setmaxnreg), which hold a 128-wide
+// score row each: 2*128*kSoftmaxRegs + 128*kProducerRegs = 384*kLaunchRegs.
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).
+// P_t (bf16, two per column) overwrites the first 64 columns of S_t and feeds
+// the PV MMA straight from TMEM.
+//
+// MMA issue order in steady state:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.
+// tcgen05 ops of one thread execute in order, so S_t{j+1} never overwrites
+// P_t{j} before PV_t{j} has read it, and the commit that publishes S_t{j+1}
+// also proves PV_t{j} finished, so softmax t may rescale O_t.  While softmax 0
+// works on tile j+1 the tensor pipe runs PV1_j and S1_{j+1}, and vice versa.
 //
 // Online softmax in the log2 domain with a lazy max: the running max m only
 // moves when a tile's max exceeds it by more than 8 (a factor of 256), so O is
 // rescaled rarely; exp2(s - m) then stays <= 256, which fp32 and bf16 carry
 // exactly as well as values <= 1.  The final O / l is the same function.
+// Three quarters of the exponentials run on the MUFU (ex2.approx), one quarter
+// on the FMA pipe (exp2_poly2), so neither pipe limits the tile.
 //
 // Keys: a tile whose keys are all masked is skipped outright (its weight is
 // exactly zero); partial tiles and the ragged tail get -inf logits per
 // column.  A batch row whose mask has no valid key attends to all keys
 // (GemmaTextEncoder.swift:306-319).
 //
-// Split-KV (short query sequences): blockIdx.x = q_tile * num_splits + split;
+// Split-KV (short query sequences): blockIdx.x = q_block * num_splits + split;
 // each split handles a contiguous share of the active KV tiles and writes an
 // fp32 partial O (normalised by its own l) and its log2-domain lse; the
 // combine kernel merges them.
@@ -41,43 +51,69 @@ namespace ltx {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;
+constexpr uint32_t kLaunchRegs = 168;   // what ptxas allots under __launch_bounds__(384, 1)
+constexpr uint32_t kProducerRegs = 72;
+constexpr uint32_t kSoftmaxRegs = 216;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs,
+              "register re-split exceeds the launch allocation");
+constexpr int kBlockM = kFwdBlockM;             // query rows per CTA (two Q tiles)
 constexpr uint32_t kChunkBytes = 128u * 128u;  // one 64-element-wide chunk of a 128-row tile
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
+constexpr int kPolyCols = 32;  // columns [128 - kPolyCols, 128) use exp2_poly2
 
 template <int D>
 struct Smem {
   static constexpr int kChunks = D / 64;
-  static constexpr uint32_t kTileBytes = kChunks * kChunkBytes;
-  // [Q][K][V] tiles (1024-aligned), then control words
-  static constexpr uint32_t kOffQ = 0;
-  static constexpr uint32_t kOffK = kTileBytes;
-  static constexpr uint32_t kOffV = 2 * kTileBytes;
-  static constexpr uint32_t kOffBar = 3 * kTileBytes;          // 8 mbarriers
-  static constexpr uint32_t kOffCtl = kOffBar + 8 * 8;          // tmem slot, abort, n_tiles
-  static constexpr uint32_t kOffTiles = kOffCtl + 16;           // uint16 [kMaxKvTiles]
+  static constexpr uint32_t kTile = kChunks * kChunkBytes;
+  static constexpr uint32_t kOffQ0 = 0, kOffQ1 = kTile, kOffK0 = 2 * kTile, kOffK1 = 3 * kTile,
+                            kOffV0 = 4 * kTile, kOffV1 = 5 * kTile;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full
+  static constexpr uint32_t kOffBar = 6 * kTile;
+  static constexpr uint32_t kOffCtl = kOffBar + 16 * 8;  // tmem slot, abort, n_tiles
+  static constexpr uint32_t kOffTiles = kOffCtl + 16;    // uint16 [kMaxKvTiles]
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;  // uint32 mask bits
-  static constexpr uint32_t kFixed = kOffBits;
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __grid_constant__ FwdParams p) {
+__device__ __forceinline__ void issue_s(uint32_t tS, uint32_t aQ, uint32_t aK) {
+  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 0);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+    umma_ss(tS, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, uint32_t aV, bool accumulate) {
+  constexpr uint32_t idesc = idesc_bf16_f32(128, D, 0, 1);
+#pragma unroll
+  for (int kk = 0; kk < kTileN / 16; ++kk)
+    // 16 keys = 16 rows of 128 B in each d-chunk; d-chunks are kChunkBytes apart
+    umma_ts(tO, tP + kk * 8, sdesc_sw128(aV + kk * 16 * 128, kChunkBytes, 1024), idesc,
+            (accumulate || kk > 0) ? 1u : 0u);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __grid_constant__ FwdParams p) {
   using S = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* sQ = sm + S::kOffQ;
-  uint8_t* sK = sm + S::kOffK;
-  uint8_t* sV = sm + S::kOffV;
+  // stage st of K lives at sK + st * kTile, of V at sV + st * kTile; Q tile t at sQ + t * kTile
+  uint8_t* sQ = sm + S::kOffQ0;
+  uint8_t* sK = sm + S::kOffK0;
+  uint8_t* sV = sm + S::kOffV0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* bar_q = bars + 0;
-  uint64_t* bar_kf = bars + 1;
-  uint64_t* bar_ke = bars + 2;
-  uint64_t* bar_vf = bars + 3;
-  uint64_t* bar_ve = bars + 4;
-  uint64_t* bar_s = bars + 5;
-  uint64_t* bar_p = bars + 6;
-  uint64_t* bar_o = bars + 7;
+  uint64_t* bar_kf = bars + 1;   // [2]
+  uint64_t* bar_ke = bars + 3;   // [2]
+  uint64_t* bar_vf = bars + 5;   // [2]
+  uint64_t* bar_ve = bars + 7;   // [2]
+  uint64_t* bar_s = bars + 9;    // [2] per Q tile
+  uint64_t* bar_p = bars + 11;   // [2] per Q tile
+  uint64_t* bar_o = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
@@ -86,32 +122,26 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_tile = blockIdx.x / p.num_splits;
+  const int q_block = blockIdx.x / p.num_splits;
   const int split = blockIdx.x % p.num_splits;
   const int hl = blockIdx.y;
   const int b = blockIdx.z;
-  const int q0 = q_tile * kTileM;
+  const int q0 = q_block * kBlockM;
+  const bool two = q0 + kTileM < p.Lq;  // is Q tile 1 inside the sequence?
   const int Lk = p.Lk;
 
   // ---------------- prologue ----------------
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1);
-    mbar_init(bar_kf, 1);
-    mbar_init(bar_ke, 1);
-    mbar_init(bar_vf, 1);
-    mbar_init(bar_ve, 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_p, 128);
-    mbar_init(bar_o, 1);
+    for (int i = 0; i < 14; ++i) mbar_init(bars + i, (i == 11 || i == 12) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, 256);
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
     tc_fence_before();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
@@ -164,83 +194,106 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
   const int qh = p.q_head_off + hl;
   const int kvh = p.kv_head_off + hl;
 
-  if (warp == 4) {
+  if (warp >= 8) {
+    setmaxnreg_dec<kProducerRegs>();
+    if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && n > 0) {
       int k_issued = 0, v_issued = 0;
-      mbar_arrive_expect_tx(bar_q, S::kTileBytes);
+      mbar_arrive_expect_tx(bar_q, (two ? 2u : 1u) * S::kTile);
 #pragma unroll
-      for (int c = 0; c < S::kChunks; ++c)
+      for (int c = 0; c < S::kChunks; ++c) {
         tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
-      for (int i = 0; i < n; ++i) {
-        const int kv0 = (int)tiles[t_begin + i] * kTileN;
-        if (i > 0 && !mbar_wait(bar_ke, (i - 1) & 1, abort_flag, p.err, 1)) break;
-        mbar_arrive_expect_tx(bar_kf, S::kTileBytes);
+        if (two) tma_load_4d(&p.tm_q, bar_q, sQ + S::kTile + c * kChunkBytes, c * 64, q0 + kTileM, qh, b);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1, u = j >> 1;
+        const int kv0 = (int)tiles[t_begin + j] * kTileN;
+        if (j >= 2 && !mbar_wait(bar_ke + st, (u - 1) & 1, abort_flag, p.err, 1)) break;
+        mbar_arrive_expect_tx(bar_kf + st, S::kTile);
 #pragma unroll
         for (int c = 0; c < S::kChunks; ++c)
-          tma_load_4d(&p.tm_k, bar_kf, sK + c * kChunkBytes, c * 64, kv0, kvh, b);
+          tma_load_4d(&p.tm_k, bar_kf + st, sK + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, b);
         ++k_issued;
-        if (i > 0 && !mbar_wait(bar_ve, (i - 1) & 1, abort_flag, p.err, 2)) break;
-        mbar_arrive_expect_tx(bar_vf, S::kTileBytes);
+        if (j >= 2 && !mbar_wait(bar_ve + st, (u - 1) & 1, abort_flag, p.err, 2)) break;
+        mbar_arrive_expect_tx(bar_vf + st, S::kTile);
 #pragma unroll
         for (int c = 0; c < S::kChunks; ++c)
-          tma_load_4d(&p.tm_v, bar_vf, sV + c * kChunkBytes, c * 64, kv0, kvh, b);
+          tma_load_4d(&p.tm_v, bar_vf + st, sV + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, b);
         ++v_issued;
       }
       // never leave the CTA with a bulk copy still writing its shared memory
       drain_wait(bar_q, 0);
-      if (k_issued > 0) drain_wait(bar_kf, (k_issued - 1) & 1);
-      if (v_issued > 0) drain_wait(bar_vf, (v_issued - 1) & 1);
+      for (int i = k_issued < 2 ? 0 : k_issued - 2; i < k_issued; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
+      for (int i = v_issued < 2 ? 0 : v_issued - 2; i < v_issued; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
     }
     __syncwarp();
-  } else if (warp == 5) {
+    } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_qk = idesc_bf16_f32(128, 128, 0, 0);
-      const uint32_t idesc_pv = idesc_bf16_f32(128, D, 0, 1);
-      const uint32_t tS = tmem;         // columns [0, 128)
-      const uint32_t tO = tmem + 128;   // columns [128, 128 + D)
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      if (mbar_wait(bar_q, 0, abort_flag, p.err, 3)) {
-        for (int i = 0; i < n; ++i) {
-          if (!mbar_wait(bar_kf, i & 1, abort_flag, p.err, 4)) break;
+      const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+      const uint32_t aQ0 = smem_u32(sQ), aQ1 = aQ0 + S::kTile;
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      if (mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4)) {
+        tc_fence_after();
+        issue_s<D>(tS0, aQ0, aK);
+        umma_commit(bar_s + 0);
+        if (two) {
+          issue_s<D>(tS1, aQ1, aK);
+          umma_commit(bar_s + 1);
+        }
+        umma_commit(bar_ke + 0);
+        for (int j = 0; j < n; ++j) {
+          const int st = j & 1, u = j >> 1;
+          const bool more = j + 1 < n;
+          const int st1 = (j + 1) & 1, u1 = (j + 1) >> 1;
+          if (!mbar_wait(bar_p + 0, j & 1, abort_flag, p.err, 5)) break;
+          if (!mbar_wait(bar_vf + st, u & 1, abort_flag, p.err, 6)) break;
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_ss(tS, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idesc_qk,
-                    kk > 0 ? 1u : 0u);
+          issue_pv<D>(tO0, tS0, aV + st * S::kTile, j > 0);
+          if (more) {
+            if (!mbar_wait(bar_kf + st1, u1 & 1, abort_flag, p.err, 7)) break;
+            tc_fence_after();
+            issue_s<D>(tS0, aQ0, aK + st1 * S::kTile);
+            umma_commit(bar_s + 0);
           }
-          umma_commit(bar_ke);
-          umma_commit(bar_s);
-          if (!mbar_wait(bar_p, i & 1, abort_flag, p.err, 5)) break;
-          if (!mbar_wait(bar_vf, i & 1, abort_flag, p.err, 6)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kTileN / 16; ++kk) {
-            // 16 keys = 16 rows of 128 B in each d-chunk; d-chunks are kChunkBytes apart
-            umma_ts(tO, tS + kk * 8, sdesc_sw128(aV + kk * 16 * 128, kChunkBytes, 1024), idesc_pv,
-                    (i > 0 || kk > 0) ? 1u : 0u);
+          if (two) {
+            if (!mbar_wait(bar_p + 1, j & 1, abort_flag, p.err, 8)) break;
+            tc_fence_after();
+            issue_pv<D>(tO1, tS1, aV + st * S::kTile, j > 0);
           }
-          umma_commit(bar_ve);
+          umma_commit(bar_ve + st);
+          if (more) {
+            if (two) {
+              issue_s<D>(tS1, aQ1, aK + st1 * S::kTile);
+              umma_commit(bar_s + 1);
+            }
+            umma_commit(bar_ke + st1);
+          }
         }
       }
       umma_commit(bar_o);
       drain_wait(bar_o, 0);
     }
     __syncwarp();
+    }
   } else {
-    // ---------------- softmax / correction / epilogue ----------------
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_off;
-    const uint32_t tO = tmem + 128 + lane_off;
+    setmaxnreg_inc<kSoftmaxRegs>();
+    if (warp < 4 || two) {
+    // ---------------- softmax / correction / epilogue of Q tile t ----------------
+    const int t = warp >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
     const float sl2 = p.scale_log2;
-    const int row = q0 + threadIdx.x;
+    const int row = q0 + t * kTileM + (threadIdx.x & 127);
+    uint64_t* my_s = bar_s + t;
+    uint64_t* my_p = bar_p + t;
     float m = -INFINITY;  // running max, log2 domain (lazy)
     float l = 0.f;
     bool ok = true;
     for (int i = 0; i < n; ++i) {
-      if (!warp_wait(bar_s, i & 1, abort_flag, p.err, 7)) { ok = false; break; }
+      if (!warp_wait(my_s, i & 1, abort_flag, p.err, 9)) { ok = false; break; }
       tc_fence_after();
       float s[128];
       {
@@ -271,9 +324,19 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
             if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
         }
       }
-      float mx = s[0];
+      // row max: eight independent 3-input-max chains, then a short tree
+      float mx;
+      {
+        float pm[8];
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        for (int e = 0; e < 8; ++e) pm[e] = fmaxf(s[e], s[8 + e]);
+#pragma unroll
+        for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pm[e] = max3(pm[e], s[c + e], s[c + 8 + e]);
+        }
+        mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+      }
       const float m_cand = mx * sl2;
       const bool need = m_cand > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need && i > 0)) {
@@ -293,14 +356,27 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
         l *= fast_exp2(m - m_cand);  // exp2(-inf) = 0 on the first tile
         m = m_cand;
       }
-      const float m_use = (m == -INFINITY) ? 0.f : m;
-      float lt = 0.f;
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      const float2 sl2x2 = make_float2(sl2, sl2), nmx2 = make_float2(neg_m, neg_m);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], sl2, -m_use));
-        lt += s[c];
+      for (int c = 0; c < 128; c += 2) {
+        const float2 x = fma2(make_float2(s[c], s[c + 1]), sl2x2, nmx2);
+        float2 e;
+        if (c < 128 - kPolyCols) {
+          e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        } else {
+          e = exp2_poly2(x);
+        }
+        s[c] = e.x;
+        s[c + 1] = e.y;
+        acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], e);
       }
-      l += lt;
+      {
+        const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+        const float2 tot = add2(a01, a23);
+        l += tot.x + tot.y;
+      }
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t pk[32];
@@ -310,11 +386,11 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p);
+      mbar_arrive(my_p);
     }
 
     // epilogue
-    const bool have_o = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 8);
+    const bool have_o = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 10);
     tc_fence_after();
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
     const int B = gridDim.z, Hc = gridDim.y;
@@ -368,14 +444,15 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_bf16_sm100_kernel(const __gri
       }
       if (row < p.Lq) p.part_lse[prow] = (have_o && l > 0.f) ? m + log2f(l) : -INFINITY;
     }
+    }
   }
 
   // ---------------- teardown ----------------
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -421,17 +498,26 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
 
 size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask) {
   const int n_tiles = (Lk + kTileN - 1) / kTileN;
-  const size_t fixed = (D == 128) ? Smem<128>::kFixed : Smem<64>::kFixed;
-  size_t bytes = 1024 /* alignment slack */ + fixed + (has_mask ? (size_t)n_tiles * 16 : 0);
-  // at most two CTAs per SM: each holds 256 TMEM columns of the SM's 512
-  const size_t two_per_sm_floor = 80 * 1024;
-  return bytes < two_per_sm_floor ? two_per_sm_floor : bytes;
+  const size_t fixed = (D == 128) ? Smem<128>::kOffBits : Smem<64>::kOffBits;
+  return 1024 /* alignment slack */ + fixed + (has_mask ? (size_t)n_tiles * 16 : 0);
 }
 
-cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int B, size_t smem,
+// The warpgroup register split is sized for kLaunchRegs per thread; refuse to
+// launch a build whose kernel was allotted a different count (a setmaxnreg.inc
+// beyond the launch allocation would never return).
+template <typename K>
+cudaError_t check_launch_regs(K kernel) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return e;
+  return fa.numRegs == (int)kLaunchRegs ? cudaSuccess : cudaErrorInvalidConfiguration;
+}
+
+cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_blocks, int Hc, int B, size_t smem,
                             cudaStream_t s) {
-  dim3 grid(q_tiles * p.num_splits, Hc, B);
-  cudaError_t e;
+  dim3 grid(q_blocks * p.num_splits, Hc, B);
+  cudaError_t e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128>) : check_launch_regs(fwd_bf16_sm100_kernel<64>);
+  if (e != cudaSuccess) return e;
   if (D == 128) {
     e = cudaFuncSetAttribute(fwd_bf16_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

@@ -174,7 +174,7 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
     if ((rc = check_rotary(a->q_rotary, "q_rotary", s.Lq))) return rc;
     if ((rc = check_rotary(*P->kr, a->k_rotary.cos ? "k_rotary" : "q_rotary (used for k)", s.Lk))) return rc;
   }
-  P->q_tiles = (s.Lq + kTileM - 1) / kTileM;
+  P->q_tiles = s.dtype == LTXATTN_BF16 ? (s.Lq + kFwdBlockM - 1) / kFwdBlockM : (s.Lq + kTileM - 1) / kTileM;
   P->kv_tiles = (s.Lk + kTileN - 1) / kTileN;
   P->splits = 1;
   if (s.dtype == LTXATTN_BF16) {

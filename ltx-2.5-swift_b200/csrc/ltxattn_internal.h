@@ -19,6 +19,7 @@ constexpr int kTileN = 128;            // keys per KV tile (UMMA N of QK^T)
 constexpr int kMaxKvLen = 131072;      // 1024 KV tiles
 constexpr int kMaxKvTiles = kMaxKvLen / kTileN;
 constexpr int kMaxSplits = 32;
+constexpr int kFwdBlockM = 2 * kTileM;  // query rows per forward CTA (two Q tiles)
 
 // Forward, bf16 tcgen05 path.
 struct FwdParams {

@@ -293,6 +293,70 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Warpgroup register re-split (all four warps of a warpgroup execute it).
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+// ---------------------------------------------------------------------------
+// paired fp32 arithmetic (sm_100 f32x2) and the 3-input max
+
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA pipe, for two values at once; x <= 8 in this library.
+// Round-to-nearest split x = n + f with f in [-1/2, 1/2] (adding 1.5*2^23
+// leaves n in the low mantissa bits), a degree-3 polynomial for 2^f, and n
+// added to the exponent field.  The coefficients are this library's own
+// relative-error least-squares fit of 2^f on [-1/2, 1/2] (iteratively
+// reweighted towards minimax): max relative error 7.5e-5, far below the
+// bf16 rounding P receives.  x < -126 returns exactly 0 (masked logits are -inf).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 t = add2(xc, make_float2(kMagic, kMagic));
+  const float2 n = add2(t, make_float2(-kMagic, -kMagic));
+  const float2 f = add2(xc, make_float2(-n.x, -n.y));
+  float2 q = fma2(f, make_float2(0.0551716573536396f, 0.0551716573536396f),
+                  make_float2(0.2426111400127411f, 0.2426111400127411f));
+  q = fma2(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = fma2(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  const int nx = __float_as_int(t.x) - __float_as_int(kMagic);
+  const int ny = __float_as_int(t.y) - __float_as_int(kMagic);
+  float2 r;
+  r.x = x.x >= -126.f ? __int_as_float(__float_as_int(q.x) + (nx << 23)) : 0.f;
+  r.y = x.y >= -126.f ? __int_as_float(__float_as_int(q.y) + (ny << 23)) : 0.f;
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // small numeric helpers
 
