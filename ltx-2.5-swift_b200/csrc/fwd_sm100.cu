@@ -61,7 +61,7 @@ constexpr int kBlockM = kFwdBlockM;             // query rows per CTA (two Q til
 constexpr uint32_t kChunkBytes = 128u * 128u;  // one 64-element-wide chunk of a 128-row tile
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr int kPolyCols = 32;  // columns [128 - kPolyCols, 128) use exp2_poly2
+constexpr int kPolyCols = 0;  // columns [128 - kPolyCols, 128) use exp2_poly2
 
 template <int D>
 struct Smem {
@@ -76,24 +76,27 @@ struct Smem {
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;  // uint32 mask bits
 };
 
+// S = Q K^T for one 128x128 tile: D/16 MMAs of K = 16.  qd / kd are base
+// descriptors of the Q and K tiles; k-step kk sits in 64-wide chunk kk/4 at
+// byte (kk%4)*32 of each 128-byte row.
 template <int D>
-__device__ __forceinline__ void issue_s(uint32_t tS, uint32_t aQ, uint32_t aK) {
+__device__ __forceinline__ void issue_s(uint32_t tS, SDesc qd, SDesc kd) {
   constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 0);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-    umma_ss(tS, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+    const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+    umma_ss2(tS, qd.lo + off, qd.hi, kd.lo + off, kd.hi, idesc, kk > 0 ? 1u : 0u);
   }
 }
 
+// O (+)= P V for one tile: 8 MMAs of K = 16 keys; P from TMEM (8 columns per
+// k-step), V MN-major (16 keys = 16 rows of 128 B; d-chunks kChunkBytes apart).
 template <int D>
-__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, uint32_t aV, bool accumulate) {
+__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, SDesc vd, bool accumulate) {
   constexpr uint32_t idesc = idesc_bf16_f32(128, D, 0, 1);
 #pragma unroll
   for (int kk = 0; kk < kTileN / 16; ++kk)
-    // 16 keys = 16 rows of 128 B in each d-chunk; d-chunks are kChunkBytes apart
-    umma_ts(tO, tP + kk * 8, sdesc_sw128(aV + kk * 16 * 128, kChunkBytes, 1024), idesc,
-            (accumulate || kk > 0) ? 1u : 0u);
+    umma_ts2(tO, tP + kk * 8, vd.lo + ((kk * 16 * 128) >> 4), vd.hi, idesc, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 template <int D>
@@ -232,14 +235,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n > 0) {
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
-      const uint32_t aQ0 = smem_u32(sQ), aQ1 = aQ0 + S::kTile;
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      // base descriptors, built once; stage st adds st * kTile >> 4 to the low word
+      const SDesc dQ0 = sdesc_split(smem_u32(sQ), 16, 1024);
+      const SDesc dQ1 = sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024);
+      const SDesc dK = sdesc_split(smem_u32(sK), 16, 1024);
+      const SDesc dV = sdesc_split(smem_u32(sV), kChunkBytes, 1024);
+      const uint32_t stage_step = S::kTile >> 4;
+      auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
+      auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
       if (mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4)) {
         tc_fence_after();
-        issue_s<D>(tS0, aQ0, aK);
+        issue_s<D>(tS0, dQ0, kdesc(0));
         umma_commit(bar_s + 0);
         if (two) {
-          issue_s<D>(tS1, aQ1, aK);
+          issue_s<D>(tS1, dQ1, kdesc(0));
           umma_commit(bar_s + 1);
         }
         umma_commit(bar_ke + 0);
@@ -250,22 +259,22 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
           if (!mbar_wait(bar_p + 0, j & 1, abort_flag, p.err, 5)) break;
           if (!mbar_wait(bar_vf + st, u & 1, abort_flag, p.err, 6)) break;
           tc_fence_after();
-          issue_pv<D>(tO0, tS0, aV + st * S::kTile, j > 0);
+          issue_pv<D>(tO0, tS0, vdesc(st), j > 0);
           if (more) {
             if (!mbar_wait(bar_kf + st1, u1 & 1, abort_flag, p.err, 7)) break;
             tc_fence_after();
-            issue_s<D>(tS0, aQ0, aK + st1 * S::kTile);
+            issue_s<D>(tS0, dQ0, kdesc(st1));
             umma_commit(bar_s + 0);
           }
           if (two) {
             if (!mbar_wait(bar_p + 1, j & 1, abort_flag, p.err, 8)) break;
             tc_fence_after();
-            issue_pv<D>(tO1, tS1, aV + st * S::kTile, j > 0);
+            issue_pv<D>(tO1, tS1, vdesc(st), j > 0);
           }
           umma_commit(bar_ve + st);
           if (more) {
             if (two) {
-              issue_s<D>(tS1, aQ1, aK + st1 * S::kTile);
+              issue_s<D>(tS1, dQ1, kdesc(st1));
               umma_commit(bar_s + 1);
             }
             umma_commit(bar_ke + st1);
