@@ -32,8 +32,11 @@
 // moves when a tile's max exceeds it by more than 8 (a factor of 256), so O is
 // rescaled rarely; exp2(s - m) then stays <= 256, which fp32 and bf16 carry
 // exactly as well as values <= 1.  The final O / l is the same function.
-// Three quarters of the exponentials run on the MUFU (ex2.approx), one quarter
-// on the FMA pipe (exp2_poly2), so neither pipe limits the tile.
+// Every exponential runs on the MUFU (ex2.approx.f32).  Measured alternatives
+// that were slower at config 2: an FMA-pipe polynomial for a quarter of them
+// (exp2_poly2; the dense FP32 stream starves the MMA issuer of issue slots --
+// kPolyCols keeps the option, at 0) and paired f16 exponentials (exp2_f16x2;
+// the widening conversions share the MUFU pipe).
 //
 // Keys: a tile whose keys are all masked is skipped outright (its weight is
 // exactly zero); partial tiles and the ragged tail get -inf logits per
