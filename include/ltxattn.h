@@ -148,6 +148,18 @@ LTXATTN_API int ltxattn_fwd(const ltxattn_fwd_args* args, void* stream);
 /* Device scratch bytes ltxattn_fwd needs for these arguments. */
 LTXATTN_API size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* args);
 
+/* ltxattn_fwd for callers that cannot allocate device memory -- for example a
+ * host whose device memory is owned by another framework's allocator, or a
+ * render loop that must not allocate between steps.  No counterpart in the
+ * reference.  args->workspace is ignored: scratch comes from a fixed 32 MiB
+ * device array inside the library (held on every GPU that loads it until
+ * exit), and arguments needing more (ltxattn_fwd_workspace) are refused with
+ * LTXATTN_ERR_WORKSPACE.  Allocates nothing.  The first call on a device
+ * looks the array up for that device; make it before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU race: keep them
+ * ordered (one stream, or explicit events). */
+LTXATTN_API int ltxattn_fwd_noalloc(const ltxattn_fwd_args* args, void* stream);
+
 /* Replaces the autodiff VJP of the SDPA core (LoRA training backward). */
 LTXATTN_API int ltxattn_bwd(const ltxattn_bwd_args* args, void* stream);
 

@@ -22,7 +22,7 @@ STATUS_NAMES = {OK: "ok", ERR_SHAPE: "shape", ERR_DTYPE: "dtype", ERR_ALIGN: "al
 F32, BF16 = 0, 1
 
 EXPORTED = (
-    "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_bwd", "ltxattn_bwd_workspace",
+    "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
@@ -97,6 +97,8 @@ def load(path: str = LIB_PATH):
     vp = ctypes.c_void_p
     L.ltxattn_fwd.argtypes = [ctypes.POINTER(FwdArgs), vp]
     L.ltxattn_fwd.restype = ctypes.c_int
+    L.ltxattn_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), vp]
+    L.ltxattn_fwd_noalloc.restype = ctypes.c_int
     L.ltxattn_fwd_workspace.argtypes = [ctypes.POINTER(FwdArgs)]
     L.ltxattn_fwd_workspace.restype = ctypes.c_size_t
     L.ltxattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), vp]
