@@ -226,30 +226,32 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_dq = idesc_bf16_f32(128, D, 0, 1);
       const uint32_t tS = tmem, tP = tmem + 128, tQ = tmem + 256;
-      const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      // base descriptors built once; per MMA only the low word moves
+      const SDesc dQd = sdesc_split(smem_u32(sQ), 16, 1024), dOd = sdesc_split(smem_u32(sDO), 16, 1024);
       if (mbar_wait(bar_q, 0, abort_flag, p.err, 22)) {
         for (int i = 0; i < n; ++i) {
           const int st = i & 1;
           if (!mbar_wait(bar_kvf + st, (i >> 1) & 1, abort_flag, p.err, 23)) break;
           tc_fence_after();
-          const uint32_t aK = smem_u32(sK[st]), aV = smem_u32(sV[st]);
+          const SDesc dKd = sdesc_split(smem_u32(sK[0]) + st * 2 * S::kTile, 16, 1024);
+          const SDesc dVd = sdesc_split(smem_u32(sV[0]) + st * 2 * S::kTile, 16, 1024);
+          const SDesc dKmn = sdesc_split(smem_u32(sK[0]) + st * 2 * S::kTile, kChunkBytes, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_ss(tS, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idesc_s, kk > 0);
+            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+            umma_ss2(tS, dQd.lo + off, dQd.hi, dKd.lo + off, dKd.hi, idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_ss(tP, sdesc_sw128(aDO + off, 16, 1024), sdesc_sw128(aV + off, 16, 1024), idesc_s, kk > 0);
+            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+            umma_ss2(tP, dOd.lo + off, dOd.hi, dVd.lo + off, dVd.hi, idesc_s, kk > 0);
           }
           umma_commit(bar_s);
           if (!mbar_wait(bar_p, i & 1, abort_flag, p.err, 24)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kTileN / 16; ++kk)
-            umma_ts(tQ, tS + kk * 8, sdesc_sw128(aK + kk * 16 * 128, kChunkBytes, 1024), idesc_dq,
-                    (i > 0 || kk > 0) ? 1u : 0u);
+            umma_ts2(tQ, tS + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
           umma_commit(bar_kve + st);
         }
       }
@@ -411,34 +413,34 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_g = idesc_bf16_f32(128, D, 0, 1);
       const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 384;
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      const SDesc dKd = sdesc_split(smem_u32(sK), 16, 1024), dVd = sdesc_split(smem_u32(sV), 16, 1024);
       if (mbar_wait(bar_kv, 0, abort_flag, p.err, 32)) {
         for (int j = 0; j < n; ++j) {
           const int st = j & 1;
           if (!mbar_wait(bar_qf + st, (j >> 1) & 1, abort_flag, p.err, 33)) break;
           tc_fence_after();
-          const uint32_t aQ = smem_u32(sQ[st]), aDO = smem_u32(sDO[st]);
+          const uint32_t aQ = smem_u32(sQ[0]) + st * 2 * S::kTile, aDO = smem_u32(sDO[0]) + st * 2 * S::kTile;
+          const SDesc dQd = sdesc_split(aQ, 16, 1024), dOd = sdesc_split(aDO, 16, 1024);
+          const SDesc dQmn = sdesc_split(aQ, kChunkBytes, 1024), dOmn = sdesc_split(aDO, kChunkBytes, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_ss(tS, sdesc_sw128(aK + off, 16, 1024), sdesc_sw128(aQ + off, 16, 1024), idesc_s, kk > 0);
+            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+            umma_ss2(tS, dKd.lo + off, dKd.hi, dQd.lo + off, dQd.hi, idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-            umma_ss(tP, sdesc_sw128(aV + off, 16, 1024), sdesc_sw128(aDO + off, 16, 1024), idesc_s, kk > 0);
+            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+            umma_ss2(tP, dVd.lo + off, dVd.hi, dOd.lo + off, dOd.hi, idesc_s, kk > 0);
           }
           umma_commit(bar_s);
           if (!mbar_wait(bar_p, j & 1, abort_flag, p.err, 34)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kTileM / 16; ++kk)
-            umma_ts(tV, tS + kk * 8, sdesc_sw128(aDO + kk * 16 * 128, kChunkBytes, 1024), idesc_g,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+            umma_ts2(tV, tS + kk * 8, dOmn.lo + ((kk * 16 * 128) >> 4), dOmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < kTileM / 16; ++kk)
-            umma_ts(tK, tP + kk * 8, sdesc_sw128(aQ + kk * 16 * 128, kChunkBytes, 1024), idesc_g,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+            umma_ts2(tK, tP + kk * 8, dQmn.lo + ((kk * 16 * 128) >> 4), dQmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(bar_qe + st);
         }
       }

@@ -30,31 +30,32 @@ __device__ __forceinline__ void rot(float x1, float x2, float c, float s, bool b
   }
 }
 
-struct Job {
-  const RopeParams* p;
-  int64_t count;  // groups of 8 pairs
-};
-
-__device__ __forceinline__ void locate(const RopeParams& p, int64_t gid, int& b, int& hl, int& t, int& g) {
-  const int groups = p.D / 16;
-  g = (int)(gid % groups);
-  t = (int)((gid / groups) % p.T);
-  hl = (int)((gid / ((int64_t)groups * p.T)) % p.Hc);
-  b = (int)(gid / ((int64_t)groups * p.T * p.Hc));
-}
-
-__global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2, int64_t na,
-                                                            int64_t nc) {
-  int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const RopeParams* pp = &a;
-  if (gid >= na) {
-    gid -= na;
-    pp = &c2;
-    if (gid >= nc) return;
+// Grid: x covers (token, 8-pair group) of one (head, batch), y = local head,
+// z = batch for job a followed by batch for job b.  Groups per row are 4 or 8
+// (D = 64 / 128), so the decode is shifts, not divisions.
+__device__ __forceinline__ bool locate(const RopeParams& a, const RopeParams& b2, const RopeParams*& pp, int& b,
+                                       int& hl, int& t, int& g) {
+  pp = &a;
+  b = blockIdx.z;
+  if (b >= a.B) {
+    pp = &b2;
+    b -= a.B;
   }
   const RopeParams& p = *pp;
+  hl = blockIdx.y;
+  if (hl >= p.Hc) return false;
+  const int shift = p.D == 128 ? 3 : 2;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  g = idx & ((1 << shift) - 1);
+  t = idx >> shift;
+  return t < p.T;
+}
+
+__global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2) {
+  const RopeParams* pp;
   int b, hl, t, g;
-  locate(p, gid, b, hl, t, g);
+  if (!locate(a, c2, pp, b, hl, t, g)) return;
+  const RopeParams& p = *pp;
   const int half = p.D / 2;
   const int h = p.head_begin + hl;
   const __nv_bfloat16* x =
@@ -104,18 +105,11 @@ __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, int64_t i, f
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2, int64_t na,
-                                                          int64_t nc) {
-  int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const RopeParams* pp = &a;
-  if (gid >= na) {
-    gid -= na;
-    pp = &c2;
-    if (gid >= nc) return;
-  }
-  const RopeParams& p = *pp;
+__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2) {
+  const RopeParams* pp;
   int b, hl, t, g;
-  locate(p, gid, b, hl, t, g);
+  if (!locate(a, c2, pp, b, hl, t, g)) return;
+  const RopeParams& p = *pp;
   const int half = p.D / 2;
   const int h = p.head_begin + hl;
   const bool bf16 = sizeof(T) == 2;
@@ -140,24 +134,25 @@ bool vec_ok(const RopeParams& p) {
          m8(p.t_sh) && m8(p.t_st);
 }
 
-int64_t groups(const RopeParams* p) { return p ? (int64_t)p->B * p->Hc * p->T * (p->D / 16) : 0; }
-
 }  // namespace
 
 // Rotate one or two tensors (b may be null) in one launch.
 cudaError_t launch_rope(const RopeParams* a, const RopeParams* b, bool bf16, cudaStream_t s) {
-  const int64_t na = groups(a), nb = groups(b);
   const RopeParams none{};
   const RopeParams& pb = b ? *b : none;
-  const int blocks = (int)((na + nb + 255) / 256);
-  if (blocks == 0) return cudaSuccess;
+  const int rows_a = a->T * (a->D / 16), rows_b = b ? b->T * (b->D / 16) : 0;
+  const int xs = ((rows_a > rows_b ? rows_a : rows_b) + 255) / 256;
+  const int ys = (b && b->Hc > a->Hc) ? b->Hc : a->Hc;
+  const int zs = a->B + (b ? b->B : 0);
+  if (xs == 0 || ys > 65535 || zs > 65535) return xs == 0 ? cudaSuccess : cudaErrorInvalidConfiguration;
+  const dim3 grid(xs, ys, zs);
   if (bf16) {
     if (vec_ok(*a) && (!b || vec_ok(*b)))
-      rope_bf16_vec_kernel<<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+      rope_bf16_vec_kernel<<<grid, 256, 0, s>>>(*a, pb);
     else
-      rope_scalar_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+      rope_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(*a, pb);
   } else {
-    rope_scalar_kernel<float><<<blocks, 256, 0, s>>>(*a, pb, na, nb);
+    rope_scalar_kernel<float><<<grid, 256, 0, s>>>(*a, pb);
   }
   return cudaGetLastError();
 }
