@@ -21,6 +21,8 @@
 // the PV-style products read them straight from TMEM (tcgen05.mma A-from-TMEM).
 // When rotary tables are given, dQ and dK leave through the transpose
 // rotation: the gradient with respect to the un-rotated input.
+#include <mutex>
+
 #include "ltxattn_internal.h"
 #include "sm100.cuh"
 
@@ -554,19 +556,43 @@ cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+namespace {
+constexpr int kMaxDev = 64;
+std::mutex g_prep_mu;
+size_t g_smem_set[kMaxDev][2][2] = {};  // [device][D == 128][dq / dkdv]
+}  // namespace
+
+// Shared-memory attributes for the two backward kernels, set once per device
+// and size (cached), so the launches of a call queue back to back.
+cudaError_t prepare_bwd_bf16(int D, size_t smem_dq, size_t smem_dkdv) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  const int di = D == 128 ? 1 : 0;
+  std::lock_guard<std::mutex> lock(g_prep_mu);
+  if (smem_dq > g_smem_set[dev][di][0]) {
+    e = D == 128 ? set_smem(bwd_dq_kernel<128>, smem_dq) : set_smem(bwd_dq_kernel<64>, smem_dq);
+    if (e != cudaSuccess) return e;
+    g_smem_set[dev][di][0] = smem_dq;
+  }
+  if (smem_dkdv > g_smem_set[dev][di][1]) {
+    e = D == 128 ? set_smem(bwd_dkdv_kernel<128>, smem_dkdv) : set_smem(bwd_dkdv_kernel<64>, smem_dkdv);
+    if (e != cudaSuccess) return e;
+    g_smem_set[dev][di][1] = smem_dkdv;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_bwd_bf16(const BwdParams& p, int D, int Hc, int B, size_t smem_dq, size_t smem_dkdv,
                             cudaStream_t s) {
   dim3 gdq(p.n_q_tiles, Hc, B), gkv(p.n_kv_tiles, Hc, B);
   cudaError_t e;
   if (D == 128) {
-    if ((e = set_smem(bwd_dq_kernel<128>, smem_dq)) != cudaSuccess) return e;
-    if ((e = set_smem(bwd_dkdv_kernel<128>, smem_dkdv)) != cudaSuccess) return e;
     bwd_dq_kernel<128><<<gdq, kThreads, smem_dq, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     bwd_dkdv_kernel<128><<<gkv, kThreads, smem_dkdv, s>>>(p);
   } else {
-    if ((e = set_smem(bwd_dq_kernel<64>, smem_dq)) != cudaSuccess) return e;
-    if ((e = set_smem(bwd_dkdv_kernel<64>, smem_dkdv)) != cudaSuccess) return e;
     bwd_dq_kernel<64><<<gdq, kThreads, smem_dq, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     bwd_dkdv_kernel<64><<<gkv, kThreads, smem_dkdv, s>>>(p);

@@ -47,6 +47,8 @@
 // each split handles a contiguous share of the active KV tiles and writes an
 // fp32 partial O (normalised by its own l) and its log2-domain lse; the
 // combine kernel merges them.
+#include <mutex>
+
 #include "ltxattn_internal.h"
 #include "sm100.cuh"
 
@@ -64,7 +66,13 @@ constexpr int kBlockM = kFwdBlockM;             // query rows per CTA (two Q til
 constexpr uint32_t kChunkBytes = 128u * 128u;  // one 64-element-wide chunk of a 128-row tile
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr int kPolyCols = 0;  // columns [128 - kPolyCols, 128) use exp2_poly2
+// Exponentials per 128-column row evaluated on the FMA pipe (exp2_poly2)
+// instead of the MUFU; pair p of a row uses the polynomial when p % 8 < kPolyCols / 16.
+#ifndef LTX_FWD_POLY_COLS
+#define LTX_FWD_POLY_COLS 0
+#endif
+constexpr int kPolyCols = LTX_FWD_POLY_COLS;
+static_assert(kPolyCols % 16 == 0 && kPolyCols <= 128, "polynomial share is whole 16-column groups");
 
 template <int D>
 struct Smem {
@@ -354,7 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         }
       }
       const int kv0 = (int)tiles[t_begin + i] * kTileN;
-      if (use_mask || kv0 + kTileN > Lk) {
+      const bool masked_tile = use_mask || kv0 + kTileN > Lk;
+      if (masked_tile) {
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint32_t bits = 0xffffffffu;
@@ -405,10 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       for (int c = 0; c < 128; c += 2) {
         const float2 x = fma2(make_float2(s[c], s[c + 1]), sl2x2, nmx2);
         float2 e;
-        if (c < 128 - kPolyCols) {
-          e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-        } else {
+        if (((c >> 1) & 7) < kPolyCols / 16) {
           e = exp2_poly2(x);
+          if (masked_tile) {  // the polynomial leaves <= 2^-126 for -inf; masked weights are exactly 0
+            e.x = (s[c] == -INFINITY) ? 0.f : e.x;
+            e.y = (s[c + 1] == -INFINITY) ? 0.f : e.y;
+          }
+        } else {
+          e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         }
         s[c] = e.x;
         s[c + 1] = e.y;
@@ -555,20 +568,45 @@ cudaError_t check_launch_regs(K kernel) {
   return fa.numRegs == (int)kLaunchRegs ? cudaSuccess : cudaErrorInvalidConfiguration;
 }
 
+// Per-device, per-head-dim launch preparation, done once (the register check)
+// or when a larger shared-memory size is first needed; calls on the hot path
+// then cost a cached comparison.
+namespace {
+constexpr int kMaxDev = 64;
+std::mutex g_prep_mu;
+size_t g_smem_set[kMaxDev][2] = {};
+bool g_regs_ok[kMaxDev][2] = {};
+}  // namespace
+
+cudaError_t prepare_fwd_bf16(int D, size_t smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  const int di = D == 128 ? 1 : 0;
+  std::lock_guard<std::mutex> lock(g_prep_mu);
+  if (!g_regs_ok[dev][di]) {
+    e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128>) : check_launch_regs(fwd_bf16_sm100_kernel<64>);
+    if (e != cudaSuccess) return e;
+    g_regs_ok[dev][di] = true;
+  }
+  if (smem > g_smem_set[dev][di]) {
+    e = D == 128 ? cudaFuncSetAttribute(fwd_bf16_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                 : cudaFuncSetAttribute(fwd_bf16_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    g_smem_set[dev][di] = smem;
+  }
+  return cudaSuccess;
+}
+
+// Launch only (prepare_fwd_bf16 must have succeeded for D and at least smem).
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_blocks, int Hc, int B, size_t smem,
                             cudaStream_t s) {
   dim3 grid(q_blocks * p.num_splits, Hc, B);
-  cudaError_t e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128>) : check_launch_regs(fwd_bf16_sm100_kernel<64>);
-  if (e != cudaSuccess) return e;
-  if (D == 128) {
-    e = cudaFuncSetAttribute(fwd_bf16_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  if (D == 128)
     fwd_bf16_sm100_kernel<128><<<grid, kThreads, smem, s>>>(p);
-  } else {
-    e = cudaFuncSetAttribute(fwd_bf16_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  else
     fwd_bf16_sm100_kernel<64><<<grid, kThreads, smem, s>>>(p);
-  }
   return cudaGetLastError();
 }
 

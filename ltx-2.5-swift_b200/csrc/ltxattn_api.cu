@@ -323,17 +323,15 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   ltxattn_tensor q = a->q, k = a->k;
   int q_head_off = s.h0, kv_head_off = s.h0;
   cudaError_t e;
+  // The rotation pre-pass is launched only after every piece of host work of
+  // this call is done, so it and the attention kernel queue back to back with
+  // no host gap between them.
+  RopeParams rope_k{}, rope_q{};
   if (P.rope_q) {
-    // k is always rotated with q (with its own table or q's); q is rotated here
-    // too unless the attention kernel does it (fuse_q)
-    const RopeParams rk = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
-    if (P.fuse_q) {
-      e = launch_rope(&rk, nullptr, bf16, st);
-    } else {
-      const RopeParams rq = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
-      e = launch_rope(&rq, &rk, bf16, st);
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+    // k is always rotated with q (with its own table or q's); q is rotated in
+    // the pre-pass too unless the attention kernel does it (fuse_q)
+    rope_k = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
+    if (!P.fuse_q) rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
     if (!P.fuse_q) {
       q.data = ws + P.off_q;
       q.stride_t = s.D;
@@ -352,7 +350,13 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   const int k_head_off = P.rope_k ? 0 : s.h0;
   const int v_head_off = s.h0;
 
+  auto launch_pre_pass = [&]() -> int {
+    if (!P.rope_q) return LTXATTN_OK;
+    const cudaError_t er = P.fuse_q ? launch_rope(&rope_k, nullptr, bf16, st) : launch_rope(&rope_q, &rope_k, bf16, st);
+    return er == cudaSuccess ? LTXATTN_OK : cuda_fail(er, "rope launch");
+  };
   if (!bf16) {
+    if ((rc = launch_pre_pass())) return rc;
     F32Params p{};
     p.q = static_cast<const float*>(q.data);
     p.k = static_cast<const float*>(k.data);
@@ -429,6 +433,11 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.part_lse = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_pl) : nullptr;
   p.err = err;
   const size_t smem = fwd_bf16_smem_bytes(s.D, s.Lk, a->key_mask != nullptr);
+  e = prepare_fwd_bf16(s.D, smem);
+  if (e == cudaErrorInvalidConfiguration)
+    return fail(LTXATTN_ERR_CUDA, "fwd_bf16: the loaded kernel's register count differs from its warpgroup split");
+  if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 setup");
+  if ((rc = launch_pre_pass())) return rc;
   e = launch_fwd_bf16(p, s.D, P.q_tiles, s.Hc, s.B, smem, st);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
   if (P.splits > 1) {
@@ -494,11 +503,11 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
   q.data = const_cast<void*>(at(a->q));
   k.data = const_cast<void*>(at(a->k));
   cudaError_t e;
+  // every launch of this call is queued after all host work (no host gaps)
+  RopeParams rope_q{}, rope_k{};
   if (P.rope) {
-    const RopeParams rq = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
-    const RopeParams rk = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
-    e = launch_rope(&rq, &rk, bf16, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+    rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
+    rope_k = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
     q.data = ws + P.off_q;
     q.stride_t = s.D;
     q.stride_h = (int64_t)s.Lq * s.D;
@@ -522,8 +531,14 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
   pp.B = s.B; pp.Hc = s.Hc; pp.Lq = s.Lq; pp.Lq_pad = P.Lq_pad; pp.D = s.D;
   pp.log2_domain = bf16 ? 1 : 0;
   pp.f32 = bf16 ? 0 : 1;
-  e = launch_bwd_prep(pp, st);
-  if (e != cudaSuccess) return cuda_fail(e, "bwd prep launch");
+  auto launch_pre = [&]() -> int {
+    if (P.rope) {
+      e = launch_rope(&rope_q, &rope_k, bf16, st);
+      if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+    }
+    e = launch_bwd_prep(pp, st);
+    return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "bwd prep launch");
+  };
 
   BwdParams p{};
   p.lse2 = lse2;
@@ -563,6 +578,7 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
     p.v_sb = a->v.stride_b; p.v_sh = a->v.stride_h; p.v_st = a->v.stride_t;
     p.dout = static_cast<const float*>(at(a->dout));
     p.do_sb = a->dout.stride_b; p.do_sh = a->dout.stride_h; p.do_st = a->dout.stride_t;
+    if ((rc = launch_pre())) return rc;
     e = launch_bwd_f32(p, s.D, s.Hc, s.B, st);
     if (e != cudaSuccess) return cuda_fail(e, "bwd_f32 launch");
     return LTXATTN_OK;
@@ -575,8 +591,11 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
                       a->dout.stride_b, "dout")))
     return rc;
   const bool has_mask = a->key_mask != nullptr;
-  e = launch_bwd_bf16(p, s.D, s.Hc, s.B, bwd_dq_smem_bytes(s.D, s.Lk, has_mask),
-                      bwd_dkdv_smem_bytes(s.D, s.Lk, has_mask), st);
+  const size_t smem_dq = bwd_dq_smem_bytes(s.D, s.Lk, has_mask), smem_kv = bwd_dkdv_smem_bytes(s.D, s.Lk, has_mask);
+  e = prepare_bwd_bf16(s.D, smem_dq, smem_kv);
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_bf16 setup");
+  if ((rc = launch_pre())) return rc;
+  e = launch_bwd_bf16(p, s.D, s.Hc, s.B, smem_dq, smem_kv, st);
   if (e != cudaSuccess) return cuda_fail(e, "bwd_bf16 launch");
   return LTXATTN_OK;
 }

@@ -139,6 +139,8 @@ struct BwdPrepParams {
 };
 
 // Launchers (return cudaError_t of the launch).
+// Once-per-device kernel attributes (cached); call before launch_fwd_bf16.
+cudaError_t prepare_fwd_bf16(int D, size_t smem_bytes);
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int B,
                             size_t smem_bytes, cudaStream_t s);
 size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
@@ -149,6 +151,8 @@ cudaError_t launch_rope(const RopeParams* a, const RopeParams* b, bool bf16, cud
 cudaError_t launch_bwd_prep(const BwdPrepParams& p, cudaStream_t s);
 size_t bwd_dq_smem_bytes(int D, int Lk, bool has_mask);
 size_t bwd_dkdv_smem_bytes(int D, int Lk, bool has_mask);
+// Once-per-device kernel attributes (cached); call before launch_bwd_bf16.
+cudaError_t prepare_bwd_bf16(int D, size_t smem_dq, size_t smem_dkdv);
 cudaError_t launch_bwd_bf16(const BwdParams& p, int D, int Hc, int B, size_t smem_dq, size_t smem_dkdv,
                             cudaStream_t s);
 cudaError_t launch_bwd_f32(const BwdParams& p, int D, int Hc, int B, cudaStream_t s);

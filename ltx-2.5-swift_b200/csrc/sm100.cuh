@@ -410,22 +410,23 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // added to the exponent field.  The coefficients are this library's own
 // relative-error least-squares fit of 2^f on [-1/2, 1/2] (iteratively
 // reweighted towards minimax): max relative error 7.5e-5, far below the
-// bf16 rounding P receives.  x < -126 returns exactly 0 (masked logits are -inf).
+// bf16 rounding P receives.  Arguments are clamped at -126: below that the
+// result is at most 2^-126 (callers zero masked columns themselves).
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
   const float2 t = add2(xc, make_float2(kMagic, kMagic));
   const float2 n = add2(t, make_float2(-kMagic, -kMagic));
-  const float2 f = add2(xc, make_float2(-n.x, -n.y));
+  const float2 f = fma2(n, make_float2(-1.f, -1.f), xc);  // exact: x - n
   float2 q = fma2(f, make_float2(0.0551716573536396f, 0.0551716573536396f),
                   make_float2(0.2426111400127411f, 0.2426111400127411f));
   q = fma2(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
   q = fma2(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  const int nx = __float_as_int(t.x) - __float_as_int(kMagic);
-  const int ny = __float_as_int(t.y) - __float_as_int(kMagic);
+  // bits(t) = bits(kMagic) + n, so bits(q) + (n << 23) = bits(q) + (bits(t) << 23) - (bits(kMagic) << 23)
+  constexpr uint32_t kBias = 0x4B400000u << 23;
   float2 r;
-  r.x = x.x >= -126.f ? __int_as_float(__float_as_int(q.x) + (nx << 23)) : 0.f;
-  r.y = x.y >= -126.f ? __int_as_float(__float_as_int(q.y) + (ny << 23)) : 0.f;
+  r.x = __uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23) - kBias);
+  r.y = __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23) - kBias);
   return r;
 }
 
