@@ -58,8 +58,8 @@ namespace {
 
 constexpr int kThreads = 384;
 constexpr uint32_t kLaunchRegs = 168;   // what ptxas allots under __launch_bounds__(384, 1)
-constexpr uint32_t kProducerRegs = 72;
-constexpr uint32_t kSoftmaxRegs = 216;
+constexpr uint32_t kProducerRegs = 88;
+constexpr uint32_t kSoftmaxRegs = 208;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs,
               "register re-split exceeds the launch allocation");
 constexpr int kBlockM = kFwdBlockM;             // query rows per CTA (two Q tiles)
@@ -128,7 +128,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   uint64_t* bar_s = bars + 9;    // [2] per Q tile
   uint64_t* bar_p = bars + 11;   // [2] per Q tile
   uint64_t* bar_o = bars + 13;
-  uint64_t* bar_qr = bars + 14;  // q tiles rotated in shared memory (fused RoPE)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
@@ -148,7 +147,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   // ---------------- prologue ----------------
   if (threadIdx.x == 0) {
     for (int i = 0; i < 14; ++i) mbar_init(bars + i, (i == 11 || i == 12) ? 128 : 1);
-    mbar_init(bars + 14, 128u * (two ? 2u : 1u));  // q_ready: every softmax thread rotated its q row
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -256,8 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       const uint32_t stage_step = S::kTile >> 4;
       auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
       auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
-      uint64_t* q_gate = p.qcos != nullptr ? bar_qr : bar_q;
-      if (mbar_wait(q_gate, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4)) {
+      if (mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4)) {
         tc_fence_after();
         issue_s<D>(tS0, dQ0, kdesc(0));
         umma_commit(bar_s + 0);
@@ -315,33 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     float m = -INFINITY;  // running max, log2 domain (lazy)
     float l = 0.f;
     bool ok = true;
-    if (p.qcos != nullptr && n > 0) {
-      // fused RoPE of q: this thread rotates its own row of Q tile t in place.
-      // In the 128-byte swizzle, 16-byte unit j of row r sits at unit j ^ (r & 7);
-      // pair partners (d, d + D/2) share that position (D = 128: the other
-      // 64-wide chunk; D = 64: four units further along the same row).
-      ok = warp_wait(bar_q, 0, abort_flag, p.err, 11);
-      const int r = threadIdx.x & 127;
-      if (ok && row < p.Lq) {
-        uint8_t* rbase = sQ + t * S::kTile + r * 128;
-        const __nv_bfloat16* cr = p.qcos + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
-        const __nv_bfloat16* sr = p.qsin + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
-#pragma unroll
-        for (int j = 0; j < D / 16; ++j) {
-          uint4* a = reinterpret_cast<uint4*>(rbase + ((j ^ (r & 7)) << 4));
-          uint4* bb = (D == 128) ? reinterpret_cast<uint4*>(rbase + kChunkBytes + ((j ^ (r & 7)) << 4))
-                                 : reinterpret_cast<uint4*>(rbase + (((j + 4) ^ (r & 7)) << 4));
-          const uint4 cv = *reinterpret_cast<const uint4*>(cr + 8 * j);
-          const uint4 sv = *reinterpret_cast<const uint4*>(sr + 8 * j);
-          uint4 o1, o2;
-          rope_bf16x8(*a, *bb, cv, sv, o1, o2);
-          *a = o1;
-          *bb = o2;
-        }
-      }
-      fence_proxy_async_smem();  // the tensor core reads these rows through the async proxy
-      mbar_arrive(bar_qr);
-    }
     for (int i = 0; i < n; ++i) {
       if (!warp_wait(my_s, i & 1, abort_flag, p.err, 9)) { ok = false; break; }
       tc_fence_after();

@@ -156,7 +156,6 @@ int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
 struct FwdPlan {
   Shape s;
   bool rope_q, rope_k;
-  bool fuse_q;  // bf16: q is rotated inside the attention kernel (no q copy)
   const ltxattn_rotary* kr;  // table used for k
   int q_tiles, kv_tiles, splits;
   size_t off_q, off_k, off_po, off_pl, total;
@@ -174,14 +173,6 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   if (P->rope_q) {
     if ((rc = check_rotary(a->q_rotary, "q_rotary", s.Lq))) return rc;
     if ((rc = check_rotary(*P->kr, a->k_rotary.cos ? "k_rotary" : "q_rotary (used for k)", s.Lk))) return rc;
-  }
-  // the bf16 kernel rotates q itself when each table row is a run of whole 16-byte vectors
-  P->fuse_q = false;
-  if (P->rope_q && s.dtype == LTXATTN_BF16) {
-    const ltxattn_rotary& r = a->q_rotary;
-    const int64_t hb = (int64_t)s.h0 * r.stride_h * 2;
-    P->fuse_q = aligned16(static_cast<const uint8_t*>(r.cos) + hb) && aligned16(static_cast<const uint8_t*>(r.sin) + hb) &&
-                r.stride_t % 8 == 0 && r.stride_h % 8 == 0 && r.stride_b % 8 == 0;
   }
   P->q_tiles = s.dtype == LTXATTN_BF16 ? (s.Lq + kFwdBlockM - 1) / kFwdBlockM : (s.Lq + kTileM - 1) / kTileM;
   P->kv_tiles = (s.Lk + kTileN - 1) / kTileN;
@@ -202,7 +193,7 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   }
   size_t off = 0;
   P->off_q = off;
-  if (P->rope_q && !P->fuse_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
+  if (P->rope_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
   P->off_k = off;
   if (P->rope_k) off += align256((size_t)s.B * s.Hc * s.Lk * s.D * s.esize);
   P->off_po = off;
@@ -303,7 +294,7 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   const Shape& s = P.s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = s.dtype == LTXATTN_BF16;
-  if ((rc = check_tensor(a->q, "q", s, bf16 && (!P.rope_q || P.fuse_q)))) return rc;
+  if ((rc = check_tensor(a->q, "q", s, bf16 && !P.rope_q))) return rc;
   if ((rc = check_tensor(a->k, "k", s, bf16 && !P.rope_k))) return rc;
   if ((rc = check_tensor(a->v, "v", s, bf16))) return rc;
   if ((rc = check_tensor(a->out, "out", s, bf16))) return rc;
@@ -328,17 +319,15 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   // no host gap between them.
   RopeParams rope_k{}, rope_q{};
   if (P.rope_q) {
-    // k is always rotated with q (with its own table or q's); q is rotated in
-    // the pre-pass too unless the attention kernel does it (fuse_q)
+    // k is always rotated with q (with its own table or q's); one launch
+    // rotates both into the workspace
     rope_k = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
-    if (!P.fuse_q) rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
-    if (!P.fuse_q) {
-      q.data = ws + P.off_q;
-      q.stride_t = s.D;
-      q.stride_h = (int64_t)s.Lq * s.D;
-      q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
-      q_head_off = 0;
-    }
+    rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
+    q.data = ws + P.off_q;
+    q.stride_t = s.D;
+    q.stride_h = (int64_t)s.Lq * s.D;
+    q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
+    q_head_off = 0;
   }
   ltxattn_tensor v = a->v;
   if (P.rope_k) {
@@ -352,7 +341,7 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
 
   auto launch_pre_pass = [&]() -> int {
     if (!P.rope_q) return LTXATTN_OK;
-    const cudaError_t er = P.fuse_q ? launch_rope(&rope_k, nullptr, bf16, st) : launch_rope(&rope_q, &rope_k, bf16, st);
+    const cudaError_t er = launch_rope(&rope_q, &rope_k, bf16, st);
     return er == cudaSuccess ? LTXATTN_OK : cuda_fail(er, "rope launch");
   };
   if (!bf16) {
@@ -387,17 +376,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   }
 
   FwdParams p{};
-  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, (P.rope_q && !P.fuse_q) ? s.Hc : s.H, s.B, q.stride_t,
+  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, P.rope_q ? s.Hc : s.H, s.B, q.stride_t,
                       q.stride_h, q.stride_b, "q")))
     return rc;
-  if (P.fuse_q) {
-    const ltxattn_rotary& r = a->q_rotary;
-    p.qcos = reinterpret_cast<const __nv_bfloat16*>(r.cos) + (int64_t)s.h0 * r.stride_h;
-    p.qsin = reinterpret_cast<const __nv_bfloat16*>(r.sin) + (int64_t)s.h0 * r.stride_h;
-    p.qt_sb = r.stride_b;
-    p.qt_sh = r.stride_h;
-    p.qt_st = r.stride_t;
-  }
   if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, P.rope_k ? s.Hc : s.H, s.B, k.stride_t, k.stride_h,
                       k.stride_b, "k")))
     return rc;

@@ -41,11 +41,6 @@ struct FwdParams {
   float scale_log2;  // softmax scale * log2(e)
   float* part_o;     // [splits][B][Hc][Lq][D] fp32 (num_splits > 1)
   float* part_lse;   // [splits][B][Hc][Lq] log2 domain (num_splits > 1)
-  // RoPE of q fused into the kernel (qcos null = q arrives rotated or unrotated
-  // by design): bf16 tables based at local head 0, 16-byte aligned rows
-  const __nv_bfloat16* qcos;
-  const __nv_bfloat16* qsin;
-  int64_t qt_sb, qt_sh, qt_st;
   int* err;
 };
 

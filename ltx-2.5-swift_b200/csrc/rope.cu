@@ -32,16 +32,11 @@ __device__ __forceinline__ void rot(float x1, float x2, float c, float s, bool b
 
 // Grid: x covers (token, 8-pair group) of one (head, batch), y = local head,
 // z = batch for job a followed by batch for job b.  Groups per row are 4 or 8
-// (D = 64 / 128), so the decode is shifts, not divisions.
-__device__ __forceinline__ bool locate(const RopeParams& a, const RopeParams& b2, const RopeParams*& pp, int& b,
-                                       int& hl, int& t, int& g) {
-  pp = &a;
-  b = blockIdx.z;
-  if (b >= a.B) {
-    pp = &b2;
-    b -= a.B;
-  }
-  const RopeParams& p = *pp;
+// (D = 64 / 128), so the decode is shifts, not divisions.  Each kernel inlines
+// its body once per job with that job's parameter block, so every field is a
+// fixed-offset parameter load (selecting a block through a pointer would make
+// each thread copy both blocks to local memory).
+__device__ __forceinline__ bool locate(const RopeParams& p, int& hl, int& t, int& g) {
   hl = blockIdx.y;
   if (hl >= p.Hc) return false;
   const int shift = p.D == 128 ? 3 : 2;
@@ -51,20 +46,18 @@ __device__ __forceinline__ bool locate(const RopeParams& a, const RopeParams& b2
   return t < p.T;
 }
 
-__global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2) {
-  const RopeParams* pp;
-  int b, hl, t, g;
-  if (!locate(a, c2, pp, b, hl, t, g)) return;
-  const RopeParams& p = *pp;
+__device__ __forceinline__ void rope_vec_job(const RopeParams& p, int b) {
+  int hl, t, g;
+  if (!locate(p, hl, t, g)) return;
   const int half = p.D / 2;
   const int h = p.head_begin + hl;
   const __nv_bfloat16* x =
       static_cast<const __nv_bfloat16*>(p.x) + (int64_t)b * p.x_sb + (int64_t)h * p.x_sh + (int64_t)t * p.x_st + g * 8;
   const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + g * 8;
-  const uint4 vx1 = *reinterpret_cast<const uint4*>(x);
-  const uint4 vx2 = *reinterpret_cast<const uint4*>(x + half);
-  const uint4 vc = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.cos) + toff);
-  const uint4 vs = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.sin) + toff);
+  const uint4 vx1 = __ldg(reinterpret_cast<const uint4*>(x));
+  const uint4 vx2 = __ldg(reinterpret_cast<const uint4*>(x + half));
+  const uint4 vc = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.cos) + toff));
+  const uint4 vs = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.sin) + toff));
   const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&vx1);
   const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&vx2);
   const __nv_bfloat162* cc = reinterpret_cast<const __nv_bfloat162*>(&vc);
@@ -87,6 +80,14 @@ __global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, 
   *reinterpret_cast<uint4*>(y + half) = o2v;
 }
 
+__global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2) {
+  const int z = blockIdx.z;
+  if (z < a.B)
+    rope_vec_job(a, z);
+  else
+    rope_vec_job(c2, z - a.B);
+}
+
 template <typename T>
 __device__ __forceinline__ float ld(const T* p, int64_t i);
 template <>
@@ -105,11 +106,9 @@ __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, int64_t i, f
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2) {
-  const RopeParams* pp;
-  int b, hl, t, g;
-  if (!locate(a, c2, pp, b, hl, t, g)) return;
-  const RopeParams& p = *pp;
+__device__ __forceinline__ void rope_scalar_job(const RopeParams& p, int b) {
+  int hl, t, g;
+  if (!locate(p, hl, t, g)) return;
   const int half = p.D / 2;
   const int h = p.head_begin + hl;
   const bool bf16 = sizeof(T) == 2;
@@ -125,6 +124,15 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, co
     st(y, i, o1);
     st(y, i + half, o2);
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2) {
+  const int z = blockIdx.z;
+  if (z < a.B)
+    rope_scalar_job<T>(a, z);
+  else
+    rope_scalar_job<T>(c2, z - a.B);
 }
 
 bool vec_ok(const RopeParams& p) {

@@ -336,15 +336,15 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Lane-0 waits, the warp learns the outcome; keeps .sync.aligned tcgen05 ops
-// warp-uniform even when a wait gives up.
+// Whole-warp wait: every lane polls the barrier and the lanes then agree, so
+// a timeout seen by one lane is seen by all.  (A lane-0 poll with the other 31
+// lanes parked at a shuffle was measured to resume the warp several hundred
+// cycles after the phase completed.)  The lanes read the same barrier state
+// and the same timer in each converged poll, so they leave the loop together.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int site) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err, site) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, site);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Drain wait used only on the way out: bounded, ignores the abort flag.
@@ -444,32 +444,6 @@ __device__ __forceinline__ float2 exp2_f16x2(float2 x) {
       : "=f"(r.x), "=f"(r.y)
       : "r"(eh));
   return r;
-}
-
-// Split RoPE on 8 pairs held as bf16x8 vectors: o1 = x1*c - x2*s, o2 = x2*c + x1*s,
-// each product and sum evaluated in fp32 and rounded to bf16 once (the
-// arithmetic of a bf16 tensor times a bf16 table, DiTAttention.swift:226-234).
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
-__device__ __forceinline__ void rope_bf16x8(const uint4& x1v, const uint4& x2v, const uint4& cv, const uint4& sv,
-                                           uint4& o1v, uint4& o2v) {
-  const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&x1v);
-  const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&x2v);
-  const __nv_bfloat162* cc = reinterpret_cast<const __nv_bfloat162*>(&cv);
-  const __nv_bfloat162* ss = reinterpret_cast<const __nv_bfloat162*>(&sv);
-  __nv_bfloat162* o1 = reinterpret_cast<__nv_bfloat162*>(&o1v);
-  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o2v);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 a = __bfloat1622float2(x1[e]), b = __bfloat1622float2(x2[e]);
-    const float2 c = __bfloat1622float2(cc[e]), s = __bfloat1622float2(ss[e]);
-    const float r1x = bf16r(__fsub_rn(bf16r(__fmul_rn(a.x, c.x)), bf16r(__fmul_rn(b.x, s.x))));
-    const float r1y = bf16r(__fsub_rn(bf16r(__fmul_rn(a.y, c.y)), bf16r(__fmul_rn(b.y, s.y))));
-    const float r2x = bf16r(__fadd_rn(bf16r(__fmul_rn(b.x, c.x)), bf16r(__fmul_rn(a.x, s.x))));
-    const float r2y = bf16r(__fadd_rn(bf16r(__fmul_rn(b.y, c.y)), bf16r(__fmul_rn(a.y, s.y))));
-    o1[e] = __floats2bfloat162_rn(r1x, r1y);
-    o2[e] = __floats2bfloat162_rn(r2x, r2y);
-  }
 }
 
 // ---------------------------------------------------------------------------
