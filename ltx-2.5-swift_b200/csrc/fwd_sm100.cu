@@ -20,7 +20,9 @@
 // score row each: 2*128*kSoftmaxRegs + 128*kProducerRegs = 384*kLaunchRegs.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).
 // P_t (bf16, two per column) overwrites the first 64 columns of S_t and feeds
-// the PV MMA straight from TMEM.
+// the PV MMA straight from TMEM.  Softmax publishes P_t in two halves (keys
+// 0-63, then 64-127; barriers p_half and p_full), so the first four k-steps
+// of PV_t run while the second half is still being exponentiated.
 //
 // MMA issue order in steady state:  PV0_j, S0_{j+1}, PV1_j, S1_{j+1}.
 // tcgen05 ops of one thread execute in order, so S_t{j+1} never overwrites
@@ -33,10 +35,9 @@
 // rescaled rarely; exp2(s - m) then stays <= 256, which fp32 and bf16 carry
 // exactly as well as values <= 1.  The final O / l is the same function.
 // Every exponential runs on the MUFU (ex2.approx.f32).  Measured alternatives
-// that were slower at config 2: an FMA-pipe polynomial for a quarter of them
-// (exp2_poly2; the dense FP32 stream starves the MMA issuer of issue slots --
-// kPolyCols keeps the option, at 0) and paired f16 exponentials (exp2_f16x2;
-// the widening conversions share the MUFU pipe).
+// that were slower at config 2: an FMA-pipe polynomial for an eighth or a
+// quarter of them (exp2_poly2; kPolyCols keeps the option, at 0) and paired
+// f16 exponentials (exp2_f16x2; the widening conversions share the MUFU pipe).
 //
 // Keys: a tile whose keys are all masked is skipped outright (its weight is
 // exactly zero); partial tiles and the ragged tail get -inf logits per
@@ -80,7 +81,7 @@ struct Smem {
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
   static constexpr uint32_t kOffQ0 = 0, kOffQ1 = kTile, kOffK0 = 2 * kTile, kOffK1 = 3 * kTile,
                             kOffV0 = 4 * kTile, kOffV1 = 5 * kTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full, p_half[2]
   static constexpr uint32_t kOffBar = 6 * kTile;
   static constexpr uint32_t kOffCtl = kOffBar + 16 * 8;  // tmem slot, abort, n_tiles
   static constexpr uint32_t kOffTiles = kOffCtl + 16;    // uint16 [kMaxKvTiles]
@@ -100,14 +101,17 @@ __device__ __forceinline__ void issue_s(uint32_t tS, SDesc qd, SDesc kd) {
   }
 }
 
-// O (+)= P V for one tile: 8 MMAs of K = 16 keys; P from TMEM (8 columns per
-// k-step), V MN-major (16 keys = 16 rows of 128 B; d-chunks kChunkBytes apart).
+// O (+)= P V for one half of a tile (keys 64*half .. 64*half+63): 4 MMAs of
+// K = 16 keys; P from TMEM (8 columns per k-step), V MN-major (16 keys = 16
+// rows of 128 B; d-chunks kChunkBytes apart).
 template <int D>
-__device__ __forceinline__ void issue_pv(uint32_t tO, uint32_t tP, SDesc vd, bool accumulate) {
+__device__ __forceinline__ void issue_pv_half(uint32_t tO, uint32_t tP, SDesc vd, bool accumulate, int half) {
   constexpr uint32_t idesc = idesc_bf16_f32(128, D, 0, 1);
 #pragma unroll
-  for (int kk = 0; kk < kTileN / 16; ++kk)
+  for (int k4 = 0; k4 < 4; ++k4) {
+    const int kk = half * 4 + k4;
     umma_ts2(tO, tP + kk * 8, vd.lo + ((kk * 16 * 128) >> 4), vd.hi, idesc, (accumulate || kk > 0) ? 1u : 0u);
+  }
 }
 
 template <int D>
@@ -128,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   uint64_t* bar_s = bars + 9;    // [2] per Q tile
   uint64_t* bar_p = bars + 11;   // [2] per Q tile
   uint64_t* bar_o = bars + 13;
+  uint64_t* bar_ph = bars + 14;  // [2] first half of P_t (keys 0-63) stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
@@ -146,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 
   // ---------------- prologue ----------------
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 14; ++i) mbar_init(bars + i, (i == 11 || i == 12) ? 128 : 1);
+    for (int i = 0; i < 16; ++i) mbar_init(bars + i, (i == 11 || i == 12 || i >= 14) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -267,10 +272,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
           const int st = j & 1, u = j >> 1;
           const bool more = j + 1 < n;
           const int st1 = (j + 1) & 1, u1 = (j + 1) >> 1;
-          if (!mbar_wait(bar_p + 0, j & 1, abort_flag, p.err, 5)) break;
+          if (!mbar_wait(bar_ph + 0, j & 1, abort_flag, p.err, 5)) break;
           if (!mbar_wait(bar_vf + st, u & 1, abort_flag, p.err, 6)) break;
           tc_fence_after();
-          issue_pv<D>(tO0, tS0, vdesc(st), j > 0);
+          issue_pv_half<D>(tO0, tS0, vdesc(st), j > 0, 0);
+          if (!mbar_wait(bar_p + 0, j & 1, abort_flag, p.err, 5)) break;
+          tc_fence_after();
+          issue_pv_half<D>(tO0, tS0, vdesc(st), true, 1);
           if (more) {
             if (!mbar_wait(bar_kf + st1, u1 & 1, abort_flag, p.err, 7)) break;
             tc_fence_after();
@@ -278,9 +286,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
             umma_commit(bar_s + 0);
           }
           if (two) {
+            if (!mbar_wait(bar_ph + 1, j & 1, abort_flag, p.err, 8)) break;
+            tc_fence_after();
+            issue_pv_half<D>(tO1, tS1, vdesc(st), j > 0, 0);
             if (!mbar_wait(bar_p + 1, j & 1, abort_flag, p.err, 8)) break;
             tc_fence_after();
-            issue_pv<D>(tO1, tS1, vdesc(st), j > 0);
+            issue_pv_half<D>(tO1, tS1, vdesc(st), true, 1);
           }
           umma_commit(bar_ve + st);
           if (more) {
@@ -381,37 +392,37 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       const float2 sl2x2 = make_float2(sl2, sl2), nmx2 = make_float2(neg_m, neg_m);
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < 128; c += 2) {
-        const float2 x = fma2(make_float2(s[c], s[c + 1]), sl2x2, nmx2);
-        float2 e;
-        if (((c >> 1) & 7) < kPolyCols / 16) {
-          e = exp2_poly2(x);
-          if (masked_tile) {  // the polynomial leaves <= 2^-126 for -inf; masked weights are exactly 0
-            e.x = (s[c] == -INFINITY) ? 0.f : e.x;
-            e.y = (s[c + 1] == -INFINITY) ? 0.f : e.y;
+      for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+        for (int c = 64 * h2; c < 64 * h2 + 64; c += 2) {
+          const float2 x = fma2(make_float2(s[c], s[c + 1]), sl2x2, nmx2);
+          float2 e;
+          if (((c >> 1) & 7) < kPolyCols / 16) {
+            e = exp2_poly2(x);
+            if (masked_tile) {  // the polynomial leaves <= 2^-126 for -inf; masked weights are exactly 0
+              e.x = (s[c] == -INFINITY) ? 0.f : e.x;
+              e.y = (s[c + 1] == -INFINITY) ? 0.f : e.y;
+            }
+          } else {
+            e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
           }
-        } else {
-          e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          s[c] = e.x;
+          s[c + 1] = e.y;
+          acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], e);
         }
-        s[c] = e.x;
-        s[c + 1] = e.y;
-        acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], e);
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
+        tmem_st32(tS + 32 * h2, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(h2 == 0 ? bar_ph + t : my_p);
       }
       {
         const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
         const float2 tot = add2(a01, a23);
         l += tot.x + tot.y;
       }
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
-        tmem_st32(tS + 32 * h2, pk);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(my_p);
     }
 
     // epilogue
