@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    tma_prefetch_desc(&p.tm_o);
   }
 
   // key-mask bits (padded with zero words to a whole tile)
@@ -431,8 +432,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
     const int B = gridDim.z, Hc = gridDim.y;
     if (p.num_splits == 1) {
-      __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)(p.head_begin + hl) * p.o_sh +
-                            (int64_t)row * p.o_st;
+      // Stage the normalised bf16 row in K stage t (idle once O is complete: every
+      // MMA has finished and no load is outstanding), 128-byte swizzled like the
+      // loads, then one thread per tile stores it with TMA (coalesced; rows past
+      // Lq are clipped by the tensor map).
+      uint8_t* stg = sK + t * S::kTile;
+      const int r = threadIdx.x & 127;
+      uint8_t* srow = stg + r * 128;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -443,19 +449,29 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
-        if (row < p.Lq) {
-          uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            pk[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+        for (int e = 0; e < 4; ++e) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv_l, __uint_as_float(o[8 * e + 1]) * inv_l);
+          v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
+          v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
+          v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
+          const int j = (c & 1) * 4 + e;  // 16-byte unit within the 64-column chunk c / 2
+          *reinterpret_cast<uint4*>(srow + (c >> 1) * kChunkBytes + ((j ^ (r & 7)) << 4)) = v;
         }
       }
       if (p.lse != nullptr && row < p.Lq) {
         p.lse[(int64_t)b * p.lse_sb + (int64_t)(p.head_begin + hl) * p.lse_sh + row] =
             (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+      }
+      fence_proxy_async_smem();  // the bulk copy reads these rows through the async proxy
+      named_barrier(1 + t, 128);
+      if (r == 0) {
+#pragma unroll
+        for (int ch = 0; ch < S::kChunks; ++ch)
+          tma_store_4d(&p.tm_o, stg + ch * kChunkBytes, ch * 64, q0 + t * kTileM, p.head_begin + hl, b);
+        bulk_commit();
+        bulk_wait_read();  // the CTA's shared memory must outlive the copy's reads
       }
     } else {
       const int64_t prow = (((int64_t)split * B + b) * Hc + hl) * p.Lq + row;

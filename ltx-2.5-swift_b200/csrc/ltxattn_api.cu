@@ -393,6 +393,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     if (!aligned16(vptr)) return fail(LTXATTN_ERR_ALIGN, "v head block is not 16-byte aligned");
   }
   if ((rc = make_tmap(&p.tm_v, vptr, s.D, s.Lk, vH, s.B, v.stride_t, v.stride_h, v.stride_b, "v"))) return rc;
+  if ((rc = make_tmap(&p.tm_o, a->out.data, s.D, s.Lq, s.H, s.B, a->out.stride_t, a->out.stride_h,
+                      a->out.stride_b, "out")))
+    return rc;
   p.out = static_cast<__nv_bfloat16*>(a->out.data);
   p.o_sb = a->out.stride_b;
   p.o_sh = a->out.stride_h;
