@@ -166,6 +166,30 @@ LTXATTN_API int ltxattn_bwd(const ltxattn_bwd_args* args, void* stream);
 /* Device scratch bytes ltxattn_bwd needs for these arguments. */
 LTXATTN_API size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* args);
 
+/* ---- split RoPE on its own ------------------------------------------------ */
+
+/* Arguments of ltxattn_rope: out = split-RoPE(x, rotary).
+ *  - dtype, batch, heads, tokens, head_dim: the shape of x and out.
+ *  - x, out: [B, H, T, D] views; out may be x itself (in place) but must not
+ *    otherwise overlap it.
+ *  - rotary: the table pair, [1|B, 1|H, >= tokens, D/2] in the activation dtype. */
+typedef struct ltxattn_rope_args {
+  int32_t dtype;
+  int32_t batch;
+  int32_t heads;
+  int32_t tokens;
+  int32_t head_dim;
+  ltxattn_tensor x;
+  ltxattn_tensor out;
+  ltxattn_rotary rotary;
+} ltxattn_rope_args;
+
+/* Replaces `applySplitRoPE` (`DiTAttention.swift:206-234`) for a caller that
+ * rotates a tensor outside the attention call (ltxattn_fwd rotates q and k
+ * itself).  bf16: every product and every sum rounds to bf16, as for a bf16
+ * MLX tensor times a bf16 table. */
+LTXATTN_API int ltxattn_rope(const ltxattn_rope_args* args, void* stream);
+
 /* ---- head-parallel all-gather (NCCL over NVLink) ------------------------- */
 
 /* Opaque NCCL communicator owned by the library. */

@@ -249,7 +249,10 @@ RopeParams rope_params(const ltxattn_tensor& x, const ltxattn_rotary& r, const S
   p.t_sb = r.stride_b;
   p.t_sh = r.stride_h;
   p.t_st = r.stride_t;
-  p.y = y;
+  p.y = y;  // contiguous [B][Hc][T][D]
+  p.y_st = s.D;
+  p.y_sh = (int64_t)T * s.D;
+  p.y_sb = (int64_t)s.Hc * T * s.D;
   p.B = s.B;
   p.Hc = s.Hc;
   p.T = T;
@@ -445,6 +448,23 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
   return LTXATTN_OK;
+}
+
+int ltxattn_rope(const ltxattn_rope_args* a, void* stream) {
+  if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
+  Shape s;
+  int rc = check_shape(a->dtype, a->batch, a->heads, a->tokens, a->tokens, a->head_dim, 0, 0, &s);
+  if (rc) return rc;
+  if (a->rotary.cos == nullptr) return fail(LTXATTN_ERR_ARG, "rotary.cos is NULL");
+  if ((rc = check_rotary(a->rotary, "rotary", s.Lq))) return rc;
+  if ((rc = check_tensor(a->x, "x", s, false))) return rc;
+  if ((rc = check_tensor(a->out, "out", s, false))) return rc;
+  RopeParams p = rope_params(a->x, a->rotary, s, s.Lq, a->out.data);
+  p.y_sb = a->out.stride_b;
+  p.y_sh = a->out.stride_h;
+  p.y_st = a->out.stride_t;
+  const cudaError_t e = launch_rope(&p, nullptr, s.dtype == LTXATTN_BF16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "rope launch");
 }
 
 size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* a) {

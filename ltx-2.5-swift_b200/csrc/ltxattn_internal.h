@@ -72,7 +72,8 @@ struct RopeParams {
   const void* cos;
   const void* sin;
   int64_t t_sb, t_sh, t_st;
-  void* y;  // contiguous [B][Hc][T][D]
+  void* y;  // [B][Hc][T][D] view, local head index
+  int64_t y_sb, y_sh, y_st;
   int B, Hc, T, D, head_begin;
 };
 

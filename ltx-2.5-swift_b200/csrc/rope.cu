@@ -4,16 +4,19 @@
 //
 // bf16: every product and sum is rounded to bf16, the arithmetic of a bf16
 // MLX tensor times a bf16 table (the tables are narrowed to the activation
-// dtype first, :231-232).  Each op is evaluated in fp32 and rounded once, so
-// no product is fused into the following add.
+// dtype first, :231-232).  The vector path uses the bf16x2 instructions
+// (rope_bf16x8); the scalar path evaluates each op in fp32 and rounds once;
+// both give the same bits.  No product is fused into the following add.
 // fp32: the same four products and two sums in fp32, unfused.
 //
-// Reads a strided [B, H, T, D] view, writes a contiguous [B, Hc, T, D] buffer
-// (the library's workspace).  One launch rotates q and k together (two jobs).
-// Each thread handles 8 rotary pairs; when every address of a job is 16-byte
-// aligned the pairs move as one 16-byte load/store per operand (bf16), else
-// element by element.
+// Reads a strided [B, H, T, D] view, writes a [B, Hc, T, D] view (the
+// library's workspace, or the caller's output for ltxattn_rope; in place is
+// allowed: each thread reads both halves of its pairs before writing them).
+// One launch can rotate two tensors (q and k).  Each thread handles 8 rotary
+// pairs; when every address of a job is 16-byte aligned the pairs move as one
+// 16-byte load/store per operand (bf16), else element by element.
 #include "ltxattn_internal.h"
+#include "sm100.cuh"
 
 namespace ltx {
 namespace {
@@ -58,24 +61,10 @@ __device__ __forceinline__ void rope_vec_job(const RopeParams& p, int b) {
   const uint4 vx2 = __ldg(reinterpret_cast<const uint4*>(x + half));
   const uint4 vc = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.cos) + toff));
   const uint4 vs = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.sin) + toff));
-  const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&vx1);
-  const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&vx2);
-  const __nv_bfloat162* cc = reinterpret_cast<const __nv_bfloat162*>(&vc);
-  const __nv_bfloat162* ss = reinterpret_cast<const __nv_bfloat162*>(&vs);
   uint4 o1v, o2v;
-  __nv_bfloat162* o1 = reinterpret_cast<__nv_bfloat162*>(&o1v);
-  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o2v);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 a1 = __bfloat1622float2(x1[e]), a2 = __bfloat1622float2(x2[e]);
-    const float2 c = __bfloat1622float2(cc[e]), s = __bfloat1622float2(ss[e]);
-    float r1x, r2x, r1y, r2y;
-    rot(a1.x, a2.x, c.x, s.x, true, r1x, r2x);
-    rot(a1.y, a2.y, c.y, s.y, true, r1y, r2y);
-    o1[e] = __floats2bfloat162_rn(r1x, r1y);
-    o2[e] = __floats2bfloat162_rn(r2x, r2y);
-  }
-  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y) + (((int64_t)b * p.Hc + hl) * p.T + t) * p.D + g * 8;
+  rope_bf16x8(vx1, vx2, vc, vs, o1v, o2v);
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y) + (int64_t)b * p.y_sb + (int64_t)hl * p.y_sh +
+                     (int64_t)t * p.y_st + g * 8;
   *reinterpret_cast<uint4*>(y) = o1v;
   *reinterpret_cast<uint4*>(y + half) = o2v;
 }
@@ -115,7 +104,7 @@ __device__ __forceinline__ void rope_scalar_job(const RopeParams& p, int b) {
   const T* x = static_cast<const T*>(p.x) + (int64_t)b * p.x_sb + (int64_t)h * p.x_sh + (int64_t)t * p.x_st;
   const T* c = static_cast<const T*>(p.cos) + (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st;
   const T* s = static_cast<const T*>(p.sin) + (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st;
-  T* y = static_cast<T*>(p.y) + (((int64_t)b * p.Hc + hl) * p.T + t) * p.D;
+  T* y = static_cast<T*>(p.y) + (int64_t)b * p.y_sb + (int64_t)hl * p.y_sh + (int64_t)t * p.y_st;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int i = g * 8 + e;
@@ -139,7 +128,7 @@ bool vec_ok(const RopeParams& p) {
   auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   auto m8 = [](int64_t s) { return (s % 8) == 0; };
   return al(p.x) && al(p.cos) && al(p.sin) && al(p.y) && m8(p.x_sb) && m8(p.x_sh) && m8(p.x_st) && m8(p.t_sb) &&
-         m8(p.t_sh) && m8(p.t_st);
+         m8(p.t_sh) && m8(p.t_st) && m8(p.y_sb) && m8(p.y_sh) && m8(p.y_st);
 }
 
 }  // namespace

@@ -465,6 +465,45 @@ __device__ __forceinline__ float2 exp2_f16x2(float2 x) {
 }
 
 // ---------------------------------------------------------------------------
+// Split RoPE on 8 rotary pairs held as bf16x8 vectors (x1 = first half, x2 =
+// second half of the rows, c / s the table entries):
+//     o1 = x1*c - x2*s ,  o2 = x2*c + x1*s
+// with every product and every sum rounded to bf16 (round to nearest even),
+// the arithmetic of a bf16 tensor times a bf16 table (DiTAttention.swift:226-234).
+// The native bf16x2 instructions round the exact result once.  That equals
+// "evaluate in fp32, round to bf16": a product of two bf16 values is exact in
+// fp32, and the fp32 sum of two bf16 values is either exact or (operands 2^16
+// apart or more) too far from any bf16 rounding midpoint for the second
+// rounding to differ.  tests/test_rope_gpu.py checks it bit for bit against
+// the oracle.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ void rope_bf16x8(const uint4& x1, const uint4& x2, const uint4& c, const uint4& s,
+                                           uint4& o1, uint4& o2) {
+  o1.x = bsub2(bmul2(x1.x, c.x), bmul2(x2.x, s.x));
+  o1.y = bsub2(bmul2(x1.y, c.y), bmul2(x2.y, s.y));
+  o1.z = bsub2(bmul2(x1.z, c.z), bmul2(x2.z, s.z));
+  o1.w = bsub2(bmul2(x1.w, c.w), bmul2(x2.w, s.w));
+  o2.x = badd2(bmul2(x2.x, c.x), bmul2(x1.x, s.x));
+  o2.y = badd2(bmul2(x2.y, c.y), bmul2(x1.y, s.y));
+  o2.z = badd2(bmul2(x2.z, c.z), bmul2(x1.z, s.z));
+  o2.w = badd2(bmul2(x2.w, c.w), bmul2(x1.w, s.w));
+}
+
+// ---------------------------------------------------------------------------
 // small numeric helpers
 
 __device__ __forceinline__ float fast_exp2(float x) {

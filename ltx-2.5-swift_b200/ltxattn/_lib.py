@@ -23,6 +23,7 @@ F32, BF16 = 0, 1
 
 EXPORTED = (
     "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
+    "ltxattn_rope",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
@@ -50,6 +51,12 @@ class FwdArgs(ctypes.Structure):
                 ("lse", ctypes.c_void_p), ("lse_stride_b", ctypes.c_int64),
                 ("lse_stride_h", ctypes.c_int64), ("workspace", ctypes.c_void_p),
                 ("workspace_bytes", ctypes.c_size_t), ("num_splits", ctypes.c_int32)]
+
+
+class RopeArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("x", Tensor), ("out", Tensor), ("rotary", Rotary)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -105,6 +112,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_bwd.restype = ctypes.c_int
     L.ltxattn_bwd_workspace.argtypes = [ctypes.POINTER(BwdArgs)]
     L.ltxattn_bwd_workspace.restype = ctypes.c_size_t
+    L.ltxattn_rope.argtypes = [ctypes.POINTER(RopeArgs), vp]
+    L.ltxattn_rope.restype = ctypes.c_int
     L.ltxattn_comm_unique_id.argtypes = [ctypes.POINTER(ctypes.c_uint8)]
     L.ltxattn_comm_unique_id.restype = ctypes.c_int
     L.ltxattn_comm_init.argtypes = [ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32,

@@ -309,6 +309,34 @@ def scaled_dot_product_attention(queries: torch.Tensor, keys: torch.Tensor, valu
     return out
 
 
+def apply_split_rope(x: torch.Tensor, rotary: Rotary, out: Optional[torch.Tensor] = None,
+                     stream=None) -> torch.Tensor:
+    """``applySplitRoPE(x, rotary)`` (DiTAttention.swift:206-234) through ``ltxattn_rope``.
+
+    ``x`` is a ``[B, heads, tokens, D]`` CUDA view; ``out`` defaults to a new
+    tensor and may be ``x`` itself (rotation in place).  In bf16 every product
+    and sum rounds to bf16.
+    """
+    _check_cuda("x", x)
+    if x.dim() != 4:
+        raise Failure.shape("x", x.shape, "[B, heads, tokens, headDim]")
+    B, H, T, D = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    a = _lib.RopeArgs()
+    a.dtype = _dtype_code(x)
+    if out.dtype != x.dtype:
+        raise Failure("dtype", "out must have the dtype of x", _lib.ERR_DTYPE)
+    a.batch, a.heads, a.tokens, a.head_dim = B, H, T, D
+    a.x = _view("x", x, (B, H, T, D))
+    a.out = _view("out", out, (B, H, T, D))
+    a.rotary = _rotary("rotary", rotary, B, H, T, D, x.dtype)
+    rc = _lib.load().ltxattn_rope(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out
+
+
 def device_status(clear: bool = True) -> int:
     """Status of the current device's kernel error word (synchronises)."""
     site = ctypes.c_int32(0)

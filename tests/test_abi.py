@@ -48,12 +48,14 @@ int main(void) {
   printf("ltxattn_bwd_args %zu\n", sizeof(ltxattn_bwd_args));
   printf("ltxattn_gather_args %zu\n", sizeof(ltxattn_gather_args));
   printf("ltxattn_device_info %zu\n", sizeof(ltxattn_device_info));
+  printf("ltxattn_rope_args %zu\n", sizeof(ltxattn_rope_args));
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
   P(ltxattn_bwd_args, dout) P(ltxattn_bwd_args, lse) P(ltxattn_bwd_args, dq) P(ltxattn_bwd_args, scale)
   P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
   P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
+  P(ltxattn_rope_args, x) P(ltxattn_rope_args, out) P(ltxattn_rope_args, rotary)
   return 0;
 }
 """
@@ -68,11 +70,12 @@ def test_ctypes_layout_matches_the_header(tmp_path):
                                                          check=True).stdout.splitlines())
     sizes = {"ltxattn_tensor": _lib.Tensor, "ltxattn_rotary": _lib.Rotary, "ltxattn_fwd_args": _lib.FwdArgs,
              "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
-             "ltxattn_device_info": _lib.DeviceInfo}
+             "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
-               "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo}
+               "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
+               "ltxattn_rope_args": _lib.RopeArgs}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")
