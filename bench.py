@@ -45,6 +45,17 @@ WORKLOADS = {
 L2_BYTES = 126 * 1024 * 1024
 
 
+# the roofline that bounds each workload's attention kernel (BASELINE/SURVEY arithmetic
+# intensity against the ~250 FLOP/B ridge of the measured peaks)
+BOUND = {"c2": "tensor", "c3": "hbm", "c4a": "hbm", "c4b": "hbm", "c4c": "hbm", "c5": "tensor"}
+
+
+def algorithmic_bytes(wl, B, H, Lq, Lk, D):
+    """Bytes one attention launch must move: Q and O, plus K and V of the valid keys (bf16)."""
+    valid = WORKLOADS[wl][6] or Lk
+    return 2 * (2 * B * H * Lq * D + 2 * B * H * valid * D)
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -283,6 +294,7 @@ def run_ours(args):
     kern_avg_ms = kern_total / args.steps
     burst, sustained, hbm, src = peaks()
     achieved = flops / (kern_avg_ms * 1e-3) / 1e12  # per GPU, one launch of the dominant kernel
+    kern_gbs = algorithmic_bytes(wl, B, Hc, Lq, Lk, D) / (kern_avg_ms * 1e-3) / 1e9
     result = None
     if rank == 0:
         cpu = None
@@ -308,10 +320,18 @@ def run_ours(args):
                        "l2": "flushed (256 MB write) before every timed step; flush outside the timed events",
                        "flops_per_step_per_gpu": flops, "effective_flops_per_step_per_gpu": eff_flops},
             "pct_of_datasheet_dense_bf16": round(100.0 * value / ws / 2250.0, 2),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": burst, "unit": "TFLOP/s",
-                         "frac": round(achieved / burst, 4), "peak_source": f"{src} bf16_tflops (burst)",
-                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5),
-                         "traffic": None},
+            "value_effective_flops": round(eff_flops * ws / (ms_per_step * 1e-3) / 1e12, 3),
+            "roofline": ({"bound": "tensor", "achieved": round(achieved, 2), "peak": burst, "unit": "TFLOP/s",
+                          "frac": round(achieved / burst, 4), "peak_source": f"{src} bf16_tflops (burst)"}
+                         if BOUND[wl] == "tensor" else
+                         {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": hbm, "unit": "GB/s",
+                          "frac": round(kern_gbs / hbm, 4), "peak_source": f"{src} hbm_gbs",
+                          "algorithmic_bytes": algorithmic_bytes(wl, B, Hc, Lq, Lk, D),
+                          "kernel_tflops": round(achieved, 2)}) | {
+                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5), "traffic": None},
+            "step_ms": {"median": round(statistics.median(step_ms), 5), "min": round(min(step_ms), 5),
+                        "max": round(max(step_ms), 5),
+                        "spread": round((max(step_ms) - min(step_ms)) / statistics.median(step_ms), 4)},
             "e2e": {"value": round(ranks_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,

@@ -150,6 +150,35 @@ int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
 }
 
 // ---------------------------------------------------------------------------
+// Split count for a launch of at least one wave.  The CTAs run in whole waves
+// of sm_count; when the last wave is thin, splitting each query block's KV
+// range s ways (s <= 4) can shorten the job: predicted time =
+//   ceil(ctas * s / sms) * (kv_tiles / s * t_tile + t_cta)  +  combine(s)
+// with t_tile ~ 1.8 us per 128-key step of a two-tile CTA, t_cta ~ 8 us of
+// per-CTA prologue and epilogue, and combine(s) moving s fp32 partials of O
+// (written and read back) at ~5 TB/s.  A split must keep >= 8 KV tiles per CTA
+// and the cheapest choice must beat no split by 3%.  (At 29,760 tokens and 4
+// heads per GPU this picks 3; at 8 or more heads it picks 1.)
+int wave_balanced_splits(int64_t ctas, int sms, int kv_tiles, double out_elems) {
+  constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBytesPerUs = 5.0e6;
+  auto cost = [&](int sp) {
+    const double waves = (double)((ctas * sp + sms - 1) / sms);
+    const double combine = sp > 1 ? 2.0 * sp * out_elems * 4.0 / kBytesPerUs : 0.0;
+    return waves * ((double)kv_tiles / sp * kTileUs + kCtaUs) + combine;
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int sp = 2; sp <= 4 && kv_tiles / sp >= 8; ++sp) {
+    const double c = cost(sp);
+    if (c < best_cost) {
+      best = sp;
+      best_cost = c;
+    }
+  }
+  return best_cost < 0.97 * cost(1) ? best : 1;
+}
+
+// ---------------------------------------------------------------------------
 // forward plan: workspace layout and split count (identical for the
 // workspace query and the call)
 
@@ -186,6 +215,8 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
       if (ctas < sms && P->kv_tiles > 1) {
         const int want = (int)((2 * (int64_t)sms + ctas - 1) / ctas);
         P->splits = std::max(1, std::min({want, P->kv_tiles, kMaxSplits}));
+      } else if (ctas >= sms) {
+        P->splits = wave_balanced_splits(ctas, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
       }
     } else {
       return fail(LTXATTN_ERR_ARG, "num_splits %d is negative", a->num_splits);

@@ -265,3 +265,52 @@ def test_determinism_bitwise():
     a, la = AttentionBackend.attention(qd, kd, vd, save_lse=True)
     b, lb = AttentionBackend.attention(qd, kd, vd, save_lse=True)
     assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.float32, 64), (torch.bfloat16, 128), (torch.bfloat16, 64)])
+def test_uniform_attention_is_mean_of_v(dtype, D):
+    # q = k = constant: every logit of a row is equal, so O is the mean of the valid V rows
+    B, H, L = 1, 2, 300
+    q = torch.full((B, H, L, D), 0.25, device="cuda", dtype=dtype)
+    v = torch.from_numpy(inputs.seeded_tensor(31, (B, H, L, D), bf16=dtype == torch.bfloat16)).to("cuda", dtype)
+    out, _ = AttentionBackend.attention(q, q, v, 1.0 / np.sqrt(D))
+    want = v.double().mean(dim=2, keepdim=True).expand(B, H, L, D)
+    check(out, want.cpu().numpy(), dtype, "uniform attention")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_one_hot_key_returns_its_value_row(dtype):
+    # key 77 aligns with every query and carries a logit ~60 above all others:
+    # its softmax weight is 1 to within e^-60, so every output row is V[77]
+    B, H, Lq, Lk, D = 1, 2, 130, 200, 64
+    g = torch.Generator(device="cpu").manual_seed(3)
+    q = torch.zeros((B, H, Lq, D))
+    q[..., 0] = 8.0
+    k = torch.randn((B, H, Lk, D), generator=g) * 0.01
+    k[:, :, 77, 0] = 60.0
+    v = torch.randn((B, H, Lk, D), generator=g)
+    qd, kd, vd = (t.to("cuda", dtype) for t in (q, k, v))
+    out, _ = AttentionBackend.attention(qd, kd, vd, 1.0 / 8.0)
+    want = vd[:, :, 77:78, :].double().expand(B, H, Lq, D)
+    check(out, want.cpu().numpy(), dtype, "one-hot key")
+
+
+@pytest.mark.parametrize("dtype,mask", [(torch.bfloat16, False), (torch.bfloat16, True), (torch.float32, True)])
+def test_lse_is_log_sum_exp_of_the_logits(dtype, mask):
+    # the saved LSE against log(sum_j exp(scale * q.k_j)) over valid keys, computed here in fp64
+    B, H, Lq, Lk, D = 2, 2, 260, 390, 64
+    q, k, v = make(41, B, H, Lq, Lk, D, dtype)
+    qd, kd, vd = dev(q, dtype), dev(k, dtype), dev(v, dtype)
+    m = None
+    valid = torch.ones((B, Lk), dtype=torch.bool)
+    if mask:
+        valid[0, 100:] = False
+        valid[1, ::3] = False
+        m = valid.to("cuda")
+    scale = 1.0 / np.sqrt(D)
+    _, lse = AttentionBackend.attention(qd, kd, vd, scale, key_mask=m, save_lse=True)
+    logits = torch.einsum("bhqd,bhkd->bhqk", qd.double().cpu(), kd.double().cpu()) * scale
+    logits = logits.masked_fill(~valid[:, None, None, :], float("-inf"))
+    want = torch.logsumexp(logits, dim=-1)
+    err = (lse.double().cpu() - want).abs().max().item()
+    assert err <= LSE_ABS, f"lse max abs error {err:.3e}"
