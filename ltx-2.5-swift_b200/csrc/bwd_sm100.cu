@@ -14,7 +14,10 @@
 // bit-identical, as gradient checkpointing expects):
 //   bwd_prep_kernel   Delta and lse*log2(e) per query row, padded to 128 rows
 //   bwd_dq_kernel     Q-stationary: per 128-row Q tile, loop over KV tiles;
-//                     TMEM: S [0,128), dP [128,256), dQ [256,256+D)
+//                     TMEM: S [0,128), dP [128,256), dQ [256,256+D),
+//                     Q [384,384+D/2), dO [448,448+D/2) (bf16 pairs: the
+//                     A operands of S = Q K^T and dP = dO V^T come from TMEM,
+//                     so those MMAs read only K or V from shared memory)
 //   bwd_dkdv_kernel   KV-stationary: per 128-key tile, loop over Q tiles;
 //                     TMEM: S^T [0,128), dP^T [128,256), dV [256,..), dK [384,..)
 // In both, the softmax warps turn S/dP into bf16 P or dS in place (TMEM) and
@@ -29,7 +32,12 @@
 namespace ltx {
 namespace {
 
-constexpr int kThreads = 192;
+// warps 0-7: softmax (warp w reads TMEM lane quadrant w % 4; warps w and w + 4
+// share a quadrant and take the two halves of its columns), warp 8: TMA
+// producer, warp 9: TMEM owner and MMA issuer
+constexpr int kThreads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr uint32_t kChunkBytes = 128u * 128u;
 
 __device__ __forceinline__ float to_f32(float x) { return x; }
@@ -139,8 +147,8 @@ struct DqSmem {
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
   static constexpr uint32_t kOffQ = 0, kOffDO = kTile, kOffK0 = 2 * kTile, kOffV0 = 3 * kTile,
                             kOffK1 = 4 * kTile, kOffV1 = 5 * kTile;
-  static constexpr uint32_t kOffBar = 6 * kTile;  // q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full
-  static constexpr uint32_t kOffCtl = kOffBar + 8 * 8;
+  static constexpr uint32_t kOffBar = 6 * kTile;  // q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full, qt_ready, p_half
+  static constexpr uint32_t kOffCtl = kOffBar + 10 * 8;
   static constexpr uint32_t kOffTiles = kOffCtl + 16;
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;
 };
@@ -152,8 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   uint8_t* sm = align1024(smem_raw);
   uint8_t* sQ = sm + S::kOffQ;
   uint8_t* sDO = sm + S::kOffDO;
-  uint8_t* sK[2] = {sm + S::kOffK0, sm + S::kOffK1};
-  uint8_t* sV[2] = {sm + S::kOffV0, sm + S::kOffV1};
+  // stage st of K / V lives at sK0 / sV0 + st * 2 * kTile (K and V stages interleave)
+  uint8_t* sK0 = sm + S::kOffK0;
+  uint8_t* sV0 = sm + S::kOffV0;
+  static_assert(S::kOffK1 == S::kOffK0 + 2 * S::kTile && S::kOffV1 == S::kOffV0 + 2 * S::kTile, "stage stride");
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_kvf = bars + 1;  // [2]
@@ -161,6 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   uint64_t* bar_s = bars + 5;
   uint64_t* bar_p = bars + 6;
   uint64_t* bar_o = bars + 7;
+  uint64_t* bar_qt = bars + 8;  // Q and dO rows copied into TMEM
+  uint64_t* bar_ph = bars + 9;  // dS for keys 0-63 stored (warps 0-3); bar_p: keys 64-127 (warps 4-7)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
@@ -171,11 +183,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   const int q0 = blockIdx.x * kTileM, hl = blockIdx.y, b = blockIdx.z;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(bars + i, i == 6 ? 128 : 1);
+    // p_full / p_half: the 128 threads of warps 4-7 / 0-3; qt_ready: all 256 softmax threads
+    for (int i = 0; i < 10; ++i) mbar_init(bars + i, i == 8 ? 256 : ((i == 6 || i == 9) ? 128 : 1));
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
     tc_fence_before();
@@ -198,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   const uint32_t tmem = *tmem_slot;
   const int n = *n_tiles_slot;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0 && n > 0) {
       int issued = 0;
       mbar_arrive_expect_tx(bar_q, 2 * S::kTile);
@@ -214,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
         mbar_arrive_expect_tx(bar_kvf + st, 2 * S::kTile);
 #pragma unroll
         for (int c = 0; c < S::kChunks; ++c) {
-          tma_load_4d(&p.tm_k, bar_kvf + st, sK[st] + c * kChunkBytes, c * 64, kv0, hl, b);
-          tma_load_4d(&p.tm_v, bar_kvf + st, sV[st] + c * kChunkBytes, c * 64, kv0, hl, b);
+          tma_load_4d(&p.tm_k, bar_kvf + st, sK0 + st * 2 * S::kTile + c * kChunkBytes, c * 64, kv0, hl, b);
+          tma_load_4d(&p.tm_v, bar_kvf + st, sV0 + st * 2 * S::kTile + c * kChunkBytes, c * 64, kv0, hl, b);
         }
         ++issued;
       }
@@ -223,37 +236,42 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
       for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i) drain_wait(bar_kvf + (i & 1), (i >> 1) & 1);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0 && n > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_dq = idesc_bf16_f32(128, D, 0, 1);
-      const uint32_t tS = tmem, tP = tmem + 128, tQ = tmem + 256;
-      // base descriptors built once; per MMA only the low word moves
-      const SDesc dQd = sdesc_split(smem_u32(sQ), 16, 1024), dOd = sdesc_split(smem_u32(sDO), 16, 1024);
-      if (mbar_wait(bar_q, 0, abort_flag, p.err, 22)) {
+      const uint32_t tS = tmem, tP = tmem + 128, tQ = tmem + 256, tQa = tmem + 384, tOa = tmem + 448;
+      if (mbar_wait(bar_qt, 0, abort_flag, p.err, 22)) {
         for (int i = 0; i < n; ++i) {
           const int st = i & 1;
           if (!mbar_wait(bar_kvf + st, (i >> 1) & 1, abort_flag, p.err, 23)) break;
           tc_fence_after();
-          const SDesc dKd = sdesc_split(smem_u32(sK[0]) + st * 2 * S::kTile, 16, 1024);
-          const SDesc dVd = sdesc_split(smem_u32(sV[0]) + st * 2 * S::kTile, 16, 1024);
-          const SDesc dKmn = sdesc_split(smem_u32(sK[0]) + st * 2 * S::kTile, kChunkBytes, 1024);
+          const SDesc dKd = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, 16, 1024);
+          const SDesc dVd = sdesc_split(smem_u32(sV0) + st * 2 * S::kTile, 16, 1024);
+          const SDesc dKmn = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, kChunkBytes, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ss2(tS, dQd.lo + off, dQd.hi, dKd.lo + off, dKd.hi, idesc_s, kk > 0);
+            umma_ts2(tS, tQa + kk * 8, dKd.lo + off, dKd.hi, idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ss2(tP, dOd.lo + off, dOd.hi, dVd.lo + off, dVd.hi, idesc_s, kk > 0);
+            umma_ts2(tP, tOa + kk * 8, dVd.lo + off, dVd.hi, idesc_s, kk > 0);
           }
           umma_commit(bar_s);
+          // dQ += dS K in two halves of 64 keys: the first runs while softmax
+          // finishes the second half of dS
+          if (!mbar_wait(bar_ph, i & 1, abort_flag, p.err, 28)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 32; ++kk)
+            umma_ts2(tQ, tS + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
           if (!mbar_wait(bar_p, i & 1, abort_flag, p.err, 24)) break;
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kTileN / 16; ++kk)
-            umma_ts2(tQ, tS + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = kTileN / 32; kk < kTileN / 16; ++kk)  // keys 64-127: dS at S columns [64, 96)
+            umma_ts2(tQ, tS + 32 + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, 1u);
           umma_commit(bar_kve + st);
         }
       }
@@ -262,20 +280,51 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
     }
     __syncwarp();
   } else {
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int quad = warp & 3, half = warp >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem + lane_off, tP = tmem + 128 + lane_off, tQ = tmem + 256 + lane_off;
-    const int row = q0 + threadIdx.x;
+    const int r = quad * 32 + lane;  // row of the tile = TMEM lane
+    const int row = q0 + r;
     const int64_t rix = ((int64_t)b * gridDim.y + hl) * p.Lq_pad + row;
     const float lse2 = p.lse2[rix];
     const float delta = p.delta[rix];
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int i = 0; i < n; ++i) {
+    if (n > 0) {
+      // Q (warps 0-3) and dO (warps 4-7) rows into TMEM as bf16 pairs, the A
+      // operands of S and dP: each thread copies its row out of the
+      // 128-byte-swizzled tile
+      ok = warp_wait(bar_q, 0, abort_flag, p.err, 27);
+      if (ok) {
+        const uint8_t* rowp = (half == 0 ? sQ : sDO) + r * 128;
+        const uint32_t dst = tmem + (half == 0 ? 384u : 448u) + lane_off;
+#pragma unroll
+        for (int c = 0; c < S::kChunks; ++c) {
+          uint32_t v[32];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 x = *reinterpret_cast<const uint4*>(rowp + c * kChunkBytes + ((j ^ (r & 7)) << 4));
+            v[4 * j] = x.x;
+            v[4 * j + 1] = x.y;
+            v[4 * j + 2] = x.z;
+            v[4 * j + 3] = x.w;
+          }
+          tmem_st32(dst + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(bar_qt);
+    }
+    // dS = P o (dP - Delta) for keys [64 * half, 64 * half + 64) of each tile;
+    // the half published first feeds the first half of dQ += dS K
+    for (int i = 0; i < n && ok; ++i) {
       if (!warp_wait(bar_s, i & 1, abort_flag, p.err, 25)) { ok = false; break; }
       tc_fence_after();
       const int kv0 = (int)tiles[i] * kTileN;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;
         uint32_t rs[32], rp[32];
         tmem_ld32(tS + c * 32, rs);
         tmem_ld32(tP + c * 32, rp);
@@ -288,33 +337,37 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
           const float p1 = ((bits >> (2 * e + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(rs[2 * e + 1]), sl2, -lse2)) : 0.f;
           pk[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - delta), p1 * (__uint_as_float(rp[2 * e + 1]) - delta));
         }
-        tmem_st16(tS + c * 16, pk);
+        // bf16 dS of keys [64h, 64h+64) packs into S columns [64h, 64h+32): each
+        // half overwrites only columns it has already read
+        tmem_st16(tS + half * 64 + cc * 16, pk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p);
+      mbar_arrive(half == 0 ? bar_ph : bar_p);
     }
-    const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
-    tc_fence_after();
-    float g[D];
-    if (have) {
-      tmem_row<D>(tQ, g);
-    } else {
+    if (half == 0) {
+      const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
+      tc_fence_after();
+      float g[D];
+      if (have) {
+        tmem_row<D>(tQ, g);
+      } else {
 #pragma unroll
-      for (int e = 0; e < D; ++e) g[e] = 0.f;
-    }
-    if (row < p.Lq) {
+        for (int e = 0; e < D; ++e) g[e] = 0.f;
+      }
+      if (row < p.Lq) {
 #pragma unroll
-      for (int e = 0; e < D; ++e) g[e] *= p.scale;
-      if (p.qcos != nullptr)
-        rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.qcos) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
-                            static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
-      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
+        for (int e = 0; e < D; ++e) g[e] *= p.scale;
+        if (p.qcos != nullptr)
+          rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.qcos) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
+                              static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
+        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -330,8 +383,8 @@ struct DkvSmem {
   static constexpr uint32_t kOffK = 0, kOffV = kTile, kOffQ0 = 2 * kTile, kOffDO0 = 3 * kTile,
                             kOffQ1 = 4 * kTile, kOffDO1 = 5 * kTile;
   static constexpr uint32_t kOffL = 6 * kTile;  // lse2[2][128], delta[2][128]
-  static constexpr uint32_t kOffBar = kOffL + 4 * 128 * 4;  // kv_full, q_full[2], q_empty[2], s_full, p_full, o_full
-  static constexpr uint32_t kOffCtl = kOffBar + 8 * 8;
+  static constexpr uint32_t kOffBar = kOffL + 4 * 128 * 4;  // kv_full, q_full[2], q_empty[2], s_full, p_full, o_full, p_half
+  static constexpr uint32_t kOffCtl = kOffBar + 10 * 8;
   static constexpr uint32_t kOffBits = kOffCtl + 16;
 };
 
@@ -342,8 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   uint8_t* sm = align1024(smem_raw);
   uint8_t* sK = sm + S::kOffK;
   uint8_t* sV = sm + S::kOffV;
-  uint8_t* sQ[2] = {sm + S::kOffQ0, sm + S::kOffQ1};
-  uint8_t* sDO[2] = {sm + S::kOffDO0, sm + S::kOffDO1};
+  // stage st of Q / dO lives at sQ0 / sDO0 + st * 2 * kTile
+  uint8_t* sQ0 = sm + S::kOffQ0;
+  uint8_t* sDO0 = sm + S::kOffDO0;
+  static_assert(S::kOffQ1 == S::kOffQ0 + 2 * S::kTile && S::kOffDO1 == S::kOffDO0 + 2 * S::kTile, "stage stride");
   float* sL = reinterpret_cast<float*>(sm + S::kOffL);  // lse2: sL[st*128 + q]; delta: sL[256 + st*128 + q]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* bar_kv = bars + 0;
@@ -352,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   uint64_t* bar_s = bars + 5;
   uint64_t* bar_p = bars + 6;
   uint64_t* bar_o = bars + 7;
+  uint64_t* bar_ph = bars + 8;  // P^T, dS^T for queries 0-63 stored (warps 0-3); bar_p: 64-127 (warps 4-7)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   uint32_t* mbits = reinterpret_cast<uint32_t*>(sm + S::kOffBits);
@@ -361,11 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   const int nq = p.n_q_tiles;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(bars + i, i == 6 ? 128 : 1);
+    for (int i = 0; i < 9; ++i) mbar_init(bars + i, (i == 6 || i == 8) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
     tc_fence_before();
@@ -383,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   const int n = (use_mask && tile_bits == 0) ? 0 : nq;
   const int64_t lrow = ((int64_t)b * gridDim.y + hl) * p.Lq_pad;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0 && n > 0) {
       int issued = 0;
       mbar_arrive_expect_tx(bar_kv, 2 * S::kTile);
@@ -399,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
         mbar_arrive_expect_tx(bar_qf + st, 2 * S::kTile + 2 * 128 * 4);
 #pragma unroll
         for (int c = 0; c < S::kChunks; ++c) {
-          tma_load_4d(&p.tm_q, bar_qf + st, sQ[st] + c * kChunkBytes, c * 64, q0, hl, b);
-          tma_load_4d(&p.tm_do, bar_qf + st, sDO[st] + c * kChunkBytes, c * 64, q0, hl, b);
+          tma_load_4d(&p.tm_q, bar_qf + st, sQ0 + st * 2 * S::kTile + c * kChunkBytes, c * 64, q0, hl, b);
+          tma_load_4d(&p.tm_do, bar_qf + st, sDO0 + st * 2 * S::kTile + c * kChunkBytes, c * 64, q0, hl, b);
         }
         bulk_load(sL + st * 128, p.lse2 + lrow + q0, 128 * 4, bar_qf + st);
         bulk_load(sL + 256 + st * 128, p.delta + lrow + q0, 128 * 4, bar_qf + st);
@@ -410,18 +466,19 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) drain_wait(bar_qf + (j & 1), (j >> 1) & 1);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0 && n > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_g = idesc_bf16_f32(128, D, 0, 1);
       const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 384;
       const SDesc dKd = sdesc_split(smem_u32(sK), 16, 1024), dVd = sdesc_split(smem_u32(sV), 16, 1024);
+      bool fail = false;
       if (mbar_wait(bar_kv, 0, abort_flag, p.err, 32)) {
         for (int j = 0; j < n; ++j) {
           const int st = j & 1;
           if (!mbar_wait(bar_qf + st, (j >> 1) & 1, abort_flag, p.err, 33)) break;
           tc_fence_after();
-          const uint32_t aQ = smem_u32(sQ[0]) + st * 2 * S::kTile, aDO = smem_u32(sDO[0]) + st * 2 * S::kTile;
+          const uint32_t aQ = smem_u32(sQ0) + st * 2 * S::kTile, aDO = smem_u32(sDO0) + st * 2 * S::kTile;
           const SDesc dQd = sdesc_split(aQ, 16, 1024), dOd = sdesc_split(aDO, 16, 1024);
           const SDesc dQmn = sdesc_split(aQ, kChunkBytes, 1024), dOmn = sdesc_split(aDO, kChunkBytes, 1024);
 #pragma unroll
@@ -435,14 +492,24 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
             umma_ss2(tP, dVd.lo + off, dVd.hi, dOd.lo + off, dOd.hi, idesc_s, kk > 0);
           }
           umma_commit(bar_s);
-          if (!mbar_wait(bar_p, j & 1, abort_flag, p.err, 34)) break;
-          tc_fence_after();
+          // dV += P^T dO and dK += dS^T Q in two halves of 64 queries: the first
+          // runs while softmax finishes the second half
 #pragma unroll
-          for (int kk = 0; kk < kTileM / 16; ++kk)
-            umma_ts2(tV, tS + kk * 8, dOmn.lo + ((kk * 16 * 128) >> 4), dOmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+            if (!mbar_wait(h == 0 ? bar_ph : bar_p, j & 1, abort_flag, p.err, 34)) { fail = true; break; }
+            tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kTileM / 16; ++kk)
-            umma_ts2(tK, tP + kk * 8, dQmn.lo + ((kk * 16 * 128) >> 4), dQmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int k4 = 0; k4 < kTileM / 32; ++k4) {
+              const int kk = h * (kTileM / 32) + k4;  // queries 16kk..; half h packed at columns 64h + 8 k4
+              umma_ts2(tV, tS + h * 64 + k4 * 8, dOmn.lo + ((kk * 16 * 128) >> 4), dOmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+#pragma unroll
+            for (int k4 = 0; k4 < kTileM / 32; ++k4) {
+              const int kk = h * (kTileM / 32) + k4;
+              umma_ts2(tK, tP + h * 64 + k4 * 8, dQmn.lo + ((kk * 16 * 128) >> 4), dQmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          if (fail) break;
           umma_commit(bar_qe + st);
         }
       }
@@ -451,10 +518,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
     }
     __syncwarp();
   } else {
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int quad = warp & 3, half = warp >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem + lane_off, tP = tmem + 128 + lane_off;
     const uint32_t tV = tmem + 256 + lane_off, tK = tmem + 384 + lane_off;
-    const int key = kv0 + threadIdx.x;
+    const int key = kv0 + quad * 32 + lane;  // key of the tile = TMEM lane
     bool kvalid = key < p.Lk;
     if (use_mask && kvalid) kvalid = (mbits[key / 32] >> (key % 32)) & 1u;
     const float sl2 = p.scale_log2;
@@ -468,7 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       const float* L2 = sL + st * 128;
       const float* DL = sL + 256 + st * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;  // queries [64 * half, 64 * half + 64)
         uint32_t rs[32], rp[32];
         tmem_ld32(tS + c * 32, rs);
         tmem_ld32(tP + c * 32, rp);
@@ -482,39 +551,40 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
           pp[e] = pack_bf16x2(p0, p1);
           pd[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - DL[q]), p1 * (__uint_as_float(rp[2 * e + 1]) - DL[q + 1]));
         }
-        tmem_st16(tS + c * 16, pp);
-        tmem_st16(tP + c * 16, pd);
+        // bf16 P^T / dS^T of queries [64h, 64h+64) pack into columns [64h, 64h+32):
+        // each half overwrites only columns it has already read
+        tmem_st16(tS + half * 64 + cc * 16, pp);
+        tmem_st16(tP + half * 64 + cc * 16, pd);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p);
+      mbar_arrive(half == 0 ? bar_ph : bar_p);  // queries 0-63 feed the first half of dV and dK
     }
     const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 37);
     tc_fence_after();
     float g[D];
     if (have) {
-      tmem_row<D>(tV, g);
+      tmem_row<D>(half == 0 ? tV : tK, g);
     } else {
 #pragma unroll
       for (int e = 0; e < D; ++e) g[e] = 0.f;
     }
-    if (key < p.Lk)
-      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
-    if (have) {
-      tmem_row<D>(tK, g);
-    }
     if (key < p.Lk) {
+      if (half == 0) {
+        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
+      } else {
 #pragma unroll
-      for (int e = 0; e < D; ++e) g[e] *= p.scale;
-      if (p.kcos != nullptr)
-        rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.kcos) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
-                            static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
-      store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
+        for (int e = 0; e < D; ++e) g[e] *= p.scale;
+        if (p.kcos != nullptr)
+          rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.kcos) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
+                              static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
+        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
