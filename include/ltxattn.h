@@ -190,6 +190,36 @@ typedef struct ltxattn_rope_args {
  * MLX tensor times a bf16 table. */
 LTXATTN_API int ltxattn_rope(const ltxattn_rope_args* args, void* stream);
 
+/* ---- rotary tables -------------------------------------------------------- */
+
+/* Arguments of ltxattn_rotary_tables: the per-head split-RoPE tables of one
+ * stream (DiTForward.rotary).
+ *  - dtype: of the tables (LTXATTN_BF16 for a bf16 model: the reference narrows
+ *    its fp32 tables to the activation dtype at use).
+ *  - n_pos (1..4), tokens: positions is a device array [n_pos][tokens][2] of
+ *    fp32 (lo, hi) bounds per positional dimension (videoPositions /
+ *    audioPositions, or IC-LoRA reference positions).
+ *  - max_pos[d]: the normaliser of dimension d; theta: the frequency base.
+ *  - inner, heads: the attention's inner width and head count; the tables are
+ *    [heads, tokens, inner / 2 / heads] (cos and sin, device memory). */
+typedef struct ltxattn_rotary_table_args {
+  int32_t dtype;
+  int32_t n_pos;
+  int32_t tokens;
+  int32_t inner;
+  int32_t heads;
+  double theta;
+  float max_pos[4];
+  const float* positions;
+  void* cos;
+  void* sin;
+} ltxattn_rotary_table_args;
+
+/* Replaces `DiTForward.rotary` (`DiTForward.swift:641-678`, with frequencyGrid
+ * `:455-466`): fp64 frequency grid, fp32 angles, leading identity pairs,
+ * positional dimension fastest, split per head. */
+LTXATTN_API int ltxattn_rotary_tables(const ltxattn_rotary_table_args* args, void* stream);
+
 /* ---- head-parallel all-gather (NCCL over NVLink) ------------------------- */
 
 /* Opaque NCCL communicator owned by the library. */

@@ -481,6 +481,36 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   return LTXATTN_OK;
 }
 
+int ltxattn_rotary_tables(const ltxattn_rotary_table_args* a, void* stream) {
+  if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
+  if (a->dtype != LTXATTN_F32 && a->dtype != LTXATTN_BF16)
+    return fail(LTXATTN_ERR_DTYPE, "dtype %d is neither LTXATTN_F32 nor LTXATTN_BF16", a->dtype);
+  if (a->n_pos < 1 || a->n_pos > 4) return fail(LTXATTN_ERR_SHAPE, "n_pos %d is outside 1..4", a->n_pos);
+  if (a->tokens < 0 || a->heads <= 0 || a->inner <= 0 || a->inner % (2 * a->heads))
+    return fail(LTXATTN_ERR_SHAPE, "inner %d does not split into %d heads of rotary pairs", a->inner, a->heads);
+  const int count = a->inner / (2 * a->n_pos);
+  if (count < 2) return fail(LTXATTN_ERR_SHAPE, "inner %d gives fewer than 2 frequencies per dimension", a->inner);
+  if (!(a->theta > 0.0)) return fail(LTXATTN_ERR_ARG, "theta must be positive");
+  for (int d = 0; d < a->n_pos; ++d)
+    if (!(a->max_pos[d] != 0.0f)) return fail(LTXATTN_ERR_ARG, "max_pos[%d] is zero", d);
+  if (a->tokens > 0 && (a->positions == nullptr || a->cos == nullptr || a->sin == nullptr))
+    return fail(LTXATTN_ERR_ARG, "positions, cos and sin must be device pointers");
+  RotaryTableParams p{};
+  p.positions = a->positions;
+  p.cos = a->cos;
+  p.sin = a->sin;
+  p.theta = a->theta;
+  for (int d = 0; d < 4; ++d) p.max_pos[d] = d < a->n_pos ? a->max_pos[d] : 1.0f;
+  p.n_pos = a->n_pos;
+  p.tokens = a->tokens;
+  p.inner = a->inner;
+  p.heads = a->heads;
+  p.count = count;
+  p.pad = a->inner / 2 - count * a->n_pos;
+  const cudaError_t e = launch_rotary_tables(p, a->dtype == LTXATTN_BF16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "rotary tables launch");
+}
+
 int ltxattn_rope(const ltxattn_rope_args* a, void* stream) {
   if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
   Shape s;

@@ -77,6 +77,17 @@ struct RopeParams {
   int B, Hc, T, D, head_begin;
 };
 
+// Rotary tables (DiTForward.rotary): see rotary.cu.
+struct RotaryTableParams {
+  const float* positions;  // [n_pos][tokens][2] fp32 (lo, hi)
+  void* cos;               // [heads][tokens][inner/2/heads], activation dtype
+  void* sin;
+  double theta;
+  float max_pos[4];
+  int n_pos, tokens, inner, heads, count, pad;
+};
+cudaError_t launch_rotary_tables(const RotaryTableParams& p, bool bf16, cudaStream_t s);
+
 struct CombineParams {
   const float* part_o;
   const float* part_lse;

@@ -23,7 +23,7 @@ F32, BF16 = 0, 1
 
 EXPORTED = (
     "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
-    "ltxattn_rope",
+    "ltxattn_rope", "ltxattn_rotary_tables",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
@@ -57,6 +57,13 @@ class RopeArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32),
                 ("x", Tensor), ("out", Tensor), ("rotary", Rotary)]
+
+
+class RotaryTableArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("n_pos", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("inner", ctypes.c_int32), ("heads", ctypes.c_int32), ("theta", ctypes.c_double),
+                ("max_pos", ctypes.c_float * 4), ("positions", ctypes.c_void_p), ("cos", ctypes.c_void_p),
+                ("sin", ctypes.c_void_p)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -114,6 +121,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_bwd_workspace.restype = ctypes.c_size_t
     L.ltxattn_rope.argtypes = [ctypes.POINTER(RopeArgs), vp]
     L.ltxattn_rope.restype = ctypes.c_int
+    L.ltxattn_rotary_tables.argtypes = [ctypes.POINTER(RotaryTableArgs), vp]
+    L.ltxattn_rotary_tables.restype = ctypes.c_int
     L.ltxattn_comm_unique_id.argtypes = [ctypes.POINTER(ctypes.c_uint8)]
     L.ltxattn_comm_unique_id.restype = ctypes.c_int
     L.ltxattn_comm_init.argtypes = [ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32,

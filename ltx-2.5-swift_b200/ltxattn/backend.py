@@ -337,6 +337,33 @@ def apply_split_rope(x: torch.Tensor, rotary: Rotary, out: Optional[torch.Tensor
     return out
 
 
+def rotary_tables(positions: torch.Tensor, max_pos, inner: int, heads: int, theta: float = 10000.0,
+                  dtype=torch.bfloat16, stream=None) -> Rotary:
+    """``DiTForward.rotary`` (DiTForward.swift:641-678) on the device through ``ltxattn_rotary_tables``.
+
+    ``positions`` is a CUDA float32 tensor ``[n_pos, tokens, 2]`` of (lo, hi)
+    bounds; returns per-head tables ``[1, heads, tokens, inner/2/heads]``.
+    """
+    _check_cuda("positions", positions)
+    if positions.dtype != torch.float32 or positions.dim() != 3 or positions.shape[2] != 2:
+        raise Failure.shape("positions", positions.shape, "[n_pos, tokens, 2] float32")
+    positions = positions.contiguous()
+    n_pos, tokens, _ = positions.shape
+    per = inner // 2 // heads if heads > 0 else 0
+    cos = torch.empty((1, heads, tokens, per), dtype=dtype, device=positions.device)
+    sin = torch.empty_like(cos)
+    a = _lib.RotaryTableArgs()
+    a.dtype = _dtype_code(cos)
+    a.n_pos, a.tokens, a.inner, a.heads, a.theta = n_pos, tokens, inner, heads, float(theta)
+    for d, v in enumerate(list(max_pos)[:4]):
+        a.max_pos[d] = float(v)
+    a.positions, a.cos, a.sin = positions.data_ptr(), cos.data_ptr(), sin.data_ptr()
+    rc = _lib.load().ltxattn_rotary_tables(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return Rotary(cos, sin)
+
+
 def device_status(clear: bool = True) -> int:
     """Status of the current device's kernel error word (synchronises)."""
     site = ctypes.c_int32(0)

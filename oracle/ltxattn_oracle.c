@@ -119,6 +119,52 @@ int oracle_rope(float* x, const float* cosv, const float* sinv,
     return 0;
 }
 
+/* Rotary tables, DiTForward.rotary (DiTForward.swift:641-678) with
+ * frequencyGrid (:455-466):
+ *   freq[i] = (float)(theta^(i/(count-1)) * pi/2), count = inner/(2*n_pos),
+ *             the exponent and power in fp64 (the last exponent is exactly 1);
+ *   middle  = (lo + hi) / 2 and frac = middle / max_pos[d], fp32;
+ *   angle   = freq[i] * (frac*2 - 1), fp32, positional dimension fastest
+ *             (column i*n_pos + d), after `pad` leading identity pairs
+ *             (cos 1, sin 0) that fill inner/2;
+ *   cos/sin in fp32, split per head: out[h][t][c] = table[t][h*per + c].
+ * positions: [n_pos][tokens][2] (lo, hi).  Outputs [heads][tokens][per]. */
+int oracle_rotary_tables(const float* positions, const float* max_pos, int n_pos, int tokens,
+                         int inner, int heads, double theta, float* cos_out, float* sin_out) {
+    const int count = inner / (2 * n_pos);
+    const int half = inner / 2;
+    const int pad = half - count * n_pos;
+    const int per = half / heads;
+    if (count < 2 || pad < 0 || half % heads) return 1;
+    float* freq = (float*)malloc(sizeof(float) * (size_t)count);
+    if (!freq) return 2;
+    const double step = 1.0 / (double)(count - 1);
+    for (int i = 0; i < count; ++i) {
+        const double e = (i == count - 1) ? 1.0 : (double)i * step;
+        freq[i] = (float)(pow(theta, e) * 3.14159265358979323846 / 2.0);
+    }
+    for (int t = 0; t < tokens; ++t) {
+        for (int j = 0; j < half; ++j) {
+            float c = 1.0f, sn = 0.0f;
+            if (j >= pad) {
+                const int k = j - pad, i = k / n_pos, d = k % n_pos;
+                const float lo = positions[((int64_t)d * tokens + t) * 2];
+                const float hi = positions[((int64_t)d * tokens + t) * 2 + 1];
+                const float middle = (lo + hi) / 2.0f;
+                const float frac = middle / max_pos[d];
+                const float ang = freq[i] * (frac * 2.0f - 1.0f);
+                c = cosf(ang);
+                sn = sinf(ang);
+            }
+            const int64_t o = ((int64_t)(j / per) * tokens + t) * per + (j % per);
+            cos_out[o] = c;
+            sin_out[o] = sn;
+        }
+    }
+    free(freq);
+    return 0;
+}
+
 /* Transpose of the rotation, for gradients w.r.t. the un-rotated input
  * (the VJP treats the bf16 roundings as identity, as autodiff does). */
 int oracle_rope_bwd(float* dx, const float* cosv, const float* sinv,

@@ -49,8 +49,9 @@ def lib():
             ctypes.c_int] * 5 + [ctypes.c_float, _f32p, _f32p, ctypes.c_int]
         L.oracle_attn_bwd.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64, _f32p] + [
             ctypes.c_int] * 5 + [ctypes.c_double, _f32p, _f32p, _f32p, ctypes.c_int]
+        L.oracle_rotary_tables.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_double, _f32p, _f32p]
         for f in ("oracle_rope", "oracle_rope_bwd", "oracle_attn_fwd",
-                  "oracle_attn_fwd_f32", "oracle_attn_bwd"):
+                  "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables"):
             getattr(L, f).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -177,3 +178,16 @@ def attention_reference(q, k, v, mask=None, q_rot=None, k_rot=None, bf16=False, 
 
 if __name__ == "__main__":  # pragma: no cover
     print(build())
+
+
+def rotary_tables(positions: np.ndarray, max_pos, inner: int, heads: int, theta: float = 10000.0):
+    """DiTForward.rotary restated in C: fp32 tables [1, heads, tokens, inner/2/heads]."""
+    pos = _f32(positions)
+    n_pos, tokens, _ = pos.shape
+    mp = np.asarray(max_pos, dtype=np.float32)
+    per = inner // 2 // heads
+    c = np.empty((heads, tokens, per), np.float32)
+    s = np.empty_like(c)
+    rc = lib().oracle_rotary_tables(_p(pos), _p(mp), n_pos, tokens, inner, heads, float(theta), _p(c), _p(s))
+    assert rc == 0
+    return c[None], s[None]

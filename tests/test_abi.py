@@ -49,6 +49,7 @@ int main(void) {
   printf("ltxattn_gather_args %zu\n", sizeof(ltxattn_gather_args));
   printf("ltxattn_device_info %zu\n", sizeof(ltxattn_device_info));
   printf("ltxattn_rope_args %zu\n", sizeof(ltxattn_rope_args));
+  printf("ltxattn_rotary_table_args %zu\n", sizeof(ltxattn_rotary_table_args));
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
@@ -56,6 +57,8 @@ int main(void) {
   P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
   P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
   P(ltxattn_rope_args, x) P(ltxattn_rope_args, out) P(ltxattn_rope_args, rotary)
+  P(ltxattn_rotary_table_args, theta) P(ltxattn_rotary_table_args, max_pos) P(ltxattn_rotary_table_args, positions)
+  P(ltxattn_rotary_table_args, sin)
   return 0;
 }
 """
@@ -70,12 +73,13 @@ def test_ctypes_layout_matches_the_header(tmp_path):
                                                          check=True).stdout.splitlines())
     sizes = {"ltxattn_tensor": _lib.Tensor, "ltxattn_rotary": _lib.Rotary, "ltxattn_fwd_args": _lib.FwdArgs,
              "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
-             "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs}
+             "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs,
+             "ltxattn_rotary_table_args": _lib.RotaryTableArgs}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
                "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
-               "ltxattn_rope_args": _lib.RopeArgs}
+               "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")

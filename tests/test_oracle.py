@@ -173,3 +173,16 @@ def test_backward_matches_finite_differences():
             args_m = [m if arr is x else x for x in (q, k, v)]
             fd = (loss(*args_p) - loss(*args_m)) / (2 * eps)
             assert abs(fd - g[idx]) < 2e-3, (idx, fd, g[idx])
+
+
+def test_rotary_tables_c_restatement_matches_the_numpy_one():
+    # DiTForward.rotary restated twice (C oracle, numpy helper): identical angle
+    # arithmetic; the two fp32 cos/sin implementations differ by at most 2 ulp
+    for pos, max_pos, inner, heads in ((inputs.video_positions(3, 4, 5), [20, 2048, 2048], 4096, 32),
+                                       (inputs.audio_positions(40), [20], 2048, 32)):
+        c, s = oracle.rotary_tables(pos, max_pos, inner, heads)
+        rc, rs = inputs.reference_rotary(pos, inner, max_pos, heads, bf16=False)
+        for a, b in ((c, rc), (s, rs)):
+            assert a.shape == b.shape
+            tol = 2 * np.spacing(np.abs(b).astype(np.float32))
+            assert (np.abs(a.astype(np.float64) - b) <= tol).all()
