@@ -147,6 +147,104 @@ def make_inputs(wl, rank, Hc, B, Lq, Lk, D):
     return q, k, v, tabs, mask
 
 
+def run_qkprep(args):
+    """q and k preparation (ltxattn_qk_prep: rmsNorm over the inner dim, head split,
+    split RoPE) at the config-2 shape; GB/s against the HBM roofline."""
+    import torch
+    import torch.distributed as dist
+    from ltxattn import Rotary, qk_prep
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from ltxattn import inputs
+    B, H, T, D = 1, 32, 3120, 128
+    inner = H * D
+    seed = 1000 + 97 * rank
+    xs = [torch.from_numpy(inputs.seeded_tensor(seed + i, (B, T, inner))).to("cuda", torch.bfloat16) for i in (2, 3)]
+    w = torch.ones(inner, device="cuda", dtype=torch.bfloat16)
+    c, sn = inputs.rope3d_grid(13, 12, 20, D)
+    rot = Rotary(torch.from_numpy(c).to("cuda", torch.bfloat16), torch.from_numpy(sn).to("cuda", torch.bfloat16))
+    outs = [torch.empty((B, H, T, D), device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for x, o in zip(xs, outs):
+            qk_prep(x, w, H, rot, eps=1e-6, out=o, stream=stream)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    clocks.start()
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    # end to end: host rows in, host heads out
+    hx = [x.cpu().pin_memory() for x in xs]
+    ho = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        for x, h in zip(xs, hx):
+            x.copy_(h, non_blocking=True)
+        step()
+        for o, h in zip(outs, ho):
+            h.copy_(o, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    vals = torch.tensor([sum(step_ms), e2e_ms], device="cuda", dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = vals.tolist()
+    ms = total_ms / args.steps
+    # algorithmic bytes per step: x in, heads out, the shared tables (cos and sin) once per tensor
+    per_tensor = 2 * B * T * inner * 2 + 2 * T * (D // 2) * 2 + inner * 2
+    step_bytes = 2 * per_tensor
+    gbs = step_bytes * ws / (ms * 1e-3) / 1e9
+    _, _, hbm, src = peaks()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "q/k prep GB/s (rmsNorm over 4096 + head split + 3D RoPE) @3120 tok (aggregate over GPUs)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1), unit norm weight, bf16)",
+            "config": {"workload": "qkprep: q and k of config 2, [1, 3120, 4096] -> [1, 32, 3120, 128]",
+                       "parallelism": f"heads x{ws}", "l2": "flushed (256 MB write) before every timed step"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / ws / hbm, 4), "peak_source": f"{src} hbm_gbs",
+                         "algorithmic_bytes": step_bytes, "kernel": "qk_prep_kernel", "traffic": None},
+            "step_ms": {"median": round(statistics.median(step_ms), 5), "min": round(min(step_ms), 5),
+                        "max": round(max(step_ms), 5)},
+            "e2e": {"value": round(step_bytes * ws / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(h.numel() * 2 for h in hx),
+                    "d2h_bytes_per_step": sum(h.numel() * 2 for h in ho)},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -416,14 +514,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + ["qkprep"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--bwd", action="store_true", help="also time the training backward")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.workload == "qkprep":
+        res = (run_reference(args) if args.impl == "reference" else run_qkprep(args)) \
+            if args.impl != "reference" else {"impl": "reference", "unavailable": "no CPU arm for the qkprep workload"}
+    else:
+        res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
         print(json.dumps(res), flush=True)
 

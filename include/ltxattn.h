@@ -190,6 +190,37 @@ typedef struct ltxattn_rope_args {
  * MLX tensor times a bf16 table. */
 LTXATTN_API int ltxattn_rope(const ltxattn_rope_args* args, void* stream);
 
+/* ---- query / key preparation ---------------------------------------------- */
+
+/* Arguments of ltxattn_qk_prep: out = split-RoPE(split(rmsNorm(x, weight))).
+ *  - dtype, batch, tokens, heads, head_dim: x is [B, tokens, heads * head_dim]
+ *    (the projection output, unit stride along the inner dim), out the
+ *    [B, heads, tokens, head_dim] view the attention consumes.
+ *  - x_stride_b, x_stride_t: element strides of x.
+ *  - weight: the norm weight [heads * head_dim] (activation dtype); eps its epsilon.
+ *  - rotary: per-head tables as for ltxattn_fwd, or cos = NULL for none (the
+ *    attention then gets q / k already rotated and is called without tables).
+ * heads * head_dim must be a multiple of 512 and at most 8192. */
+typedef struct ltxattn_qk_prep_args {
+  int32_t dtype;
+  int32_t batch;
+  int32_t tokens;
+  int32_t heads;
+  int32_t head_dim;
+  const void* x;
+  int64_t x_stride_b;
+  int64_t x_stride_t;
+  const void* weight;
+  float eps;
+  ltxattn_rotary rotary;
+  ltxattn_tensor out;
+} ltxattn_qk_prep_args;
+
+/* Replaces the query / key preparation of `DiTAttention.callAsFunction`
+ * (`DiTAttention.swift:358-367`): `rmsNorm` over the whole inner dim (`:190-204`),
+ * the head split (`:346-348`) and `applySplitRoPE` (`:206-234`), in one pass. */
+LTXATTN_API int ltxattn_qk_prep(const ltxattn_qk_prep_args* args, void* stream);
+
 /* ---- rotary tables -------------------------------------------------------- */
 
 /* Arguments of ltxattn_rotary_tables: the per-head split-RoPE tables of one

@@ -481,6 +481,48 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   return LTXATTN_OK;
 }
 
+int ltxattn_qk_prep(const ltxattn_qk_prep_args* a, void* stream) {
+  if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
+  Shape s;
+  int rc = check_shape(a->dtype, a->batch, a->heads, a->tokens, a->tokens, a->head_dim, 0, 0, &s);
+  if (rc) return rc;
+  const int inner = s.H * s.D;
+  if (inner % 512 != 0 || inner > 8192)
+    return fail(LTXATTN_ERR_UNSUPPORTED, "heads * head_dim = %d is not a multiple of 512 up to 8192", inner);
+  if (a->x == nullptr || a->weight == nullptr) return fail(LTXATTN_ERR_ARG, "x and weight must be device pointers");
+  if (a->x_stride_b < 0 || a->x_stride_t < 0) return fail(LTXATTN_ERR_SHAPE, "x has a negative stride");
+  if (!(a->eps >= 0.0f)) return fail(LTXATTN_ERR_ARG, "eps must be non-negative");
+  if ((rc = check_rotary(a->rotary, "rotary", s.Lq))) return rc;
+  if ((rc = check_tensor(a->out, "out", s, false))) return rc;
+  const bool bf16 = s.dtype == LTXATTN_BF16;
+  QkPrepParams p{};
+  p.x = a->x;
+  p.x_sb = a->x_stride_b;
+  p.x_st = a->x_stride_t;
+  p.w = a->weight;
+  p.eps = a->eps;
+  p.cos = a->rotary.cos;
+  p.sin = a->rotary.sin;
+  p.t_sb = a->rotary.stride_b;
+  p.t_sh = a->rotary.stride_h;
+  p.t_st = a->rotary.stride_t;
+  p.out = a->out.data;
+  p.o_sb = a->out.stride_b;
+  p.o_sh = a->out.stride_h;
+  p.o_st = a->out.stride_t;
+  p.B = s.B;
+  p.tokens = s.Lq;
+  p.inner = inner;
+  p.D = s.D;
+  auto m8 = [](int64_t v) { return v % 8 == 0; };
+  p.vec = bf16 && aligned16(a->x) && m8(a->x_stride_b) && m8(a->x_stride_t) && aligned16(a->weight) &&
+          aligned16(a->out.data) && m8(a->out.stride_b) && m8(a->out.stride_h) && m8(a->out.stride_t) &&
+          (a->rotary.cos == nullptr || (aligned16(a->rotary.cos) && aligned16(a->rotary.sin) &&
+                                        m8(a->rotary.stride_b) && m8(a->rotary.stride_h) && m8(a->rotary.stride_t)));
+  const cudaError_t e = launch_qk_prep(p, bf16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "qk_prep launch");
+}
+
 int ltxattn_rotary_tables(const ltxattn_rotary_table_args* a, void* stream) {
   if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
   if (a->dtype != LTXATTN_F32 && a->dtype != LTXATTN_BF16)

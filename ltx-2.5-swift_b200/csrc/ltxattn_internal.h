@@ -77,6 +77,22 @@ struct RopeParams {
   int B, Hc, T, D, head_begin;
 };
 
+// q / k preparation (rmsNorm over the inner dim, head split, split RoPE): see qkprep.cu.
+struct QkPrepParams {
+  const void* x;  // [B, tokens, inner] rows, unit stride along inner
+  int64_t x_sb, x_st;
+  const void* w;  // [inner] norm weight (activation dtype)
+  float eps;
+  const void* cos;  // per-head tables or null (no rotation)
+  const void* sin;
+  int64_t t_sb, t_sh, t_st;
+  void* out;  // [B, H, tokens, D] view
+  int64_t o_sb, o_sh, o_st;
+  int B, tokens, inner, D;
+  int vec;  // every row, table and output address is 16-byte aligned (bf16 vector path)
+};
+cudaError_t launch_qk_prep(const QkPrepParams& p, bool bf16, cudaStream_t s);
+
 // Rotary tables (DiTForward.rotary): see rotary.cu.
 struct RotaryTableParams {
   const float* positions;  // [n_pos][tokens][2] fp32 (lo, hi)

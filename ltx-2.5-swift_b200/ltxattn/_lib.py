@@ -23,7 +23,7 @@ F32, BF16 = 0, 1
 
 EXPORTED = (
     "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
-    "ltxattn_rope", "ltxattn_rotary_tables",
+    "ltxattn_rope", "ltxattn_rotary_tables", "ltxattn_qk_prep",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
@@ -64,6 +64,13 @@ class RotaryTableArgs(ctypes.Structure):
                 ("inner", ctypes.c_int32), ("heads", ctypes.c_int32), ("theta", ctypes.c_double),
                 ("max_pos", ctypes.c_float * 4), ("positions", ctypes.c_void_p), ("cos", ctypes.c_void_p),
                 ("sin", ctypes.c_void_p)]
+
+
+class QkPrepArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("x", ctypes.c_void_p),
+                ("x_stride_b", ctypes.c_int64), ("x_stride_t", ctypes.c_int64), ("weight", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("rotary", Rotary), ("out", Tensor)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -123,6 +130,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_rope.restype = ctypes.c_int
     L.ltxattn_rotary_tables.argtypes = [ctypes.POINTER(RotaryTableArgs), vp]
     L.ltxattn_rotary_tables.restype = ctypes.c_int
+    L.ltxattn_qk_prep.argtypes = [ctypes.POINTER(QkPrepArgs), vp]
+    L.ltxattn_qk_prep.restype = ctypes.c_int
     L.ltxattn_comm_unique_id.argtypes = [ctypes.POINTER(ctypes.c_uint8)]
     L.ltxattn_comm_unique_id.restype = ctypes.c_int
     L.ltxattn_comm_init.argtypes = [ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32,

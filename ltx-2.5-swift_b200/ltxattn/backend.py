@@ -364,6 +364,37 @@ def rotary_tables(positions: torch.Tensor, max_pos, inner: int, heads: int, thet
     return Rotary(cos, sin)
 
 
+def qk_prep(x: torch.Tensor, weight: torch.Tensor, heads: int, rotary: Optional[Rotary] = None,
+            eps: float = 1e-6, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """q / k preparation of ``DiTAttention`` (DiTAttention.swift:358-367) through ``ltxattn_qk_prep``.
+
+    ``x`` is the projection output ``[B, tokens, heads * D]`` (unit stride along
+    the last dim); returns ``split-RoPE(split(rmsNorm(x, weight)))`` as
+    ``[B, heads, tokens, D]`` (or into ``out``).
+    """
+    _check_cuda("x", x)
+    if x.dim() != 3 or x.stride(2) != 1 or x.shape[2] % heads:
+        raise Failure.shape("x", x.shape, f"[B, tokens, {heads} * headDim] with a unit last stride")
+    B, T, inner = x.shape
+    D = inner // heads
+    if out is None:
+        out = torch.empty((B, heads, T, D), dtype=x.dtype, device=x.device)
+    _check_cuda("weight", weight)
+    if weight.dtype != x.dtype or tuple(weight.shape) != (inner,) or not weight.is_contiguous():
+        raise Failure.shape("weight", weight.shape, f"[{inner}] contiguous, dtype {x.dtype}")
+    a = _lib.QkPrepArgs()
+    a.dtype = _dtype_code(x)
+    a.batch, a.tokens, a.heads, a.head_dim = B, T, heads, D
+    a.x, a.x_stride_b, a.x_stride_t = x.data_ptr(), x.stride(0), x.stride(1)
+    a.weight, a.eps = weight.data_ptr(), float(eps)
+    a.rotary = _rotary("rotary", rotary, B, heads, T, D, x.dtype)
+    a.out = _view("out", out, (B, heads, T, D))
+    rc = _lib.load().ltxattn_qk_prep(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out
+
+
 def device_status(clear: bool = True) -> int:
     """Status of the current device's kernel error word (synchronises)."""
     site = ctypes.c_int32(0)

@@ -119,6 +119,54 @@ int oracle_rope(float* x, const float* cosv, const float* sinv,
     return 0;
 }
 
+/* q / k preparation, DiTAttention.swift:358-367: rmsNorm over the whole inner
+ * dim (:190-204, MLX's kernel arithmetic: mean square, r = 1/sqrt(mean + eps),
+ * y = T(w * T(x * r))), the head split (:346-348) and split RoPE (:206-234).
+ * x: [B][T][H*D]; w: [H*D]; tables as oracle_rope ([Bt][Ht][T][D/2], cos NULL
+ * for none); out: [B][H][T][D].  The mean square accumulates in fp64 here
+ * (the device's fp32 tree sum may differ from it in the last ulp of r). */
+int oracle_qk_prep(const float* x, const float* w, int B, int T, int H, int D, float eps,
+                   const float* cosv, const float* sinv, int64_t tab_stride_b, int64_t tab_stride_h,
+                   int round_bf16, float* out) {
+    const int inner = H * D, half = D / 2;
+    for (int b = 0; b < B; ++b)
+    for (int t = 0; t < T; ++t) {
+        const float* xr = x + ((int64_t)b * T + t) * inner;
+        double ss = 0.0;
+        for (int i = 0; i < inner; ++i) ss += (double)xr[i] * (double)xr[i];
+        const float r = (float)(1.0 / sqrt((double)(float)(ss / inner) + (double)eps));
+        for (int h = 0; h < H; ++h) {
+            float* o = out + (((int64_t)b * H + h) * T + t) * D;
+            for (int d = 0; d < D; ++d) {
+                float n = xr[h * D + d] * r;
+                if (round_bf16) n = bf16_round(n);
+                float y = w[h * D + d] * n;
+                if (round_bf16) y = bf16_round(y);
+                o[d] = y;
+            }
+            if (cosv) {
+                const float* c = cosv + b * tab_stride_b + h * tab_stride_h + (int64_t)t * half;
+                const float* sn = sinv + b * tab_stride_b + h * tab_stride_h + (int64_t)t * half;
+                for (int i = 0; i < half; ++i) {
+                    const float x1 = o[i], x2 = o[i + half];
+                    float cc = c[i], ss2 = sn[i];
+                    if (round_bf16) {
+                        cc = bf16_round(cc); ss2 = bf16_round(ss2);
+                        const float a = bf16_round(x1 * cc), bb = bf16_round(x2 * ss2);
+                        const float e = bf16_round(x2 * cc), f = bf16_round(x1 * ss2);
+                        o[i] = bf16_round(a - bb);
+                        o[i + half] = bf16_round(e + f);
+                    } else {
+                        o[i] = x1 * cc - x2 * ss2;
+                        o[i + half] = x2 * cc + x1 * ss2;
+                    }
+                }
+            }
+        }
+    }
+    return 0;
+}
+
 /* Rotary tables, DiTForward.rotary (DiTForward.swift:641-678) with
  * frequencyGrid (:455-466):
  *   freq[i] = (float)(theta^(i/(count-1)) * pi/2), count = inner/(2*n_pos),

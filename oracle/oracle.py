@@ -50,8 +50,11 @@ def lib():
         L.oracle_attn_bwd.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64, _f32p] + [
             ctypes.c_int] * 5 + [ctypes.c_double, _f32p, _f32p, _f32p, ctypes.c_int]
         L.oracle_rotary_tables.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_double, _f32p, _f32p]
+        L.oracle_qk_prep.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, _f32p, _f32p,
+                                                                         ctypes.c_int64, ctypes.c_int64,
+                                                                         ctypes.c_int, _f32p]
         for f in ("oracle_rope", "oracle_rope_bwd", "oracle_attn_fwd",
-                  "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables"):
+                  "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables", "oracle_qk_prep"):
             getattr(L, f).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -191,3 +194,24 @@ def rotary_tables(positions: np.ndarray, max_pos, inner: int, heads: int, theta:
     rc = lib().oracle_rotary_tables(_p(pos), _p(mp), n_pos, tokens, inner, heads, float(theta), _p(c), _p(s))
     assert rc == 0
     return c[None], s[None]
+
+
+def qk_prep(x: np.ndarray, w: np.ndarray, heads: int, eps: float = 1e-6, cos=None, sin=None,
+            bf16: bool = True) -> np.ndarray:
+    """DiTAttention q/k preparation restated in C: rmsNorm over the inner dim, head
+    split, split RoPE.  x [B, T, inner] -> [B, heads, T, inner / heads]."""
+    xx = _f32(x)
+    B, T, inner = xx.shape
+    D = inner // heads
+    out = np.empty((B, heads, T, D), np.float32)
+    c = s = None
+    sb = sh = 0
+    if cos is not None:
+        c, s = _f32(cos), _f32(sin)
+        sb, sh = _table_strides(c, heads)
+    null = ctypes.POINTER(ctypes.c_float)()
+    rc = lib().oracle_qk_prep(_p(xx), _p(_f32(w)), B, T, heads, D, float(eps),
+                              _p(c) if c is not None else null, _p(s) if s is not None else null,
+                              sb, sh, int(bf16), _p(out))
+    assert rc == 0
+    return out

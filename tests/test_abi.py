@@ -50,6 +50,7 @@ int main(void) {
   printf("ltxattn_device_info %zu\n", sizeof(ltxattn_device_info));
   printf("ltxattn_rope_args %zu\n", sizeof(ltxattn_rope_args));
   printf("ltxattn_rotary_table_args %zu\n", sizeof(ltxattn_rotary_table_args));
+  printf("ltxattn_qk_prep_args %zu\n", sizeof(ltxattn_qk_prep_args));
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
@@ -59,6 +60,8 @@ int main(void) {
   P(ltxattn_rope_args, x) P(ltxattn_rope_args, out) P(ltxattn_rope_args, rotary)
   P(ltxattn_rotary_table_args, theta) P(ltxattn_rotary_table_args, max_pos) P(ltxattn_rotary_table_args, positions)
   P(ltxattn_rotary_table_args, sin)
+  P(ltxattn_qk_prep_args, x) P(ltxattn_qk_prep_args, weight) P(ltxattn_qk_prep_args, eps)
+  P(ltxattn_qk_prep_args, rotary) P(ltxattn_qk_prep_args, out)
   return 0;
 }
 """
@@ -74,12 +77,13 @@ def test_ctypes_layout_matches_the_header(tmp_path):
     sizes = {"ltxattn_tensor": _lib.Tensor, "ltxattn_rotary": _lib.Rotary, "ltxattn_fwd_args": _lib.FwdArgs,
              "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
              "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs,
-             "ltxattn_rotary_table_args": _lib.RotaryTableArgs}
+             "ltxattn_rotary_table_args": _lib.RotaryTableArgs, "ltxattn_qk_prep_args": _lib.QkPrepArgs}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
                "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
-               "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs}
+               "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs,
+               "ltxattn_qk_prep_args": _lib.QkPrepArgs}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")

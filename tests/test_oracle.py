@@ -186,3 +186,15 @@ def test_rotary_tables_c_restatement_matches_the_numpy_one():
             assert a.shape == b.shape
             tol = 2 * np.spacing(np.abs(b).astype(np.float32))
             assert (np.abs(a.astype(np.float64) - b) <= tol).all()
+
+
+def test_qk_prep_restatement():
+    # rmsNorm over the inner dim (mean square, r = 1/sqrt(mean + eps), y = T(w * T(x * r)))
+    # then the head split: the C oracle against the same formula in numpy
+    x = inputs.seeded_tensor(5, (2, 9, 512), bf16=True) * 2.0
+    w = inputs.round_bf16(np.random.default_rng(0).uniform(0.5, 1.5, 512).astype(np.float32))
+    got = oracle.qk_prep(x, w, 4, 1e-6)
+    ms = (x.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(np.float32).astype(np.float64)
+    r = (1.0 / np.sqrt(ms + np.float64(np.float32(1e-6)))).astype(np.float32)
+    y = inputs.round_bf16(w * inputs.round_bf16(x * r))
+    np.testing.assert_array_equal(got, y.reshape(2, 9, 4, 128).transpose(0, 2, 1, 3))
