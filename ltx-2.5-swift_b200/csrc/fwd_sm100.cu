@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
     tma_prefetch_desc(&p.tm_o);
+    if (p.num_splits > 1) tma_prefetch_desc(&p.tm_part);
   }
 
   // key-mask bits (padded with zero words to a whole tile)
@@ -474,8 +475,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         bulk_wait_read();  // the CTA's shared memory must outlive the copy's reads
       }
     } else {
+      // fp32 partial of this split: staged like the bf16 output (128 rows x D fp32
+      // = two K/V tiles' worth, so tile t uses 2 * kTile bytes from sK + 2t * kTile),
+      // in 32-column chunks of 128-byte rows, and stored with TMA by one thread
       const int64_t prow = (((int64_t)split * B + b) * Hc + hl) * p.Lq + row;
-      float* po = p.part_o + prow * D;
+      uint8_t* stg = sK + t * 2 * S::kTile;
+      const int r = threadIdx.x & 127;
+      uint8_t* srow = stg + r * 128;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -486,15 +492,22 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
-        if (row < p.Lq) {
-          float4* dst = reinterpret_cast<float4*>(po + c * 32);
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv_l, __uint_as_float(o[4 * e + 1]) * inv_l,
-                                 __uint_as_float(o[4 * e + 2]) * inv_l, __uint_as_float(o[4 * e + 3]) * inv_l);
-        }
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(srow + c * (128 * 128) + ((j ^ (r & 7)) << 4)) =
+              make_float4(__uint_as_float(o[4 * j]) * inv_l, __uint_as_float(o[4 * j + 1]) * inv_l,
+                          __uint_as_float(o[4 * j + 2]) * inv_l, __uint_as_float(o[4 * j + 3]) * inv_l);
       }
       if (row < p.Lq) p.part_lse[prow] = (have_o && l > 0.f) ? m + log2f(l) : -INFINITY;
+      fence_proxy_async_smem();
+      named_barrier(1 + t, 128);
+      if (r == 0) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tma_store_4d(&p.tm_part, stg + c * (128 * 128), c * 32, q0 + t * kTileM, hl, split * B + b);
+        bulk_commit();
+        bulk_wait_read();
+      }
     }
     }
   }

@@ -81,6 +81,22 @@ int make_tmap(CUtensorMap* map, const void* ptr, int D, int T, int H, int B, int
   return LTXATTN_OK;
 }
 
+// fp32 [D, T, H, B] contiguous buffer, box {32, 128, 1, 1} (128-byte rows), 128-byte swizzle
+int make_tmap_f32(CUtensorMap* map, void* ptr, int D, int T, int H, int B, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(LTXATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 4, (cuuint64_t)D * T * 4, (cuuint64_t)D * T * H * 4};
+  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LTXATTN_ERR_ALIGN, "%s: cuTensorMapEncodeTiled rejected the view (CUresult %d)", name, (int)r);
+  return LTXATTN_OK;
+}
+
 int current_sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -448,6 +464,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.num_splits = P.splits;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.part_o = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_po) : nullptr;
+  if (P.splits > 1 &&
+      (rc = make_tmap_f32(&p.tm_part, ws + P.off_po, s.D, s.Lq, s.Hc, P.splits * s.B, "split partials")))
+    return rc;
   p.part_lse = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_pl) : nullptr;
   p.err = err;
   const size_t smem = fwd_bf16_smem_bytes(s.D, s.Lk, a->key_mask != nullptr);

@@ -27,6 +27,7 @@ struct FwdParams {
   CUtensorMap tm_k;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
   CUtensorMap tm_v;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
   CUtensorMap tm_o;  // [D, Lq, H, B] box {64, 128, 1, 1}: the output (stored by TMA when num_splits == 1)
+  CUtensorMap tm_part;  // fp32 [D, Lq, Hc, splits*B] box {32, 128, 1, 1}: split partials (num_splits > 1)
   __nv_bfloat16* out;
   int64_t o_sb, o_sh, o_st;
   float* lse;  // natural log, may be null
