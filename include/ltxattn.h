@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define LTXATTN_ABI_VERSION 1
+#define LTXATTN_ABI_VERSION 2
 
 /* Entry points are the only symbols the library exports. */
 #if defined(__GNUC__)
@@ -101,7 +101,15 @@ typedef struct ltxattn_rotary {
  *  - lse: [B, H, q_len] float32, natural-log log-sum-exp of the scaled
  *    logits, or NULL.  The backward needs it.
  *  - workspace: device scratch of ltxattn_fwd_workspace() bytes (may be 0).
- *  - num_splits: KV splits for short-query shapes (0 = choose). */
+ *  - num_splits: KV splits for short-query shapes (0 = choose).
+ *  - causal, window, kv_heads: the Gemma text encoder's self-attention
+ *    (`GemmaTextEncoder.swift:218-233,292-323`); all zero for the DiT.  causal
+ *    (requires q_len == kv_len): query i attends key j only if j <= i; window
+ *    > 0: also i - j < window (a sliding layer).  A query row these rules and
+ *    key_mask leave without keys attends every key instead (the reference's
+ *    un-masking of fully masked rows).  kv_heads (0 = heads) must divide heads:
+ *    k and v are [B, kv_heads, kv_len, D] and query head h reads kv head
+ *    h / (heads / kv_heads); grouped heads take no rotary (rotate before). */
 typedef struct ltxattn_fwd_args {
   int32_t dtype;
   int32_t batch, heads, q_len, kv_len, head_dim;
@@ -116,6 +124,9 @@ typedef struct ltxattn_fwd_args {
   void* workspace;
   size_t workspace_bytes;
   int32_t num_splits;
+  int32_t causal;
+  int32_t window;
+  int32_t kv_heads;
 } ltxattn_fwd_args;
 
 /* Backward arguments: gradients of sum(dout * out) with respect to q, k and v

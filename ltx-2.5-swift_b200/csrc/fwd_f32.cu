@@ -31,8 +31,9 @@ __global__ void __launch_bounds__(128) fwd_f32_kernel(const F32Params p) {
   const int q0 = blockIdx.x * kRows;
   const int Lk = p.Lk;
   const float* qb = p.q + (int64_t)b * p.q_sb + (int64_t)(p.q_head_off + hl) * p.q_sh;
-  const float* kb = p.k + (int64_t)b * p.k_sb + (int64_t)(p.kv_head_off + hl) * p.k_sh;
-  const float* vb = p.v + (int64_t)b * p.v_sb + (int64_t)(p.kv_head_off + hl) * p.v_sh;
+  const int kvh = (p.kv_head_off + hl) / p.group;  // grouped heads share a kv head
+  const float* kb = p.k + (int64_t)b * p.k_sb + (int64_t)kvh * p.k_sh;
+  const float* vb = p.v + (int64_t)b * p.v_sb + (int64_t)kvh * p.v_sh;
   const uint8_t* mrow = p.mask ? p.mask + (int64_t)b * p.mask_sb : nullptr;
 
   // unmask rule: a batch row with no valid key attends to every key
@@ -45,6 +46,29 @@ __global__ void __launch_bounds__(128) fwd_f32_kernel(const F32Params p) {
   for (int i = threadIdx.x; i < kRows * D; i += blockDim.x) {
     const int r = i / D, d = i % D;
     sQ[i] = (q0 + r < p.Lq) ? qb[(int64_t)(q0 + r) * p.q_st + d] : 0.f;
+  }
+  // causal / sliding rows (GemmaTextEncoder.swift:292-323): row i attends key j
+  // when j <= i and i - j < window; a row left with no such valid key attends
+  // every key.  free_row[r]: this warp's row r is such an un-masked row.
+  bool free_row[kRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) free_row[r] = false;
+  // a batch row whose mask has no valid key leaves every query row without keys
+  const bool batch_empty = mrow != nullptr && any_valid == 0;
+  const bool banded = p.causal || p.window > 0 || batch_empty;
+  if (batch_empty) {
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) free_row[r] = true;
+  } else if (banded) {
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+      const int row = q0 + warp * kRowsPerWarp + r;
+      const int lo = p.window > 0 ? max(0, row - p.window + 1) : 0;
+      const int hi = p.causal ? min(row, Lk - 1) : Lk - 1;
+      int any = 0;
+      for (int j = lo + lane; j <= hi; j += 32) any |= (!use_mask || mrow[j] != 0);
+      free_row[r] = __any_sync(0xffffffffu, any) == 0;
+    }
   }
 
   constexpr int kPer = D / 32;
@@ -82,8 +106,19 @@ __global__ void __launch_bounds__(128) fwd_f32_kernel(const F32Params p) {
         a0 = fmaf(qd, k0[d], a0);
         a1 = fmaf(qd, k1[d], a1);
       }
-      const float s0 = ok0 ? a0 * p.scale : -INFINITY;
-      const float s1 = ok1 ? a1 * p.scale : -INFINITY;
+      bool k0ok = ok0, k1ok = ok1;
+      if (banded) {
+        const int row = q0 + warp * kRowsPerWarp + r;
+        if (free_row[r]) {
+          k0ok = j0 < Lk;
+          k1ok = j1 < Lk;
+        } else {
+          k0ok = ok0 && (!p.causal || j0 <= row) && (p.window <= 0 || row - j0 < p.window);
+          k1ok = ok1 && (!p.causal || j1 <= row) && (p.window <= 0 || row - j1 < p.window);
+        }
+      }
+      const float s0 = k0ok ? a0 * p.scale : -INFINITY;
+      const float s1 = k1ok ? a1 * p.scale : -INFINITY;
       float mt = fmaxf(s0, s1);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));

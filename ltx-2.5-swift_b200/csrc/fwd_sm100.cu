@@ -114,7 +114,10 @@ __device__ __forceinline__ void issue_pv_half(uint32_t tO, uint32_t tP, SDesc vd
   }
 }
 
-template <int D>
+// kBanded: causal / sliding-window rows and the free-row rule (the Gemma
+// encoder's self-attention); the DiT's attention runs the kBanded = false
+// instance, which carries none of that per-row state.
+template <int D, bool kBanded>
 __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __grid_constant__ FwdParams p) {
   using S = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -189,13 +192,44 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   const int any_valid = __syncthreads_or(local_any);
   use_mask = use_mask && (any_valid != 0);
 
-  // the list of KV tiles with at least one valid key
+  // Causal / sliding rows (GemmaTextEncoder.swift:292-323): row i attends key j
+  // when j <= i and i - j < window, and j is valid.  A row left with no such key
+  // attends every key instead ("free" row) -- so does every row of a batch whose
+  // mask has no valid key.  Softmax thread x (x < 256) owns row q0 + x.
+  constexpr bool banded = kBanded;
+  const bool batch_empty = p.mask != nullptr && any_valid == 0;
+  bool free_row = batch_empty;
+  if (banded && !batch_empty && use_mask && threadIdx.x < kBlockM) {
+    const int row = q0 + threadIdx.x;
+    if (row < p.Lq) {
+      const int lo = p.window > 0 ? max(0, row - p.window + 1) : 0;
+      const int hi = p.causal ? min(row, Lk - 1) : Lk - 1;
+      bool any = false;
+      for (int w = hi >> 5; w >= (lo >> 5) && !any; --w) {  // from the diagonal down
+        uint32_t bits = mbits[w];
+        if (w == (hi >> 5) && (hi & 31) != 31) bits &= (1u << ((hi & 31) + 1)) - 1u;
+        if (w == (lo >> 5)) bits &= ~0u << (lo & 31);
+        any = bits != 0u;
+      }
+      free_row = !any;
+    }
+  }
+  bool cta_free = batch_empty;
+  if constexpr (banded) cta_free = __syncthreads_or(free_row ? 1 : 0) != 0;
+
+  // the list of KV tiles this CTA needs: every tile when one of its rows is free,
+  // else the tiles inside its rows' band that hold a valid key
   if (warp == 0) {
+    const int q_last = min(q0 + (two ? kBlockM : kTileM) - 1, p.Lq - 1);
     int count = 0;
     for (int j0 = 0; j0 < p.n_kv_tiles; j0 += 32) {
       const int j = j0 + lane;
       bool act = j < p.n_kv_tiles;
-      if (act && use_mask) {
+      if (banded && act && !cta_free) {
+        if (p.causal) act = j * kTileN <= q_last;
+        if (p.window > 0) act = act && j * kTileN + kTileN - 1 >= q0 - p.window + 1;
+      }
+      if (act && use_mask && !(banded && cta_free)) {
         const uint32_t* w4 = mbits + j * 4;
         act = (w4[0] | w4[1] | w4[2] | w4[3]) != 0u;
       }
@@ -213,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   const int t_end = (int)(((int64_t)(split + 1) * n_all) / p.num_splits);
   const int n = t_end - t_begin;
   const int qh = p.q_head_off + hl;
-  const int kvh = p.kv_head_off + hl;
+  const int kvh = (p.kv_head_off + hl) / p.group;  // grouped query heads share a kv head
 
   if (warp >= 8) {
     setmaxnreg_dec<kProducerRegs>();
@@ -345,14 +379,25 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         }
       }
       const int kv0 = (int)tiles[t_begin + i] * kTileN;
-      const bool masked_tile = use_mask || kv0 + kTileN > Lk;
+      const bool masked_tile = use_mask || kv0 + kTileN > Lk || banded;
       if (masked_tile) {
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint32_t bits = 0xffffffffu;
-          if (use_mask) bits = mbits[kv0 / 32 + w];
+          if (use_mask && !(banded && free_row)) bits = mbits[kv0 / 32 + w];
           const int lim = Lk - (kv0 + 32 * w);
           if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
+          if (banded && !free_row) {  // compiled only into the kBanded instance
+            const int kw0 = kv0 + 32 * w;
+            if (p.causal) {
+              const int cnt = row - kw0 + 1;  // keys kw0 .. row
+              bits &= cnt >= 32 ? ~0u : (cnt <= 0 ? 0u : ((1u << cnt) - 1u));
+            }
+            if (p.window > 0) {
+              const int skip = row - p.window + 1 - kw0;  // keys below row - window + 1
+              bits &= skip <= 0 ? ~0u : (skip >= 32 ? 0u : (~0u << skip));
+            }
+          }
 #pragma unroll
           for (int c = 0; c < 32; ++c)
             if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
@@ -596,13 +641,20 @@ cudaError_t prepare_fwd_bf16(int D, size_t smem) {
   const int di = D == 128 ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_prep_mu);
   if (!g_regs_ok[dev][di]) {
-    e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128>) : check_launch_regs(fwd_bf16_sm100_kernel<64>);
+    e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128, false>)
+                 : check_launch_regs(fwd_bf16_sm100_kernel<64, false>);
+    if (e == cudaSuccess)
+      e = D == 128 ? check_launch_regs(fwd_bf16_sm100_kernel<128, true>)
+                   : check_launch_regs(fwd_bf16_sm100_kernel<64, true>);
     if (e != cudaSuccess) return e;
     g_regs_ok[dev][di] = true;
   }
   if (smem > g_smem_set[dev][di]) {
-    e = D == 128 ? cudaFuncSetAttribute(fwd_bf16_sm100_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                 : cudaFuncSetAttribute(fwd_bf16_sm100_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    for (int banded = 0; banded < 2 && e == cudaSuccess; ++banded) {
+      const void* k = D == 128 ? (banded ? (const void*)fwd_bf16_sm100_kernel<128, true> : (const void*)fwd_bf16_sm100_kernel<128, false>)
+                               : (banded ? (const void*)fwd_bf16_sm100_kernel<64, true> : (const void*)fwd_bf16_sm100_kernel<64, false>);
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
     if (e != cudaSuccess) return e;
     g_smem_set[dev][di] = smem;
   }
@@ -613,10 +665,15 @@ cudaError_t prepare_fwd_bf16(int D, size_t smem) {
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_blocks, int Hc, int B, size_t smem,
                             cudaStream_t s) {
   dim3 grid(q_blocks * p.num_splits, Hc, B);
-  if (D == 128)
-    fwd_bf16_sm100_kernel<128><<<grid, kThreads, smem, s>>>(p);
+  const bool banded = p.causal || p.window > 0;
+  if (D == 128 && banded)
+    fwd_bf16_sm100_kernel<128, true><<<grid, kThreads, smem, s>>>(p);
+  else if (D == 128)
+    fwd_bf16_sm100_kernel<128, false><<<grid, kThreads, smem, s>>>(p);
+  else if (banded)
+    fwd_bf16_sm100_kernel<64, true><<<grid, kThreads, smem, s>>>(p);
   else
-    fwd_bf16_sm100_kernel<64><<<grid, kThreads, smem, s>>>(p);
+    fwd_bf16_sm100_kernel<64, false><<<grid, kThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 

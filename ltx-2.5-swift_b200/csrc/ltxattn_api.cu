@@ -202,6 +202,8 @@ struct FwdPlan {
   Shape s;
   bool rope_q, rope_k;
   const ltxattn_rotary* kr;  // table used for k
+  int kv_heads, group;        // grouped KV heads: query head h reads kv head h / group
+  int causal, window;
   int q_tiles, kv_tiles, splits;
   size_t off_q, off_k, off_po, off_pl, total;
 };
@@ -212,7 +214,18 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
                        a->head_count, &P->s);
   if (rc) return rc;
   const Shape& s = P->s;
+  P->kv_heads = a->kv_heads == 0 ? s.H : a->kv_heads;
+  if (P->kv_heads < 1 || s.H % P->kv_heads)
+    return fail(LTXATTN_ERR_SHAPE, "kv_heads %d does not divide heads %d", a->kv_heads, s.H);
+  P->group = s.H / P->kv_heads;
+  P->causal = a->causal != 0;
+  P->window = a->window;
+  if (a->window < 0) return fail(LTXATTN_ERR_ARG, "window %d is negative", a->window);
+  if (P->causal && s.Lq != s.Lk)
+    return fail(LTXATTN_ERR_SHAPE, "causal attention needs q_len == kv_len (got %d and %d)", s.Lq, s.Lk);
   P->rope_q = a->q_rotary.cos != nullptr;
+  if (P->rope_q && P->group > 1)
+    return fail(LTXATTN_ERR_UNSUPPORTED, "grouped KV heads take no rotary tables: rotate q and k before the call");
   P->kr = (a->k_rotary.cos != nullptr) ? &a->k_rotary : &a->q_rotary;
   P->rope_k = P->rope_q;  // k_rotary without q_rotary is ignored (DiTAttention.swift:364)
   if (P->rope_q) {
@@ -420,6 +433,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     p.mask_sb = a->key_mask_stride_b;
     p.Lq = s.Lq; p.Lk = s.Lk; p.head_begin = s.h0;
     p.scale = a->scale;
+    p.group = P.group;
+    p.causal = P.causal;
+    p.window = P.window;
     e = launch_fwd_f32(p, s.D, s.Hc, s.B, st);
     if (e != cudaSuccess) return cuda_fail(e, "fwd_f32 launch");
     return LTXATTN_OK;
@@ -429,14 +445,14 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, P.rope_q ? s.Hc : s.H, s.B, q.stride_t,
                       q.stride_h, q.stride_b, "q")))
     return rc;
-  if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, P.rope_k ? s.Hc : s.H, s.B, k.stride_t, k.stride_h,
+  if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, P.rope_k ? s.Hc : P.kv_heads, s.B, k.stride_t, k.stride_h,
                       k.stride_b, "k")))
     return rc;
   // v keeps the caller's head indexing; k may be local.  One kv_head_off
   // serves both only when they agree, so v is re-based to local heads when
   // k is a local copy.
   const void* vptr = v.data;
-  int vH = s.H;
+  int vH = P.kv_heads;
   if (P.rope_k) {
     vptr = static_cast<const __nv_bfloat16*>(v.data) + (int64_t)s.h0 * v.stride_h;
     vH = s.Hc;
@@ -462,6 +478,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.kv_head_off = P.rope_k ? 0 : s.h0;
   p.n_kv_tiles = P.kv_tiles;
   p.num_splits = P.splits;
+  p.group = P.group;
+  p.causal = P.causal;
+  p.window = P.window;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.part_o = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_po) : nullptr;
   if (P.splits > 1 &&

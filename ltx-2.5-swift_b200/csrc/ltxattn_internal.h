@@ -40,6 +40,9 @@ struct FwdParams {
   int kv_head_off;  // head coordinate of local head 0 in tm_k / tm_v
   int n_kv_tiles;
   int num_splits;
+  int group;   // query heads per kv head: kv head = (kv_head_off + local head) / group
+  int causal;  // key j attends query i only if j <= i (q_len == kv_len)
+  int window;  // > 0: also i - j < window
   float scale_log2;  // softmax scale * log2(e)
   float* part_o;     // [splits][B][Hc][Lq][D] fp32 (num_splits > 1)
   float* part_lse;   // [splits][B][Hc][Lq] log2 domain (num_splits > 1)
@@ -63,6 +66,7 @@ struct F32Params {
   int64_t mask_sb;
   int Lq, Lk, head_begin;
   float scale;
+  int group, causal, window;  // as FwdParams
 };
 
 // Split-RoPE pre-pass: y[b][hl][t][:] = rope(x[b][head_begin+hl][t][:]) into a

@@ -50,7 +50,8 @@ class FwdArgs(ctypes.Structure):
                 ("key_mask_stride_b", ctypes.c_int64), ("q_rotary", Rotary), ("k_rotary", Rotary),
                 ("lse", ctypes.c_void_p), ("lse_stride_b", ctypes.c_int64),
                 ("lse_stride_h", ctypes.c_int64), ("workspace", ctypes.c_void_p),
-                ("workspace_bytes", ctypes.c_size_t), ("num_splits", ctypes.c_int32)]
+                ("workspace_bytes", ctypes.c_size_t), ("num_splits", ctypes.c_int32),
+                ("causal", ctypes.c_int32), ("window", ctypes.c_int32), ("kv_heads", ctypes.c_int32)]
 
 
 class RopeArgs(ctypes.Structure):

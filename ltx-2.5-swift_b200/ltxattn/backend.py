@@ -145,14 +145,17 @@ class AttentionBackend:
 
     @staticmethod
     def make_fwd_args(q, k, v, scale, key_mask=None, q_rotary=None, k_rotary=None, lse=None,
-                      out=None, head_begin=0, head_count=0, num_splits=0) -> Tuple[_lib.FwdArgs, torch.Tensor]:
+                      out=None, head_begin=0, head_count=0, num_splits=0, causal=False,
+                      window=0) -> Tuple[_lib.FwdArgs, torch.Tensor]:
         for name, t in (("q", q), ("k", k), ("v", v)):
             _check_cuda(name, t)
         if q.dim() != 4:
             raise Failure.shape("q", q.shape, "[B, heads, tokens, headDim]")
         B, H, Lq, D = q.shape
-        if k.dim() != 4 or k.shape[0] != B or k.shape[1] != H or k.shape[3] != D:
-            raise Failure.shape("k", k.shape, f"[{B}, {H}, kvTokens, {D}]")
+        # k / v may carry fewer heads than q (grouped KV heads, the Gemma encoder's GQA)
+        if k.dim() != 4 or k.shape[0] != B or k.shape[1] < 1 or H % k.shape[1] or k.shape[3] != D:
+            raise Failure.shape("k", k.shape, f"[{B}, {H} or a divisor of it, kvTokens, {D}]")
+        Hk = k.shape[1]
         Lk = k.shape[2]
         dt = _dtype_code(q)
         if k.dtype != q.dtype or v.dtype != q.dtype:
@@ -164,8 +167,8 @@ class AttentionBackend:
         a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = B, H, Lq, Lk, D
         a.head_begin, a.head_count = head_begin, head_count
         a.q = _view("q", q, (B, H, Lq, D))
-        a.k = _view("k", k, (B, H, Lk, D))
-        a.v = _view("v", v, (B, H, Lk, D))
+        a.k = _view("k", k, (B, Hk, Lk, D))
+        a.v = _view("v", v, (B, Hk, Lk, D))
         a.out = _view("out", out, (B, H, Lq, D))
         a.scale = float(scale)
         if key_mask is not None:
@@ -185,6 +188,7 @@ class AttentionBackend:
             a.lse = lse.data_ptr()
             a.lse_stride_b, a.lse_stride_h = lse.stride(0), lse.stride(1)
         a.num_splits = num_splits
+        a.causal, a.window, a.kv_heads = int(bool(causal)), int(window), Hk
         return a, out
 
     @staticmethod
@@ -212,8 +216,13 @@ class AttentionBackend:
                   k_rotary: Optional[Rotary] = None, save_lse: bool = False,
                   variant: Optional[Variant] = None, head_begin: int = 0, head_count: int = 0,
                   num_splits: int = 0, out: Optional[torch.Tensor] = None,
-                  lse: Optional[torch.Tensor] = None, stream=None):
-        """Fused split-RoPE + SDPA.  Returns ``(out, lse)``; lse is None unless requested."""
+                  lse: Optional[torch.Tensor] = None, stream=None, causal: bool = False, window: int = 0):
+        """Fused split-RoPE + SDPA.  Returns ``(out, lse)``; lse is None unless requested.
+
+        ``causal`` / ``window`` / grouped KV heads (``k`` with fewer heads than ``q``)
+        give the Gemma text encoder's self-attention (GemmaTextEncoder.swift:218-233,
+        292-323); the DiT's attention uses none of them.
+        """
         if variant is not None and q_rotary is not None and not variant.takes_rotary:
             raise Failure.rotary_without_position(variant)
         if scale is None:
@@ -221,7 +230,7 @@ class AttentionBackend:
         if save_lse and lse is None:
             lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
         a, out = AttentionBackend.make_fwd_args(q, k, v, scale, key_mask, q_rotary, k_rotary, lse, out,
-                                                head_begin, head_count, num_splits)
+                                                head_begin, head_count, num_splits, causal, window)
         L = _lib.load()
         ws_bytes = int(L.ltxattn_fwd_workspace(ctypes.byref(a)))
         ws = None

@@ -252,6 +252,62 @@ static void allowed_keys(const uint8_t* mask, int64_t mask_stride_b, int b, int 
         for (int j = 0; j < Lk; ++j) allowed[j] = 1;
 }
 
+/* Self-attention of the Gemma text encoder (GemmaTextEncoder.swift:218-233,
+ * 292-323): query i may attend key j when j <= i (causal), i - j < window (a
+ * sliding layer, window > 0) and key j is not padding; a query row left with
+ * no such key attends every key instead (the reference's un-masking of fully
+ * masked rows).  Grouped KV heads: query head h reads KV head h / (Hq / Hkv).
+ * q [B][Hq][L][D], k / v [B][Hkv][L][D], valid [B][L] (NULL: all valid);
+ * fp64 accumulation; lse natural-log over the attended keys. */
+int oracle_attn_fwd_gemma(const float* q, const float* k, const float* v, const uint8_t* valid,
+                          int B, int Hq, int Hkv, int L, int D, double scale, int causal, int window,
+                          float* out, float* lse) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || L <= 0 || D <= 0) return 1;
+    const int group = Hq / Hkv;
+    double* logit = (double*)malloc(sizeof(double) * (size_t)L);
+    unsigned char* allow = (unsigned char*)malloc((size_t)L);
+    if (!logit || !allow) { free(logit); free(allow); return 2; }
+    for (int b = 0; b < B; ++b)
+    for (int h = 0; h < Hq; ++h)
+    for (int i = 0; i < L; ++i) {
+        int any = 0;
+        for (int j = 0; j < L; ++j) {
+            int ok = valid ? (valid[(int64_t)b * L + j] != 0) : 1;
+            if (causal && j > i) ok = 0;
+            if (window > 0 && i - j >= window) ok = 0;
+            allow[j] = (unsigned char)ok;
+            any |= ok;
+        }
+        if (!any) memset(allow, 1, (size_t)L);
+        const float* qr = q + (((int64_t)b * Hq + h) * L + i) * D;
+        const float* kh = k + ((int64_t)b * Hkv + h / group) * L * D;
+        const float* vh = v + ((int64_t)b * Hkv + h / group) * L * D;
+        double mx = -INFINITY;
+        for (int j = 0; j < L; ++j) {
+            if (!allow[j]) { logit[j] = -INFINITY; continue; }
+            double sdot = 0.0;
+            for (int d = 0; d < D; ++d) sdot += (double)qr[d] * (double)kh[(int64_t)j * D + d];
+            logit[j] = sdot * scale;
+            if (logit[j] > mx) mx = logit[j];
+        }
+        double sum = 0.0;
+        for (int j = 0; j < L; ++j) {
+            logit[j] = allow[j] ? exp(logit[j] - mx) : 0.0;
+            sum += logit[j];
+        }
+        float* o = out + (((int64_t)b * Hq + h) * L + i) * D;
+        for (int d = 0; d < D; ++d) {
+            double acc = 0.0;
+            for (int j = 0; j < L; ++j) acc += logit[j] * (double)vh[(int64_t)j * D + d];
+            o[d] = (float)(acc / sum);
+        }
+        if (lse) lse[((int64_t)b * Hq + h) * L + i] = (float)(mx + log(sum));
+    }
+    free(logit);
+    free(allow);
+    return 0;
+}
+
 /* Forward, fp64 accumulation (the parity oracle).  lse is the natural-log
  * log-sum-exp of the scaled logits over allowed keys, [B, H, Lq]. */
 int oracle_attn_fwd(const float* q, const float* k, const float* v,

@@ -50,11 +50,14 @@ def lib():
         L.oracle_attn_bwd.argtypes = [_f32p, _f32p, _f32p, _u8p, ctypes.c_int64, _f32p] + [
             ctypes.c_int] * 5 + [ctypes.c_double, _f32p, _f32p, _f32p, ctypes.c_int]
         L.oracle_rotary_tables.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_double, _f32p, _f32p]
+        L.oracle_attn_fwd_gemma.argtypes = [_f32p, _f32p, _f32p, _u8p] + [ctypes.c_int] * 5 + [
+            ctypes.c_double, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
         L.oracle_qk_prep.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, _f32p, _f32p,
                                                                          ctypes.c_int64, ctypes.c_int64,
                                                                          ctypes.c_int, _f32p]
         for f in ("oracle_rope", "oracle_rope_bwd", "oracle_attn_fwd",
-                  "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables", "oracle_qk_prep"):
+                  "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables", "oracle_qk_prep",
+                  "oracle_attn_fwd_gemma"):
             getattr(L, f).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -215,3 +218,19 @@ def qk_prep(x: np.ndarray, w: np.ndarray, heads: int, eps: float = 1e-6, cos=Non
                               sb, sh, int(bf16), _p(out))
     assert rc == 0
     return out
+
+
+def attention_gemma(q, k, v, valid=None, scale=1.0, causal=True, window=0):
+    """Gemma text-encoder self-attention (causal / sliding / padding masks with the
+    un-masking of empty rows, grouped KV heads), fp64: returns (out, lse)."""
+    qq, kk, vv = _f32(q), _f32(k), _f32(v)
+    B, Hq, L, D = qq.shape
+    Hkv = kk.shape[1]
+    out = np.empty_like(qq)
+    lse = np.empty((B, Hq, L), np.float32)
+    m = np.ascontiguousarray(valid, dtype=np.uint8) if valid is not None else None
+    mp = m.ctypes.data_as(_u8p) if m is not None else ctypes.POINTER(ctypes.c_uint8)()
+    rc = lib().oracle_attn_fwd_gemma(_p(qq), _p(kk), _p(vv), mp, B, Hq, Hkv, L, D, float(scale),
+                                     int(causal), int(window), _p(out), _p(lse))
+    assert rc == 0
+    return out, lse

@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
     exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln and "ltxattn_" in ln}
     assert exported == declared, f"exports differ from the header: {exported ^ declared}"
-    assert L.ltxattn_abi_version() == 1
+    assert L.ltxattn_abi_version() == 2
 
 
 PROBE = r"""
@@ -54,6 +54,7 @@ int main(void) {
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
+  P(ltxattn_fwd_args, causal) P(ltxattn_fwd_args, window) P(ltxattn_fwd_args, kv_heads)
   P(ltxattn_bwd_args, dout) P(ltxattn_bwd_args, lse) P(ltxattn_bwd_args, dq) P(ltxattn_bwd_args, scale)
   P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
   P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
