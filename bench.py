@@ -50,6 +50,10 @@ L2_BYTES = 126 * 1024 * 1024
 BOUND = {"c2": "tensor", "c3": "hbm", "c4a": "hbm", "c4b": "hbm", "c4c": "hbm", "c5": "tensor"}
 
 
+# DRAM bytes per attention launch measured by ncu (profiles/fwd_bf16_sm100_c2.md)
+TRAFFIC = {"c2": 85.8e6}
+
+
 def algorithmic_bytes(wl, B, H, Lq, Lk, D):
     """Bytes one attention launch must move: Q and O, plus K and V of the valid keys (bf16)."""
     valid = WORKLOADS[wl][6] or Lk
@@ -426,7 +430,10 @@ def run_ours(args):
                           "frac": round(kern_gbs / hbm, 4), "peak_source": f"{src} hbm_gbs",
                           "algorithmic_bytes": algorithmic_bytes(wl, B, Hc, Lq, Lk, D),
                           "kernel_tflops": round(achieved, 2)}) | {
-                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5), "traffic": None},
+                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5),
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch, from the ncu
+                         # capture summarised in profiles/fwd_bf16_sm100_c2.md (config 2 only)
+                         "traffic": TRAFFIC.get(wl)},
             "step_ms": {"median": round(statistics.median(step_ms), 5), "min": round(min(step_ms), 5),
                         "max": round(max(step_ms), 5),
                         "spread": round((max(step_ms) - min(step_ms)) / statistics.median(step_ms), 4)},
