@@ -107,6 +107,9 @@ def _args(**kw):
     (dict(kv_len=0), _lib.ERR_SHAPE),
     (dict(head_begin=1, head_count=2), _lib.ERR_ARG),
     (dict(kv_len=200000), _lib.ERR_UNSUPPORTED),
+    (dict(causal=1, kv_len=32), _lib.ERR_SHAPE),      # causal needs q_len == kv_len
+    (dict(kv_heads=3), _lib.ERR_SHAPE),               # kv_heads must divide heads
+    (dict(window=-1), _lib.ERR_ARG),
 ])
 def test_validation_refuses_before_any_device_work(kw, status):
     L = _lib.load()
@@ -141,3 +144,28 @@ def test_variant_rotary_rule_mirrors_the_reference():
     e = backend.Failure.rotary_without_position(backend.Variant.video_cross)
     assert e.kind == "rotaryWithoutPosition" and "attn2 takes no rotary" in str(e)
     assert str(backend.Failure.shape("q", (1, 2), "[B, H, T, D]")) == "q is [1, 2], expected [B, H, T, D]"
+
+
+def test_grouped_kv_heads_take_no_rotary():
+    # grouped KV heads (the Gemma encoder) rotate before the call (GemmaTextEncoder.swift:173,193)
+    L = _lib.load()
+    a = _args(heads=4, kv_heads=2)
+    a.q_rotary = _lib.Rotary(cos=1024, sin=2048, stride_b=0, stride_h=0, stride_t=32, tokens=16)
+    assert L.ltxattn_fwd(ctypes.byref(a), None) == _lib.ERR_UNSUPPORTED
+    assert "grouped KV heads" in _lib.last_error()
+
+
+def test_new_entry_points_refuse_bad_arguments():
+    L = _lib.load()
+    assert L.ltxattn_rope(None, None) == _lib.ERR_ARG
+    assert L.ltxattn_rotary_tables(None, None) == _lib.ERR_ARG
+    assert L.ltxattn_qk_prep(None, None) == _lib.ERR_ARG
+    r = _lib.RopeArgs()
+    r.dtype, r.batch, r.heads, r.tokens, r.head_dim = _lib.BF16, 1, 1, 4, 64
+    assert L.ltxattn_rope(ctypes.byref(r), None) == _lib.ERR_ARG  # no tables
+    t = _lib.RotaryTableArgs()
+    t.dtype, t.n_pos, t.tokens, t.inner, t.heads, t.theta = _lib.BF16, 5, 4, 4096, 32, 10000.0
+    assert L.ltxattn_rotary_tables(ctypes.byref(t), None) == _lib.ERR_SHAPE  # n_pos > 4
+    q = _lib.QkPrepArgs()
+    q.dtype, q.batch, q.tokens, q.heads, q.head_dim = _lib.BF16, 1, 4, 3, 64  # inner 192
+    assert L.ltxattn_qk_prep(ctypes.byref(q), None) == _lib.ERR_UNSUPPORTED
