@@ -54,12 +54,15 @@ public enum AttentionBackend {
 
     /// The fused RoPE + SDPA the `.fused` and `.explicit` arms collapse into.
     /// `keyRotary == nil` with `rotary` given rotates k with `rotary`
-    /// (`keyRotary ?? rotary`, DiTAttention.swift:366).
+    /// (`keyRotary ?? rotary`, DiTAttention.swift:366).  `causal`, `window` and
+    /// `kvHeads` give the Gemma encoder's self-attention
+    /// (GemmaTextEncoder.swift:218-233, mask :292-323); the DiT passes none.
     public static func attention(
         bf16: Bool, batch: Int32, heads: Int32, queryTokens: Int32, keyTokens: Int32, headDim: Int32,
         q: DeviceTensor, k: DeviceTensor, v: DeviceTensor, out: DeviceTensor, scale: Float,
         keyMask: UnsafePointer<UInt8>? = nil, rotary: DeviceRotary? = nil, keyRotary: DeviceRotary? = nil,
         lse: UnsafeMutablePointer<Float>? = nil, workspace: UnsafeMutableRawPointer?, workspaceBytes: Int,
+        causal: Bool = false, window: Int32 = 0, kvHeads: Int32 = 0,
         stream: UnsafeMutableRawPointer?
     ) throws {
         var a = ltxattn_fwd_args()
@@ -78,7 +81,59 @@ public enum AttentionBackend {
         }
         a.workspace = workspace
         a.workspace_bytes = workspaceBytes
+        a.causal = causal ? 1 : 0
+        a.window = window
+        a.kv_heads = kvHeads
         try check(ltxattn_fwd(&a, stream))
+    }
+
+    /// `applySplitRoPE` (DiTAttention.swift:206-234) of one [B, H, T, D] view;
+    /// `out` may be `x` itself.
+    public static func splitRoPE(
+        bf16: Bool, batch: Int32, heads: Int32, tokens: Int32, headDim: Int32,
+        x: DeviceTensor, out: DeviceTensor, rotary: DeviceRotary, stream: UnsafeMutableRawPointer?
+    ) throws {
+        var a = ltxattn_rope_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.heads = heads; a.tokens = tokens; a.head_dim = headDim
+        a.x = x.c; a.out = out.c; a.rotary = rotary.c
+        try check(ltxattn_rope(&a, stream))
+    }
+
+    /// `DiTForward.rotary` (DiTForward.swift:641-678) on the device: per-head tables
+    /// [heads, tokens, inner / 2 / heads] from fp32 (lo, hi) positions [nPos, tokens, 2].
+    public static func rotaryTables(
+        bf16: Bool, positions: UnsafePointer<Float>, nPos: Int32, tokens: Int32, maxPos: [Float],
+        inner: Int32, heads: Int32, theta: Double, cos: UnsafeMutableRawPointer, sin: UnsafeMutableRawPointer,
+        stream: UnsafeMutableRawPointer?
+    ) throws {
+        var a = ltxattn_rotary_table_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.n_pos = nPos; a.tokens = tokens; a.inner = inner; a.heads = heads; a.theta = theta
+        withUnsafeMutableBytes(of: &a.max_pos) { raw in
+            let mp = raw.bindMemory(to: Float.self)
+            for (d, v) in maxPos.prefix(4).enumerated() { mp[d] = v }
+        }
+        a.positions = positions; a.cos = cos; a.sin = sin
+        try check(ltxattn_rotary_tables(&a, stream))
+    }
+
+    /// The q / k preparation of DiTAttention.swift:358-367 in one pass: rmsNorm over the
+    /// inner dim, the head split and split RoPE, from the projection output
+    /// [B, tokens, heads * headDim] (element strides `xStrides`) into `out`.
+    public static func prepareQK(
+        bf16: Bool, batch: Int32, tokens: Int32, heads: Int32, headDim: Int32,
+        x: UnsafeRawPointer, xStrides: (b: Int64, t: Int64), weight: UnsafeRawPointer, eps: Float,
+        rotary: DeviceRotary?, out: DeviceTensor, stream: UnsafeMutableRawPointer?
+    ) throws {
+        var a = ltxattn_qk_prep_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.tokens = tokens; a.heads = heads; a.head_dim = headDim
+        a.x = x; a.x_stride_b = xStrides.b; a.x_stride_t = xStrides.t
+        a.weight = weight; a.eps = eps
+        if let rotary { a.rotary = rotary.c }
+        a.out = out.c
+        try check(ltxattn_qk_prep(&a, stream))
     }
 
     /// Device scratch the same arguments need (call once per shape; the caller allocates).
