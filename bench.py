@@ -291,9 +291,9 @@ def run_ours(args):
     def step():
         call.run(stream)
 
-    sms = torch.cuda.get_device_properties(local).multi_processor_count
-    ctas = math.ceil(Lq / 128) * Hc * B
-    splits = ctas < sms and math.ceil(Lk / 128) > 1
+    # without rotary tables the only scratch is the split-KV partials: a workspace
+    # means the planner split some units and the call adds a combine launch
+    splits = kernel_call.workspace is not None
     launches_per_step = 1 + (1 if qrot is not None else 0) + (1 if splits else 0)
     flops = 4.0 * B * Hc * Lq * Lk * D
     if mask is not None:

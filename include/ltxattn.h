@@ -101,7 +101,10 @@ typedef struct ltxattn_rotary {
  *  - lse: [B, H, q_len] float32, natural-log log-sum-exp of the scaled
  *    logits, or NULL.  The backward needs it.
  *  - workspace: device scratch of ltxattn_fwd_workspace() bytes (may be 0).
- *  - num_splits: KV splits for short-query shapes (0 = choose).
+ *  - num_splits: 0 = choose: short query sequences split every 256-row
+ *    query block's KV range across CTAs, and dense calls whose last wave of
+ *    blocks would leave most SMs idle split only those last blocks; n > 0
+ *    splits every block n ways.  The choice changes only the summation order.
  *  - causal, window, kv_heads: the Gemma text encoder's self-attention
  *    (`GemmaTextEncoder.swift:218-233,292-323`); all zero for the DiT.  causal
  *    (requires q_len == kv_len): query i attends key j only if j <= i; window

@@ -44,10 +44,13 @@
 // column.  A batch row whose mask has no valid key attends to all keys
 // (GemmaTextEncoder.swift:306-319).
 //
-// Split-KV (short query sequences): blockIdx.x = q_block * num_splits + split;
-// each split handles a contiguous share of the active KV tiles and writes an
-// fp32 partial O (normalised by its own l) and its log2-domain lse; the
-// combine kernel merges them.
+// Work units are (256-row query block, head, batch), q_block fastest, on a
+// 1-D grid.  The first n_full units run whole, one CTA each, and store O
+// directly.  Each later ("tail") unit runs as num_splits CTAs, each over a
+// contiguous share of the unit's active KV tiles, writing an fp32 partial O
+// (normalised by its own l) and its log2-domain lse; the combine kernel merges
+// them.  CTAs start roughly in index order, so the split CTAs fill what would
+// otherwise be a thin last wave; short query sequences split every unit.
 #include <mutex>
 
 #include "ltxattn_internal.h"
@@ -114,6 +117,39 @@ __device__ __forceinline__ void issue_pv_half(uint32_t tO, uint32_t tP, SDesc vd
   }
 }
 
+// The work unit and KV share of CTA `cta` (see the grid layout above).
+struct Unit {
+  int q_block, hl, b;  // 256-row query block, local head, batch
+  int split, ns;       // KV share split of ns (ns == 1: the whole unit)
+  int tail;            // index among the split units (ns > 1)
+};
+
+__device__ __forceinline__ Unit decode_unit(const FwdParams& p, int cta) {
+  Unit u;
+  int unit = cta;
+  u.split = 0;
+  u.ns = 1;
+  if (unit >= p.n_full) {
+    const int c = unit - p.n_full;
+    u.ns = p.num_splits;
+    unit = p.n_full + c / u.ns;
+    u.split = c - (c / u.ns) * u.ns;
+  }
+  u.tail = unit - p.n_full;
+  u.q_block = unit % p.q_blocks;
+  u.hl = (unit / p.q_blocks) % p.Hc;
+  u.b = unit / (p.q_blocks * p.Hc);
+  return u;
+}
+
+// %ctaid.x read that the compiler cannot merge with an earlier read: the
+// epilogue decodes its unit again instead of keeping it live through the loop.
+__device__ __forceinline__ int ctaid_x_fresh() {
+  int x;
+  asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(x));
+  return x;
+}
+
 // kBanded: causal / sliding-window rows and the free-row rule (the Gemma
 // encoder's self-attention); the DiT's attention runs the kBanded = false
 // instance, which carries none of that per-row state.
@@ -144,11 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_block = blockIdx.x / p.num_splits;
-  const int split = blockIdx.x % p.num_splits;
-  const int hl = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q0 = q_block * kBlockM;
+  const Unit un = decode_unit(p, blockIdx.x);
+  const int hl = un.hl, b = un.b;
+  const int q0 = un.q_block * kBlockM;
   const bool two = q0 + kTileM < p.Lq;  // is Q tile 1 inside the sequence?
   const int Lk = p.Lk;
 
@@ -168,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
     tma_prefetch_desc(&p.tm_o);
-    if (p.num_splits > 1) tma_prefetch_desc(&p.tm_part);
+    if (un.ns > 1) tma_prefetch_desc(&p.tm_part);
   }
 
   // key-mask bits (padded with zero words to a whole tile)
@@ -243,8 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_all = *n_tiles_slot;
-  const int t_begin = (int)(((int64_t)split * n_all) / p.num_splits);
-  const int t_end = (int)(((int64_t)(split + 1) * n_all) / p.num_splits);
+  const int t_begin = (int)(((int64_t)un.split * n_all) / un.ns);
+  const int t_end = (int)(((int64_t)(un.split + 1) * n_all) / un.ns);
   const int n = t_end - t_begin;
   const int qh = p.q_head_off + hl;
   const int kvh = (p.kv_head_off + hl) / p.group;  // grouped query heads share a kv head
@@ -476,8 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     const bool have_o = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 10);
     tc_fence_after();
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-    const int B = gridDim.z, Hc = gridDim.y;
-    if (p.num_splits == 1) {
+    const Unit ue = decode_unit(p, ctaid_x_fresh());
+    if (ue.ns == 1) {
       // Stage the normalised bf16 row in K stage t (idle once O is complete: every
       // MMA has finished and no load is outstanding), 128-byte swizzled like the
       // loads, then one thread per tile stores it with TMA (coalesced; rows past
@@ -507,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         }
       }
       if (p.lse != nullptr && row < p.Lq) {
-        p.lse[(int64_t)b * p.lse_sb + (int64_t)(p.head_begin + hl) * p.lse_sh + row] =
+        p.lse[(int64_t)ue.b * p.lse_sb + (int64_t)(p.head_begin + ue.hl) * p.lse_sh + row] =
             (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
       }
       fence_proxy_async_smem();  // the bulk copy reads these rows through the async proxy
@@ -515,7 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       if (r == 0) {
 #pragma unroll
         for (int ch = 0; ch < S::kChunks; ++ch)
-          tma_store_4d(&p.tm_o, stg + ch * kChunkBytes, ch * 64, q0 + t * kTileM, p.head_begin + hl, b);
+          tma_store_4d(&p.tm_o, stg + ch * kChunkBytes, ch * 64, ue.q_block * kBlockM + t * kTileM,
+                       p.head_begin + ue.hl, ue.b);
         bulk_commit();
         bulk_wait_read();  // the CTA's shared memory must outlive the copy's reads
       }
@@ -523,7 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       // fp32 partial of this split: staged like the bf16 output (128 rows x D fp32
       // = two K/V tiles' worth, so tile t uses 2 * kTile bytes from sK + 2t * kTile),
       // in 32-column chunks of 128-byte rows, and stored with TMA by one thread
-      const int64_t prow = (((int64_t)split * B + b) * Hc + hl) * p.Lq + row;
+      // into the [split][tail unit][256 rows] partial layout
+      const int64_t prow = ((int64_t)ue.split * p.n_tail + ue.tail) * kBlockM + t * kTileM + (threadIdx.x & 127);
       uint8_t* stg = sK + t * 2 * S::kTile;
       const int r = threadIdx.x & 127;
       uint8_t* srow = stg + r * 128;
@@ -549,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       if (r == 0) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          tma_store_4d(&p.tm_part, stg + c * (128 * 128), c * 32, q0 + t * kTileM, hl, split * B + b);
+          tma_store_4d(&p.tm_part, stg + c * (128 * 128), c * 32, t * kTileM, ue.tail, ue.split);
         bulk_commit();
         bulk_wait_read();
       }
@@ -567,16 +603,18 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 }
 
 // Merge split partials: lse = log2-sum-exp2 of the splits' lse, O = sum_s w_s O_s.
-// One warp per output row.
+// One warp per row of the split units (partial row gw = tail unit * 256 + r).
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)p.B * p.Hc * p.Lq;
+  const int64_t rows = (int64_t)p.n_tail * kBlockM;
   if (gw >= rows) return;
-  const int row = (int)(gw % p.Lq);
-  const int hl = (int)((gw / p.Lq) % p.Hc);
-  const int b = (int)(gw / ((int64_t)p.Lq * p.Hc));
+  const int unit = p.n_full + (int)(gw / kBlockM);
+  const int row = (unit % p.q_blocks) * kBlockM + (int)(gw % kBlockM);
+  const int hl = (unit / p.q_blocks) % p.Hc;
+  const int b = unit / (p.q_blocks * p.Hc);
+  if (row >= p.Lq) return;
   float mx = -INFINITY;
   for (int s = 0; s < p.num_splits; ++s) mx = fmaxf(mx, p.part_lse[(int64_t)s * rows + gw]);
   constexpr int kPer = D / 32;
@@ -662,9 +700,8 @@ cudaError_t prepare_fwd_bf16(int D, size_t smem) {
 }
 
 // Launch only (prepare_fwd_bf16 must have succeeded for D and at least smem).
-cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_blocks, int Hc, int B, size_t smem,
-                            cudaStream_t s) {
-  dim3 grid(q_blocks * p.num_splits, Hc, B);
+cudaError_t launch_fwd_bf16(const FwdParams& p, int D, size_t smem, cudaStream_t s) {
+  const dim3 grid(p.n_full + p.n_tail * p.num_splits);
   const bool banded = p.causal || p.window > 0;
   if (D == 128 && banded)
     fwd_bf16_sm100_kernel<128, true><<<grid, kThreads, smem, s>>>(p);
@@ -678,7 +715,7 @@ cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_blocks, int Hc, int
 }
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s) {
-  const int64_t rows = (int64_t)p.B * p.Hc * p.Lq;
+  const int64_t rows = (int64_t)p.n_tail * kFwdBlockM;
   const int64_t threads = rows * 32;
   const int blocks = (int)((threads + 255) / 256);
   if (p.D == 128)

@@ -166,19 +166,54 @@ int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
 }
 
 // ---------------------------------------------------------------------------
-// Split count for a launch of at least one wave.  The CTAs run in whole waves
-// of sm_count; when the last wave is thin, splitting each query block's KV
-// range s ways (s <= 4) can shorten the job: predicted time =
-//   ceil(ctas * s / sms) * (kv_tiles / s * t_tile + t_cta)  +  combine(s)
+// KV splitting for a launch of at least one wave.  One CTA per SM: the units
+// (256-row query block, head, batch) run in waves of sm_count, and a thin last
+// wave leaves most SMs idle for a whole unit's time.  Splitting the KV range
+// of the last n_tail units s ways (n_tail = the last partial wave plus k whole
+// waves) replaces that wave by ceil(n_tail * s / sms) waves of 1/s-size CTAs:
+//   time = (waves - k) * t(1) + ceil(n_tail * s / sms) * t(s) + combine
+//   t(s) = t_cta + ceil(kv_tiles / s) * t_tile
 // with t_tile ~ 1.8 us per 128-key step of a two-tile CTA, t_cta ~ 8 us of
-// per-CTA prologue and epilogue, and combine(s) moving s fp32 partials of O
-// (written and read back) at ~5 TB/s.  A split must keep >= 8 KV tiles per CTA
-// and the cheapest choice must beat no split by 3%.  (At 29,760 tokens and 4
-// heads per GPU this picks 3; at 8 or more heads it picks 1.)
-int wave_balanced_splits(int64_t ctas, int sms, int kv_tiles, double out_elems) {
+// per-CTA prologue and epilogue, and the combine moving s fp32 partials of the
+// tail units' O (written and read back) at ~5 TB/s plus ~3 us for its launch.
+// The cheapest choice must beat no split by 1.5%.  (29,760 tokens and 4 heads
+// per GPU: 468 units = 3 waves + 24, split 6 ways; 32 heads at 3,120 tokens:
+// 416 units, no split.)
+struct SplitChoice {
+  int64_t n_tail;
+  int splits;
+};
+
+SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
+  constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBytesPerUs = 5.0e6, kLaunchUs = 3.0;
+  auto unit_us = [&](int sp) { return kCtaUs + (double)((kv_tiles + sp - 1) / sp) * kTileUs; };
+  const int64_t waves = units / sms, rem = units % sms;
+  const double whole = (double)((units + sms - 1) / sms) * unit_us(1);
+  SplitChoice best{0, 1};
+  double best_us = whole;
+  for (int64_t k = 0; k <= waves; ++k) {
+    const int64_t n_tail = rem + k * sms;
+    if (n_tail == 0) continue;
+    for (int sp = 2; sp <= kMaxSplits && kv_tiles / sp >= 2; ++sp) {
+      const double combine = kLaunchUs + 2.0 * sp * (double)n_tail * kFwdBlockM * D * 4.0 / kBytesPerUs;
+      const double us = (double)(waves - k) * unit_us(1) + (double)((n_tail * sp + sms - 1) / sms) * unit_us(sp) +
+                        combine;
+      if (us < best_us) {
+        best_us = us;
+        best = {n_tail, sp};
+      }
+    }
+  }
+  return best_us < 0.985 * whole ? best : SplitChoice{0, 1};
+}
+
+// Uniform split count (every unit split) for masked or banded calls, whose
+// per-unit work the planner cannot see: the same cost terms over all units,
+// at most 4 splits of >= 8 KV tiles each, and 3% better than no split.
+int uniform_splits(int64_t units, int sms, int kv_tiles, double out_elems) {
   constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBytesPerUs = 5.0e6;
   auto cost = [&](int sp) {
-    const double waves = (double)((ctas * sp + sms - 1) / sms);
+    const double waves = (double)((units * sp + sms - 1) / sms);
     const double combine = sp > 1 ? 2.0 * sp * out_elems * 4.0 / kBytesPerUs : 0.0;
     return waves * ((double)kv_tiles / sp * kTileUs + kCtaUs) + combine;
   };
@@ -205,6 +240,7 @@ struct FwdPlan {
   int kv_heads, group;        // grouped KV heads: query head h reads kv head h / group
   int causal, window;
   int q_tiles, kv_tiles, splits;
+  int64_t units, n_full, n_tail;  // bf16: n_tail units split `splits` ways after n_full whole ones
   size_t off_q, off_k, off_po, off_pl, total;
 };
 
@@ -235,31 +271,42 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   P->q_tiles = s.dtype == LTXATTN_BF16 ? (s.Lq + kFwdBlockM - 1) / kFwdBlockM : (s.Lq + kTileM - 1) / kTileM;
   P->kv_tiles = (s.Lk + kTileN - 1) / kTileN;
   P->splits = 1;
+  P->units = (int64_t)P->q_tiles * s.Hc * s.B;
+  P->n_tail = 0;
   if (s.dtype == LTXATTN_BF16) {
+    const int64_t units = P->units;
     if (a->num_splits > 0) {
       P->splits = std::min({a->num_splits, P->kv_tiles, kMaxSplits});
+      P->n_tail = units;
     } else if (a->num_splits == 0) {
-      const int64_t ctas = (int64_t)P->q_tiles * s.Hc * s.B;
       const int sms = current_sm_count();
-      if (ctas < sms && P->kv_tiles > 1) {
-        const int want = (int)((2 * (int64_t)sms + ctas - 1) / ctas);
+      if (units < sms && P->kv_tiles > 1) {
+        const int want = (int)((2 * (int64_t)sms + units - 1) / units);
         P->splits = std::max(1, std::min({want, P->kv_tiles, kMaxSplits}));
-      } else if (ctas >= sms) {
-        P->splits = wave_balanced_splits(ctas, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
+        P->n_tail = units;
+      } else if (units >= sms && (a->key_mask != nullptr || P->causal || P->window > 0)) {
+        P->splits = uniform_splits(units, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
+        P->n_tail = units;
+      } else if (units >= sms) {
+        const SplitChoice c = tail_splits(units, sms, P->kv_tiles, s.D);
+        P->splits = c.splits;
+        P->n_tail = c.n_tail;
       }
     } else {
       return fail(LTXATTN_ERR_ARG, "num_splits %d is negative", a->num_splits);
     }
+    if (P->splits == 1) P->n_tail = 0;
   }
+  P->n_full = P->units - P->n_tail;
   size_t off = 0;
   P->off_q = off;
   if (P->rope_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
   P->off_k = off;
   if (P->rope_k) off += align256((size_t)s.B * s.Hc * s.Lk * s.D * s.esize);
   P->off_po = off;
-  if (P->splits > 1) off += align256((size_t)P->splits * s.B * s.Hc * s.Lq * s.D * sizeof(float));
+  if (P->splits > 1) off += align256((size_t)P->splits * P->n_tail * kFwdBlockM * s.D * sizeof(float));
   P->off_pl = off;
-  if (P->splits > 1) off += align256((size_t)P->splits * s.B * s.Hc * s.Lq * sizeof(float));
+  if (P->splits > 1) off += align256((size_t)P->splits * P->n_tail * kFwdBlockM * sizeof(float));
   P->total = off;
   return LTXATTN_OK;
 }
@@ -477,14 +524,17 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.q_head_off = q_head_off;
   p.kv_head_off = P.rope_k ? 0 : s.h0;
   p.n_kv_tiles = P.kv_tiles;
+  p.q_blocks = P.q_tiles;
+  p.Hc = s.Hc;
+  p.n_full = (int)P.n_full;
+  p.n_tail = (int)P.n_tail;
   p.num_splits = P.splits;
   p.group = P.group;
   p.causal = P.causal;
   p.window = P.window;
   p.scale_log2 = a->scale * 1.4426950408889634f;
-  p.part_o = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_po) : nullptr;
-  if (P.splits > 1 &&
-      (rc = make_tmap_f32(&p.tm_part, ws + P.off_po, s.D, s.Lq, s.Hc, P.splits * s.B, "split partials")))
+  if (P.splits > 1 && (rc = make_tmap_f32(&p.tm_part, ws + P.off_po, s.D, kFwdBlockM, (int)P.n_tail, P.splits,
+                                          "split partials")))
     return rc;
   p.part_lse = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_pl) : nullptr;
   p.err = err;
@@ -494,11 +544,11 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     return fail(LTXATTN_ERR_CUDA, "fwd_bf16: the loaded kernel's register count differs from its warpgroup split");
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 setup");
   if ((rc = launch_pre_pass())) return rc;
-  e = launch_fwd_bf16(p, s.D, P.q_tiles, s.Hc, s.B, smem, st);
+  e = launch_fwd_bf16(p, s.D, smem, st);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
   if (P.splits > 1) {
     CombineParams c{};
-    c.part_o = p.part_o;
+    c.part_o = reinterpret_cast<const float*>(ws + P.off_po);
     c.part_lse = p.part_lse;
     c.out = p.out;
     c.o_sb = p.o_sb;
@@ -507,12 +557,14 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     c.lse = a->lse;
     c.lse_sb = a->lse_stride_b;
     c.lse_sh = a->lse_stride_h;
-    c.B = s.B;
     c.Hc = s.Hc;
     c.Lq = s.Lq;
     c.D = s.D;
     c.num_splits = P.splits;
     c.head_begin = s.h0;
+    c.q_blocks = P.q_tiles;
+    c.n_full = (int)P.n_full;
+    c.n_tail = (int)P.n_tail;
     e = launch_combine(c, st);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }

@@ -26,8 +26,8 @@ struct FwdParams {
   CUtensorMap tm_q;  // [D, Lq, Hq, B] box {64, 128, 1, 1}, 128B swizzle
   CUtensorMap tm_k;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
   CUtensorMap tm_v;  // [D, Lk, Hk, B] box {64, 128, 1, 1}
-  CUtensorMap tm_o;  // [D, Lq, H, B] box {64, 128, 1, 1}: the output (stored by TMA when num_splits == 1)
-  CUtensorMap tm_part;  // fp32 [D, Lq, Hc, splits*B] box {32, 128, 1, 1}: split partials (num_splits > 1)
+  CUtensorMap tm_o;  // [D, Lq, H, B] box {64, 128, 1, 1}: the output of unsplit units
+  CUtensorMap tm_part;  // fp32 [D, 256, n_tail, splits] box {32, 128, 1, 1}: partials of split units
   __nv_bfloat16* out;
   int64_t o_sb, o_sh, o_st;
   float* lse;  // natural log, may be null
@@ -39,13 +39,18 @@ struct FwdParams {
   int q_head_off;   // head coordinate of local head 0 in tm_q
   int kv_head_off;  // head coordinate of local head 0 in tm_k / tm_v
   int n_kv_tiles;
+  // Work units are (256-row query block, local head, batch), q_block fastest.
+  // Units [0, n_full) run whole, one CTA each; each of the n_tail units after
+  // them runs as num_splits CTAs over shares of its KV tiles (1-D grid of
+  // n_full + n_tail * num_splits CTAs, so the split CTAs fill the last wave).
+  int q_blocks, Hc;
+  int n_full, n_tail;
   int num_splits;
   int group;   // query heads per kv head: kv head = (kv_head_off + local head) / group
   int causal;  // key j attends query i only if j <= i (q_len == kv_len)
   int window;  // > 0: also i - j < window
   float scale_log2;  // softmax scale * log2(e)
-  float* part_o;     // [splits][B][Hc][Lq][D] fp32 (num_splits > 1)
-  float* part_lse;   // [splits][B][Hc][Lq] log2 domain (num_splits > 1)
+  float* part_lse;   // [splits][n_tail][256] log2 domain (n_tail > 0)
   int* err;
 };
 
@@ -116,7 +121,8 @@ struct CombineParams {
   int64_t o_sb, o_sh, o_st;
   float* lse;
   int64_t lse_sb, lse_sh;
-  int B, Hc, Lq, D, num_splits, head_begin;
+  int Hc, Lq, D, num_splits, head_begin;
+  int q_blocks, n_full, n_tail;  // the forward's unit split (FwdParams)
 };
 
 // Backward.  Every pointer and tensor map is based at local head 0 (the
@@ -170,8 +176,7 @@ struct BwdPrepParams {
 // Launchers (return cudaError_t of the launch).
 // Once-per-device kernel attributes (cached); call before launch_fwd_bf16.
 cudaError_t prepare_fwd_bf16(int D, size_t smem_bytes);
-cudaError_t launch_fwd_bf16(const FwdParams& p, int D, int q_tiles, int Hc, int B,
-                            size_t smem_bytes, cudaStream_t s);
+cudaError_t launch_fwd_bf16(const FwdParams& p, int D, size_t smem_bytes, cudaStream_t s);
 size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);

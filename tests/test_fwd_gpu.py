@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import oracle
-from ltxattn import AttentionBackend, Rotary, device_status, inputs, scaled_dot_product_attention
+from ltxattn import AttentionBackend, Rotary, device_info, device_status, inputs, scaled_dot_product_attention
 
 pytestmark = pytest.mark.gpu
 
@@ -195,6 +195,33 @@ def test_split_kv_matches_single_pass(splits):
     assert np.abs(lse.cpu().numpy() - ref_lse).max() < LSE_ABS
     one, lse1 = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True, num_splits=1)
     assert (out.float() - one.float()).abs().max().item() <= 2e-2
+
+
+def _partials_bytes(splits, n_tail, D):
+    a256 = lambda x: (x + 255) // 256 * 256
+    return a256(splits * n_tail * 256 * D * 4) + a256(splits * n_tail * 256 * 4)
+
+
+@pytest.mark.parametrize("D,Lq,Lk,extra", [(64, 160, 1024, 12), (128, 256, 2048, 20)])
+def test_thin_last_wave_splits_only_the_tail_units(D, Lq, Lk, extra):
+    # one 256-row query block per head and sm_count + extra heads: the planner
+    # splits the KV range of the `extra` units of the thin last wave only
+    sms = device_info()["sm_count"]
+    B, H = 1, sms + extra
+    q, k, v = make(41, B, H, Lq, Lk, D, torch.bfloat16)
+    qd, kd, vd = dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16)
+    prep = AttentionBackend.prepare(qd, kd, vd, save_lse=True)
+    ws = 0 if prep.workspace is None else prep.workspace.numel()
+    assert 0 < ws <= _partials_bytes(32, extra, D), ws  # partials of the tail units only
+    out, lse = prep.run()
+    one, lse1 = AttentionBackend.attention(qd, kd, vd, save_lse=True, num_splits=1)
+    assert (out.float() - one.float()).abs().max().item() <= 2e-2
+    assert (lse - lse1).abs().max().item() <= LSE_ABS
+    # the oracle on the split heads and on a few whole ones
+    hs = list(range(H - extra - 4, H))
+    ref, ref_lse = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs])
+    check(out[:, hs], ref, torch.bfloat16, f"D={D} tail heads")
+    assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
