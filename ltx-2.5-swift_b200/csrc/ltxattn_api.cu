@@ -298,6 +298,8 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
     if (P->splits == 1) P->n_tail = 0;
   }
   P->n_full = P->units - P->n_tail;
+  if (P->n_full + P->n_tail * P->splits > (int64_t)INT32_MAX)
+    return fail(LTXATTN_ERR_UNSUPPORTED, "%lld query blocks exceed one launch", (long long)P->units);
   size_t off = 0;
   P->off_q = off;
   if (P->rope_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
@@ -604,11 +606,13 @@ int ltxattn_qk_prep(const ltxattn_qk_prep_args* a, void* stream) {
   p.tokens = s.Lq;
   p.inner = inner;
   p.D = s.D;
-  auto m8 = [](int64_t v) { return v % 8 == 0; };
-  p.vec = bf16 && aligned16(a->x) && m8(a->x_stride_b) && m8(a->x_stride_t) && aligned16(a->weight) &&
+  const int64_t per16 = bf16 ? 8 : 4;  // elements per 16 bytes
+  auto m8 = [per16](int64_t v) { return v % per16 == 0; };
+  p.vec = aligned16(a->x) && m8(a->x_stride_b) && m8(a->x_stride_t) && aligned16(a->weight) &&
           aligned16(a->out.data) && m8(a->out.stride_b) && m8(a->out.stride_h) && m8(a->out.stride_t) &&
           (a->rotary.cos == nullptr || (aligned16(a->rotary.cos) && aligned16(a->rotary.sin) &&
                                         m8(a->rotary.stride_b) && m8(a->rotary.stride_h) && m8(a->rotary.stride_t)));
+  p.err = device_error_word();
   const cudaError_t e = launch_qk_prep(p, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "qk_prep launch");
 }

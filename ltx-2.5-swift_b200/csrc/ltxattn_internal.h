@@ -99,7 +99,8 @@ struct QkPrepParams {
   void* out;  // [B, H, tokens, D] view
   int64_t o_sb, o_sh, o_st;
   int B, tokens, inner, D;
-  int vec;  // every row, table and output address is 16-byte aligned (bf16 vector path)
+  int vec;  // every row, weight, table and output address is 16-byte aligned (vector loads and stores)
+  int* err;  // device error word (bounded waits)
 };
 cudaError_t launch_qk_prep(const QkPrepParams& p, bool bf16, cudaStream_t s);
 

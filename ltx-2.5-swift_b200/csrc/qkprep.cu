@@ -9,140 +9,289 @@
 // fp32, r = 1 / sqrt(mean + eps), each element is normalised in fp32 and cast
 // to the activation dtype, then multiplied by the weight (also cast):
 //   y = T(w * T(x * r)).
-// RoPE then rounds every product and sum to bf16 (rope_bf16x8), or runs in
-// plain fp32 for fp32 activations.
+// RoPE then rounds every product and sum to bf16 (bf16x2 arithmetic), or runs
+// in plain fp32 for fp32 activations.
 //
-// One block per token row; inner / 16 threads hold 16 elements each.  The
-// mean square reduces in a fixed order (warp shuffles, then warp partials in
-// warp order), so results are deterministic.  The normalised row is staged in
-// shared memory so that each thread can take 8 rotary pairs (d, d + D/2) of
-// one head; the outputs go straight into the [B, H, T, D] view.
+// Thread i of a row holds elements [16i, 16i + 16): 16 values of one half of
+// one head (D / 16 threads per head, so a head's lower and upper halves sit
+// D / 32 lanes apart in the same warp and RoPE pairs meet by warp shuffle).
+// The mean square reduces in a fixed order (each thread's even and odd
+// products in two sequential f32x2 lanes, warp shuffles, then warp partials in
+// warp order), so results are deterministic.  Blocks walk rows with a grid stride; each thread keeps its
+// weight slice in registers, loads the next row's x before working on the
+// current one, and issues the current row's table loads before the reduction,
+// so a block has two rows' loads in flight and one barrier per row.
+#include <algorithm>
+
 #include "ltxattn_internal.h"
 #include "sm100.cuh"
 
 namespace ltx {
 namespace {
 
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+#ifndef LTX_QK_MIN_BLOCKS_BF16
+#define LTX_QK_MIN_BLOCKS_BF16 1
+#endif
+
+// 16 consecutive elements of one row: two (bf16) or four (fp32) 16-byte words.
+template <typename T>
+struct Raw16 {
+  uint4 w[sizeof(T)];
+};
 
 template <typename T>
-__device__ __forceinline__ float tof(T v);
-template <>
-__device__ __forceinline__ float tof<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ void load16(Raw16<T>& r, const T* src, bool vec) {
+  if (vec) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int i = 0; i < (int)sizeof(T); ++i) r.w[i] = s4[i];
+  } else {
+    T* d = reinterpret_cast<T*>(r.w);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) d[e] = src[e];
+  }
+}
 
 template <typename T>
-__device__ __forceinline__ float cast_t(float v);
-template <>
-__device__ __forceinline__ float cast_t<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ float cast_t<__nv_bfloat16>(float v) { return bf16r(v); }
+__device__ __forceinline__ void store16(T* dst, const Raw16<T>& r, bool vec) {
+  if (vec) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < (int)sizeof(T); ++i) d4[i] = r.w[i];
+  } else {
+    const T* d = reinterpret_cast<const T*>(r.w);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) dst[e] = d[e];
+  }
+}
 
+// y = T(w * T(x * r)), then split RoPE (lower half  out = y c - y' s,  upper
+// half  out = y c + y' s,  y' = the partner lane's value of the same pair;
+// products and sums rounded to T), stored to the thread's 16 output elements.
 template <typename T>
-__device__ __forceinline__ void store_t(T* p, float v);
-template <>
-__device__ __forceinline__ void store_t<float>(float* p, float v) { *p = v; }
-template <>
-__device__ __forceinline__ void store_t<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
-
-template <typename T>
-__global__ void __launch_bounds__(512) qk_prep_kernel(const QkPrepParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  T* srow = reinterpret_cast<T*>(smem_raw);                  // the normalised row
-  float* wsum = reinterpret_cast<float*>(smem_raw + (size_t)p.inner * sizeof(T));  // per-warp partials
-  const int row = blockIdx.x;  // b * T + t
-  const int b = row / p.tokens, t = row - (row / p.tokens) * p.tokens;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const T* x = static_cast<const T*>(p.x) + (int64_t)b * p.x_sb + (int64_t)t * p.x_st;
-  const T* w = static_cast<const T*>(p.w);
-
-  // 1. mean square of the row (fp32), fixed reduction order
-  float xv[16], wv[16];
-  bool loaded = false;
+__device__ __forceinline__ void finish_row(const Raw16<T>& xc, const Raw16<T>& wr, float r, bool rope,
+                                           const Raw16<T>& cr, const Raw16<T>& sr, bool lower, int partner,
+                                           T* out, bool vec) {
+  Raw16<T> yr;
   if constexpr (sizeof(T) == 2) {
-    if (p.vec) {  // 16-byte rows: two vector loads each for x and the weight
-      const uint4* xs = reinterpret_cast<const uint4*>(x + tid * 16);
-      const uint4* ws = reinterpret_cast<const uint4*>(w + tid * 16);
+    // pairs: T(x r) by one f32x2 multiply and one packing conversion, then
+    // T(w * that) as one bf16x2 multiply (the product of two bf16 values is
+    // exact in fp32, so a single rounding gives the same bits)
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(xc.w);
+    const uint32_t* ww = reinterpret_cast<const uint32_t*>(wr.w);
+    uint32_t* yw = reinterpret_cast<uint32_t*>(yr.w);
+    const float2 r2 = make_float2(r, r);
 #pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const uint4 a = xs[v], c = __ldg(ws + v);
-        const uint32_t au[4] = {a.x, a.y, a.z, a.w}, cu[4] = {c.x, c.y, c.z, c.w};
+    for (int k = 0; k < 8; ++k) {
+      const float2 xr = mul2(make_float2(__uint_as_float(xw[k] << 16), __uint_as_float(xw[k] & 0xffff0000u)), r2);
+      yw[k] = bmul2(pack_bf16x2(xr.x, xr.y), ww[k]);
+    }
+  } else {
+    T* y = reinterpret_cast<T*>(yr.w);
+    const T* w = reinterpret_cast<const T*>(wr.w);
+    const T* xe = reinterpret_cast<const T*>(xc.w);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          xv[8 * v + 2 * k] = __uint_as_float(au[k] << 16);
-          xv[8 * v + 2 * k + 1] = __uint_as_float(au[k] & 0xffff0000u);
-          wv[8 * v + 2 * k] = __uint_as_float(cu[k] << 16);
-          wv[8 * v + 2 * k + 1] = __uint_as_float(cu[k] & 0xffff0000u);
-        }
+    for (int e = 0; e < 16; ++e) y[e] = __fmul_rn(w[e], __fmul_rn(xe[e], r));
+  }
+  Raw16<T> outr = yr;
+  if (rope) {
+    Raw16<T> pr;
+#pragma unroll
+    for (int i = 0; i < (int)sizeof(T); ++i) {
+      pr.w[i].x = __shfl_xor_sync(0xffffffffu, yr.w[i].x, partner);
+      pr.w[i].y = __shfl_xor_sync(0xffffffffu, yr.w[i].y, partner);
+      pr.w[i].z = __shfl_xor_sync(0xffffffffu, yr.w[i].z, partner);
+      pr.w[i].w = __shfl_xor_sync(0xffffffffu, yr.w[i].w, partner);
+    }
+    if constexpr (sizeof(T) == 2) {
+      const uint32_t* a = reinterpret_cast<const uint32_t*>(yr.w);
+      const uint32_t* a2 = reinterpret_cast<const uint32_t*>(pr.w);
+      const uint32_t* c = reinterpret_cast<const uint32_t*>(cr.w);
+      const uint32_t* sn = reinterpret_cast<const uint32_t*>(sr.w);
+      uint32_t* o = reinterpret_cast<uint32_t*>(outr.w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t ac = bmul2(a[i], c[i]), ps = bmul2(a2[i], sn[i]);
+        o[i] = lower ? bsub2(ac, ps) : badd2(ac, ps);
       }
-      loaded = true;
+    } else {
+      const float* a = reinterpret_cast<const float*>(yr.w);
+      const float* a2 = reinterpret_cast<const float*>(pr.w);
+      const float* c = reinterpret_cast<const float*>(cr.w);
+      const float* sn = reinterpret_cast<const float*>(sr.w);
+      float* o = reinterpret_cast<float*>(outr.w);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float ac = __fmul_rn(a[e], c[e]), ps = __fmul_rn(a2[e], sn[e]);
+        o[e] = lower ? __fsub_rn(ac, ps) : __fadd_rn(ac, ps);
+      }
     }
   }
-  if (!loaded) {
+  store16<T>(out, outr, vec);
+}
+
+// Sum of squares of the thread's 16 values, then over the warp (fixed order:
+// even and odd elements in two f32x2 lanes, in sequence, then their sum).
+template <typename T>
+__device__ __forceinline__ float warp_sumsq(const Raw16<T>& xc) {
+  float ss;
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(xc.w);
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      xv[e] = tof<T>(x[tid * 16 + e]);
-      wv[e] = tof<T>(w[tid * 16 + e]);
+    for (int k = 0; k < 8; ++k) {
+      const float2 v = make_float2(__uint_as_float(xw[k] << 16), __uint_as_float(xw[k] & 0xffff0000u));
+      acc = fma2(v, v, acc);
     }
-  }
-  float ss = 0.f;
+    ss = acc.x + acc.y;
+  } else {
+    const float* xe = reinterpret_cast<const float*>(xc.w);
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int e = 0; e < 16; ++e) ss = fmaf(xv[e], xv[e], ss);
+    for (int k = 0; k < 8; ++k) {
+      const float2 v = make_float2(xe[2 * k], xe[2 * k + 1]);
+      acc = fma2(v, v, acc);
+    }
+    ss = acc.x + acc.y;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) wsum[warp] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += wsum[i];
-  const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)p.inner), p.eps));
+  return ss;
+}
 
-  // 2. y = T(w * T(x * r)) into shared memory
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const int i = tid * 16 + e;
-    const float n = cast_t<T>(__fmul_rn(xv[e], r));
-    store_t<T>(srow + i, __fmul_rn(wv[e], n));
-  }
-  __syncthreads();
-
-  // 3. head split (+ split RoPE): thread tid takes 8 pairs (d, d + D/2) of one head
+// Register path (any alignment): x of the next row is loaded into registers
+// before the current row is worked on.
+template <typename T>
+__global__ void __launch_bounds__(512, sizeof(T) == 2 ? LTX_QK_MIN_BLOCKS_BF16 : 1) qk_prep_kernel(const QkPrepParams p) {
+  __shared__ float wsum[2][16];  // per-warp partials, alternating by row
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int rows = p.B * p.tokens;
+  const int e0 = tid * 16;
+  const int h = e0 / p.D, d0 = e0 - h * p.D;
   const int half = p.D / 2;
-  const int groups = half / 8;  // 8-pair groups per head
-  const int h = tid / groups, j0 = (tid - h * groups) * 8;
-  const T* y1 = srow + h * p.D + j0;
-  const T* y2 = y1 + half;
-  T* o = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)t * p.o_st + j0;
-  if (p.cos == nullptr) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      o[e] = y1[e];
-      o[half + e] = y2[e];
+  const bool lower = d0 < half;  // holds x1 of its pairs (x2 sits D / 32 lanes up)
+  const int j0 = lower ? d0 : d0 - half;
+  const int partner = p.D / 32;
+  const bool rope = p.cos != nullptr;
+
+  Raw16<T> wr;  // the weight slice, kept packed
+  load16<T>(wr, static_cast<const T*>(p.w) + e0, p.vec);
+
+  int row = blockIdx.x;
+  Raw16<T> xr;
+  if (row < rows) {
+    const int b = row / p.tokens, t = row - b * p.tokens;
+    load16<T>(xr, static_cast<const T*>(p.x) + (int64_t)b * p.x_sb + (int64_t)t * p.x_st + e0, p.vec);
+  }
+  int par = 0;
+  for (; row < rows; row += gridDim.x, par ^= 1) {
+    const int b = row / p.tokens, t = row - b * p.tokens;
+    Raw16<T> cr, sr;
+    if (rope) {
+      const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + j0;
+      load16<T>(cr, static_cast<const T*>(p.cos) + toff, p.vec);
+      load16<T>(sr, static_cast<const T*>(p.sin) + toff, p.vec);
     }
-    return;
+    const Raw16<T> xc = xr;  // this row's x, packed
+    const int nrow = row + gridDim.x;
+    if (nrow < rows) {
+      const int nb = nrow / p.tokens, nt = nrow - nb * p.tokens;
+      load16<T>(xr, static_cast<const T*>(p.x) + (int64_t)nb * p.x_sb + (int64_t)nt * p.x_st + e0, p.vec);
+    }
+    const float ss = warp_sumsq<T>(xc);
+    if (lane == 0) wsum[par][warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nwarps; ++i) tot += wsum[par][i];
+    const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)p.inner), p.eps));
+    T* out = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)t * p.o_st + d0;
+    finish_row<T>(xc, wr, r, rope, cr, sr, lower, partner, out, p.vec);
   }
-  const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + j0;
-  const T* cs = static_cast<const T*>(p.cos) + toff;
-  const T* sn = static_cast<const T*>(p.sin) + toff;
-  if constexpr (sizeof(T) == 2) {
-    if (p.vec) {
-      const uint4 a1 = *reinterpret_cast<const uint4*>(y1), a2 = *reinterpret_cast<const uint4*>(y2);
-      const uint4 c = __ldg(reinterpret_cast<const uint4*>(cs)), s = __ldg(reinterpret_cast<const uint4*>(sn));
-      uint4 o1, o2;
-      rope_bf16x8(a1, a2, c, s, o1, o2);
-      *reinterpret_cast<uint4*>(o) = o1;
-      *reinterpret_cast<uint4*>(o + half) = o2;
-      return;
+}
+
+// Bulk path (16-byte aligned rows): thread 0 streams whole x rows into a ring
+// of `stages` shared-memory rows with 1-D bulk copies (cp.async.bulk, one
+// mbarrier per stage), so each block keeps up to `stages` rows in flight; a
+// stage is refilled as soon as the block's per-row barrier shows that every
+// thread has read it.  Waits are bounded; a wait that gives up ends every
+// thread of the block at that row's barrier, and thread 0 drains the copies
+// still in flight before the block exits.
+template <typename T>
+__global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p, int stages) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float wsum[2][16];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int rows = p.B * p.tokens, G = gridDim.x;
+  const uint32_t row_bytes = (uint32_t)p.inner * sizeof(T);
+  T* ring = reinterpret_cast<T*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)stages * row_bytes);
+  const int e0 = tid * 16;
+  const int h = e0 / p.D, d0 = e0 - h * p.D;
+  const int half = p.D / 2;
+  const bool lower = d0 < half;
+  const int j0 = lower ? d0 : d0 - half;
+  const int partner = p.D / 32;
+  const bool rope = p.cos != nullptr;
+  auto row_src = [&](int r) {
+    const int b = r / p.tokens, t = r - b * p.tokens;
+    return static_cast<const T*>(p.x) + (int64_t)b * p.x_sb + (int64_t)t * p.x_st;
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(full + s, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int issued = 0;  // pipeline slots whose copy thread 0 has issued (slot k: row blockIdx.x + k * G)
+  if (tid == 0) {
+    for (; issued < stages && blockIdx.x + issued * G < rows; ++issued) {
+      mbar_arrive_expect_tx(full + issued, row_bytes);
+      bulk_load(ring + (size_t)issued * p.inner, row_src(blockIdx.x + issued * G), row_bytes, full + issued);
     }
   }
+  Raw16<T> wr;
+  load16<T>(wr, static_cast<const T*>(p.w) + e0, true);
+
+  int i = 0, par = 0;
+  for (int row = blockIdx.x; row < rows; row += G, ++i, par ^= 1) {
+    const int b = row / p.tokens, t = row - b * p.tokens;
+    Raw16<T> cr, sr;
+    if (rope) {
+      const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + j0;
+      load16<T>(cr, static_cast<const T*>(p.cos) + toff, true);
+      load16<T>(sr, static_cast<const T*>(p.sin) + toff, true);
+    }
+    const int s = i % stages;
+    const bool ok = mbar_wait(full + s, (uint32_t)(i / stages) & 1u, &abort_flag, p.err, 40);
+    Raw16<T> xc;
+    if (ok) {
+      const uint4* src = reinterpret_cast<const uint4*>(ring + (size_t)s * p.inner + e0);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float a1 = tof<T>(y1[e]), a2 = tof<T>(y2[e]), c = tof<T>(cs[e]), s = tof<T>(sn[e]);
-    const float o1 = cast_t<T>(__fsub_rn(cast_t<T>(__fmul_rn(a1, c)), cast_t<T>(__fmul_rn(a2, s))));
-    const float o2 = cast_t<T>(__fadd_rn(cast_t<T>(__fmul_rn(a2, c)), cast_t<T>(__fmul_rn(a1, s))));
-    store_t<T>(o + e, o1);
-    store_t<T>(o + half + e, o2);
+      for (int k = 0; k < (int)sizeof(T); ++k) xc.w[k] = src[k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < (int)sizeof(T); ++k) xc.w[k] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    const float ss = warp_sumsq<T>(xc);
+    if (lane == 0) wsum[par][warp] = ss;
+    if (!__syncthreads_and(ok)) break;
+    // every thread has read stage s: refill it with slot i + stages
+    if (tid == 0 && issued == i + stages && blockIdx.x + issued * G < rows) {
+      mbar_arrive_expect_tx(full + s, row_bytes);
+      bulk_load(ring + (size_t)s * p.inner, row_src(blockIdx.x + issued * G), row_bytes, full + s);
+      ++issued;
+    }
+    float tot = 0.f;
+    for (int k = 0; k < nwarps; ++k) tot += wsum[par][k];
+    const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)p.inner), p.eps));
+    T* out = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)t * p.o_st + d0;
+    finish_row<T>(xc, wr, r, rope, cr, sr, lower, partner, out, true);
   }
+  // never leave with a bulk copy still writing this block's shared memory
+  if (tid == 0)
+    for (int k = i; k < issued; ++k) drain_wait(full + k % stages, (uint32_t)(k / stages) & 1u);
 }
 
 }  // namespace
@@ -151,11 +300,32 @@ cudaError_t launch_qk_prep(const QkPrepParams& p, bool bf16, cudaStream_t s) {
   const int rows = p.B * p.tokens;
   if (rows == 0) return cudaSuccess;
   const int threads = p.inner / 16;
-  const size_t smem = (size_t)p.inner * (bf16 ? 2 : 4) + 32 * sizeof(float);
+  int dev = 0, sms = 148, per_sm = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // bulk path: as many row stages (<= 8) as fit in 47 KB of dynamic shared memory
+  const size_t row_bytes = (size_t)p.inner * (bf16 ? 2 : 4);
+  const int stages = (int)std::min<size_t>(8, (47 * 1024) / (row_bytes + 8));
+  cudaError_t e;
+  if (p.vec && stages >= 2) {
+    const size_t smem = (size_t)stages * (row_bytes + 8);
+    e = bf16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_bulk_kernel<__nv_bfloat16>, threads, smem)
+             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_bulk_kernel<float>, threads, smem);
+    if (e != cudaSuccess) return e;
+    const int grid = std::min(rows, std::max(1, per_sm) * sms);
+    if (bf16)
+      qk_prep_bulk_kernel<__nv_bfloat16><<<grid, threads, smem, s>>>(p, stages);
+    else
+      qk_prep_bulk_kernel<float><<<grid, threads, smem, s>>>(p, stages);
+    return cudaGetLastError();
+  }
+  e = bf16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_kernel<__nv_bfloat16>, threads, 0)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_kernel<float>, threads, 0);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(rows, std::max(1, per_sm) * sms);
   if (bf16)
-    qk_prep_kernel<__nv_bfloat16><<<rows, threads, smem, s>>>(p);
+    qk_prep_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(p);
   else
-    qk_prep_kernel<float><<<rows, threads, smem, s>>>(p);
+    qk_prep_kernel<float><<<grid, threads, 0, s>>>(p);
   return cudaGetLastError();
 }
 
