@@ -84,9 +84,9 @@ struct Smem {
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
   static constexpr uint32_t kOffQ0 = 0, kOffQ1 = kTile, kOffK0 = 2 * kTile, kOffK1 = 3 * kTile,
                             kOffV0 = 4 * kTile, kOffV1 = 5 * kTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full, p_half[2]
+  // q0_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full, p_half[2], q1_full
   static constexpr uint32_t kOffBar = 6 * kTile;
-  static constexpr uint32_t kOffCtl = kOffBar + 16 * 8;  // tmem slot, abort, n_tiles
+  static constexpr uint32_t kOffCtl = kOffBar + 17 * 8;  // tmem slot, abort, n_tiles
   static constexpr uint32_t kOffTiles = kOffCtl + 16;    // uint16 [kMaxKvTiles]
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;  // uint32 mask bits
 };
@@ -163,7 +163,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   uint8_t* sK = sm + S::kOffK0;
   uint8_t* sV = sm + S::kOffV0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
-  uint64_t* bar_q = bars + 0;
+  uint64_t* bar_q = bars + 0;   // Q tile 0 loaded
+  uint64_t* bar_q1 = bars + 16; // Q tile 1 loaded
   uint64_t* bar_kf = bars + 1;   // [2]
   uint64_t* bar_ke = bars + 3;   // [2]
   uint64_t* bar_vf = bars + 5;   // [2]
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
 
   // ---------------- prologue ----------------
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 16; ++i) mbar_init(bars + i, (i == 11 || i == 12 || i >= 14) ? 128 : 1);
+    for (int i = 0; i < 17; ++i) mbar_init(bars + i, (i == 11 || i == 12 || i == 14 || i == 15) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -289,12 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     // ---------------- TMA producer ----------------
     if (lane == 0 && n > 0) {
       int k_issued = 0, v_issued = 0;
-      mbar_arrive_expect_tx(bar_q, (two ? 2u : 1u) * S::kTile);
+      // issue order Q0, K0, Q1, V0, ...: S0 needs only the first two, so it can
+      // start while the rest of the CTA's first loads are still arriving
+      mbar_arrive_expect_tx(bar_q, S::kTile);
 #pragma unroll
-      for (int c = 0; c < S::kChunks; ++c) {
-        tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
-        if (two) tma_load_4d(&p.tm_q, bar_q, sQ + S::kTile + c * kChunkBytes, c * 64, q0 + kTileM, qh, b);
-      }
+      for (int c = 0; c < S::kChunks; ++c) tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
       for (int j = 0; j < n; ++j) {
         const int st = j & 1, u = j >> 1;
         const int kv0 = (int)tiles[t_begin + j] * kTileN;
@@ -304,6 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         for (int c = 0; c < S::kChunks; ++c)
           tma_load_4d(&p.tm_k, bar_kf + st, sK + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, b);
         ++k_issued;
+        if (j == 0 && two) {
+          mbar_arrive_expect_tx(bar_q1, S::kTile);
+#pragma unroll
+          for (int c = 0; c < S::kChunks; ++c)
+            tma_load_4d(&p.tm_q, bar_q1, sQ + S::kTile + c * kChunkBytes, c * 64, q0 + kTileM, qh, b);
+        }
         if (j >= 2 && !mbar_wait(bar_ve + st, (u - 1) & 1, abort_flag, p.err, 2)) break;
         mbar_arrive_expect_tx(bar_vf + st, S::kTile);
 #pragma unroll
@@ -313,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       }
       // never leave the CTA with a bulk copy still writing its shared memory
       drain_wait(bar_q, 0);
+      if (two) drain_wait(bar_q1, 0);
       for (int i = k_issued < 2 ? 0 : k_issued - 2; i < k_issued; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
       for (int i = v_issued < 2 ? 0 : v_issued - 2; i < v_issued; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
     }
@@ -329,14 +336,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       const uint32_t stage_step = S::kTile >> 4;
       auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
       auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
-      if (mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4)) {
+      bool go = mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4);
+      if (go) {
         tc_fence_after();
         issue_s<D>(tS0, dQ0, kdesc(0));
         umma_commit(bar_s + 0);
-        if (two) {
+      }
+      if (go && two) {
+        go = mbar_wait(bar_q1, 0, abort_flag, p.err, 3);
+        if (go) {
+          tc_fence_after();
           issue_s<D>(tS1, dQ1, kdesc(0));
           umma_commit(bar_s + 1);
         }
+      }
+      if (go) {
         umma_commit(bar_ke + 0);
         for (int j = 0; j < n; ++j) {
           const int st = j & 1, u = j >> 1;
