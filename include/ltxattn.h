@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define LTXATTN_ABI_VERSION 2
+#define LTXATTN_ABI_VERSION 3
 
 /* Entry points are the only symbols the library exports. */
 #if defined(__GNUC__)
@@ -112,7 +112,14 @@ typedef struct ltxattn_rotary {
  *    key_mask leave without keys attends every key instead (the reference's
  *    un-masking of fully masked rows).  kv_heads (0 = heads) must divide heads:
  *    k and v are [B, kv_heads, kv_len, D] and query head h reads kv head
- *    h / (heads / kv_heads); grouped heads take no rotary (rotate before). */
+ *    h / (heads / kv_heads); grouped heads take no rotary (rotate before).
+ *  - gate: the per-head output gate of `DiTAttention.swift:395-399`, fused
+ *    into the store of out: the `to_gate_logits` output [B, q_len, heads] in
+ *    the activation dtype T (element strides gate_stride_b / _t / _h; any
+ *    layout), or NULL.  out = T(T(O) * g), g = 2 * T(sigmoid(float(logit)))
+ *    per query row and head (the sigmoid in fp32 and cast back, `:240-242`;
+ *    the doubling is exact).  lse is not gated.  The backward wants the
+ *    un-gated out, so a training forward keeps gate NULL and gates outside. */
 typedef struct ltxattn_fwd_args {
   int32_t dtype;
   int32_t batch, heads, q_len, kv_len, head_dim;
@@ -130,6 +137,9 @@ typedef struct ltxattn_fwd_args {
   int32_t causal;
   int32_t window;
   int32_t kv_heads;
+  /* ABI 3 */
+  const void* gate;
+  int64_t gate_stride_b, gate_stride_t, gate_stride_h;
 } ltxattn_fwd_args;
 
 /* Backward arguments: gradients of sum(dout * out) with respect to q, k and v

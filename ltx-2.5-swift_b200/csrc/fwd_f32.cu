@@ -10,6 +10,7 @@
 // rows.  KV tiles of 64 keys are staged in shared memory (K rows padded by one
 // word so the per-lane dot products are bank-conflict free).
 #include "ltxattn_internal.h"
+#include "sm100.cuh"
 
 namespace ltx {
 namespace {
@@ -157,8 +158,10 @@ __global__ void __launch_bounds__(128) fwd_f32_kernel(const F32Params p) {
     if (row >= p.Lq) continue;
     const float inv = l[r] > 0.f ? 1.f / l[r] : 0.f;
     float* orow = p.out + (int64_t)b * p.o_sb + (int64_t)(p.head_begin + hl) * p.o_sh + (int64_t)row * p.o_st;
+    const float g = p.gate == nullptr ? 1.f
+                    : gate_f32(p.gate[(int64_t)b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + hl) * p.g_sh]);
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) orow[lane + 32 * e] = o[r][e] * inv;
+    for (int e = 0; e < kPer; ++e) orow[lane + 32 * e] = p.gate == nullptr ? o[r][e] * inv : (o[r][e] * inv) * g;
     if (p.lse != nullptr && lane == 0)
       p.lse[(int64_t)b * p.lse_sb + (int64_t)(p.head_begin + hl) * p.lse_sh + row] =
           l[r] > 0.f ? m[r] + logf(l[r]) : -INFINITY;

@@ -521,10 +521,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     }
 
     // epilogue
+    const Unit ue = decode_unit(p, ctaid_x_fresh());
+    // the output gate of this row and head (its load overlaps the wait for O)
+    uint32_t g2 = 0x3f803f80u;  // bf16x2 (1, 1)
+    if (p.gate != nullptr && ue.ns == 1 && row < p.Lq) {
+      const float g = gate_bf16(__bfloat162float(
+          p.gate[(int64_t)ue.b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + ue.hl) * p.g_sh]));
+      g2 = pack_bf16x2(g, g);
+    }
     const bool have_o = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 10);
     tc_fence_after();
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-    const Unit ue = decode_unit(p, ctaid_x_fresh());
     if (ue.ns == 1) {
       // Stage the normalised bf16 row in K stage t (idle once O is complete: every
       // MMA has finished and no load is outstanding), 128-byte swizzled like the
@@ -550,6 +557,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
           v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
           v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
           v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
+          if (p.gate != nullptr) {  // T(T(O) * g): one bf16x2 multiply (the product is exact in fp32)
+            v.x = bmul2(v.x, g2);
+            v.y = bmul2(v.y, g2);
+            v.z = bmul2(v.z, g2);
+            v.w = bmul2(v.w, g2);
+          }
           const int j = (c & 1) * 4 + e;  // 16-byte unit within the 64-column chunk c / 2
           *reinterpret_cast<uint4*>(srow + (c >> 1) * kChunkBytes + ((j ^ (r & 7)) << 4)) = v;
         }
@@ -649,8 +662,16 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)(p.head_begin + hl) * p.o_sh + (int64_t)row * p.o_st;
+  if (p.gate != nullptr) {  // T(T(O) * g)
+    const float g = gate_bf16(
+        __bfloat162float(p.gate[(int64_t)b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + hl) * p.g_sh]));
 #pragma unroll
-  for (int e = 0; e < kPer; ++e) orow[lane + 32 * e] = __float2bfloat16_rn(acc[e] * inv);
+    for (int e = 0; e < kPer; ++e)
+      orow[lane + 32 * e] = __float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(acc[e] * inv)) * g);
+  } else {
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) orow[lane + 32 * e] = __float2bfloat16_rn(acc[e] * inv);
+  }
   if (p.lse != nullptr && lane == 0)
     p.lse[(int64_t)b * p.lse_sb + (int64_t)(p.head_begin + hl) * p.lse_sh + row] =
         (wsum > 0.f) ? (mx + log2f(wsum)) * kLn2 : -INFINITY;

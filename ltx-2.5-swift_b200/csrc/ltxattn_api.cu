@@ -410,6 +410,8 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   if ((rc = check_tensor(a->k, "k", s, bf16 && !P.rope_k))) return rc;
   if ((rc = check_tensor(a->v, "v", s, bf16))) return rc;
   if ((rc = check_tensor(a->out, "out", s, bf16))) return rc;
+  if (a->gate != nullptr && (a->gate_stride_b < 0 || a->gate_stride_t < 0 || a->gate_stride_h < 0))
+    return fail(LTXATTN_ERR_SHAPE, "gate has a negative stride");
   if (P.total > 0) {
     if (a->workspace == nullptr || a->workspace_bytes < P.total)
       return fail(LTXATTN_ERR_WORKSPACE, "workspace of %zu bytes is needed, %zu given", P.total,
@@ -485,6 +487,8 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     p.group = P.group;
     p.causal = P.causal;
     p.window = P.window;
+    p.gate = static_cast<const float*>(a->gate);
+    p.g_sb = a->gate_stride_b; p.g_st = a->gate_stride_t; p.g_sh = a->gate_stride_h;
     e = launch_fwd_f32(p, s.D, s.Hc, s.B, st);
     if (e != cudaSuccess) return cuda_fail(e, "fwd_f32 launch");
     return LTXATTN_OK;
@@ -534,6 +538,10 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.group = P.group;
   p.causal = P.causal;
   p.window = P.window;
+  p.gate = static_cast<const __nv_bfloat16*>(a->gate);
+  p.g_sb = a->gate_stride_b;
+  p.g_st = a->gate_stride_t;
+  p.g_sh = a->gate_stride_h;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   if (P.splits > 1 && (rc = make_tmap_f32(&p.tm_part, ws + P.off_po, s.D, kFwdBlockM, (int)P.n_tail, P.splits,
                                           "split partials")))
@@ -567,6 +575,10 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     c.q_blocks = P.q_tiles;
     c.n_full = (int)P.n_full;
     c.n_tail = (int)P.n_tail;
+    c.gate = p.gate;
+    c.g_sb = p.g_sb;
+    c.g_st = p.g_st;
+    c.g_sh = p.g_sh;
     e = launch_combine(c, st);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }

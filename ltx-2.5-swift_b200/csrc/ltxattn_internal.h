@@ -51,6 +51,8 @@ struct FwdParams {
   int window;  // > 0: also i - j < window
   float scale_log2;  // softmax scale * log2(e)
   float* part_lse;   // [splits][n_tail][256] log2 domain (n_tail > 0)
+  const __nv_bfloat16* gate;  // [B, Lq, H] gate logits or null (global head index)
+  int64_t g_sb, g_st, g_sh;
   int* err;
 };
 
@@ -72,6 +74,8 @@ struct F32Params {
   int Lq, Lk, head_begin;
   float scale;
   int group, causal, window;  // as FwdParams
+  const float* gate;          // as FwdParams (fp32 logits)
+  int64_t g_sb, g_st, g_sh;
 };
 
 // Split-RoPE pre-pass: y[b][hl][t][:] = rope(x[b][head_begin+hl][t][:]) into a
@@ -124,6 +128,8 @@ struct CombineParams {
   int64_t lse_sb, lse_sh;
   int Hc, Lq, D, num_splits, head_begin;
   int q_blocks, n_full, n_tail;  // the forward's unit split (FwdParams)
+  const __nv_bfloat16* gate;     // as FwdParams
+  int64_t g_sb, g_st, g_sh;
 };
 
 // Backward.  Every pointer and tensor map is based at local head 0 (the

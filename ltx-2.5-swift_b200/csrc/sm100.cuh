@@ -522,6 +522,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// The per-head output gate of DiTAttention.swift:395-399: 2 * sigmoid(logit),
+// the sigmoid evaluated in fp32 as 1 / (1 + e^-x) (CUDA's expf, IEEE division)
+// and, for bf16 activations, cast back to bf16 before the exact doubling
+// (DiTAttention.swift:240-242).
+__device__ __forceinline__ float gate_f32(float logit) { return 2.0f * (1.0f / (1.0f + expf(-logit))); }
+__device__ __forceinline__ float gate_bf16(float logit) {
+  return 2.0f * __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-logit))));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

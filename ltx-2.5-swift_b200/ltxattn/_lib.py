@@ -51,7 +51,9 @@ class FwdArgs(ctypes.Structure):
                 ("lse", ctypes.c_void_p), ("lse_stride_b", ctypes.c_int64),
                 ("lse_stride_h", ctypes.c_int64), ("workspace", ctypes.c_void_p),
                 ("workspace_bytes", ctypes.c_size_t), ("num_splits", ctypes.c_int32),
-                ("causal", ctypes.c_int32), ("window", ctypes.c_int32), ("kv_heads", ctypes.c_int32)]
+                ("causal", ctypes.c_int32), ("window", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+                ("gate", ctypes.c_void_p), ("gate_stride_b", ctypes.c_int64), ("gate_stride_t", ctypes.c_int64),
+                ("gate_stride_h", ctypes.c_int64)]
 
 
 class RopeArgs(ctypes.Structure):

@@ -146,7 +146,7 @@ class AttentionBackend:
     @staticmethod
     def make_fwd_args(q, k, v, scale, key_mask=None, q_rotary=None, k_rotary=None, lse=None,
                       out=None, head_begin=0, head_count=0, num_splits=0, causal=False,
-                      window=0) -> Tuple[_lib.FwdArgs, torch.Tensor]:
+                      window=0, gate=None) -> Tuple[_lib.FwdArgs, torch.Tensor]:
         for name, t in (("q", q), ("k", k), ("v", v)):
             _check_cuda(name, t)
         if q.dim() != 4:
@@ -189,6 +189,13 @@ class AttentionBackend:
             a.lse_stride_b, a.lse_stride_h = lse.stride(0), lse.stride(1)
         a.num_splits = num_splits
         a.causal, a.window, a.kv_heads = int(bool(causal)), int(window), Hk
+        if gate is not None:
+            # to_gate_logits output [B, tokens, heads] (DiTAttention.swift:395-399), any strides
+            _check_cuda("gate", gate)
+            if tuple(gate.shape) != (B, Lq, H) or gate.dtype != q.dtype:
+                raise Failure.shape("gate", gate.shape, f"[{B}, {Lq}, {H}] {q.dtype}")
+            a.gate = gate.data_ptr()
+            a.gate_stride_b, a.gate_stride_t, a.gate_stride_h = gate.stride(0), gate.stride(1), gate.stride(2)
         return a, out
 
     @staticmethod
@@ -196,7 +203,7 @@ class AttentionBackend:
                 key_mask: Optional[torch.Tensor] = None, q_rotary: Optional[Rotary] = None,
                 k_rotary: Optional[Rotary] = None, save_lse: bool = False, head_begin: int = 0,
                 head_count: int = 0, num_splits: int = 0, out: Optional[torch.Tensor] = None,
-                lse: Optional[torch.Tensor] = None) -> "PreparedAttention":
+                lse: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None) -> "PreparedAttention":
         """Validate and marshal once; ``run()`` then issues just ``ltxattn_fwd``.
 
         For repeated calls on the same buffers (a render loop, a benchmark): the
@@ -207,8 +214,8 @@ class AttentionBackend:
         if save_lse and lse is None:
             lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
         a, out = AttentionBackend.make_fwd_args(q, k, v, scale, key_mask, q_rotary, k_rotary, lse, out,
-                                                head_begin, head_count, num_splits)
-        return PreparedAttention(a, out, lse, (q, k, v, key_mask, q_rotary, k_rotary))
+                                                head_begin, head_count, num_splits, gate=gate)
+        return PreparedAttention(a, out, lse, (q, k, v, key_mask, q_rotary, k_rotary, gate))
 
     @staticmethod
     def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
@@ -216,12 +223,16 @@ class AttentionBackend:
                   k_rotary: Optional[Rotary] = None, save_lse: bool = False,
                   variant: Optional[Variant] = None, head_begin: int = 0, head_count: int = 0,
                   num_splits: int = 0, out: Optional[torch.Tensor] = None,
-                  lse: Optional[torch.Tensor] = None, stream=None, causal: bool = False, window: int = 0):
+                  lse: Optional[torch.Tensor] = None, stream=None, causal: bool = False, window: int = 0,
+                  gate: Optional[torch.Tensor] = None):
         """Fused split-RoPE + SDPA.  Returns ``(out, lse)``; lse is None unless requested.
 
         ``causal`` / ``window`` / grouped KV heads (``k`` with fewer heads than ``q``)
         give the Gemma text encoder's self-attention (GemmaTextEncoder.swift:218-233,
-        292-323); the DiT's attention uses none of them.
+        292-323); the DiT's attention uses none of them.  ``gate`` ([B, tokens, heads]
+        ``to_gate_logits`` output) fuses the per-head gate out * 2*sigmoid(logit)
+        (DiTAttention.swift:395-399) into the store; ``out`` may be the merged
+        [B, tokens, heads * headDim] buffer seen as [B, heads, tokens, headDim].
         """
         if variant is not None and q_rotary is not None and not variant.takes_rotary:
             raise Failure.rotary_without_position(variant)
@@ -230,7 +241,7 @@ class AttentionBackend:
         if save_lse and lse is None:
             lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
         a, out = AttentionBackend.make_fwd_args(q, k, v, scale, key_mask, q_rotary, k_rotary, lse, out,
-                                                head_begin, head_count, num_splits, causal, window)
+                                                head_begin, head_count, num_splits, causal, window, gate)
         L = _lib.load()
         ws_bytes = int(L.ltxattn_fwd_workspace(ctypes.byref(a)))
         ws = None

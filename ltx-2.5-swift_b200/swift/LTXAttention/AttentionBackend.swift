@@ -41,6 +41,17 @@ public enum AttentionBackend {
         }
     }
 
+    /// The `to_gate_logits` output [B, T, heads] on the device (DiTAttention.swift:395-399),
+    /// element strides (b, t, h) in the activation dtype.
+    public struct DeviceGate {
+        public var logits: UnsafeRawPointer
+        public var strides: (b: Int64, t: Int64, h: Int64)
+        public init(logits: UnsafeRawPointer, strides: (b: Int64, t: Int64, h: Int64)) {
+            self.logits = logits
+            self.strides = strides
+        }
+    }
+
     /// Mirrors DiTAttention.Failure (DiTAttention.swift:107-122) for library errors.
     public struct Failure: Error, CustomStringConvertible {
         public let status: Int32
@@ -57,12 +68,15 @@ public enum AttentionBackend {
     /// (`keyRotary ?? rotary`, DiTAttention.swift:366).  `causal`, `window` and
     /// `kvHeads` give the Gemma encoder's self-attention
     /// (GemmaTextEncoder.swift:218-233, mask :292-323); the DiT passes none.
+    /// `gate` fuses the per-head gate `out * 2 * sigmoid(logits)` (DiTAttention.swift:395-399)
+    /// into the store; with `out` viewing the merged [B, T, heads * headDim] buffer the
+    /// transpose of :401-403 is free as well, so `to_out` reads the result directly.
     public static func attention(
         bf16: Bool, batch: Int32, heads: Int32, queryTokens: Int32, keyTokens: Int32, headDim: Int32,
         q: DeviceTensor, k: DeviceTensor, v: DeviceTensor, out: DeviceTensor, scale: Float,
         keyMask: UnsafePointer<UInt8>? = nil, rotary: DeviceRotary? = nil, keyRotary: DeviceRotary? = nil,
         lse: UnsafeMutablePointer<Float>? = nil, workspace: UnsafeMutableRawPointer?, workspaceBytes: Int,
-        causal: Bool = false, window: Int32 = 0, kvHeads: Int32 = 0,
+        causal: Bool = false, window: Int32 = 0, kvHeads: Int32 = 0, gate: DeviceGate? = nil,
         stream: UnsafeMutableRawPointer?
     ) throws {
         var a = ltxattn_fwd_args()
@@ -84,6 +98,12 @@ public enum AttentionBackend {
         a.causal = causal ? 1 : 0
         a.window = window
         a.kv_heads = kvHeads
+        if let gate {
+            a.gate = gate.logits
+            a.gate_stride_b = gate.strides.b
+            a.gate_stride_t = gate.strides.t
+            a.gate_stride_h = gate.strides.h
+        }
         try check(ltxattn_fwd(&a, stream))
     }
 

@@ -234,3 +234,23 @@ def attention_gemma(q, k, v, valid=None, scale=1.0, causal=True, window=0):
                                      int(causal), int(window), _p(out), _p(lse))
     assert rc == 0
     return out, lse
+
+
+def gate_value(logits, bf16=True):
+    """The per-head gate 2 * sigmoid(logit) of DiTAttention.swift:395-396: the
+    sigmoid in fp32 and cast back to the activation dtype (:240-242; here fp64
+    rounded to fp32, then to bf16 for bf16 activations), then the exact doubling."""
+    x = _f32(logits).astype(np.float64)
+    s = (1.0 / (1.0 + np.exp(-x))).astype(np.float32)
+    if bf16:
+        s = round_bf16(s)
+    return (2.0 * s).astype(np.float32)
+
+
+def gate_output(out, logits, bf16=True):
+    """out [B, H, T, D] (values in the activation dtype) times the gate of
+    logits [B, T, H], broadcast over D and rounded to the activation dtype
+    (DiTAttention.swift:397-399: `out * gates.transposed(0, 2, 1)[..., None]`)."""
+    g = gate_value(logits, bf16).transpose(0, 2, 1)[..., None]
+    y = (_f32(out).astype(np.float64) * g.astype(np.float64)).astype(np.float32)
+    return round_bf16(y) if bf16 else y

@@ -33,7 +33,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
     exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln and "ltxattn_" in ln}
     assert exported == declared, f"exports differ from the header: {exported ^ declared}"
-    assert L.ltxattn_abi_version() == 2
+    assert L.ltxattn_abi_version() == 3
 
 
 PROBE = r"""
@@ -55,6 +55,7 @@ int main(void) {
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
   P(ltxattn_fwd_args, causal) P(ltxattn_fwd_args, window) P(ltxattn_fwd_args, kv_heads)
+  P(ltxattn_fwd_args, gate) P(ltxattn_fwd_args, gate_stride_b) P(ltxattn_fwd_args, gate_stride_h)
   P(ltxattn_bwd_args, dout) P(ltxattn_bwd_args, lse) P(ltxattn_bwd_args, dq) P(ltxattn_bwd_args, scale)
   P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
   P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
@@ -153,6 +154,16 @@ def test_grouped_kv_heads_take_no_rotary():
     a.q_rotary = _lib.Rotary(cos=1024, sin=2048, stride_b=0, stride_h=0, stride_t=32, tokens=16)
     assert L.ltxattn_fwd(ctypes.byref(a), None) == _lib.ERR_UNSUPPORTED
     assert "grouped KV heads" in _lib.last_error()
+
+
+def test_gate_strides_must_be_non_negative():
+    L = _lib.load()
+    a = _args()
+    for name in ("q", "k", "v", "out"):
+        setattr(a, name, _lib.Tensor(data=4096, stride_b=2 * 16 * 64, stride_h=16 * 64, stride_t=64))
+    a.gate, a.gate_stride_b, a.gate_stride_t, a.gate_stride_h = 8192, 32, 2, -1
+    assert L.ltxattn_fwd(ctypes.byref(a), None) == _lib.ERR_SHAPE
+    assert "gate has a negative stride" in _lib.last_error()
 
 
 def test_new_entry_points_refuse_bad_arguments():
