@@ -255,13 +255,114 @@ def run_qkprep(args):
                        "parallelism": f"heads x{ws}", "l2": L2_NOTE},
             "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / ws / hbm, 4), "peak_source": f"{src} hbm_gbs",
-                         "algorithmic_bytes": step_bytes, "kernel": "qk_prep_kernel", "traffic": None},
+                         "algorithmic_bytes": step_bytes, "kernel": "qk_prep_bulk_kernel", "traffic": None},
             "step_ms": {"median": round(statistics.median(step_ms), 5), "min": round(min(step_ms), 5),
                         "max": round(max(step_ms), 5)},
             "e2e": {"value": round(step_bytes * ws / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(h.numel() * 2 for h in hx),
                     "d2h_bytes_per_step": sum(h.numel() * 2 for h in ho)},
             "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_module(args):
+    """One whole video self-attention module (DiTAttention.callAsFunction) at the
+    config-2 shape: x [1, 3120, 4096] -> [1, 3120, 4096], 32 heads of 128, biases,
+    q/k norms, the gate, 3D RoPE.  Projections on the library GEMM, the rest in
+    libltxattn_cuda.  TFLOP/s of the module's GEMM + attention FLOPs."""
+    import torch
+    import torch.distributed as dist
+    from ltxattn import DiTAttentionModule, Rotary, inputs
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    B, T, H, D = 1, 3120, 32, 128
+    dim = inner = H * D
+    g = torch.Generator(device="cuda").manual_seed(1000 + 97 * rank)
+    dt = torch.bfloat16
+
+    def mat(o, i):
+        return (torch.randn((o, i), device="cuda", generator=g) / math.sqrt(i)).to(dt)
+
+    def vec(n, lo=-0.1, hi=0.1):
+        return (lo + (hi - lo) * torch.rand(n, device="cuda", generator=g)).to(dt)
+
+    w = {"to_q.weight": mat(inner, dim), "to_q.bias": vec(inner), "to_k.weight": mat(inner, dim),
+         "to_k.bias": vec(inner), "to_v.weight": mat(inner, dim), "to_v.bias": vec(inner),
+         "to_out.0.weight": mat(dim, inner), "to_out.0.bias": vec(dim), "q_norm.weight": vec(inner, 0.5, 1.5),
+         "k_norm.weight": vec(inner, 0.5, 1.5), "to_gate_logits.weight": mat(H, dim), "to_gate_logits.bias": vec(H)}
+    mod = DiTAttentionModule(w, H)
+    x = torch.from_numpy(inputs.seeded_tensor(1000 + 97 * rank, (B, T, dim))).to("cuda", dt)
+    c, sn = inputs.rope3d_grid(13, 12, 20, D)
+    rot = Rotary(torch.from_numpy(c).to("cuda", dt), torch.from_numpy(sn).to("cuda", dt))
+    flush = L2Flush(torch)
+    stream = torch.cuda.current_stream()
+    gemm_flops = 2.0 * B * T * dim * inner * 4 + 2.0 * B * T * dim * H
+    attn_flops = 4.0 * B * H * T * T * D
+    flops = gemm_flops + attn_flops
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    clocks.start()
+    for _ in range(args.warmup):
+        mod(x, rotary=rot)
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush()
+        evs[i][0].record(stream)
+        mod(x, rotary=rot)
+        evs[i][1].record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    hx = x.cpu().pin_memory()
+    ho = torch.empty((B, T, dim), dtype=dt).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(hx, non_blocking=True)
+        y = mod(x, rotary=rot)
+        ho.copy_(y, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    vals = torch.tensor([statistics.median(step_ms), e2e_ms], device="cuda", dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = vals.tolist()
+    burst, sustained, _, src = peaks()
+    tf = flops * ws / (ms * 1e-3) / 1e12
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "DiT attention module TFLOP/s bf16 (projections + fused attention) @3120-tok video self-attn "
+                      "(aggregate over GPUs)",
+            "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, random-init weights of the module's shapes)",
+            "config": {"workload": "module: DiTAttention attn1, x [1, 3120, 4096], 32 heads x 128, gate, 3D RoPE",
+                       "parallelism": f"dp{ws}", "l2": L2_NOTE,
+                       "flops_per_step": {"gemm": gemm_flops, "attention": attn_flops}},
+            "roofline": {"bound": "tensor", "achieved": round(tf / ws, 1), "peak": burst, "unit": "TFLOP/s",
+                         "frac": round(tf / ws / burst, 4), "peak_source": f"{src} bf16_tflops (burst)",
+                         "kernel": "whole module (cuBLAS GEMMs + qk_prep + fwd_bf16_sm100_kernel)", "traffic": None},
+            "e2e": {"value": round(flops * ws / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2},
+            "gpu_launches": 3 * args.steps,  # qk_prep for q and k, the attention (gate fused); GEMMs are cuBLAS
             "clocks": clk,
         }
     if ws > 1:
@@ -542,7 +643,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + ["qkprep"])
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + ["qkprep", "module"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--bwd", action="store_true", help="also time the training backward")
@@ -552,6 +653,9 @@ def main():
     if args.workload == "qkprep":
         res = (run_reference(args) if args.impl == "reference" else run_qkprep(args)) \
             if args.impl != "reference" else {"impl": "reference", "unavailable": "no CPU arm for the qkprep workload"}
+    elif args.workload == "module":
+        res = {"impl": "reference", "unavailable": "no CPU arm for the module workload"} \
+            if args.impl == "reference" else run_module(args)
     else:
         res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:

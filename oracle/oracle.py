@@ -254,3 +254,35 @@ def gate_output(out, logits, bf16=True):
     g = gate_value(logits, bf16).transpose(0, 2, 1)[..., None]
     y = (_f32(out).astype(np.float64) * g.astype(np.float64)).astype(np.float32)
     return round_bf16(y) if bf16 else y
+
+
+def dit_attention_module(x, w, heads, cos=None, sin=None, k_cos=None, k_sin=None, context=None):
+    """DiTAttention.callAsFunction (DiTAttention.swift:315-404) for bf16
+    activations, on the CPU: every projection is an fp64 matmul rounded to bf16
+    plus a bf16-rounded bias add (:178-189); q and k take ``qk_prep`` (rmsNorm
+    over the inner dim, split, split RoPE with ``k_cos/k_sin`` or else the q
+    tables for k, :358-367); the attention is ``attn_fwd`` rounded to bf16; the
+    gate (when ``to_gate_logits.weight`` is present) ``gate_output``; then the
+    merge and ``to_out.0``.  ``w`` maps checkpoint names without the block
+    prefix to float32 arrays holding bf16 values."""
+    def lin(a, name):
+        y = round_bf16(a.astype(np.float64) @ w[name + ".weight"].astype(np.float64).T)
+        if name + ".bias" in w:
+            y = round_bf16(y.astype(np.float64) + w[name + ".bias"].astype(np.float64))
+        return y
+    kv = x if context is None else context
+    B, T, _ = x.shape
+    Tk = kv.shape[1]
+    inner = w["to_q.weight"].shape[0]
+    D = inner // heads
+    v = lin(kv, "to_v")
+    q = qk_prep(lin(x, "to_q"), w["q_norm.weight"], heads, 1e-6, cos, sin, bf16=True)
+    kc, ks = (k_cos, k_sin) if k_cos is not None else (cos, sin)
+    k = qk_prep(lin(kv, "to_k"), w["k_norm.weight"], heads, 1e-6, kc, ks, bf16=True)
+    vh = np.ascontiguousarray(v.reshape(B, Tk, heads, D).transpose(0, 2, 1, 3))
+    out, _ = attn_fwd(q, k, vh)
+    out = round_bf16(out)
+    if "to_gate_logits.weight" in w:
+        out = gate_output(out, lin(x, "to_gate_logits"), True)
+    merged = np.ascontiguousarray(out.transpose(0, 2, 1, 3).reshape(B, T, inner))
+    return lin(merged, "to_out.0")
