@@ -51,7 +51,7 @@ BOUND = {"c2": "tensor", "c3": "hbm", "c4a": "hbm", "c4b": "hbm", "c4c": "hbm", 
 
 
 # DRAM bytes per attention launch measured by ncu (profiles/fwd_bf16_sm100_c2.md)
-TRAFFIC = {"c2": 85.8e6}
+TRAFFIC = {"c2": 83.2e6}
 
 
 class L2Flush:
