@@ -188,25 +188,34 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   const int Lk = p.Lk;
 
   // ---------------- prologue ----------------
-  if (threadIdx.x == 0) {
+  // The producer thread initialises the barriers and starts the Q0 load at
+  // once: Q does not depend on the key mask or the tile list, so its latency
+  // overlaps the rest of the prologue.  (Every other thread first touches a
+  // barrier after the __syncthreads below.)
+  const int qh = p.q_head_off + hl;
+  if (warp == 8 && lane == 0) {
     for (int i = 0; i < 17; ++i) mbar_init(bars + i, (i == 11 || i == 12 || i == 14 || i == 15) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&p.tm_q);
+    mbar_arrive_expect_tx(bar_q, S::kTile);
+#pragma unroll
+    for (int c = 0; c < S::kChunks; ++c) tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+    tma_prefetch_desc(&p.tm_o);
+    if (un.ns > 1) tma_prefetch_desc(&p.tm_part);
   }
   if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
     tc_fence_before();
   }
-  if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&p.tm_q);
-    tma_prefetch_desc(&p.tm_k);
-    tma_prefetch_desc(&p.tm_v);
-    tma_prefetch_desc(&p.tm_o);
-    if (un.ns > 1) tma_prefetch_desc(&p.tm_part);
-  }
 
-  // key-mask bits (padded with zero words to a whole tile)
+  // key-mask bits (padded with zero words to a whole tile), one 32-key word
+  // per thread: two 16-byte loads when the rows are aligned, else byte loads: word w is one
+  // warp's ballot over keys 32w .. 32w + 31, each lane reading one mask byte;
+  // a warp loads up to four words before it ballots
   bool use_mask = p.mask != nullptr;
   int local_any = 0;
   if (use_mask) {
@@ -215,10 +224,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     for (int w = threadIdx.x; w < nwords; w += kThreads) {
       uint32_t bits = 0;
       const int k0 = w * 32;
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i) {
-        const int key = k0 + i;
-        if (key < Lk && mrow[key] != 0) bits |= 1u << i;
+      if (p.mask_vec && k0 + 32 <= Lk) {
+        // two 16-byte loads, then per byte "nonzero" as one bit
+        const uint4 lo = *reinterpret_cast<const uint4*>(mrow + k0);
+        const uint4 hi = *reinterpret_cast<const uint4*>(mrow + k0 + 16);
+        const uint32_t wd[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t m = __vcmpne4(wd[i], 0u);  // 0xff in each nonzero byte
+          bits |= (((m >> 7) & 1u) | ((m >> 14) & 2u) | ((m >> 21) & 4u) | ((m >> 28) & 8u)) << (4 * i);
+        }
+      } else {
+        for (int i = 0; i < 32; ++i) {
+          const int key = k0 + i;
+          if (key < Lk && mrow[key] != 0) bits |= 1u << i;
+        }
       }
       mbits[w] = bits;
       local_any |= (bits != 0);
@@ -281,20 +301,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   const int t_begin = (int)(((int64_t)un.split * n_all) / un.ns);
   const int t_end = (int)(((int64_t)(un.split + 1) * n_all) / un.ns);
   const int n = t_end - t_begin;
-  const int qh = p.q_head_off + hl;
   const int kvh = (p.kv_head_off + hl) / p.group;  // grouped query heads share a kv head
 
   if (warp >= 8) {
     setmaxnreg_dec<kProducerRegs>();
     if (warp == 8) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       int k_issued = 0, v_issued = 0;
-      // issue order Q0, K0, Q1, V0, ...: S0 needs only the first two, so it can
-      // start while the rest of the CTA's first loads are still arriving
-      mbar_arrive_expect_tx(bar_q, S::kTile);
-#pragma unroll
-      for (int c = 0; c < S::kChunks; ++c) tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
+      bool q1_issued = false;
+      // issue order Q0 (already in flight), K0, Q1, V0, ...: S0 needs only the
+      // first two, so it can start while the CTA's other first loads arrive
       for (int j = 0; j < n; ++j) {
         const int st = j & 1, u = j >> 1;
         const int kv0 = (int)tiles[t_begin + j] * kTileN;
@@ -305,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
           tma_load_4d(&p.tm_k, bar_kf + st, sK + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, b);
         ++k_issued;
         if (j == 0 && two) {
+          q1_issued = true;
           mbar_arrive_expect_tx(bar_q1, S::kTile);
 #pragma unroll
           for (int c = 0; c < S::kChunks; ++c)
@@ -319,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       }
       // never leave the CTA with a bulk copy still writing its shared memory
       drain_wait(bar_q, 0);
-      if (two) drain_wait(bar_q1, 0);
+      if (q1_issued) drain_wait(bar_q1, 0);
       for (int i = k_issued < 2 ? 0 : k_issued - 2; i < k_issued; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
       for (int i = v_issued < 2 ? 0 : v_issued - 2; i < v_issued; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
     }

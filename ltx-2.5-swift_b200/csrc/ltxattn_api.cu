@@ -524,6 +524,7 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   p.lse_sh = a->lse_stride_h;
   p.mask = a->key_mask;
   p.mask_sb = a->key_mask_stride_b;
+  p.mask_vec = a->key_mask != nullptr && aligned16(a->key_mask) && (s.B == 1 || a->key_mask_stride_b % 16 == 0);
   p.Lq = s.Lq;
   p.Lk = s.Lk;
   p.head_begin = s.h0;

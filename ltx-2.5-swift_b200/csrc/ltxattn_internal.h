@@ -34,6 +34,7 @@ struct FwdParams {
   int64_t lse_sb, lse_sh;
   const uint8_t* mask;  // [B, Lk] or null
   int64_t mask_sb;
+  int mask_vec;  // every mask row is 16-byte aligned (vector loads)
   int Lq, Lk;
   int head_begin;   // global index of local head 0 (out / lse / mask addressing)
   int q_head_off;   // head coordinate of local head 0 in tm_q

@@ -117,6 +117,24 @@ def test_key_padding_masks(dtype):
     assert np.abs(lse.cpu().numpy() - ref_lse).max() < (1e-5 if dtype == torch.float32 else LSE_ABS)
 
 
+def test_unaligned_mask_rows_give_the_same_result():
+    # aligned rows take 16-byte loads, unaligned ones byte loads: same bits, same output
+    B, H, Lq, Lk, D = 2, 2, 130, 300, 64
+    q, k, v = make(29, B, H, Lq, Lk, D, torch.bfloat16)
+    rng = np.random.default_rng(9)
+    m = (rng.random((B, Lk)) < 0.5).astype(np.uint8)
+    qd, kd, vd = dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16)
+    aligned = torch.from_numpy(m).cuda()
+    wide = torch.zeros((B, Lk + 1), dtype=torch.uint8, device="cuda")
+    wide[:, 1:] = aligned
+    odd = wide[:, 1:]  # base and row stride not 16-byte multiples
+    a, _ = AttentionBackend.attention(qd, kd, vd, key_mask=aligned)
+    b, _ = AttentionBackend.attention(qd, kd, vd, key_mask=odd)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    ref, _ = oracle.attn_fwd(q, k, v, mask=m)
+    check(a, ref, torch.bfloat16, "aligned mask")
+
+
 def test_mask_with_one_valid_key_returns_that_value_row():
     B, H, Lq, Lk, D = 1, 2, 64, 700, 64
     q, k, v = make(13, B, H, Lq, Lk, D, torch.bfloat16)
