@@ -178,7 +178,8 @@ int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
 // tail units' O (written and read back) at ~5 TB/s plus ~3 us for its launch.
 // The cheapest choice must beat no split by 1.5%.  (29,760 tokens and 4 heads
 // per GPU: 468 units = 3 waves + 24, split 6 ways; 32 heads at 3,120 tokens:
-// 416 units, no split.)
+// 416 units, no split; 126 queries against 3,120 keys, 32 heads: all 32 units
+// split 4 ways, one wave.)
 struct SplitChoice {
   int64_t n_tail;
   int splits;
@@ -280,11 +281,16 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
       P->n_tail = units;
     } else if (a->num_splits == 0) {
       const int sms = current_sm_count();
-      if (units < sms && P->kv_tiles > 1) {
-        const int want = (int)((2 * (int64_t)sms + units - 1) / units);
-        P->splits = std::max(1, std::min({want, P->kv_tiles, kMaxSplits}));
+      const bool opaque = a->key_mask != nullptr || P->causal || P->window > 0;  // per-unit work unknown
+      if (units < sms && P->kv_tiles > 1 && opaque) {
+        // fewer units than SMs: as many splits as keep one wave
+        P->splits = std::max(1, std::min({(int)(sms / units), P->kv_tiles, kMaxSplits}));
         P->n_tail = units;
-      } else if (units >= sms && (a->key_mask != nullptr || P->causal || P->window > 0)) {
+      } else if (units < sms && P->kv_tiles > 1) {
+        const SplitChoice c = tail_splits(units, sms, P->kv_tiles, s.D);
+        P->splits = c.splits;
+        P->n_tail = c.n_tail;
+      } else if (units >= sms && opaque) {
         P->splits = uniform_splits(units, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
         P->n_tail = units;
       } else if (units >= sms) {
