@@ -413,10 +413,15 @@ def run_ours(args):
     def step():
         call.run(stream)
 
-    # without rotary tables the only scratch is the split-KV partials: a workspace
-    # means the planner split some units and the call adds a combine launch
-    splits = kernel_call.workspace is not None
-    launches_per_step = 1 + (1 if qrot is not None else 0) + (1 if splits else 0)
+    # what the library launches per call (ltxattn_fwd_plan): RoPE pre-pass,
+    # attention kernel, split combine
+    import ctypes
+    from ltxattn import _lib
+    plan, kplan = _lib.FwdPlanInfo(), _lib.FwdPlanInfo()
+    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(call.args), ctypes.byref(plan)) == 0
+    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(kernel_call.args), ctypes.byref(kplan)) == 0
+    launches_per_step = plan.launches
+    kernel_name = "fwd_short_sm100_kernel" if kplan.kernel == 2 else "fwd_bf16_sm100_kernel"
     flops = 4.0 * B * Hc * Lq * Lk * D
     if mask is not None:
         eff_flops = 4.0 * B * Hc * Lq * WORKLOADS[wl][6] * D
@@ -552,7 +557,7 @@ def run_ours(args):
                           "frac": round(kern_gbs / hbm, 4), "peak_source": f"{src} hbm_gbs",
                           "algorithmic_bytes": algorithmic_bytes(wl, B, Hc, Lq, Lk, D),
                           "kernel_tflops": round(achieved, 2)}) | {
-                         "kernel": "fwd_bf16_sm100_kernel", "kernel_ms": round(kern_avg_ms, 5),
+                         "kernel": kernel_name, "kernel_ms": round(kern_avg_ms, 5),
                          # dram__bytes_read.sum + dram__bytes_write.sum of one launch, from the ncu
                          # capture summarised in profiles/fwd_bf16_sm100_c2.md (config 2 only)
                          "traffic": TRAFFIC.get(wl)},

@@ -172,6 +172,17 @@ LTXATTN_API int ltxattn_fwd(const ltxattn_fwd_args* args, void* stream);
 /* Device scratch bytes ltxattn_fwd needs for these arguments. */
 LTXATTN_API size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* args);
 
+/* What ltxattn_fwd will launch for these arguments (introspection for
+ * benchmarks and logs; no counterpart in the reference). */
+typedef struct ltxattn_fwd_plan_info {
+  int32_t kernel;       /* 0: fp32 path; 1: tiled bf16 forward; 2: persistent bf16 forward (kv_len <= 128) */
+  int32_t splits;       /* KV splits of the split units (1: none) */
+  int64_t units;        /* 256-row query blocks x heads x batch (bf16) or 128-row blocks (fp32) */
+  int64_t split_units;  /* how many of them run split */
+  int32_t launches;     /* kernel launches of one call: RoPE pre-pass + attention + combine */
+} ltxattn_fwd_plan_info;
+LTXATTN_API int ltxattn_fwd_plan(const ltxattn_fwd_args* args, ltxattn_fwd_plan_info* info);
+
 /* ltxattn_fwd for callers that cannot allocate device memory -- for example a
  * host whose device memory is owned by another framework's allocator, or a
  * render loop that must not allocate between steps.  No counterpart in the

@@ -242,6 +242,8 @@ struct FwdPlan {
   int causal, window;
   int q_tiles, kv_tiles, splits;
   int64_t units, n_full, n_tail;  // bf16: n_tail units split `splits` ways after n_full whole ones
+  bool short_kv;                  // bf16, one KV tile, more units than SMs: the persistent kernel
+  int sms;
   size_t off_q, off_k, off_po, off_pl, total;
 };
 
@@ -274,6 +276,8 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   P->splits = 1;
   P->units = (int64_t)P->q_tiles * s.Hc * s.B;
   P->n_tail = 0;
+  P->short_kv = false;
+  P->sms = 0;
   if (s.dtype == LTXATTN_BF16) {
     const int64_t units = P->units;
     if (a->num_splits > 0) {
@@ -281,11 +285,17 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
       P->n_tail = units;
     } else if (a->num_splits == 0) {
       const int sms = current_sm_count();
+      P->sms = sms;
+      // one KV tile and more units than SMs: a persistent CTA per SM overlaps
+      // its units (fwd_short_sm100.cu); no split
+      P->short_kv = P->kv_tiles == 1 && !P->causal && P->window == 0 && units > sms;
       const bool opaque = a->key_mask != nullptr || P->causal || P->window > 0;  // per-unit work unknown
       if (units < sms && P->kv_tiles > 1 && opaque) {
         // fewer units than SMs: as many splits as keep one wave
         P->splits = std::max(1, std::min({(int)(sms / units), P->kv_tiles, kMaxSplits}));
         P->n_tail = units;
+      } else if (P->short_kv) {
+        P->splits = 1;
       } else if (units < sms && P->kv_tiles > 1) {
         const SplitChoice c = tail_splits(units, sms, P->kv_tiles, s.D);
         P->splits = c.splits;
@@ -403,6 +413,20 @@ size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* a) {
   FwdPlan P;
   if (plan_fwd(a, &P) != LTXATTN_OK) return 0;
   return P.total;
+}
+
+int ltxattn_fwd_plan(const ltxattn_fwd_args* a, ltxattn_fwd_plan_info* info) {
+  if (info == nullptr) return fail(LTXATTN_ERR_ARG, "info is NULL");
+  FwdPlan P;
+  const int rc = plan_fwd(a, &P);
+  if (rc) return rc;
+  const bool bf16 = P.s.dtype == LTXATTN_BF16;
+  info->kernel = !bf16 ? 0 : (P.short_kv ? 2 : 1);
+  info->splits = P.splits;
+  info->units = P.units;
+  info->split_units = P.n_tail;
+  info->launches = 1 + ((P.rope_q || P.rope_k) ? 1 : 0) + (P.splits > 1 ? 1 : 0);
+  return LTXATTN_OK;
 }
 
 int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
@@ -561,6 +585,15 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     return fail(LTXATTN_ERR_CUDA, "fwd_bf16: the loaded kernel's register count differs from its warpgroup split");
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 setup");
   if ((rc = launch_pre_pass())) return rc;
+  if (P.short_kv) {
+    e = prepare_fwd_short(s.D);
+    if (e == cudaErrorInvalidConfiguration)
+      return fail(LTXATTN_ERR_CUDA, "fwd_short: the loaded kernel's register count differs from its warpgroup split");
+    if (e != cudaSuccess) return cuda_fail(e, "fwd_short setup");
+    e = launch_fwd_short(p, s.D, (int)P.units, P.sms, st);
+    if (e != cudaSuccess) return cuda_fail(e, "fwd_short launch");
+    return LTXATTN_OK;
+  }
   e = launch_fwd_bf16(p, s.D, smem, st);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
   if (P.splits > 1) {

@@ -186,6 +186,9 @@ struct BwdPrepParams {
 cudaError_t prepare_fwd_bf16(int D, size_t smem_bytes);
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, size_t smem_bytes, cudaStream_t s);
 size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
+// Persistent forward for kv_len <= 128 (one KV tile); see fwd_short_sm100.cu.
+cudaError_t prepare_fwd_short(int D);
+cudaError_t launch_fwd_short(const FwdParams& p, int D, int units, int sms, cudaStream_t s);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);
 // Rotate one tensor (b == nullptr) or two in one launch.

@@ -139,6 +139,20 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// The same barrier, returning whether `pred` held in every participating thread.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMEM allocation (one full warp executes these)
 

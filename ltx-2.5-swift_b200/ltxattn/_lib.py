@@ -22,7 +22,7 @@ STATUS_NAMES = {OK: "ok", ERR_SHAPE: "shape", ERR_DTYPE: "dtype", ERR_ALIGN: "al
 F32, BF16 = 0, 1
 
 EXPORTED = (
-    "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
+    "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_plan", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
     "ltxattn_rope", "ltxattn_rotary_tables", "ltxattn_qk_prep",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
@@ -54,6 +54,11 @@ class FwdArgs(ctypes.Structure):
                 ("causal", ctypes.c_int32), ("window", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
                 ("gate", ctypes.c_void_p), ("gate_stride_b", ctypes.c_int64), ("gate_stride_t", ctypes.c_int64),
                 ("gate_stride_h", ctypes.c_int64)]
+
+
+class FwdPlanInfo(ctypes.Structure):
+    _fields_ = [("kernel", ctypes.c_int32), ("splits", ctypes.c_int32), ("units", ctypes.c_int64),
+                ("split_units", ctypes.c_int64), ("launches", ctypes.c_int32)]
 
 
 class RopeArgs(ctypes.Structure):
@@ -125,6 +130,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_fwd_noalloc.restype = ctypes.c_int
     L.ltxattn_fwd_workspace.argtypes = [ctypes.POINTER(FwdArgs)]
     L.ltxattn_fwd_workspace.restype = ctypes.c_size_t
+    L.ltxattn_fwd_plan.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(FwdPlanInfo)]
+    L.ltxattn_fwd_plan.restype = ctypes.c_int
     L.ltxattn_bwd.argtypes = [ctypes.POINTER(BwdArgs), vp]
     L.ltxattn_bwd.restype = ctypes.c_int
     L.ltxattn_bwd_workspace.argtypes = [ctypes.POINTER(BwdArgs)]

@@ -51,11 +51,13 @@ int main(void) {
   printf("ltxattn_rope_args %zu\n", sizeof(ltxattn_rope_args));
   printf("ltxattn_rotary_table_args %zu\n", sizeof(ltxattn_rotary_table_args));
   printf("ltxattn_qk_prep_args %zu\n", sizeof(ltxattn_qk_prep_args));
+  printf("ltxattn_fwd_plan_info %zu\n", sizeof(ltxattn_fwd_plan_info));
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
   P(ltxattn_fwd_args, causal) P(ltxattn_fwd_args, window) P(ltxattn_fwd_args, kv_heads)
   P(ltxattn_fwd_args, gate) P(ltxattn_fwd_args, gate_stride_b) P(ltxattn_fwd_args, gate_stride_h)
+  P(ltxattn_fwd_plan_info, units) P(ltxattn_fwd_plan_info, split_units) P(ltxattn_fwd_plan_info, launches)
   P(ltxattn_bwd_args, dout) P(ltxattn_bwd_args, lse) P(ltxattn_bwd_args, dq) P(ltxattn_bwd_args, scale)
   P(ltxattn_bwd_args, k_rotary) P(ltxattn_bwd_args, workspace_bytes)
   P(ltxattn_rotary, tokens) P(ltxattn_device_info, total_memory_bytes) P(ltxattn_device_info, supported)
@@ -79,13 +81,14 @@ def test_ctypes_layout_matches_the_header(tmp_path):
     sizes = {"ltxattn_tensor": _lib.Tensor, "ltxattn_rotary": _lib.Rotary, "ltxattn_fwd_args": _lib.FwdArgs,
              "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
              "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs,
-             "ltxattn_rotary_table_args": _lib.RotaryTableArgs, "ltxattn_qk_prep_args": _lib.QkPrepArgs}
+             "ltxattn_rotary_table_args": _lib.RotaryTableArgs, "ltxattn_qk_prep_args": _lib.QkPrepArgs,
+             "ltxattn_fwd_plan_info": _lib.FwdPlanInfo}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
                "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
                "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs,
-               "ltxattn_qk_prep_args": _lib.QkPrepArgs}
+               "ltxattn_qk_prep_args": _lib.QkPrepArgs, "ltxattn_fwd_plan_info": _lib.FwdPlanInfo}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")
@@ -154,6 +157,26 @@ def test_grouped_kv_heads_take_no_rotary():
     a.q_rotary = _lib.Rotary(cos=1024, sin=2048, stride_b=0, stride_h=0, stride_t=32, tokens=16)
     assert L.ltxattn_fwd(ctypes.byref(a), None) == _lib.ERR_UNSUPPORTED
     assert "grouped KV heads" in _lib.last_error()
+
+
+@pytest.mark.parametrize("shape,want", [
+    # (B, H, Lq, Lk, D), (kernel, splits, split_units, launches); 148 SMs (no device here)
+    ((1, 32, 3120, 3120, 128), (1, 1, 0, 1)),     # config 2: 416 units, no split
+    ((1, 32, 3120, 126, 64), (2, 1, 0, 1)),       # config 4b: one KV tile -> persistent kernel
+    ((1, 32, 126, 3120, 64), (1, 4, 32, 2)),      # config 4c: one wave of 4-way splits + combine
+    ((1, 4, 29760, 29760, 128), (1, 6, 24, 2)),   # config 5 on 8 GPUs: the last 24 units split 6 ways
+    ((1, 32, 126, 126, 64), (1, 1, 0, 1)),        # config 4a: 32 units, one KV tile, nothing to split
+])
+def test_forward_plan(shape, want):
+    B, H, Lq, Lk, D = shape
+    a = _lib.FwdArgs()
+    a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, B, H, Lq, Lk, D
+    info = _lib.FwdPlanInfo()
+    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK, _lib.last_error()
+    assert (info.kernel, info.splits, info.split_units, info.launches) == want
+    a.dtype = _lib.F32
+    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK
+    assert info.kernel == 0 and info.splits == 1
 
 
 def test_gate_strides_must_be_non_negative():
