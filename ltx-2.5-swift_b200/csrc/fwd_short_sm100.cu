@@ -11,25 +11,29 @@
 // and overlaps consecutive units:
 //   - the producer loads Q of unit i+1 as soon as the S MMAs of unit i have
 //     read Q, and K/V only when the (kv head, batch) changes;
-//   - the MMA thread issues S of unit i+1 right after P V of unit i, while the
-//     softmax warps run unit i's epilogue;
-//   - each softmax warpgroup stages its O rows in its own shared-memory tile
-//     and stores them with TMA, waiting for the previous unit's store to have
-//     read the staging area only when it needs it again.
+//   - the MMA thread issues S of unit i+1 right behind P V of unit i, per Q
+//     tile (PV0_i, S0_{i+1}, PV1_i, S1_{i+1}), so the two tiles' softmaxes
+//     alternate on the exponential unit instead of competing for it;
+//   - a dedicated epilogue warpgroup normalises, gates and stores unit i's O
+//     (staged in shared memory, stored with TMA) while the softmax warpgroups
+//     already work on unit i+1.
 // The arithmetic per row is the forward kernel's with a single KV tile (the
 // same exponentials, the same P rounding, the same row-sum order), so both
 // kernels give the same bits.
 //
-// Warp roles as in the forward kernel: warps 0-3 softmax + epilogue of Q tile
-// 0, warps 4-7 of Q tile 1, warp 8 TMA producer (lane 0), warp 9 TMEM owner
-// and MMA issuer (lane 0).  TMEM: S0 [0,128), S1 [128,256), O0 [256,256+D),
-// O1 [384,384+D); P_t overwrites the first 64 columns of S_t.  Both Q tiles
-// of a unit are always computed; a tile past q_len reads zeros and is not
-// stored.
+// 512 threads: warps 0-3 softmax of Q tile 0, warps 4-7 of Q tile 1, warp 8
+// TMA producer (lane 0), warp 9 TMEM owner and MMA issuer (lane 0), warps
+// 12-15 the epilogue of both tiles (thread r owns row r of each; warps 10-11
+// idle).  Registers: launched at 128 per thread, the softmax warpgroups take
+// 184 and the other two 72 (2*128*184 + 2*128*72 = 512*128).  TMEM: S0
+// [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D); P_t overwrites the
+// first 64 columns of S_t.  The softmax hands each row's max and sum to the
+// epilogue through shared memory, double-buffered by unit.  Both Q tiles of a
+// unit are always computed; a tile past q_len reads zeros and is not stored.
 //
-// Every wait is bounded.  A softmax warpgroup decides to stop only at a
-// reducing named barrier that all four of its warps reach each unit, so a
-// timeout seen by one warp never leaves another parked at a barrier.
+// Every wait is bounded.  A warpgroup decides to stop only at a reducing named
+// barrier that all four of its warps reach each unit, so a timeout seen by one
+// warp never leaves another parked at a barrier.
 #include <mutex>
 
 #include "fwd_common.cuh"
@@ -38,16 +42,29 @@ namespace ltx {
 
 namespace {
 
+constexpr int kShortThreads = 512;
+constexpr uint32_t kShortLaunchRegs = 128;  // 65536 / 512
+constexpr uint32_t kShortSoftmaxRegs = 184;
+constexpr uint32_t kShortOtherRegs = 72;
+static_assert(2 * 128 * kShortSoftmaxRegs + 2 * 128 * kShortOtherRegs <= kShortThreads * kShortLaunchRegs,
+              "register re-split exceeds the launch allocation");
+
+// Q is double-buffered where shared memory allows (D = 64: the next unit's Q
+// loads a whole unit ahead); with D = 128 one buffer fits beside K, V and the
+// staging tiles.
 template <int D>
 struct ShortSmem {
   static constexpr int kChunks = D / 64;
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
-  static constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 3 * kTile, kOffO = 4 * kTile;
-  // q_full, q_free, kv_full, kv_free, s_full[2], p_half[2], p_full[2], o_full, o_free[2], mma_done
-  static constexpr int kBars = 14;
-  static constexpr uint32_t kOffBar = 6 * kTile;
+  static constexpr int kQBuf = D == 64 ? 2 : 1;
+  static constexpr uint32_t kOffQ = 0, kOffK = 2 * kQBuf * kTile, kOffV = kOffK + kTile, kOffO = kOffV + kTile;
+  // q_full[2], q_free[2], kv_full, kv_free, s_full[2], p_half[2], p_full[2], o_full, o_free[2],
+  // mma_done, stat[2 unit parities][2 tiles]
+  static constexpr int kBars = 20;
+  static constexpr uint32_t kOffBar = kOffO + 2 * kTile;
   static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
-  static constexpr uint32_t kBytes = kOffCtl + 16;
+  static constexpr uint32_t kOffRow = kOffCtl + 16;         // float2 (max, sum) [2 units][2 tiles][128 rows]
+  static constexpr uint32_t kBytes = kOffRow + 2 * 2 * 128 * 8;
 };
 
 struct ShortUnit {
@@ -64,28 +81,33 @@ __device__ __forceinline__ ShortUnit short_unit(const FwdParams& p, int unit) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kShortThreads, 1)
     fwd_short_sm100_kernel(const __grid_constant__ FwdParams p, int per_cta, int units) {
   using S = ShortSmem<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* sQ = sm + S::kOffQ;  // Q tile t at sQ + t * kTile
+  uint8_t* sQ = sm + S::kOffQ;  // Q tile t of buffer qb at sQ + (2 * qb + t) * kTile
   uint8_t* sK = sm + S::kOffK;
   uint8_t* sV = sm + S::kOffV;
   uint8_t* sO = sm + S::kOffO;  // epilogue staging of tile t at sO + t * kTile
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
-  uint64_t* bar_qfull = bars + 0;
-  uint64_t* bar_qfree = bars + 1;
-  uint64_t* bar_kvfull = bars + 2;
-  uint64_t* bar_kvfree = bars + 3;
-  uint64_t* bar_s = bars + 4;      // [2]
-  uint64_t* bar_ph = bars + 6;     // [2]
-  uint64_t* bar_p = bars + 8;      // [2]
-  uint64_t* bar_o = bars + 10;
-  uint64_t* bar_ofree = bars + 11; // [2]
-  uint64_t* bar_done = bars + 13;
+  uint64_t* bar_qfull = bars + 0;  // [Q buffer]
+  uint64_t* bar_qfree = bars + 2;  // [Q buffer]
+  uint64_t* bar_kvfull = bars + 4;
+  uint64_t* bar_kvfree = bars + 5;
+  uint64_t* bar_s = bars + 6;      // [2]
+  uint64_t* bar_ph = bars + 8;     // [2]
+  uint64_t* bar_p = bars + 10;     // [2]
+  uint64_t* bar_o = bars + 12;
+  uint64_t* bar_ofree = bars + 13; // [2]
+  uint64_t* bar_done = bars + 15;
+  // (max, sum) of unit i's rows of tile t written: stat[(i & 1) * 2 + t], one
+  // phase every second unit, so the epilogue (which must release O of unit i
+  // before the softmax can reach unit i + 2) never sees it two phases ahead
+  uint64_t* bar_stat = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+  float2* rowstat = reinterpret_cast<float2*>(sm + S::kOffRow);  // [(i & 1) * 2 + t][row]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -93,7 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cnt = min(per_cta, units - u0);
 
   if (warp == 8 && lane == 0) {
-    for (int i = 0; i < S::kBars; ++i) mbar_init(bars + i, (i >= 6 && i <= 9) || i == 11 || i == 12 ? 128 : 1);
+    for (int i = 0; i < S::kBars; ++i)
+      mbar_init(bars + i, (i >= 8 && i <= 11) || i == 13 || i == 14 || i >= 16 ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
@@ -110,8 +133,81 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8) {
-    setmaxnreg_dec<kProducerRegs>();
+  if (warp >= 12) {
+    setmaxnreg_dec<kShortOtherRegs>();
+    // ---------------- epilogue of both Q tiles ----------------
+    const int r = threadIdx.x & 127;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < cnt; ++i) {
+      const ShortUnit u = short_unit(p, u0 + i);
+      ok = ok && warp_wait(bar_o, i & 1, abort_flag, p.err, 27);
+      tc_fence_after();
+      if (r == 0) bulk_wait_read();  // the previous unit's store has read the staging tiles
+      named_barrier(3, 128);
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        const int row = u.q0 + t * kTileM + r;
+        ok = ok && warp_wait(bar_stat + (i & 1) * 2 + t, (i >> 1) & 1, abort_flag, p.err, 28);
+        const float2 ms = rowstat[((i & 1) * 2 + t) * 128 + r];
+        const float l = ms.y;
+        const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+        uint32_t g2 = 0x3f803f80u;  // bf16x2 (1, 1)
+        if (p.gate != nullptr && row < p.Lq) {
+          const float g = gate_bf16(__bfloat162float(
+              p.gate[(int64_t)u.b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + u.hl) * p.g_sh]));
+          g2 = pack_bf16x2(g, g);
+        }
+        const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+        uint8_t* srow = sO + t * S::kTile + r * 128;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv_l, __uint_as_float(o[8 * e + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
+            if (p.gate != nullptr) {
+              v.x = bmul2(v.x, g2);
+              v.y = bmul2(v.y, g2);
+              v.z = bmul2(v.z, g2);
+              v.w = bmul2(v.w, g2);
+            }
+            const int j = (c & 1) * 4 + e;
+            *reinterpret_cast<uint4*>(srow + (c >> 1) * kChunkBytes + ((j ^ (r & 7)) << 4)) = v;
+          }
+        }
+        // O_t is in registers and shared memory: the next unit's P V may overwrite it
+        tc_fence_before();
+        mbar_arrive(bar_ofree + t);
+        if (p.lse != nullptr && row < p.Lq) {
+          p.lse[(int64_t)u.b * p.lse_sb + (int64_t)(p.head_begin + u.hl) * p.lse_sh + row] =
+              (l > 0.f) ? (ms.x + log2f(l)) * kLn2 : -INFINITY;
+        }
+      }
+      fence_proxy_async_smem();  // the bulk copy reads these rows through the async proxy
+      const bool all_ok = named_barrier_and(3, 128, ok);
+      if (r == 0 && all_ok) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (u.q0 + t * kTileM >= p.Lq) continue;
+#pragma unroll
+          for (int ch = 0; ch < S::kChunks; ++ch)
+            tma_store_4d(&p.tm_o, sO + t * S::kTile + ch * kChunkBytes, ch * 64, u.q0 + t * kTileM,
+                         p.head_begin + u.hl, u.b);
+        }
+        bulk_commit();
+      }
+      if (!all_ok) break;
+    }
+    if (r == 0) bulk_wait_read();  // the CTA's shared memory must outlive the copies' reads
+  } else if (warp >= 8) {
+    setmaxnreg_dec<kShortOtherRegs>();
     if (warp == 8) {
       // ---------------- TMA producer ----------------
       if (lane == 0) {
@@ -119,17 +215,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < cnt; ++i) {
           const ShortUnit u = short_unit(p, u0 + i);
           const int qh = p.q_head_off + u.hl;
-          if (i > 0 && !mbar_wait(bar_qfree, (i - 1) & 1, abort_flag, p.err, 20)) break;
-          mbar_arrive_expect_tx(bar_qfull, 2 * S::kTile);
+          const int qb = i % S::kQBuf, qn = i / S::kQBuf;  // buffer, and its use count
+          // the S MMAs of the unit that last used this buffer must have read it
+          if (i >= S::kQBuf && !mbar_wait(bar_qfree + qb, (qn - 1) & 1, abort_flag, p.err, 20)) break;
+          uint8_t* dst = sQ + 2 * qb * S::kTile;
+          mbar_arrive_expect_tx(bar_qfull + qb, 2 * S::kTile);
 #pragma unroll
           for (int c = 0; c < S::kChunks; ++c) {
-            tma_load_4d(&p.tm_q, bar_qfull, sQ + c * kChunkBytes, c * 64, u.q0, qh, u.b);
-            tma_load_4d(&p.tm_q, bar_qfull, sQ + S::kTile + c * kChunkBytes, c * 64, u.q0 + kTileM, qh, u.b);
+            tma_load_4d(&p.tm_q, bar_qfull + qb, dst + c * kChunkBytes, c * 64, u.q0, qh, u.b);
+            tma_load_4d(&p.tm_q, bar_qfull + qb, dst + S::kTile + c * kChunkBytes, c * 64, u.q0 + kTileM, qh, u.b);
           }
           ++q_issued;
           if (u.kv_key != kv_prev) {
-            // the previous unit's P V must have read V (and its S MMAs K)
-            if (i > 0 && !mbar_wait(bar_kvfree, (i - 1) & 1, abort_flag, p.err, 21)) break;
+            // the units of the previous K/V must be done with it: kv_free
+            // completes one phase per reload (the MMA thread commits it only
+            // after the last unit before a reload), so a phase-parity wait is
+            // never more than one phase away from the barrier
+            if (kv_issued > 0 && !mbar_wait(bar_kvfree, (kv_issued - 1) & 1, abort_flag, p.err, 21)) break;
             const int kvh = (p.kv_head_off + u.hl) / p.group;
             mbar_arrive_expect_tx(bar_kvfull, 2 * S::kTile);
 #pragma unroll
@@ -142,52 +244,84 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // never leave the CTA with a bulk copy still writing its shared memory
-        // (every earlier copy was consumed before the next one was issued)
-        if (q_issued > 0) drain_wait(bar_qfull, (q_issued - 1) & 1);
+        // (only the last copy into each buffer can still be in flight)
+        for (int j = q_issued > S::kQBuf ? q_issued - S::kQBuf : 0; j < q_issued; ++j)
+          drain_wait(bar_qfull + j % S::kQBuf, (j / S::kQBuf) & 1);
         if (kv_issued > 0) drain_wait(bar_kvfull, (kv_issued - 1) & 1);
       }
       __syncwarp();
     } else if (warp == 9) {
       // ---------------- MMA issuer ----------------
       if (lane == 0) {
-        const uint32_t tS0 = tmem, tO0 = tmem + 256;
-        const SDesc dQ0 = sdesc_split(smem_u32(sQ), 16, 1024);
-        const SDesc dQ1 = sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024);
+        const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+        const SDesc dQ = sdesc_split(smem_u32(sQ), 16, 1024);
         const SDesc dK = sdesc_split(smem_u32(sK), 16, 1024);
         const SDesc dV = sdesc_split(smem_u32(sV), kChunkBytes, 1024);
+        auto qdesc = [&](int i, int t) {
+          return SDesc{dQ.lo + (uint32_t)((i % S::kQBuf) * 2 + t) * (S::kTile >> 4), dQ.hi};
+        };
         int kv_loads = 0, kv_prev = -1;
-        bool go = true;
-        for (int i = 0; i < cnt && go; ++i) {
-          const ShortUnit u = short_unit(p, u0 + i);
-          if (!mbar_wait(bar_qfull, i & 1, abort_flag, p.err, 22)) break;
+        // Q (and K/V when they change) of unit i in shared memory
+        auto inputs_ready = [&](int i, const ShortUnit& u) {
+          if (!mbar_wait(bar_qfull + i % S::kQBuf, (i / S::kQBuf) & 1, abort_flag, p.err, 22)) return false;
           if (u.kv_key != kv_prev) {
-            if (!mbar_wait(bar_kvfull, kv_loads & 1, abort_flag, p.err, 23)) break;
+            if (!mbar_wait(bar_kvfull, kv_loads & 1, abort_flag, p.err, 23)) return false;
             ++kv_loads;
             kv_prev = u.kv_key;
           }
           tc_fence_after();
-          issue_s<D>(tS0, dQ0, dK);
+          return true;
+        };
+        // P V of tile t of unit i (after its P halves, and after the epilogue
+        // has read O_t of unit i - 1)
+        auto pv = [&](int i, int t) {
+          const uint32_t tS = t ? tS1 : tS0, tO = t ? tO1 : tO0;
+          if (!mbar_wait(bar_ph + t, i & 1, abort_flag, p.err, 24)) return false;
+          if (i > 0 && !mbar_wait(bar_ofree + t, (i - 1) & 1, abort_flag, p.err, 25)) return false;
+          tc_fence_after();
+          issue_pv_half<D>(tO, tS, dV, false, 0);
+          if (!mbar_wait(bar_p + t, i & 1, abort_flag, p.err, 24)) return false;
+          tc_fence_after();
+          issue_pv_half<D>(tO, tS, dV, true, 1);
+          return true;
+        };
+        ShortUnit cur = short_unit(p, u0);
+        bool go = inputs_ready(0, cur);
+        if (go) {
+          issue_s<D>(tS0, qdesc(0, 0), dK);
           umma_commit(bar_s + 0);
-          issue_s<D>(tS0 + 128, dQ1, dK);
+          issue_s<D>(tS1, qdesc(0, 1), dK);
           umma_commit(bar_s + 1);
-          umma_commit(bar_qfree);  // both S MMAs have read Q
-#pragma unroll 1
-          for (int t = 0; t < 2 && go; ++t) {
-            const uint32_t tS = tS0 + t * 128, tO = tO0 + t * 128;
-            go = mbar_wait(bar_ph + t, i & 1, abort_flag, p.err, 24);
-            // O_t of the previous unit must have been read by its epilogue
-            if (go && i > 0) go = mbar_wait(bar_ofree + t, (i - 1) & 1, abort_flag, p.err, 25);
-            if (!go) break;
-            tc_fence_after();
-            issue_pv_half<D>(tO, tS, dV, false, 0);
-            go = mbar_wait(bar_p + t, i & 1, abort_flag, p.err, 24);
-            if (!go) break;
-            tc_fence_after();
-            issue_pv_half<D>(tO, tS, dV, true, 1);
+          umma_commit(bar_qfree + 0);
+        }
+        // Issue order PV0_i, S0_{i+1}, PV1_i, S1_{i+1} when unit i+1 reuses
+        // K/V and its Q has its own buffer, so the two tiles' softmaxes
+        // alternate; otherwise both P V first (a K/V reload needs P V of
+        // unit i done, and a single Q buffer fills only after S_i).
+        for (int i = 0; i < cnt && go; ++i) {
+          const bool more = i + 1 < cnt;
+          const ShortUnit nxt = more ? short_unit(p, u0 + i + 1) : cur;
+          const bool pingpong = S::kQBuf == 2 && more && nxt.kv_key == cur.kv_key;
+          if (!(go = pv(i, 0))) break;
+          if (pingpong) {
+            if (!(go = inputs_ready(i + 1, nxt))) break;
+            issue_s<D>(tS0, qdesc(i + 1, 0), dK);
+            umma_commit(bar_s + 0);
           }
-          if (!go) break;
+          if (!(go = pv(i, 1))) break;
           umma_commit(bar_o);
-          umma_commit(bar_kvfree);
+          if (more && nxt.kv_key != cur.kv_key) umma_commit(bar_kvfree);  // the next unit reloads K/V
+          if (more) {
+            if (!pingpong) {
+              if (!(go = inputs_ready(i + 1, nxt))) break;
+              issue_s<D>(tS0, qdesc(i + 1, 0), dK);
+              umma_commit(bar_s + 0);
+            }
+            issue_s<D>(tS1, qdesc(i + 1, 1), dK);
+            umma_commit(bar_s + 1);
+            umma_commit(bar_qfree + (i + 1) % S::kQBuf);
+          }
+          cur = nxt;
         }
         umma_commit(bar_done);
         drain_wait(bar_done, 0);  // every issued MMA has completed
@@ -195,24 +329,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   } else {
-    setmaxnreg_inc<kSoftmaxRegs>();
-    // ---------------- softmax and epilogue of Q tile t ----------------
+    setmaxnreg_inc<kShortSoftmaxRegs>();
+    // ---------------- softmax of Q tile t ----------------
     const int t = warp >> 2;
     const int r = threadIdx.x & 127;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + t * 128 + lane_off;
-    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
     const float sl2 = p.scale_log2;
     const int Lk = p.Lk;
-    uint8_t* stg = sO + t * S::kTile;
-    uint8_t* srow = stg + r * 128;
     int mask_b = -1;
     bool mask_on = false;
     uint32_t mw[4] = {~0u, ~0u, ~0u, ~0u};
     bool ok = true;
     for (int i = 0; i < cnt; ++i) {
       const ShortUnit u = short_unit(p, u0 + i);
-      const int row = u.q0 + t * kTileM + r;
       // key-mask words of batch row b (each warp its own copy); a row with no
       // valid key attends to every key (GemmaTextEncoder.swift:306-319)
       if (p.mask != nullptr && u.b != mask_b) {
@@ -227,14 +357,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mask_on = any != 0u;
         mask_b = u.b;
       }
-      uint32_t g2 = 0x3f803f80u;  // bf16x2 (1, 1)
-      if (p.gate != nullptr && row < p.Lq) {
-        const float g = gate_bf16(__bfloat162float(
-            p.gate[(int64_t)u.b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + u.hl) * p.g_sh]));
-        g2 = pack_bf16x2(g, g);
-      }
-
-      // softmax of the unit's single KV tile
       ok = ok && warp_wait(bar_s + t, i & 1, abort_flag, p.err, 26);
       tc_fence_after();
       float s[128];
@@ -288,6 +410,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           s[c + 1] = e.y;
           acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], e);
         }
+        if (h2 == 1) {  // the row's (max, sum) for the epilogue, before the hand-off
+          const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+          const float2 tot = add2(a01, a23);
+          float l = 0.f;
+          l += tot.x + tot.y;
+          rowstat[((i & 1) * 2 + t) * 128 + r] = make_float2(m, l);
+          mbar_arrive(bar_stat + (i & 1) * 2 + t);
+        }
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
@@ -296,60 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(h2 == 0 ? bar_ph + t : bar_p + t);
       }
-      float l;
-      {
-        const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
-        const float2 tot = add2(a01, a23);
-        l = 0.f;
-        l += tot.x + tot.y;
-      }
-
-      // epilogue: O_t to registers, release it to the next unit's P V, then
-      // stage (128-byte swizzle) and store with TMA
-      ok = ok && warp_wait(bar_o, i & 1, abort_flag, p.err, 27);
-      tc_fence_after();
-      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-      if (r == 0) bulk_wait_read();  // the previous unit's store has read the staging tile
-      named_barrier(1 + t, 128);
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv_l, __uint_as_float(o[8 * e + 1]) * inv_l);
-          v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
-          v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
-          v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
-          if (p.gate != nullptr) {
-            v.x = bmul2(v.x, g2);
-            v.y = bmul2(v.y, g2);
-            v.z = bmul2(v.z, g2);
-            v.w = bmul2(v.w, g2);
-          }
-          const int j = (c & 1) * 4 + e;
-          *reinterpret_cast<uint4*>(srow + (c >> 1) * kChunkBytes + ((j ^ (r & 7)) << 4)) = v;
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bar_ofree + t);
-      if (p.lse != nullptr && row < p.Lq) {
-        p.lse[(int64_t)u.b * p.lse_sb + (int64_t)(p.head_begin + u.hl) * p.lse_sh + row] =
-            (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
-      }
-      fence_proxy_async_smem();  // the bulk copy reads these rows through the async proxy
-      const bool all_ok = named_barrier_and(1 + t, 128, ok);
-      if (r == 0 && all_ok && u.q0 + t * kTileM < p.Lq) {
-#pragma unroll
-        for (int ch = 0; ch < S::kChunks; ++ch)
-          tma_store_4d(&p.tm_o, stg + ch * kChunkBytes, ch * 64, u.q0 + t * kTileM, p.head_begin + u.hl, u.b);
-        bulk_commit();
-      }
-      if (!all_ok) break;
+      if (!named_barrier_and(1 + t, 128, ok)) break;
     }
-    if (r == 0) bulk_wait_read();  // the CTA's shared memory must outlive the copies' reads
   }
 
   // ---------------- teardown ----------------
@@ -384,7 +462,7 @@ cudaError_t prepare_fwd_short(int D) {
   const void* k = D == 128 ? (const void*)fwd_short_sm100_kernel<128> : (const void*)fwd_short_sm100_kernel<64>;
   cudaFuncAttributes fa;
   if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
-  if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
+  if (fa.numRegs != (int)kShortLaunchRegs) return cudaErrorInvalidConfiguration;
   if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_short_smem_bytes(D))) !=
       cudaSuccess)
     return e;
@@ -397,9 +475,9 @@ cudaError_t launch_fwd_short(const FwdParams& p, int D, int units, int sms, cuda
   const int grid = (units + per - 1) / per;
   const size_t smem = fwd_short_smem_bytes(D);
   if (D == 128)
-    fwd_short_sm100_kernel<128><<<grid, kThreads, smem, s>>>(p, per, units);
+    fwd_short_sm100_kernel<128><<<grid, kShortThreads, smem, s>>>(p, per, units);
   else
-    fwd_short_sm100_kernel<64><<<grid, kThreads, smem, s>>>(p, per, units);
+    fwd_short_sm100_kernel<64><<<grid, kShortThreads, smem, s>>>(p, per, units);
   return cudaGetLastError();
 }
 

@@ -70,6 +70,21 @@ def test_matches_the_forward_kernel_bit_for_bit(D, Lk):
     assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_kv_reloads_inside_a_cta(D):
+    # two query blocks per head: every CTA's range of units crosses heads and
+    # batches, so K/V are reloaded mid-range behind units still using them
+    B, H, Lq, Lk = 2, 160, 300, 100
+    q, k, v = make(141 + D, B, H, H, Lq, Lk, D)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out, lse = AttentionBackend.attention(qd, kd, vd, save_lse=True)
+    one, lse1 = AttentionBackend.attention(qd, kd, vd, save_lse=True, num_splits=1)
+    assert same_bits(out, one) and torch.equal(lse, lse1)
+    hs = [0, 1, 2, 159]
+    ref, _ = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs])
+    check(out[:, hs], ref, f"reloads D={D}")
+
+
 def test_key_masks_and_the_free_row_rule():
     # batch 0: ragged mask; batch 1: no valid key -> every key (GemmaTextEncoder.swift:306-319)
     B, H, Lq, Lk, D = 2, 80, 300, 100, 128
