@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kShortThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the kernel that wrote q / k (the RoPE pre-pass) has completed
 
   if (warp >= 12) {
     setmaxnreg_dec<kShortOtherRegs>();
@@ -474,11 +475,8 @@ cudaError_t launch_fwd_short(const FwdParams& p, int D, int units, int sms, cuda
   const int per = (units + sms - 1) / sms;
   const int grid = (units + per - 1) / per;
   const size_t smem = fwd_short_smem_bytes(D);
-  if (D == 128)
-    fwd_short_sm100_kernel<128><<<grid, kShortThreads, smem, s>>>(p, per, units);
-  else
-    fwd_short_sm100_kernel<64><<<grid, kShortThreads, smem, s>>>(p, per, units);
-  return cudaGetLastError();
+  if (D == 128) return launch_pdl(fwd_short_sm100_kernel<128>, dim3(grid), dim3(kShortThreads), smem, s, p, per, units);
+  return launch_pdl(fwd_short_sm100_kernel<64>, dim3(grid), dim3(kShortThreads), smem, s, p, per, units);
 }
 
 }  // namespace ltx

@@ -161,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
+    grid_dep_wait();  // the kernel that wrote q (the RoPE pre-pass) has completed
     mbar_arrive_expect_tx(bar_q, S::kTile);
 #pragma unroll
     for (int c = 0; c < S::kChunks; ++c) tma_load_4d(&p.tm_q, bar_q, sQ + c * kChunkBytes, c * 64, q0, qh, b);
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     tc_fence_before();
   }
 
+  grid_dep_wait();  // every thread, before its first global access
   // key-mask bits (padded with zero words to a whole tile), one 32-key word
   // per thread: two 16-byte loads when the rows are aligned, else byte loads: word w is one
   // warp's ballot over keys 32w .. 32w + 31, each lane reading one mask byte;
@@ -719,15 +721,12 @@ cudaError_t prepare_fwd_bf16(int D, size_t smem) {
 cudaError_t launch_fwd_bf16(const FwdParams& p, int D, size_t smem, cudaStream_t s) {
   const dim3 grid(p.n_full + p.n_tail * p.num_splits);
   const bool banded = p.causal || p.window > 0;
-  if (D == 128 && banded)
-    fwd_bf16_sm100_kernel<128, true><<<grid, kThreads, smem, s>>>(p);
-  else if (D == 128)
-    fwd_bf16_sm100_kernel<128, false><<<grid, kThreads, smem, s>>>(p);
-  else if (banded)
-    fwd_bf16_sm100_kernel<64, true><<<grid, kThreads, smem, s>>>(p);
-  else
-    fwd_bf16_sm100_kernel<64, false><<<grid, kThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  // programmatic launch: CTAs set up barriers and TMEM while the kernel
+  // before (the RoPE pre-pass, a q/k preparation) finishes
+  if (D == 128 && banded) return launch_pdl(fwd_bf16_sm100_kernel<128, true>, grid, dim3(kThreads), smem, s, p);
+  if (D == 128) return launch_pdl(fwd_bf16_sm100_kernel<128, false>, grid, dim3(kThreads), smem, s, p);
+  if (banded) return launch_pdl(fwd_bf16_sm100_kernel<64, true>, grid, dim3(kThreads), smem, s, p);
+  return launch_pdl(fwd_bf16_sm100_kernel<64, false>, grid, dim3(kThreads), smem, s, p);
 }
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s) {

@@ -181,6 +181,25 @@ struct BwdPrepParams {
   int f32;          // o / dout are float32
 };
 
+// Launch with programmatic stream serialization: the kernel's CTAs may start
+// while the previous kernel in the stream finishes (their prologue overlaps
+// its tail) and must call grid_dep_wait() before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Launchers (return cudaError_t of the launch).
 // Once-per-device kernel attributes (cached); call before launch_fwd_bf16.
 cudaError_t prepare_fwd_bf16(int D, size_t smem_bytes);

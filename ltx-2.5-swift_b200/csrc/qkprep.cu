@@ -163,6 +163,7 @@ __device__ __forceinline__ float warp_sumsq(const Raw16<T>& xc) {
 // before the current row is worked on.
 template <typename T>
 __global__ void __launch_bounds__(512, sizeof(T) == 2 ? LTX_QK_MIN_BLOCKS_BF16 : 1) qk_prep_kernel(const QkPrepParams p) {
+  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
   __shared__ float wsum[2][16];  // per-warp partials, alternating by row
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int rows = p.B * p.tokens;
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(512, sizeof(T) == 2 ? LTX_QK_MIN_BLOCKS_BF16 :
 // still in flight before the block exits.
 template <typename T>
 __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p, int stages) {
+  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ float wsum[2][16];
   __shared__ int abort_flag;

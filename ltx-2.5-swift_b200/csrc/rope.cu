@@ -70,6 +70,7 @@ __device__ __forceinline__ void rope_vec_job(const RopeParams& p, int b) {
 }
 
 __global__ void __launch_bounds__(256) rope_bf16_vec_kernel(const RopeParams a, const RopeParams c2) {
+  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
   const int z = blockIdx.z;
   if (z < a.B)
     rope_vec_job(a, z);
@@ -117,6 +118,7 @@ __device__ __forceinline__ void rope_scalar_job(const RopeParams& p, int b) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) rope_scalar_kernel(const RopeParams a, const RopeParams c2) {
+  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
   const int z = blockIdx.z;
   if (z < a.B)
     rope_scalar_job<T>(a, z);

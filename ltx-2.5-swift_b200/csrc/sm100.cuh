@@ -139,6 +139,15 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch.  A grid launched with the programmatic
+// stream-serialization attribute may start while the grid before it in the
+// stream is finishing; grid_dep_wait() then holds the calling thread until that
+// grid has completed and its memory is visible (a no-op without the
+// attribute).  grid_dep_launch_dependents() lets the next grid start launching
+// once every CTA of this grid has issued it or exited.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // The same barrier, returning whether `pred` held in every participating thread.
 __device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool pred) {
   uint32_t r;
