@@ -50,7 +50,8 @@ def _stale(target: str, deps) -> bool:
 # launched with exactly the per-thread count their split was sized for: a
 # setmaxnreg.inc that asks for more than the launch provided never returns.
 # ptxas' report is checked against the value the kernel source assumes.
-REGISTER_PINS = {"fwd_sm100.cu": ("fwd_bf16_sm100_kernel", 168)}
+REGISTER_PINS = {"fwd_sm100.cu": ("fwd_bf16_sm100_kernel", 168),
+                 "fwd_short_sm100.cu": ("fwd_short_sm100_kernel", 128)}
 
 
 def _check_register_pin(src: str, ptxas_log: str) -> None:
