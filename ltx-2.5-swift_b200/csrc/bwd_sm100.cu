@@ -17,9 +17,13 @@
 //                     TMEM: S [0,128), dP [128,256), dQ [256,256+D),
 //                     Q [384,384+D/2), dO [448,448+D/2) (bf16 pairs: the
 //                     A operands of S = Q K^T and dP = dO V^T come from TMEM,
-//                     so those MMAs read only K or V from shared memory)
+//                     so those MMAs read only K or V from shared memory).
+//                     dS overwrites dP, so S_{i+1} runs while the softmax
+//                     warps turn S_i / dP_i into dS_i.
 //   bwd_dkdv_kernel   KV-stationary: per 128-key tile, loop over Q tiles;
-//                     TMEM: S^T [0,128), dP^T [128,256), dV [256,..), dK [384,..)
+//                     TMEM: S^T [0,128), dP^T [128,256), dV [256,..), dK [384,..);
+//                     P^T and dS^T overwrite dP^T, so S^T of the next Q tile
+//                     runs while the softmax warps work on this one
 // In both, the softmax warps turn S/dP into bf16 P or dS in place (TMEM) and
 // the PV-style products read them straight from TMEM (tcgen05.mma A-from-TMEM).
 // When rotary tables are given, dQ and dK leave through the transpose
@@ -147,8 +151,9 @@ struct DqSmem {
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
   static constexpr uint32_t kOffQ = 0, kOffDO = kTile, kOffK0 = 2 * kTile, kOffV0 = 3 * kTile,
                             kOffK1 = 4 * kTile, kOffV1 = 5 * kTile;
-  static constexpr uint32_t kOffBar = 6 * kTile;  // q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full, qt_ready, p_half
-  static constexpr uint32_t kOffCtl = kOffBar + 10 * 8;
+  // q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full, qt_ready, p_half, s_read
+  static constexpr uint32_t kOffBar = 6 * kTile;
+  static constexpr uint32_t kOffCtl = kOffBar + 11 * 8;
   static constexpr uint32_t kOffTiles = kOffCtl + 16;
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;
 };
@@ -173,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   uint64_t* bar_o = bars + 7;
   uint64_t* bar_qt = bars + 8;  // Q and dO rows copied into TMEM
   uint64_t* bar_ph = bars + 9;  // dS for keys 0-63 stored (warps 0-3); bar_p: keys 64-127 (warps 4-7)
+  uint64_t* bar_sr = bars + 10; // every softmax thread has loaded its S columns: S may be overwritten
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   int* n_tiles_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
@@ -183,8 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
   const int q0 = blockIdx.x * kTileM, hl = blockIdx.y, b = blockIdx.z;
 
   if (threadIdx.x == 0) {
-    // p_full / p_half: the 128 threads of warps 4-7 / 0-3; qt_ready: all 256 softmax threads
-    for (int i = 0; i < 10; ++i) mbar_init(bars + i, i == 8 ? 256 : ((i == 6 || i == 9) ? 128 : 1));
+    // p_full / p_half: the 128 threads of warps 4-7 / 0-3; qt_ready, s_read: all 256 softmax threads
+    for (int i = 0; i < 11; ++i) mbar_init(bars + i, (i == 8 || i == 10) ? 256 : ((i == 6 || i == 9) ? 128 : 1));
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -241,38 +247,59 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_dq = idesc_bf16_f32(128, D, 0, 1);
       const uint32_t tS = tmem, tP = tmem + 128, tQ = tmem + 256, tQa = tmem + 384, tOa = tmem + 448;
-      if (mbar_wait(bar_qt, 0, abort_flag, p.err, 22)) {
-        for (int i = 0; i < n; ++i) {
-          const int st = i & 1;
-          if (!mbar_wait(bar_kvf + st, (i >> 1) & 1, abort_flag, p.err, 23)) break;
+      // S_i = Q K_i^T and dP_i = dO V_i^T (A operands from TMEM)
+      auto issue_s = [&](int st) {
+        const SDesc dKd = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+          umma_ts2(tS, tQa + kk * 8, dKd.lo + off, dKd.hi, idesc_s, kk > 0);
+        }
+      };
+      auto issue_dp = [&](int st) {
+        const SDesc dVd = sdesc_split(smem_u32(sV0) + st * 2 * S::kTile, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+          umma_ts2(tP, tOa + kk * 8, dVd.lo + off, dVd.hi, idesc_s, kk > 0);
+        }
+      };
+      // Order per KV tile i: S_{i+1} as soon as softmax has loaded S_i (dS_i
+      // goes to the dP columns, so the S columns are free early), then
+      // dQ += dS_i K_i in two halves, then dP_{i+1} (after dQ has read dS_i).
+      bool go = mbar_wait(bar_qt, 0, abort_flag, p.err, 22) && mbar_wait(bar_kvf, 0, abort_flag, p.err, 23);
+      if (go) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
+        umma_commit(bar_s);
+      }
+      for (int i = 0; i < n && go; ++i) {
+        const int st = i & 1, st1 = (i + 1) & 1;
+        const bool more = i + 1 < n;
+        const SDesc dKmn = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, kChunkBytes, 1024);
+        if (more) {
+          if (!(go = mbar_wait(bar_sr, i & 1, abort_flag, p.err, 29))) break;
+          if (!(go = mbar_wait(bar_kvf + st1, ((i + 1) >> 1) & 1, abort_flag, p.err, 23))) break;
           tc_fence_after();
-          const SDesc dKd = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, 16, 1024);
-          const SDesc dVd = sdesc_split(smem_u32(sV0) + st * 2 * S::kTile, 16, 1024);
-          const SDesc dKmn = sdesc_split(smem_u32(sK0) + st * 2 * S::kTile, kChunkBytes, 1024);
+          issue_s(st1);
+        }
+        // dQ += dS K in two halves of 64 keys: the first runs while softmax
+        // finishes the second half of dS
+        if (!(go = mbar_wait(bar_ph, i & 1, abort_flag, p.err, 28))) break;
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ts2(tS, tQa + kk * 8, dKd.lo + off, dKd.hi, idesc_s, kk > 0);
-          }
+        for (int kk = 0; kk < kTileN / 32; ++kk)  // keys 0-63: dS at dP columns [0, 32)
+          umma_ts2(tQ, tP + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
+        if (!(go = mbar_wait(bar_p, i & 1, abort_flag, p.err, 24))) break;
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ts2(tP, tOa + kk * 8, dVd.lo + off, dVd.hi, idesc_s, kk > 0);
-          }
+        for (int kk = kTileN / 32; kk < kTileN / 16; ++kk)  // keys 64-127: dS at dP columns [64, 96)
+          umma_ts2(tQ, tP + 32 + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, 1u);
+        umma_commit(bar_kve + st);
+        if (more) {
+          issue_dp(st1);
           umma_commit(bar_s);
-          // dQ += dS K in two halves of 64 keys: the first runs while softmax
-          // finishes the second half of dS
-          if (!mbar_wait(bar_ph, i & 1, abort_flag, p.err, 28)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kTileN / 32; ++kk)
-            umma_ts2(tQ, tS + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
-          if (!mbar_wait(bar_p, i & 1, abort_flag, p.err, 24)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = kTileN / 32; kk < kTileN / 16; ++kk)  // keys 64-127: dS at S columns [64, 96)
-            umma_ts2(tQ, tS + 32 + kk * 8, dKmn.lo + ((kk * 16 * 128) >> 4), dKmn.hi, idesc_dq, 1u);
-          umma_commit(bar_kve + st);
         }
       }
       umma_commit(bar_o);
@@ -329,6 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
         tmem_ld32(tS + c * 32, rs);
         tmem_ld32(tP + c * 32, rp);
         tmem_wait_ld();
+        if (cc == 1) {  // this thread's S columns are read: S_{i+1} may overwrite them
+          tc_fence_before();
+          mbar_arrive(bar_sr);
+        }
         const uint32_t bits = key_bits(mbits, use_mask, kv0 + 32 * c, p.Lk);
         uint32_t pk[16];
 #pragma unroll
@@ -337,9 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dq_kernel(const __grid_consta
           const float p1 = ((bits >> (2 * e + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(rs[2 * e + 1]), sl2, -lse2)) : 0.f;
           pk[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - delta), p1 * (__uint_as_float(rp[2 * e + 1]) - delta));
         }
-        // bf16 dS of keys [64h, 64h+64) packs into S columns [64h, 64h+32): each
-        // half overwrites only columns it has already read
-        tmem_st16(tS + half * 64 + cc * 16, pk);
+        // bf16 dS of keys [64h, 64h+64) packs into dP columns [64h, 64h+32):
+        // each half overwrites only columns it has already read
+        tmem_st16(tP + half * 64 + cc * 16, pk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -383,7 +414,7 @@ struct DkvSmem {
   static constexpr uint32_t kOffK = 0, kOffV = kTile, kOffQ0 = 2 * kTile, kOffDO0 = 3 * kTile,
                             kOffQ1 = 4 * kTile, kOffDO1 = 5 * kTile;
   static constexpr uint32_t kOffL = 6 * kTile;  // lse2[2][128], delta[2][128]
-  static constexpr uint32_t kOffBar = kOffL + 4 * 128 * 4;  // kv_full, q_full[2], q_empty[2], s_full, p_full, o_full, p_half
+  static constexpr uint32_t kOffBar = kOffL + 4 * 128 * 4;  // kv_full, q_full[2], q_empty[2], s_full, p_full, o_full, p_half, s_read
   static constexpr uint32_t kOffCtl = kOffBar + 10 * 8;
   static constexpr uint32_t kOffBits = kOffCtl + 16;
 };
@@ -408,6 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   uint64_t* bar_p = bars + 6;
   uint64_t* bar_o = bars + 7;
   uint64_t* bar_ph = bars + 8;  // P^T, dS^T for queries 0-63 stored (warps 0-3); bar_p: 64-127 (warps 4-7)
+  uint64_t* bar_sr = bars + 9;  // every softmax thread has loaded its S^T columns: S^T may be overwritten
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   uint32_t* mbits = reinterpret_cast<uint32_t*>(sm + S::kOffBits);
@@ -417,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
   const int nq = p.n_q_tiles;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 9; ++i) mbar_init(bars + i, (i == 6 || i == 8) ? 128 : 1);
+    for (int i = 0; i < 10; ++i) mbar_init(bars + i, i == 9 ? 256 : ((i == 6 || i == 8) ? 128 : 1));
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -472,45 +504,68 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       const uint32_t idesc_g = idesc_bf16_f32(128, D, 0, 1);
       const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 384;
       const SDesc dKd = sdesc_split(smem_u32(sK), 16, 1024), dVd = sdesc_split(smem_u32(sV), 16, 1024);
-      bool fail = false;
-      if (mbar_wait(bar_kv, 0, abort_flag, p.err, 32)) {
-        for (int j = 0; j < n; ++j) {
-          const int st = j & 1;
-          if (!mbar_wait(bar_qf + st, (j >> 1) & 1, abort_flag, p.err, 33)) break;
+      // S^T_j = K Q_j^T and dP^T_j = V dO_j^T (both operands from shared memory)
+      auto issue_s = [&](int st) {
+        const SDesc dQd = sdesc_split(smem_u32(sQ0) + st * 2 * S::kTile, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+          umma_ss2(tS, dKd.lo + off, dKd.hi, dQd.lo + off, dQd.hi, idesc_s, kk > 0);
+        }
+      };
+      auto issue_dp = [&](int st) {
+        const SDesc dOd = sdesc_split(smem_u32(sDO0) + st * 2 * S::kTile, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
+          umma_ss2(tP, dVd.lo + off, dVd.hi, dOd.lo + off, dOd.hi, idesc_s, kk > 0);
+        }
+      };
+      // Order per Q tile j: S^T_{j+1} as soon as softmax has loaded S^T_j (P^T
+      // and dS^T go to the dP^T columns, so the S^T columns are free early),
+      // then dV += P^T dO and dK += dS^T Q in two halves, then dP^T_{j+1}.
+      bool go = mbar_wait(bar_kv, 0, abort_flag, p.err, 32) && mbar_wait(bar_qf, 0, abort_flag, p.err, 33);
+      if (go) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
+        umma_commit(bar_s);
+      }
+      for (int j = 0; j < n && go; ++j) {
+        const int st = j & 1, st1 = (j + 1) & 1;
+        const bool more = j + 1 < n;
+        const uint32_t aQ = smem_u32(sQ0) + st * 2 * S::kTile, aDO = smem_u32(sDO0) + st * 2 * S::kTile;
+        const SDesc dQmn = sdesc_split(aQ, kChunkBytes, 1024), dOmn = sdesc_split(aDO, kChunkBytes, 1024);
+        if (more) {
+          if (!(go = mbar_wait(bar_sr, j & 1, abort_flag, p.err, 38))) break;
+          if (!(go = mbar_wait(bar_qf + st1, ((j + 1) >> 1) & 1, abort_flag, p.err, 33))) break;
           tc_fence_after();
-          const uint32_t aQ = smem_u32(sQ0) + st * 2 * S::kTile, aDO = smem_u32(sDO0) + st * 2 * S::kTile;
-          const SDesc dQd = sdesc_split(aQ, 16, 1024), dOd = sdesc_split(aDO, 16, 1024);
-          const SDesc dQmn = sdesc_split(aQ, kChunkBytes, 1024), dOmn = sdesc_split(aDO, kChunkBytes, 1024);
+          issue_s(st1);
+        }
+        // dV += P^T dO and dK += dS^T Q in two halves of 64 queries: the first
+        // runs while softmax finishes the second half
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ss2(tS, dKd.lo + off, dKd.hi, dQd.lo + off, dQd.hi, idesc_s, kk > 0);
+        for (int h = 0; h < 2 && go; ++h) {
+          if (!(go = mbar_wait(h == 0 ? bar_ph : bar_p, j & 1, abort_flag, p.err, 34))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k4 = 0; k4 < kTileM / 32; ++k4) {
+            const int kk = h * (kTileM / 32) + k4;  // queries 16kk..; P^T of half h at dP^T columns 64h + 16 (k4/2) + 8 (k4%2)
+            umma_ts2(tV, tP + h * 64 + (k4 >> 1) * 32 + (k4 & 1) * 8, dOmn.lo + ((kk * 16 * 128) >> 4), dOmn.hi, idesc_g,
+                     (j > 0 || kk > 0) ? 1u : 0u);
           }
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
-            umma_ss2(tP, dVd.lo + off, dVd.hi, dOd.lo + off, dOd.hi, idesc_s, kk > 0);
+          for (int k4 = 0; k4 < kTileM / 32; ++k4) {
+            const int kk = h * (kTileM / 32) + k4;  // dS^T of half h at dP^T columns 64h + 16 + 16 (k4/2) + 8 (k4%2)
+            umma_ts2(tK, tP + h * 64 + 16 + (k4 >> 1) * 32 + (k4 & 1) * 8, dQmn.lo + ((kk * 16 * 128) >> 4), dQmn.hi,
+                     idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
           }
+        }
+        if (!go) break;
+        umma_commit(bar_qe + st);
+        if (more) {
+          issue_dp(st1);
           umma_commit(bar_s);
-          // dV += P^T dO and dK += dS^T Q in two halves of 64 queries: the first
-          // runs while softmax finishes the second half
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (!mbar_wait(h == 0 ? bar_ph : bar_p, j & 1, abort_flag, p.err, 34)) { fail = true; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int k4 = 0; k4 < kTileM / 32; ++k4) {
-              const int kk = h * (kTileM / 32) + k4;  // queries 16kk..; half h packed at columns 64h + 8 k4
-              umma_ts2(tV, tS + h * 64 + k4 * 8, dOmn.lo + ((kk * 16 * 128) >> 4), dOmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
-            }
-#pragma unroll
-            for (int k4 = 0; k4 < kTileM / 32; ++k4) {
-              const int kk = h * (kTileM / 32) + k4;
-              umma_ts2(tK, tP + h * 64 + k4 * 8, dQmn.lo + ((kk * 16 * 128) >> 4), dQmn.hi, idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
-          if (fail) break;
-          umma_commit(bar_qe + st);
         }
       }
       umma_commit(bar_o);
@@ -535,13 +590,24 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
       tc_fence_after();
       const float* L2 = sL + st * 128;
       const float* DL = sL + 256 + st * 128;
+      // this warp's queries [64 * half, 64 * half + 64): both dP^T chunks are
+      // loaded first, because P^T and dS^T of the first 32 queries land in the
+      // second chunk's columns (16-column groups: P^T c0, dS^T c0, P^T c1,
+      // dS^T c1 from column 64 * half)
+      uint32_t rp0[32], rp1[32];
+      tmem_ld32(tP + (2 * half) * 32, rp0);
+      tmem_ld32(tP + (2 * half + 1) * 32, rp1);
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * half + cc;  // queries [64 * half, 64 * half + 64)
-        uint32_t rs[32], rp[32];
+        const int c = 2 * half + cc;
+        uint32_t rs[32];
         tmem_ld32(tS + c * 32, rs);
-        tmem_ld32(tP + c * 32, rp);
         tmem_wait_ld();
+        if (cc == 1) {  // this thread's S^T columns are read: S^T_{j+1} may overwrite them
+          tc_fence_before();
+          mbar_arrive(bar_sr);
+        }
+        const uint32_t* rp = cc == 0 ? rp0 : rp1;
         uint32_t pp[16], pd[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -551,10 +617,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_dkdv_kernel(const __grid_cons
           pp[e] = pack_bf16x2(p0, p1);
           pd[e] = pack_bf16x2(p0 * (__uint_as_float(rp[2 * e]) - DL[q]), p1 * (__uint_as_float(rp[2 * e + 1]) - DL[q + 1]));
         }
-        // bf16 P^T / dS^T of queries [64h, 64h+64) pack into columns [64h, 64h+32):
-        // each half overwrites only columns it has already read
-        tmem_st16(tS + half * 64 + cc * 16, pp);
-        tmem_st16(tP + half * 64 + cc * 16, pd);
+        tmem_st16(tP + half * 64 + cc * 32, pp);
+        tmem_st16(tP + half * 64 + cc * 32 + 16, pd);
       }
       tmem_wait_st();
       tc_fence_before();
