@@ -393,10 +393,21 @@ int set_error_message(int status, const char* msg) {
   return status;
 }
 
+// The device error word's address, looked up once per device (a call then
+// makes no runtime query that could disturb a stream capture).
 int* device_error_word() {
-  int* p = nullptr;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) != cudaSuccess) return nullptr;
-  return p;
+  constexpr int kDevs = 64;
+  static std::mutex mu;
+  static int* cache[kDevs] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevs) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) != cudaSuccess) return nullptr;
+    cache[dev] = p;
+  }
+  return cache[dev];
 }
 
 }  // namespace ltx
