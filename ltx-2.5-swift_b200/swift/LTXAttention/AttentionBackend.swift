@@ -160,4 +160,11 @@ public enum AttentionBackend {
     public static func workspaceBytes(_ a: inout ltxattn_fwd_args) -> Int {
         Int(ltxattn_fwd_workspace(&a))
     }
+
+    /// What `ltxattn_fwd` will launch for these arguments (for logs and benchmarks).
+    public static func plan(_ a: inout ltxattn_fwd_args) throws -> ltxattn_fwd_plan_info {
+        var info = ltxattn_fwd_plan_info()
+        try check(ltxattn_fwd_plan(&a, &info))
+        return info
+    }
 }
