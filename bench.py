@@ -45,7 +45,7 @@ WORKLOADS = {
 L2_BYTES = 126 * 1024 * 1024
 
 
-# the roofline that bounds each workload's attention kernel (BASELINE/SURVEY arithmetic
+# the roofline that bounds each workload's attention kernel (the workload's arithmetic
 # intensity against the ~250 FLOP/B ridge of the measured peaks)
 BOUND = {"c2": "tensor", "c3": "hbm", "c4a": "hbm", "c4b": "hbm", "c4c": "hbm", "c5": "tensor"}
 

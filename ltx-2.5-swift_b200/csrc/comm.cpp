@@ -1,7 +1,7 @@
 // comm.cpp -- head-parallel all-gather over NCCL (NVLink / NVSwitch).
 //
-// The reference has no collective (a single device, SURVEY of
-// RenderEngine.swift:16-24).  Heads are independent, so a head-sharded job
+// The reference has no collective: it renders on a single device
+// (RenderEngine.swift:16-24).  Heads are independent, so a head-sharded job
 // needs communication only where a caller wants every head's output on every
 // rank; this file provides exactly that gather.
 //
