@@ -198,3 +198,49 @@ def test_qk_prep_restatement():
     r = (1.0 / np.sqrt(ms + np.float64(np.float32(1e-6)))).astype(np.float32)
     y = inputs.round_bf16(w * inputs.round_bf16(x * r))
     np.testing.assert_array_equal(got, y.reshape(2, 9, 4, 128).transpose(0, 2, 1, 3))
+
+
+def test_gate_restatement_known_answers():
+    # DiTAttention.swift:395-399: gates = 2 * sigmoid(logits), sigmoid in fp32 cast to bf16
+    logits = np.array([[[0.0, 100.0, -100.0, 1.0]]], np.float32)  # [B=1, T=1, H=4]
+    g = oracle.gate_value(logits, bf16=True)
+    assert g[0, 0, 0] == 1.0 and g[0, 0, 1] == 2.0 and g[0, 0, 2] == 0.0
+    s1 = 1.0 / (1.0 + np.exp(-1.0))
+    assert g[0, 0, 3] == 2.0 * inputs.round_bf16(np.float32(s1))
+    out = np.full((1, 4, 1, 8), 0.75, np.float32)  # [B, H, T, D]
+    y = oracle.gate_output(out, logits, bf16=True)
+    np.testing.assert_array_equal(y[0, :, 0, 0], inputs.round_bf16(0.75 * g[0, 0]))
+    # fp32 activations: no rounding of the sigmoid
+    assert oracle.gate_value(logits[..., 3:], bf16=False)[0, 0, 0] == np.float32(2.0 * np.float32(s1))
+
+
+def test_module_composition_is_the_reference_order():
+    # the oracle's whole module on a tiny case against the steps written out in
+    # numpy: projections (matmul then bias, each rounded), rmsNorm + split + RoPE,
+    # SDPA, gate, merge, to_out (DiTAttention.swift:315-404)
+    rng = np.random.default_rng(1)
+    B, T, heads, D = 1, 8, 4, 128
+    dim = heads * D
+
+    def bf(a):
+        return inputs.round_bf16(np.asarray(a, np.float32))
+
+    w = {n: bf(rng.normal(0, 1 / np.sqrt(dim), (dim, dim))) for n in ("to_q.weight", "to_k.weight",
+                                                                       "to_v.weight", "to_out.0.weight")}
+    w.update({n: bf(rng.uniform(-0.1, 0.1, dim)) for n in ("to_q.bias", "to_k.bias", "to_v.bias", "to_out.0.bias")})
+    w.update({"q_norm.weight": bf(np.ones(dim)), "k_norm.weight": bf(np.ones(dim)),
+              "to_gate_logits.weight": bf(rng.normal(0, 0.05, (heads, dim)))})
+    x = bf(rng.normal(0, 1, (B, T, dim)))
+    got = oracle.dit_attention_module(x, w, heads)
+
+    def lin(a, n):
+        y = bf(a.astype(np.float64) @ w[n + ".weight"].astype(np.float64).T)
+        return bf(y.astype(np.float64) + w[n + ".bias"]) if n + ".bias" in w else y
+
+    q = oracle.qk_prep(lin(x, "to_q"), w["q_norm.weight"], heads, 1e-6)
+    k = oracle.qk_prep(lin(x, "to_k"), w["k_norm.weight"], heads, 1e-6)
+    v = np.ascontiguousarray(lin(x, "to_v").reshape(B, T, heads, D).transpose(0, 2, 1, 3))
+    att = bf(oracle.attn_fwd(q, k, v)[0])
+    gated = oracle.gate_output(att, lin(x, "to_gate_logits"), True)
+    want = lin(np.ascontiguousarray(gated.transpose(0, 2, 1, 3).reshape(B, T, dim)), "to_out.0")
+    np.testing.assert_array_equal(got, want)
