@@ -642,6 +642,27 @@ def run_reference(args):
     }
 
 
+def provenance():
+    """What produced the line: the repository revision (when a git checkout is
+    present), whether the tree was dirty, and a digest of the library loaded."""
+    import hashlib
+    rev = dirty = None
+    try:
+        rev = subprocess.run(["git", "-C", ROOT, "rev-parse", "--short", "HEAD"], capture_output=True,
+                             text=True, timeout=10).stdout.strip() or None
+        if rev:
+            dirty = bool(subprocess.run(["git", "-C", ROOT, "status", "--porcelain", "--untracked-files=no"],
+                                        capture_output=True, text=True, timeout=10).stdout.strip())
+    except (OSError, subprocess.SubprocessError):
+        pass
+    lib = os.path.join(ROOT, "ltx-2.5-swift_b200", "libltxattn_cuda.so")
+    digest = None
+    if os.path.exists(lib):
+        with open(lib, "rb") as f:
+            digest = hashlib.sha256(f.read()).hexdigest()[:16]
+    return {"revision": rev, "dirty": dirty, "library_sha256": digest}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -664,6 +685,8 @@ def main():
     else:
         res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
+        if "unavailable" not in res:
+            res["build"] = provenance()
         print(json.dumps(res), flush=True)
 
 
