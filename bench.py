@@ -177,7 +177,7 @@ def run_qkprep(args):
     split RoPE) at the config-2 shape; GB/s against the HBM roofline."""
     import torch
     import torch.distributed as dist
-    from ltxattn import Rotary, qk_prep
+    from ltxattn import Rotary, qk_prep_pair
 
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -196,9 +196,8 @@ def run_qkprep(args):
     flush = L2Flush(torch)
     stream = torch.cuda.current_stream()
 
-    def step():
-        for x, o in zip(xs, outs):
-            qk_prep(x, w, H, rot, eps=1e-6, out=o, stream=stream)
+    def step():  # q and k in one launch (ltxattn_qk_prep_pair)
+        qk_prep_pair(xs[0], w, xs[1], w, H, rot, rot, eps=1e-6, out_q=outs[0], out_k=outs[1], stream=stream)
 
     def barrier():
         if ws > 1:
@@ -255,13 +254,13 @@ def run_qkprep(args):
                        "parallelism": f"heads x{ws}", "l2": L2_NOTE},
             "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / ws / hbm, 4), "peak_source": f"{src} hbm_gbs",
-                         "algorithmic_bytes": step_bytes, "kernel": "qk_prep_bulk_kernel", "traffic": None},
+                         "algorithmic_bytes": step_bytes, "kernel": "qk_prep_bulk_pair_kernel", "traffic": None},
             "step_ms": {"median": round(statistics.median(step_ms), 5), "min": round(min(step_ms), 5),
                         "max": round(max(step_ms), 5)},
             "e2e": {"value": round(step_bytes * ws / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(h.numel() * 2 for h in hx),
                     "d2h_bytes_per_step": sum(h.numel() * 2 for h in ho)},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,
             "clocks": clk,
         }
     if ws > 1:

@@ -256,6 +256,11 @@ typedef struct ltxattn_qk_prep_args {
  * the head split (`:346-348`) and `applySplitRoPE` (`:206-234`), in one pass. */
 LTXATTN_API int ltxattn_qk_prep(const ltxattn_qk_prep_args* args, void* stream);
 
+/* q and k preparations (same dtype and inner width; token counts may differ,
+ * as in a cross-attention) in one launch; each result is exactly what
+ * ltxattn_qk_prep gives for its arguments. */
+LTXATTN_API int ltxattn_qk_prep_pair(const ltxattn_qk_prep_args* q, const ltxattn_qk_prep_args* k, void* stream);
+
 /* ---- rotary tables -------------------------------------------------------- */
 
 /* Arguments of ltxattn_rotary_tables: the per-head split-RoPE tables of one

@@ -636,7 +636,10 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   return LTXATTN_OK;
 }
 
-int ltxattn_qk_prep(const ltxattn_qk_prep_args* a, void* stream) {
+}  // extern "C"
+
+// Validation and parameter block of one q / k preparation.
+static int qk_prep_params(const ltxattn_qk_prep_args* a, QkPrepParams* out, bool* is_bf16) {
   if (a == nullptr) return fail(LTXATTN_ERR_ARG, "args is NULL");
   Shape s;
   int rc = check_shape(a->dtype, a->batch, a->heads, a->tokens, a->tokens, a->head_dim, 0, 0, &s);
@@ -676,8 +679,32 @@ int ltxattn_qk_prep(const ltxattn_qk_prep_args* a, void* stream) {
           (a->rotary.cos == nullptr || (aligned16(a->rotary.cos) && aligned16(a->rotary.sin) &&
                                         m8(a->rotary.stride_b) && m8(a->rotary.stride_h) && m8(a->rotary.stride_t)));
   p.err = device_error_word();
+  *out = p;
+  *is_bf16 = bf16;
+  return LTXATTN_OK;
+}
+
+extern "C" {
+
+int ltxattn_qk_prep(const ltxattn_qk_prep_args* a, void* stream) {
+  QkPrepParams p;
+  bool bf16 = false;
+  const int rc = qk_prep_params(a, &p, &bf16);
+  if (rc) return rc;
   const cudaError_t e = launch_qk_prep(p, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "qk_prep launch");
+}
+
+int ltxattn_qk_prep_pair(const ltxattn_qk_prep_args* q, const ltxattn_qk_prep_args* k, void* stream) {
+  QkPrepParams pq, pk;
+  bool bq = false, bk = false;
+  int rc = qk_prep_params(q, &pq, &bq);
+  if (rc) return rc;
+  if ((rc = qk_prep_params(k, &pk, &bk))) return rc;
+  if (bq != bk) return fail(LTXATTN_ERR_DTYPE, "q and k preparations must share one dtype");
+  if (pq.inner != pk.inner) return fail(LTXATTN_ERR_SHAPE, "q and k inner widths differ (%d, %d)", pq.inner, pk.inner);
+  const cudaError_t e = launch_qk_prep_pair(pq, pk, bq, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LTXATTN_OK : cuda_fail(e, "qk_prep_pair launch");
 }
 
 int ltxattn_rotary_tables(const ltxattn_rotary_table_args* a, void* stream) {

@@ -108,6 +108,7 @@ struct QkPrepParams {
   int* err;  // device error word (bounded waits)
 };
 cudaError_t launch_qk_prep(const QkPrepParams& p, bool bf16, cudaStream_t s);
+cudaError_t launch_qk_prep_pair(const QkPrepParams& p0, const QkPrepParams& p1, bool bf16, cudaStream_t s);
 
 // Rotary tables (DiTForward.rotary): see rotary.cu.
 struct RotaryTableParams {

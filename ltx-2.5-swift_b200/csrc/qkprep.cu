@@ -217,14 +217,13 @@ __global__ void __launch_bounds__(512, sizeof(T) == 2 ? LTX_QK_MIN_BLOCKS_BF16 :
 // thread has read it.  Waits are bounded; a wait that gives up ends every
 // thread of the block at that row's barrier, and thread 0 drains the copies
 // still in flight before the block exits.
+// The bulk path for one tensor, run by blocks [0, G) of the job (blk is this
+// block's index among them); inlined into the single and the paired kernels.
 template <typename T>
-__global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p, int stages) {
-  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float wsum[2][16];
-  __shared__ int abort_flag;
+__device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int stages, int blk, int G,
+                                                  uint8_t* smem_raw, float (*wsum)[16], int& abort_flag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  const int rows = p.B * p.tokens, G = gridDim.x;
+  const int rows = p.B * p.tokens;
   const uint32_t row_bytes = (uint32_t)p.inner * sizeof(T);
   T* ring = reinterpret_cast<T*>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)stages * row_bytes);
@@ -246,18 +245,18 @@ __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p,
     fence_mbar_init();
   }
   __syncthreads();
-  int issued = 0;  // pipeline slots whose copy thread 0 has issued (slot k: row blockIdx.x + k * G)
+  int issued = 0;  // pipeline slots whose copy thread 0 has issued (slot k: row blk + k * G)
   if (tid == 0) {
-    for (; issued < stages && blockIdx.x + issued * G < rows; ++issued) {
+    for (; issued < stages && blk + issued * G < rows; ++issued) {
       mbar_arrive_expect_tx(full + issued, row_bytes);
-      bulk_load(ring + (size_t)issued * p.inner, row_src(blockIdx.x + issued * G), row_bytes, full + issued);
+      bulk_load(ring + (size_t)issued * p.inner, row_src(blk + issued * G), row_bytes, full + issued);
     }
   }
   Raw16<T> wr;
   load16<T>(wr, static_cast<const T*>(p.w) + e0, true);
 
   int i = 0, par = 0;
-  for (int row = blockIdx.x; row < rows; row += G, ++i, par ^= 1) {
+  for (int row = blk; row < rows; row += G, ++i, par ^= 1) {
     const int b = row / p.tokens, t = row - b * p.tokens;
     Raw16<T> cr, sr;
     if (rope) {
@@ -266,7 +265,7 @@ __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p,
       load16<T>(sr, static_cast<const T*>(p.sin) + toff, true);
     }
     const int s = i % stages;
-    const bool ok = mbar_wait(full + s, (uint32_t)(i / stages) & 1u, &abort_flag, p.err, 40);
+    const bool ok = mbar_wait(full + s, (uint32_t)(i / stages) & 1u, (volatile int*)&abort_flag, p.err, 40);
     Raw16<T> xc;
     if (ok) {
       const uint4* src = reinterpret_cast<const uint4*>(ring + (size_t)s * p.inner + e0);
@@ -280,9 +279,9 @@ __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p,
     if (lane == 0) wsum[par][warp] = ss;
     if (!__syncthreads_and(ok)) break;
     // every thread has read stage s: refill it with slot i + stages
-    if (tid == 0 && issued == i + stages && blockIdx.x + issued * G < rows) {
+    if (tid == 0 && issued == i + stages && blk + issued * G < rows) {
       mbar_arrive_expect_tx(full + s, row_bytes);
-      bulk_load(ring + (size_t)s * p.inner, row_src(blockIdx.x + issued * G), row_bytes, full + s);
+      bulk_load(ring + (size_t)s * p.inner, row_src(blk + issued * G), row_bytes, full + s);
       ++issued;
     }
     float tot = 0.f;
@@ -294,6 +293,30 @@ __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p,
   // never leave with a bulk copy still writing this block's shared memory
   if (tid == 0)
     for (int k = i; k < issued; ++k) drain_wait(full + k % stages, (uint32_t)(k / stages) & 1u);
+}
+
+
+template <typename T>
+__global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p, int stages) {
+  grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float wsum[2][16];
+  __shared__ int abort_flag;
+  qk_prep_bulk_body<T>(p, stages, blockIdx.x, gridDim.x, smem_raw, wsum, abort_flag);
+}
+
+// q and k in one launch: blocks [0, g0) prepare p0, the rest p1.
+template <typename T>
+__global__ void __launch_bounds__(512) qk_prep_bulk_pair_kernel(const QkPrepParams p0, const QkPrepParams p1,
+                                                                 int stages, int g0) {
+  grid_dep_launch_dependents();
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float wsum[2][16];
+  __shared__ int abort_flag;
+  if ((int)blockIdx.x < g0)
+    qk_prep_bulk_body<T>(p0, stages, blockIdx.x, g0, smem_raw, wsum, abort_flag);
+  else
+    qk_prep_bulk_body<T>(p1, stages, blockIdx.x - g0, gridDim.x - g0, smem_raw, wsum, abort_flag);
 }
 
 }  // namespace
@@ -328,6 +351,39 @@ cudaError_t launch_qk_prep(const QkPrepParams& p, bool bf16, cudaStream_t s) {
     qk_prep_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(p);
   else
     qk_prep_kernel<float><<<grid, threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+// q and k (same dtype and inner width; token counts may differ) in one launch;
+// shapes the bulk path cannot take run as two launches.
+cudaError_t launch_qk_prep_pair(const QkPrepParams& p0, const QkPrepParams& p1, bool bf16, cudaStream_t s) {
+  const int64_t rows0 = (int64_t)p0.B * p0.tokens, rows1 = (int64_t)p1.B * p1.tokens;
+  const size_t row_bytes = (size_t)p0.inner * (bf16 ? 2 : 4);
+  const int stages = (int)std::min<size_t>(8, (47 * 1024) / (row_bytes + 8));
+  if (rows0 == 0 || rows1 == 0 || !p0.vec || !p1.vec || stages < 2 || p0.inner != p1.inner) {
+    cudaError_t e = launch_qk_prep(p0, bf16, s);
+    return e != cudaSuccess ? e : launch_qk_prep(p1, bf16, s);
+  }
+  const int threads = p0.inner / 16;
+  int dev = 0, sms = 148, per_sm = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = (size_t)stages * (row_bytes + 8);
+  cudaError_t e = bf16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_bulk_pair_kernel<__nv_bfloat16>, threads, smem)
+                       : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_prep_bulk_pair_kernel<float>, threads, smem);
+  if (e != cudaSuccess) return e;
+  const int grid = (int)std::min<int64_t>(rows0 + rows1, (int64_t)std::max(1, per_sm) * sms);
+  if (grid < 2) {
+    e = launch_qk_prep(p0, bf16, s);
+    return e != cudaSuccess ? e : launch_qk_prep(p1, bf16, s);
+  }
+  // blocks in proportion to rows, at least one per job and none beyond a job's rows
+  int g0 = (int)((grid * rows0 + (rows0 + rows1) / 2) / (rows0 + rows1));
+  g0 = (int)std::min<int64_t>(std::max(1, std::min(g0, grid - 1)), rows0);
+  const int g1 = (int)std::min<int64_t>(grid - g0, rows1);
+  if (bf16)
+    qk_prep_bulk_pair_kernel<__nv_bfloat16><<<g0 + g1, threads, smem, s>>>(p0, p1, stages, g0);
+  else
+    qk_prep_bulk_pair_kernel<float><<<g0 + g1, threads, smem, s>>>(p0, p1, stages, g0);
   return cudaGetLastError();
 }
 

@@ -23,7 +23,7 @@ F32, BF16 = 0, 1
 
 EXPORTED = (
     "ltxattn_fwd", "ltxattn_fwd_workspace", "ltxattn_fwd_plan", "ltxattn_fwd_noalloc", "ltxattn_bwd", "ltxattn_bwd_workspace",
-    "ltxattn_rope", "ltxattn_rotary_tables", "ltxattn_qk_prep",
+    "ltxattn_rope", "ltxattn_rotary_tables", "ltxattn_qk_prep", "ltxattn_qk_prep_pair",
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
@@ -142,6 +142,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_rotary_tables.restype = ctypes.c_int
     L.ltxattn_qk_prep.argtypes = [ctypes.POINTER(QkPrepArgs), vp]
     L.ltxattn_qk_prep.restype = ctypes.c_int
+    L.ltxattn_qk_prep_pair.argtypes = [ctypes.POINTER(QkPrepArgs), ctypes.POINTER(QkPrepArgs), vp]
+    L.ltxattn_qk_prep_pair.restype = ctypes.c_int
     L.ltxattn_comm_unique_id.argtypes = [ctypes.POINTER(ctypes.c_uint8)]
     L.ltxattn_comm_unique_id.restype = ctypes.c_int
     L.ltxattn_comm_init.argtypes = [ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32,

@@ -384,14 +384,8 @@ def rotary_tables(positions: torch.Tensor, max_pos, inner: int, heads: int, thet
     return Rotary(cos, sin)
 
 
-def qk_prep(x: torch.Tensor, weight: torch.Tensor, heads: int, rotary: Optional[Rotary] = None,
-            eps: float = 1e-6, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """q / k preparation of ``DiTAttention`` (DiTAttention.swift:358-367) through ``ltxattn_qk_prep``.
-
-    ``x`` is the projection output ``[B, tokens, heads * D]`` (unit stride along
-    the last dim); returns ``split-RoPE(split(rmsNorm(x, weight)))`` as
-    ``[B, heads, tokens, D]`` (or into ``out``).
-    """
+def _qk_args(x: torch.Tensor, weight: torch.Tensor, heads: int, rotary: Optional[Rotary], eps: float,
+             out: Optional[torch.Tensor]):
     _check_cuda("x", x)
     if x.dim() != 3 or x.stride(2) != 1 or x.shape[2] % heads:
         raise Failure.shape("x", x.shape, f"[B, tokens, {heads} * headDim] with a unit last stride")
@@ -409,10 +403,35 @@ def qk_prep(x: torch.Tensor, weight: torch.Tensor, heads: int, rotary: Optional[
     a.weight, a.eps = weight.data_ptr(), float(eps)
     a.rotary = _rotary("rotary", rotary, B, heads, T, D, x.dtype)
     a.out = _view("out", out, (B, heads, T, D))
+    return a, out
+
+
+def qk_prep(x: torch.Tensor, weight: torch.Tensor, heads: int, rotary: Optional[Rotary] = None,
+            eps: float = 1e-6, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """q / k preparation of ``DiTAttention`` (DiTAttention.swift:358-367) through ``ltxattn_qk_prep``.
+
+    ``x`` is the projection output ``[B, tokens, heads * D]`` (unit stride along
+    the last dim); returns ``split-RoPE(split(rmsNorm(x, weight)))`` as
+    ``[B, heads, tokens, D]`` (or into ``out``).
+    """
+    a, out = _qk_args(x, weight, heads, rotary, eps, out)
     rc = _lib.load().ltxattn_qk_prep(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
     if rc != _lib.OK:
         raise Failure.from_status(rc)
     return out
+
+
+def qk_prep_pair(xq: torch.Tensor, wq: torch.Tensor, xk: torch.Tensor, wk: torch.Tensor, heads: int,
+                 q_rotary: Optional[Rotary] = None, k_rotary: Optional[Rotary] = None, eps: float = 1e-6,
+                 out_q: Optional[torch.Tensor] = None, out_k: Optional[torch.Tensor] = None, stream=None):
+    """``qk_prep`` of q and of k in one launch (``ltxattn_qk_prep_pair``); returns ``(qh, kh)``.
+    The key stream may have its own token count (a cross-attention)."""
+    aq, out_q = _qk_args(xq, wq, heads, q_rotary, eps, out_q)
+    ak, out_k = _qk_args(xk, wk, heads, k_rotary, eps, out_k)
+    rc = _lib.load().ltxattn_qk_prep_pair(ctypes.byref(aq), ctypes.byref(ak), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out_q, out_k
 
 
 def device_status(clear: bool = True) -> int:

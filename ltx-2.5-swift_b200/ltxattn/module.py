@@ -3,7 +3,7 @@
 
     v = linear(kv, to_v)                                   # :341
     q = rmsNorm(linear(x, to_q)), k = rmsNorm(linear(kv, to_k))
-    qh, kh = split-RoPE(split(q)), split-RoPE(split(k))    # ltxattn_qk_prep, :358-367
+    qh, kh = split-RoPE(split(q)), split-RoPE(split(k))    # ltxattn_qk_prep_pair, :358-367
     out = SDPA(qh, kh, split(v), 1/sqrt(D))                # ltxattn_fwd, :369-382
     out = out * 2 sigmoid(linear(x, to_gate_logits))       # fused into ltxattn_fwd's store, :395-399
     return linear(merge(out), to_out.0)                    # merge by view, :401-403
@@ -23,7 +23,7 @@ from typing import Dict, Optional
 
 import torch
 
-from .backend import AttentionBackend, Failure, Rotary, Variant, qk_prep
+from .backend import AttentionBackend, Failure, Rotary, Variant, qk_prep_pair
 
 NORM_EPS = 1e-6  # DiTAttention.normEpsilon
 
@@ -82,8 +82,7 @@ class DiTAttentionModule:
         else:
             q = linear(x, w, "to_q")
             k = linear(kv, w, "to_k")
-            qh = qk_prep(q, w["q_norm.weight"].to(q.dtype), H, rotary, eps=NORM_EPS)
-            kh = qk_prep(k, w["k_norm.weight"].to(k.dtype), H, key_rotary if key_rotary is not None else rotary,
-                         eps=NORM_EPS)
+            qh, kh = qk_prep_pair(q, w["q_norm.weight"].to(q.dtype), k, w["k_norm.weight"].to(k.dtype), H,
+                                  rotary, key_rotary if key_rotary is not None else rotary, eps=NORM_EPS)
             AttentionBackend.attention(qh, kh, vh, scale=1.0 / math.sqrt(D), out=out_view, gate=logits)
         return linear(merged, w, "to_out.0")

@@ -80,3 +80,42 @@ def test_qk_prep_refuses_unsupported_widths():
     x = torch.zeros((1, 4, 24 * 16), device="cuda", dtype=torch.bfloat16)  # inner 384
     with pytest.raises(Failure):
         qk_prep(x, torch.ones(384, device="cuda", dtype=torch.bfloat16), 6)
+
+
+@pytest.mark.parametrize("dtype,Tq,Tk,D", [(torch.bfloat16, 150, 150, 128), (torch.bfloat16, 300, 126, 64),
+                                           (torch.float32, 40, 70, 64)])
+def test_pair_matches_two_single_calls(dtype, Tq, Tk, D):
+    # ltxattn_qk_prep_pair: q and k (token counts may differ) in one launch, the same bits
+    from ltxattn import qk_prep_pair
+    H, B = 32, 2
+    inner = H * D
+    bf = dtype == torch.bfloat16
+    xq = torch.from_numpy(inputs.seeded_tensor(21, (B, Tq, inner), bf16=bf) * 2.0).to("cuda", dtype)
+    xk = torch.from_numpy(inputs.seeded_tensor(22, (B, Tk, inner), bf16=bf) * 2.0).to("cuda", dtype)
+    wq = torch.from_numpy(norm_weight(inner, 4, bf)).to("cuda", dtype)
+    wk = torch.from_numpy(norm_weight(inner, 5, bf)).to("cuda", dtype)
+    cq, sq = inputs.rope1d(np.arange(Tq, dtype=np.float64), D, bf16=bf)
+    ck, sk = inputs.rope1d(np.arange(Tk, dtype=np.float64) * 0.5, D, bf16=bf)
+    rq = Rotary(torch.from_numpy(cq).to("cuda", dtype), torch.from_numpy(sq).to("cuda", dtype))
+    rk = Rotary(torch.from_numpy(ck).to("cuda", dtype), torch.from_numpy(sk).to("cuda", dtype))
+    qh, kh = qk_prep_pair(xq, wq, xk, wk, H, rq, rk)
+    q1 = qk_prep(xq, wq, H, rq)
+    k1 = qk_prep(xk, wk, H, rk)
+    torch.cuda.synchronize()
+    # (the single calls are checked against the oracle above)
+    assert torch.equal(qh, q1) and torch.equal(kh, k1)
+
+
+def test_pair_with_a_strided_input_takes_two_launches():
+    # an x view whose rows are not 16-byte aligned cannot stream by bulk copies:
+    # the pair falls back to two single launches, with the same results
+    from ltxattn import qk_prep_pair
+    H, D, T = 32, 64, 20
+    inner = H * D
+    base = torch.from_numpy(inputs.seeded_tensor(23, (1, T, inner + 1))).to("cuda", torch.bfloat16)
+    xq = base[:, :, 1:]  # offset by one element
+    xk = torch.from_numpy(inputs.seeded_tensor(24, (1, T, inner))).to("cuda", torch.bfloat16)
+    w = torch.from_numpy(norm_weight(inner)).to("cuda", torch.bfloat16)
+    qh, kh = qk_prep_pair(xq, w, xk, w, H)
+    torch.cuda.synchronize()
+    assert torch.equal(qh, qk_prep(xq, w, H)) and torch.equal(kh, qk_prep(xk, w, H))
