@@ -156,6 +156,13 @@ public enum AttentionBackend {
         try check(ltxattn_qk_prep(&a, stream))
     }
 
+    /// `prepareQK` for q and k in one launch (the key stream may have its own token count);
+    /// each result is what `prepareQK` gives for its arguments.
+    public static func prepareQKPair(_ q: inout ltxattn_qk_prep_args, _ k: inout ltxattn_qk_prep_args,
+                                     stream: UnsafeMutableRawPointer?) throws {
+        try check(ltxattn_qk_prep_pair(&q, &k, stream))
+    }
+
     /// Device scratch the same arguments need (call once per shape; the caller allocates).
     public static func workspaceBytes(_ a: inout ltxattn_fwd_args) -> Int {
         Int(ltxattn_fwd_workspace(&a))
