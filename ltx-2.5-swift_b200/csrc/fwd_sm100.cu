@@ -37,7 +37,7 @@
 // Every exponential runs on the MUFU (ex2.approx.f32).  Measured alternatives
 // that were slower at config 2: an FMA-pipe polynomial for an eighth or a
 // quarter of them (exp2_poly2; kPolyCols keeps the option, at 0) and paired
-// f16 exponentials (exp2_f16x2; the widening conversions share the MUFU pipe).
+// f16 exponentials (ex2.approx.f16x2; the widening conversions share the MUFU pipe).
 //
 // Keys: a tile whose keys are all masked is skipped outright (its weight is
 // exactly zero); partial tiles and the ragged tail get -inf logits per

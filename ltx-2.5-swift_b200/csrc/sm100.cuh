@@ -481,22 +481,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   return r;
 }
 
-// Two exponentials per MUFU operation: 2^x for a pair, evaluated by
-// ex2.approx.f16x2 on f16 arguments and widened back to fp32.  For this
-// library's arguments (x <= 8; large weights have |x| small, where f16 spacing
-// is <= 2^-11) the result is well inside the bf16 rounding P receives; values
-// below 2^-24 flush to 0.  Halves the MUFU load of the softmax.
-__device__ __forceinline__ float2 exp2_f16x2(float2 x) {
-  uint32_t xh, eh;
-  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(xh) : "f"(x.x), "f"(x.y));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(eh) : "r"(xh));
-  float2 r;
-  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "r"(eh));
-  return r;
-}
-
 // ---------------------------------------------------------------------------
 // Split RoPE on 8 rotary pairs held as bf16x8 vectors (x1 = first half, x2 =
 // second half of the rows, c / s the table entries):
