@@ -122,3 +122,27 @@ def test_rotary_gate_merged_view_and_grouped_heads():
     assert same_bits(a, b)
     ref, _ = oracle.attention_reference(q2[:, :2], k2[:, :2], v2[:, :2], q_rot=(qc, qs), k_rot=(kc, ks), bf16=True)
     check(a[:, :2], ref, "cross-modal rotary")
+
+
+def test_head_block_and_per_batch_masks():
+    # a rank's head block of a sharded job, three batch rows with different masks
+    # (one with no valid key), through the persistent kernel
+    B, H, Lq, Lk, D = 3, 64, 640, 96, 128  # 3 query blocks x 56 heads x 3 batches = 504 units
+    q, k, v = make(171, B, H, H, Lq, Lk, D)
+    m = np.zeros((B, Lk), np.uint8)
+    m[0, :50] = 1
+    m[1] = np.random.default_rng(8).random(Lk) < 0.7
+    md = torch.from_numpy(m).cuda()
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.zeros_like(qd)
+    lse = torch.zeros((B, H, Lq), device="cuda", dtype=torch.float32)
+    AttentionBackend.attention(qd, kd, vd, key_mask=md, out=out, lse=lse, head_begin=8, head_count=56)
+    one = torch.zeros_like(qd)
+    lse1 = torch.zeros_like(lse)
+    AttentionBackend.attention(qd, kd, vd, key_mask=md, out=one, lse=lse1, head_begin=8, head_count=56, num_splits=1)
+    assert same_bits(out, one) and torch.equal(lse, lse1)
+    assert torch.count_nonzero(out[:, :8]).item() == 0  # heads outside the block untouched
+    hs = [8, 40, 63]
+    ref, ref_lse = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs], mask=m)
+    check(out[:, hs], ref, "head block")
+    assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS
