@@ -8,7 +8,8 @@
  * core it stands in for is the SDPA switch of
  * `Sources/LTXModules/DiTAttention.swift:369-382`, together with the split
  * RoPE applied just before it (`:364-367`, `:206-234`).  A Swift caller binds
- * this header through a module map.
+ * this header through a SwiftPM system-library target whose module map names
+ * it (ltx-2.5-swift_b200/swift/CLTXAttnCUDA/module.modulemap).
  *
  * Conventions
  *  - Plain pointers and sizes only.  Device pointers are CUDA device memory;
@@ -319,6 +320,11 @@ typedef struct ltxattn_gather_args {
 
 LTXATTN_API int ltxattn_allgather_heads(const ltxattn_gather_args* args, ltxattn_comm* comm, void* stream);
 
+/* The rank count and this rank's index as NCCL itself reports them
+ * (ncclCommCount / ncclCommUserRank), for checking a launch's world size.
+ * No counterpart in the reference. */
+LTXATTN_API int ltxattn_comm_size(const ltxattn_comm* comm, int32_t* nranks, int32_t* rank);
+
 /* ---- device discovery ----------------------------------------------------- */
 
 /* Replaces `LTXHardware.Machine.detect` (`Machine.swift:31-36`) and the Metal
@@ -352,6 +358,20 @@ LTXATTN_API const char* ltxattn_last_error(void);
  * encoded wait site (may be NULL). */
 LTXATTN_API int ltxattn_device_status(int32_t clear, int32_t* site);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one
+ * CTA on `stream` that waits, with the same bounded wait as the attention
+ * kernels, on an mbarrier nothing ever arrives at.  After limit_us
+ * microseconds (1 .. 1000000) the wait gives up, records LTXATTN_ERR_TIMEOUT
+ * with site 99 in the device error word, and the CTA frees its tensor memory
+ * and exits normally; no fault, and the context stays usable.  Returns
+ * LTXATTN_OK once launched; ltxattn_device_status then reports the timeout. */
+LTXATTN_API int ltxattn_selftest_wait_timeout(uint32_t limit_us, void* stream);
+
+/* Library state: the device error word's address and the no-allocation
+ * forward's scratch address are looked up once per device and kept for the
+ * life of the process.  Do not keep using the library on a device after
+ * cudaDeviceReset (or any teardown of the device's primary context) in the
+ * same process: those addresses then no longer belong to the new context. */
 LTXATTN_API int ltxattn_abi_version(void);
 
 #ifdef __cplusplus

@@ -41,6 +41,8 @@ struct NcclApi {
   ncclResult_t (*GroupStart)();
   ncclResult_t (*GroupEnd)();
   const char* (*GetErrorString)(ncclResult_t);
+  ncclResult_t (*CommCount)(const ncclComm_t, int*);
+  ncclResult_t (*CommUserRank)(const ncclComm_t, int*);
   bool ok;
 };
 
@@ -59,8 +61,10 @@ const NcclApi& nccl() {
     api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
     api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+    api.CommCount = reinterpret_cast<decltype(api.CommCount)>(dlsym(h, "ncclCommCount"));
+    api.CommUserRank = reinterpret_cast<decltype(api.CommUserRank)>(dlsym(h, "ncclCommUserRank"));
     api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GroupStart &&
-             api.GroupEnd && api.GetErrorString;
+             api.GroupEnd && api.GetErrorString && api.CommCount && api.CommUserRank;
   });
   return api;
 }
@@ -116,6 +120,19 @@ int ltxattn_comm_destroy(ltxattn_comm* comm) {
   }
   delete comm;
   return rc;
+}
+
+int ltxattn_comm_size(const ltxattn_comm* comm, int32_t* nranks, int32_t* rank) {
+  if (!comm || !nranks || !rank) return ltx::set_error_message(LTXATTN_ERR_ARG, "comm, nranks or rank is NULL");
+  if (int rc = need_nccl()) return rc;
+  int n = 0, r = 0;
+  ncclResult_t res = nccl().CommCount(comm->nccl, &n);
+  if (res != ncclSuccess) return nccl_fail("ncclCommCount", res);
+  res = nccl().CommUserRank(comm->nccl, &r);
+  if (res != ncclSuccess) return nccl_fail("ncclCommUserRank", res);
+  *nranks = n;
+  *rank = r;
+  return LTXATTN_OK;
 }
 
 int ltxattn_allgather_heads(const ltxattn_gather_args* a, ltxattn_comm* comm, void* stream) {

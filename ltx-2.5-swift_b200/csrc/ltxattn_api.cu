@@ -394,7 +394,9 @@ int set_error_message(int status, const char* msg) {
 }
 
 // The device error word's address, looked up once per device (a call then
-// makes no runtime query that could disturb a stream capture).
+// makes no runtime query that could disturb a stream capture).  The address
+// belongs to the context of that first call; after a cudaDeviceReset in the
+// same process it is stale, so the library is not used across one.
 int* device_error_word() {
   constexpr int kDevs = 64;
   static std::mutex mu;

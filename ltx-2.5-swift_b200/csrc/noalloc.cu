@@ -23,6 +23,10 @@
 //    GPU (different streams, or different host threads without ordering)
 //    race on the array and corrupt each other's results; serialise them.
 //  - No cudaMalloc, cudaFree or allocating library routine is called.
+//  - The looked-up address belongs to the device's context at that first
+//    call: after cudaDeviceReset (or any other teardown of the primary
+//    context) in the same process it is stale, so the library must not be
+//    used on that device again in that process.
 #include <cstdio>
 #include <mutex>
 

@@ -74,15 +74,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on an mbarrier phase.  `abort_flag` (shared) lets one thread's
 // timeout release every other waiter of the CTA quickly.  Returns false when
 // the wait gave up; the caller must then stop issuing work.
+// `limit_ns` is LTX_WAIT_LIMIT_NS everywhere but in the failure-detection
+// self-test, which gives a short one.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err_word, int site) {
+                                          volatile int* abort_flag, int* err_word, int site,
+                                          uint64_t limit_ns = LTX_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         if (err_word) atomicCAS(err_word, 0, (site << 8) | kErrTimeout);
         return false;
@@ -383,8 +386,8 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // cycles after the phase completed.)  The lanes read the same barrier state
 // and the same timer in each converged poll, so they leave the loop together.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int site) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, err, site);
+                                          int* err, int site, uint64_t limit_ns = LTX_WAIT_LIMIT_NS) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, site, limit_ns);
   return __all_sync(0xffffffffu, ok);
 }
 

@@ -27,6 +27,7 @@ EXPORTED = (
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
+    "ltxattn_comm_size", "ltxattn_selftest_wait_timeout",
 )
 
 
@@ -161,6 +162,10 @@ def load(path: str = LIB_PATH):
     L.ltxattn_last_error.restype = ctypes.c_char_p
     L.ltxattn_device_status.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
     L.ltxattn_device_status.restype = ctypes.c_int
+    L.ltxattn_comm_size.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
+    L.ltxattn_comm_size.restype = ctypes.c_int
+    L.ltxattn_selftest_wait_timeout.argtypes = [ctypes.c_uint32, vp]
+    L.ltxattn_selftest_wait_timeout.restype = ctypes.c_int
     L.ltxattn_abi_version.argtypes = []
     L.ltxattn_abi_version.restype = ctypes.c_int
     _lib = L

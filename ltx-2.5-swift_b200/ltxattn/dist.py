@@ -78,6 +78,14 @@ class HeadGather:
             raise Failure.from_status(rc)
         self.world, self.rank = world, rank
 
+    def size(self) -> Tuple[int, int]:
+        """(ranks, this rank) as NCCL reports them for the communicator."""
+        n, r = ctypes.c_int32(), ctypes.c_int32()
+        rc = _lib.load().ltxattn_comm_size(self._comm, ctypes.byref(n), ctypes.byref(r))
+        if rc != _lib.OK:
+            raise Failure.from_status(rc)
+        return n.value, r.value
+
     def gather(self, local: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
         """[B, H/N, T, D] contiguous on every rank -> [B, H, T, D] on every rank."""
         if not local.is_contiguous() or local.dim() != 4:

@@ -34,18 +34,34 @@ def _splitmix64_at(seed: int, idx: np.ndarray) -> np.ndarray:
         return z ^ (z >> np.uint64(31))
 
 
-def normal(seed: int, n: int, chunk: int = 1 << 22) -> np.ndarray:
-    """n draws of N(0,1) as float32; element i depends only on (seed, i)."""
+def normal(seed: int, n: int, chunk: int = 1 << 22, start: int = 0) -> np.ndarray:
+    """Draws start .. start+n-1 of N(0,1) as float32; element i depends only on (seed, i)."""
     out = np.empty(n, dtype=np.float32)
     for s in range(0, n, chunk):
         e = min(n, s + chunk)
-        i = np.arange(s, e, dtype=np.uint64)
+        i = np.arange(start + s, start + e, dtype=np.uint64)
         a = _splitmix64_at(seed, np.uint64(2) * i)
         b = _splitmix64_at(seed, np.uint64(2) * i + np.uint64(1))
         u1 = ((a >> np.uint64(11)).astype(np.float64) + 1.0) * 2.0 ** -53
         u2 = (b >> np.uint64(11)).astype(np.float64) * 2.0 ** -53
         out[s:e] = (np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * math.pi * u2)).astype(np.float32)
     return out
+
+
+def bench_bits(seed: int, n: int) -> np.ndarray:
+    """The reference bench's operands (``BenchOperand.bits``,
+    ``Sources/ltx/Bench.swift:474-493``): a sequential splitmix64 stream whose
+    state starts at seed + golden and advances by golden before each draw; the
+    top 24 bits of each output as a unit in [0, 1), centred to (unit - 0.5) * 2
+    and rounded to bf16.  Returned as float32 values (exactly the bf16 ones)."""
+    i = np.arange(n, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + GOLDEN * (i + np.uint64(2))
+        z = (z ^ (z >> np.uint64(30))) * M1
+        z = (z ^ (z >> np.uint64(27))) * M2
+        z = z ^ (z >> np.uint64(31))
+    unit = (z >> np.uint64(40)).astype(np.float32) / np.float32(1 << 24)
+    return round_bf16((unit - np.float32(0.5)) * np.float32(2.0))
 
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:
@@ -74,10 +90,22 @@ def rms_norm_heads(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
     return (x * (1.0 / np.sqrt(ms + np.float32(eps))).astype(np.float32)).astype(np.float32)
 
 
-def seeded_tensor(seed: int, shape, *, rmsnorm: bool = False, bf16: bool = True) -> np.ndarray:
-    """A float32 array holding exactly the values the device receives."""
-    n = int(np.prod(shape))
-    x = normal(seed, n).reshape(shape)
+def seeded_tensor(seed: int, shape, *, rmsnorm: bool = False, bf16: bool = True, heads=None) -> np.ndarray:
+    """A float32 array holding exactly the values the device receives.
+
+    ``heads=(h0, hc)`` with a [B, H, T, D] shape gives heads h0 .. h0+hc-1 of
+    that tensor, the same values as slicing the whole one (how a rank of a
+    head-sharded job builds only its own block)."""
+    if heads is None:
+        n = int(np.prod(shape))
+        x = normal(seed, n).reshape(shape)
+    else:
+        B, H, T, D = shape
+        h0, hc = heads
+        if not (0 <= h0 and hc >= 1 and h0 + hc <= H):
+            raise ValueError(f"heads {heads} outside [0, {H})")
+        per = T * D
+        x = np.stack([normal(seed, hc * per, start=(b * H + h0) * per).reshape(hc, T, D) for b in range(B)])
     if rmsnorm:
         x = rms_norm_heads(x)
     if bf16:

@@ -522,4 +522,54 @@ int oracle_attn_bwd(const float* q, const float* k, const float* v,
     return 0;
 }
 
+/* dK and dV of selected keys of one unmasked head, streaming over the query rows
+ * so that no Lq x Lk matrix is held (the 29,760-token configuration's P would
+ * take 7 GB).  The same closed-form VJP as oracle_attn_bwd, with the row terms
+ * supplied by the caller from a forward of the same head:
+ *     P_ij = exp(scale * q_i.k_j - lse_i),   lse_i the natural log-sum-exp
+ *     delta_i = sum_d dout_id * out_id       (= sum_j P_ij dP_ij)
+ *     dV_j = sum_i P_ij dout_i,   dK_j = scale sum_i P_ij (dout_i.v_j - delta_i) q_i
+ * q, dout [Lq, D]; k, v [Lk, D]; keys[n_keys] the key indices; dk, dv [n_keys, D].
+ * fp64 accumulation. */
+int oracle_attn_bwd_keys(const float* q, const float* k, const float* v, const float* dout,
+                         const float* lse, const float* delta, int Lq, int Lk, int D, double scale,
+                         const int* keys, int n_keys, float* dk, float* dv, int threads) {
+    if (Lq <= 0 || Lk <= 0 || D <= 0 || n_keys < 0) return 1;
+    if (D > 256) return 3;
+    for (int n = 0; n < n_keys; ++n)
+        if (keys[n] < 0 || keys[n] >= Lk) return 1;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int n = 0; n < n_keys; ++n) {
+        const float* kj = k + (int64_t)keys[n] * D;
+        const float* vj = v + (int64_t)keys[n] * D;
+        double ak[256], av[256];
+        for (int d = 0; d < D; ++d) ak[d] = av[d] = 0.0;
+        for (int i = 0; i < Lq; ++i) {
+            const float* qi = q + (int64_t)i * D;
+            const float* gi = dout + (int64_t)i * D;
+            double s = 0.0, dp = 0.0;
+            for (int d = 0; d < D; ++d) {
+                s += (double)qi[d] * kj[d];
+                dp += (double)gi[d] * vj[d];
+            }
+            const double p = exp(s * scale - (double)lse[i]);
+            const double ds = p * (dp - (double)delta[i]);
+            for (int d = 0; d < D; ++d) {
+                ak[d] += ds * qi[d];
+                av[d] += p * gi[d];
+            }
+        }
+        for (int d = 0; d < D; ++d) {
+            dk[(int64_t)n * D + d] = (float)(scale * ak[d]);
+            dv[(int64_t)n * D + d] = (float)av[d];
+        }
+    }
+    return 0;
+}
+
 int oracle_abi_version(void) { return 1; }

@@ -55,6 +55,9 @@ def lib():
         L.oracle_qk_prep.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, _f32p, _f32p,
                                                                          ctypes.c_int64, ctypes.c_int64,
                                                                          ctypes.c_int, _f32p]
+        L.oracle_attn_bwd_keys.argtypes = [_f32p] * 6 + [ctypes.c_int] * 3 + [
+            ctypes.c_double, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _f32p, _f32p, ctypes.c_int]
+        L.oracle_attn_bwd_keys.restype = ctypes.c_int
         for f in ("oracle_rope", "oracle_rope_bwd", "oracle_attn_fwd",
                   "oracle_attn_fwd_f32", "oracle_attn_bwd", "oracle_rotary_tables", "oracle_qk_prep",
                   "oracle_attn_fwd_gemma"):
@@ -165,6 +168,26 @@ def attn_bwd(q, k, v, dout, mask=None, scale=None, threads=0):
                                float(scale), _p(dq), _p(dk), _p(dv), threads)
     assert rc == 0
     return dq, dk, dv
+
+
+def attn_bwd_keys(q, k, v, dout, lse, delta, keys, scale=None, threads=0):
+    """dK, dV of the key indices ``keys`` of one unmasked head ([Lq, D] / [Lk, D]
+    arrays), streaming over query rows; ``lse`` and ``delta`` = rowsum(dout * out)
+    come from a forward of the same head.  Returns (dk, dv) as [len(keys), D]."""
+    q, k, v, dout = _f32(q), _f32(k), _f32(v), _f32(dout)
+    lse, delta = _f32(lse).reshape(-1), _f32(delta).reshape(-1)
+    Lq, D = q.shape
+    Lk = k.shape[0]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    idx = np.ascontiguousarray(keys, dtype=np.int32)
+    dk = np.empty((idx.size, D), np.float32)
+    dv = np.empty((idx.size, D), np.float32)
+    rc = lib().oracle_attn_bwd_keys(_p(q), _p(k), _p(v), _p(dout), _p(lse), _p(delta), Lq, Lk, D, float(scale),
+                                    idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), idx.size, _p(dk), _p(dv),
+                                    threads)
+    assert rc == 0
+    return dk, dv
 
 
 def attention_reference(q, k, v, mask=None, q_rot=None, k_rot=None, bf16=False, scale=None):

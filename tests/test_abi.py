@@ -203,3 +203,13 @@ def test_new_entry_points_refuse_bad_arguments():
     q = _lib.QkPrepArgs()
     q.dtype, q.batch, q.tokens, q.heads, q.head_dim = _lib.BF16, 1, 4, 3, 64  # inner 192
     assert L.ltxattn_qk_prep(ctypes.byref(q), None) == _lib.ERR_UNSUPPORTED
+
+
+def test_selftest_and_comm_size_refuse_bad_arguments():
+    # argument checks that run before any device work
+    L = _lib.load()
+    assert L.ltxattn_selftest_wait_timeout(0, None) == _lib.ERR_ARG
+    assert L.ltxattn_selftest_wait_timeout(1000001, None) == _lib.ERR_ARG
+    assert "limit_us" in _lib.last_error()
+    n = ctypes.c_int32()
+    assert L.ltxattn_comm_size(None, ctypes.byref(n), ctypes.byref(n)) == _lib.ERR_ARG

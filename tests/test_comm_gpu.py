@@ -16,6 +16,7 @@ def test_single_rank_gather_is_identity_layout():
     assert _lib.load().ltxattn_comm_unique_id(raw) == _lib.OK, _lib.last_error()
     g = HeadGather(1, 0, bytes(raw), torch.cuda.current_device())
     try:
+        assert g.size() == (1, 0)  # what NCCL itself reports
         for dt in (torch.bfloat16, torch.float32):
             local = torch.randn(2, 4, 33, 64, device="cuda").to(dt)
             out = g.gather(local)

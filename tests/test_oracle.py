@@ -90,6 +90,32 @@ def test_generators_agree():
     assert np.array_equal(inputs.round_bf16(a), oracle.round_bf16(a))
 
 
+def test_bench_bits_is_the_reference_operand_stream():
+    # Sources/ltx/Bench.swift:479-493 stepped one element at a time with Python
+    # integers, against the vectorised restatement the benchmark uses
+    mask = (1 << 64) - 1
+    seed = 0x5EED + 2
+    state = (seed + 0x9E3779B97F4A7C15) & mask
+    want = []
+    for _ in range(64):
+        state = (state + 0x9E3779B97F4A7C15) & mask
+        z = state
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & mask
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & mask
+        z ^= z >> 31
+        unit = np.float32(z >> 40) / np.float32(1 << 24)
+        want.append((unit - np.float32(0.5)) * np.float32(2))
+    got = inputs.bench_bits(seed, 64)
+    assert np.array_equal(got, inputs.round_bf16(np.array(want, np.float32)))
+    assert got.min() >= -1.0 and got.max() <= 1.0
+
+
+def test_head_slices_are_slices_of_the_whole_tensor():
+    whole = inputs.seeded_tensor(5, (2, 6, 10, 16), rmsnorm=True)
+    part = inputs.seeded_tensor(5, (2, 6, 10, 16), rmsnorm=True, heads=(2, 3))
+    assert np.array_equal(whole[:, 2:5], part)
+
+
 def test_uniform_attention_is_mean_of_v():
     rng = np.random.default_rng(0)
     q = np.zeros((1, 2, 5, 64), np.float32)
@@ -173,6 +199,22 @@ def test_backward_matches_finite_differences():
             args_m = [m if arr is x else x for x in (q, k, v)]
             fd = (loss(*args_p) - loss(*args_m)) / (2 * eps)
             assert abs(fd - g[idx]) < 2e-3, (idx, fd, g[idx])
+
+
+def test_streaming_key_backward_matches_the_full_backward():
+    # oracle_attn_bwd_keys (rows streamed, lse and delta from a forward) against
+    # oracle_attn_bwd on the same head, for a scattered set of keys
+    q = inputs.seeded_tensor(21, (1, 1, 300, 64), rmsnorm=True)
+    k = inputs.seeded_tensor(22, (1, 1, 257, 64), rmsnorm=True)
+    v = inputs.seeded_tensor(23, (1, 1, 257, 64))
+    do = inputs.seeded_tensor(24, (1, 1, 300, 64))
+    dq, dk, dv = oracle.attn_bwd(q, k, v, do)
+    out, lse = oracle.attn_fwd(q, k, v)
+    delta = np.sum(out.astype(np.float64) * do, axis=-1)
+    keys = [0, 1, 77, 128, 200, 256]
+    dk_s, dv_s = oracle.attn_bwd_keys(q[0, 0], k[0, 0], v[0, 0], do[0, 0], lse[0, 0], delta[0, 0], keys)
+    np.testing.assert_allclose(dk_s, dk[0, 0, keys], atol=2e-6)
+    np.testing.assert_allclose(dv_s, dv[0, 0, keys], atol=2e-6)
 
 
 def test_rotary_tables_c_restatement_matches_the_numpy_one():

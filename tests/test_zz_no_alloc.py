@@ -7,8 +7,11 @@ fixed 32 MiB array inside the library.  This file runs last (pytest collects
 files in name order) so that a failure here leaves every other test already
 run; it also passes when run alone in a fresh process.
 
-Each case is called twice in a row: the shared array keeps the previous call's
-contents, and the second call must not depend on them.
+Each case is called twice, with a call of another shape and other data in
+between: the shared array keeps the previous call's contents, so the second
+call of a case starts from scratch bytes another call wrote and must not
+depend on them.  Every case needs scratch (asserted), so the array is always
+exercised; one case is also checked against the CPU oracle directly.
 """
 import ctypes
 
@@ -16,6 +19,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from ltxattn import AttentionBackend, Rotary, _lib, inputs
 
 pytestmark = pytest.mark.gpu
@@ -46,6 +50,7 @@ def _noalloc(q, k, v, qr, kr):
     a, out = AttentionBackend.make_fwd_args(q, k, v, 1.0 / np.sqrt(q.shape[-1]), q_rotary=qr, k_rotary=kr,
                                             lse=lse, out=out)
     L = _lib.load()
+    assert L.ltxattn_fwd_workspace(ctypes.byref(a)) > 0  # the case really uses the scratch array
     rc = L.ltxattn_fwd_noalloc(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == _lib.OK, _lib.last_error()
     torch.cuda.synchronize()
@@ -67,10 +72,26 @@ def test_noalloc_matches_fwd_on_two_calls(shape, rope):
     B, H, Lq, Lk, D = shape
     q, k, v, qr, kr = _case(B, H, Lq, Lk, D, seed=900 + Lq, rope=rope)
     ref, ref_lse = AttentionBackend.attention(q, k, v, q_rotary=qr, k_rotary=kr, save_lse=True)
-    for _ in range(2):
+    # a call of another shape and other data, so the array holds other bytes
+    other = _case(1, 6, 140, 2000, 128, seed=77, rope=True)
+    for i in range(2):
         out, lse = _noalloc(q, k, v, qr, kr)
         _check(out, ref)
         assert (lse - ref_lse).abs().max().item() <= 2e-3
+        if i == 0:
+            _noalloc(*other)
+
+
+def test_noalloc_against_the_oracle():
+    B, H, Lq, Lk, D = 1, 4, 126, 3120, 64
+    seed = 930
+    qh = inputs.seeded_tensor(seed + 2, (B, H, Lq, D), rmsnorm=True)
+    kh = inputs.seeded_tensor(seed + 3, (B, H, Lk, D), rmsnorm=True)
+    vh = inputs.seeded_tensor(seed + 4, (B, H, Lk, D))
+    out, lse = _noalloc(_dev(qh), _dev(kh), _dev(vh), None, None)
+    ref, ref_lse = oracle.attn_fwd(qh, kh, vh)
+    _check(out.cpu(), torch.from_numpy(ref))
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() <= 2e-3
 
 
 def test_noalloc_refuses_scratch_beyond_its_array():
