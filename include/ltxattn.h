@@ -347,6 +347,39 @@ typedef struct ltxattn_device_info {
 LTXATTN_API int ltxattn_device_count(int32_t* count);
 LTXATTN_API int ltxattn_device_query(int32_t device, ltxattn_device_info* info);
 
+/* ---- memory planning ------------------------------------------------------ */
+
+/* Whether an attention working set fits the current device: the counterpart of
+ * `LTXHardware.MemoryPlan` (`MemoryPlan.swift:27-34,62-74`).  The reference fits
+ * its fused-path activation bytes to MLX allocator peaks (4.67e5 B per video
+ * token); here the bytes are the exact buffers of one call at this shape: q, k,
+ * v, out and the fp32 lse, the library's workspace for the call
+ * (ltxattn_fwd_workspace), and with `training` the backward's dout, dq, dk, dv
+ * and ltxattn_bwd_workspace.  A self-attention shape (q, k, v of `tokens`
+ * rows) is planned; `rotary` = 1 when the call rotates q and k. */
+typedef struct ltxattn_memory_plan_args {
+  int32_t dtype;
+  int32_t batch, heads, tokens, head_dim;
+  int32_t rotary;
+  int32_t training;
+  int64_t resident_bytes;   /* already held on the device (weights; the reference's DiT is 42.06e9) */
+  int64_t available_bytes;  /* 0: the current device's free memory (cudaMemGetInfo) */
+  double margin_fraction;   /* MemoryPlan.plan's margin (0.15 there) */
+} ltxattn_memory_plan_args;
+
+typedef struct ltxattn_memory_plan_info {
+  int64_t tensor_bytes;     /* q, k, v, out, lse */
+  int64_t workspace_bytes;  /* ltxattn_fwd_workspace of the call */
+  int64_t backward_bytes;   /* dout, dq, dk, dv and ltxattn_bwd_workspace (0 unless training) */
+  int64_t peak_bytes;       /* resident + the three above */
+  int64_t available_bytes;
+  int64_t headroom_bytes;   /* available - peak * (1 + margin), as MemoryPlan.headroomBytes */
+  int32_t fits;             /* headroom > 0 */
+  double bytes_per_token;   /* attention bytes per batch row token: the counterpart of 4.67e5 */
+} ltxattn_memory_plan_info;
+
+LTXATTN_API int ltxattn_memory_plan(const ltxattn_memory_plan_args* args, ltxattn_memory_plan_info* info);
+
 /* ---- status --------------------------------------------------------------- */
 
 /* Message for this thread's most recent failure ("" if none). */

@@ -940,8 +940,12 @@ int ltxattn_device_query(int32_t device, ltxattn_device_info* info) {
 int ltxattn_device_status(int32_t clear, int32_t* site) {
   int* w = device_error_word();
   if (!w) return fail(LTXATTN_ERR_CUDA, "no device error word");
+  // every stream of the device, including non-blocking ones that a plain
+  // cudaMemcpy would not wait for
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "synchronising the device");
   int v = 0;
-  cudaError_t e = cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost);
+  e = cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
   if (clear && v != 0) {
     const int z = 0;

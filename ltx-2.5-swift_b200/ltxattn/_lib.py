@@ -27,7 +27,7 @@ EXPORTED = (
     "ltxattn_comm_unique_id", "ltxattn_comm_init", "ltxattn_comm_destroy",
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
-    "ltxattn_comm_size", "ltxattn_selftest_wait_timeout",
+    "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
 )
 
 
@@ -114,6 +114,20 @@ class DeviceInfo(ctypes.Structure):
 _lib = None
 
 
+class MemoryPlanArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("rotary", ctypes.c_int32),
+                ("training", ctypes.c_int32), ("resident_bytes", ctypes.c_int64),
+                ("available_bytes", ctypes.c_int64), ("margin_fraction", ctypes.c_double)]
+
+
+class MemoryPlanInfo(ctypes.Structure):
+    _fields_ = [("tensor_bytes", ctypes.c_int64), ("workspace_bytes", ctypes.c_int64),
+                ("backward_bytes", ctypes.c_int64), ("peak_bytes", ctypes.c_int64),
+                ("available_bytes", ctypes.c_int64), ("headroom_bytes", ctypes.c_int64),
+                ("fits", ctypes.c_int32), ("bytes_per_token", ctypes.c_double)]
+
+
 def load(path: str = LIB_PATH):
     """Load the in-tree library; raises when it has not been built."""
     global _lib
@@ -166,6 +180,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_comm_size.restype = ctypes.c_int
     L.ltxattn_selftest_wait_timeout.argtypes = [ctypes.c_uint32, vp]
     L.ltxattn_selftest_wait_timeout.restype = ctypes.c_int
+    L.ltxattn_memory_plan.argtypes = [ctypes.POINTER(MemoryPlanArgs), ctypes.POINTER(MemoryPlanInfo)]
+    L.ltxattn_memory_plan.restype = ctypes.c_int
     L.ltxattn_abi_version.argtypes = []
     L.ltxattn_abi_version.restype = ctypes.c_int
     _lib = L

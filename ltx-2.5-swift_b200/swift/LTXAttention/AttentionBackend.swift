@@ -107,6 +107,63 @@ public enum AttentionBackend {
         try check(ltxattn_fwd(&a, stream))
     }
 
+    /// The VJP of `attention` for LoRA training under gradient checkpointing
+    /// (LoRATrainingStep.swift:283-304, GradientCheckpoint.swift:48-67): dq, dk, dv of
+    /// sum(dout * out), P recomputed from the forward's `lse` (no stored score matrix).
+    /// With rotary tables the gradients are with respect to the un-rotated q and k.
+    /// `out` is the forward's un-gated output; `workspace` holds
+    /// `backwardWorkspaceBytes` bytes.
+    public static func attentionBackward(
+        bf16: Bool, batch: Int32, heads: Int32, queryTokens: Int32, keyTokens: Int32, headDim: Int32,
+        q: DeviceTensor, k: DeviceTensor, v: DeviceTensor, out: DeviceTensor, dout: DeviceTensor,
+        lse: UnsafePointer<Float>, dq: DeviceTensor, dk: DeviceTensor, dv: DeviceTensor, scale: Float,
+        keyMask: UnsafePointer<UInt8>? = nil, rotary: DeviceRotary? = nil, keyRotary: DeviceRotary? = nil,
+        workspace: UnsafeMutableRawPointer?, workspaceBytes: Int, stream: UnsafeMutableRawPointer?
+    ) throws {
+        var a = backwardArgs(bf16: bf16, batch: batch, heads: heads, queryTokens: queryTokens,
+                             keyTokens: keyTokens, headDim: headDim, q: q, k: k, v: v, out: out, dout: dout,
+                             lse: lse, dq: dq, dk: dk, dv: dv, scale: scale, keyMask: keyMask, rotary: rotary,
+                             keyRotary: keyRotary)
+        a.workspace = workspace
+        a.workspace_bytes = workspaceBytes
+        try check(ltxattn_bwd(&a, stream))
+    }
+
+    /// The argument block of `attentionBackward` (for `backwardWorkspaceBytes`).
+    public static func backwardArgs(
+        bf16: Bool, batch: Int32, heads: Int32, queryTokens: Int32, keyTokens: Int32, headDim: Int32,
+        q: DeviceTensor, k: DeviceTensor, v: DeviceTensor, out: DeviceTensor, dout: DeviceTensor,
+        lse: UnsafePointer<Float>, dq: DeviceTensor, dk: DeviceTensor, dv: DeviceTensor, scale: Float,
+        keyMask: UnsafePointer<UInt8>? = nil, rotary: DeviceRotary? = nil, keyRotary: DeviceRotary? = nil
+    ) -> ltxattn_bwd_args {
+        var a = ltxattn_bwd_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.heads = heads; a.q_len = queryTokens; a.kv_len = keyTokens; a.head_dim = headDim
+        a.q = q.c; a.k = k.c; a.v = v.c; a.out = out.c; a.dout = dout.c
+        a.lse = lse
+        a.lse_stride_b = Int64(heads) * Int64(queryTokens)
+        a.lse_stride_h = Int64(queryTokens)
+        a.dq = dq.c; a.dk = dk.c; a.dv = dv.c
+        a.scale = scale
+        a.key_mask = keyMask
+        a.key_mask_stride_b = Int64(keyTokens)
+        if let rotary { a.q_rotary = rotary.c }
+        if let keyRotary { a.k_rotary = keyRotary.c }
+        return a
+    }
+
+    /// Device scratch the backward needs for these arguments (the caller allocates it).
+    public static func backwardWorkspaceBytes(_ a: inout ltxattn_bwd_args) -> Int {
+        Int(ltxattn_bwd_workspace(&a))
+    }
+
+    /// Reads and clears the device's kernel error word (synchronises the device): throws
+    /// `Failure` with status LTXATTN_ERR_TIMEOUT when a kernel's bounded wait gave up.
+    public static func deviceStatus() throws {
+        var site: Int32 = 0
+        try check(ltxattn_device_status(1, &site))
+    }
+
     /// `applySplitRoPE` (DiTAttention.swift:206-234) of one [B, H, T, D] view;
     /// `out` may be `x` itself.
     public static func splitRoPE(
@@ -173,5 +230,136 @@ public enum AttentionBackend {
         var info = ltxattn_fwd_plan_info()
         try check(ltxattn_fwd_plan(&a, &info))
         return info
+    }
+}
+
+
+/// The CUDA device this process renders on, measured rather than assumed: the
+/// counterpart of `LTXHardware.Machine` (Machine.swift:31-36), whose fields come from
+/// sysctl on a Mac.  Every field here comes from the CUDA runtime through
+/// ltxattn_device_query.
+public struct CUDAMachine: Equatable {
+    public let name: String
+    public let device: Int
+    public let computeCapability: (major: Int, minor: Int)
+    public let smCount: Int
+    public let memoryBytes: UInt64
+    public let freeBytes: UInt64
+    public let l2Bytes: Int
+    public let smClockKHz: Int
+    /// True when the attention kernels run on this device (sm_100, a B200).
+    public let supported: Bool
+
+    public static func == (a: CUDAMachine, b: CUDAMachine) -> Bool {
+        a.name == b.name && a.device == b.device && a.computeCapability == b.computeCapability
+            && a.smCount == b.smCount && a.memoryBytes == b.memoryBytes && a.l2Bytes == b.l2Bytes
+    }
+
+    public var memoryGB: Double { Double(memoryBytes) / 1e9 }
+
+    public static func count() throws -> Int {
+        var n: Int32 = 0
+        try AttentionBackend.check(ltxattn_device_count(&n))
+        return Int(n)
+    }
+
+    public static func detect(device: Int = 0) throws -> CUDAMachine {
+        var info = ltxattn_device_info()
+        try AttentionBackend.check(ltxattn_device_query(Int32(device), &info))
+        let name = withUnsafeBytes(of: &info.name) { raw in
+            String(decoding: raw.prefix { $0 != 0 }, as: UTF8.self)
+        }
+        return CUDAMachine(name: name, device: Int(info.device),
+                           computeCapability: (Int(info.cc_major), Int(info.cc_minor)),
+                           smCount: Int(info.sm_count), memoryBytes: UInt64(info.total_memory_bytes),
+                           freeBytes: UInt64(info.free_memory_bytes), l2Bytes: Int(info.l2_bytes),
+                           smClockKHz: Int(info.sm_clock_khz), supported: info.supported != 0)
+    }
+
+    public var summary: String {
+        String(format: "%@ (sm_%d%d), %.0f GB HBM, %d SMs", name, computeCapability.major,
+               computeCapability.minor, memoryGB, smCount)
+    }
+}
+
+/// Whether the attention working set fits the device: the counterpart of
+/// `LTXHardware.MemoryPlan` (MemoryPlan.swift:27-34, 62-74).  The reference fits its
+/// fused-path activation bytes to MLX allocator peaks (4.67e5 B per video token); here
+/// they are the exact buffers of one call (q, k, v, out, lse and the library's
+/// workspace; with `training` the backward's too).  `headroomBytes` keeps the
+/// reference's meaning: available - peak * (1 + margin).
+public struct AttentionMemoryPlan {
+    public let info: ltxattn_memory_plan_info
+    public var fits: Bool { info.fits != 0 }
+    public var peakBytes: Int64 { info.peak_bytes }
+    public var headroomBytes: Int64 { info.headroom_bytes }
+    public var bytesPerToken: Double { info.bytes_per_token }
+
+    /// `availableBytes == 0` reads the current device's free memory.
+    public static func plan(bf16: Bool = true, batch: Int32 = 1, heads: Int32, tokens: Int32, headDim: Int32,
+                            rotary: Bool, training: Bool, residentBytes: Int64,
+                            availableBytes: Int64 = 0, marginFraction: Double = 0.15) throws -> AttentionMemoryPlan {
+        var a = ltxattn_memory_plan_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.heads = heads; a.tokens = tokens; a.head_dim = headDim
+        a.rotary = rotary ? 1 : 0
+        a.training = training ? 1 : 0
+        a.resident_bytes = residentBytes
+        a.available_bytes = availableBytes
+        a.margin_fraction = marginFraction
+        var info = ltxattn_memory_plan_info()
+        try AttentionBackend.check(ltxattn_memory_plan(&a, &info))
+        return AttentionMemoryPlan(info: info)
+    }
+}
+
+/// Head-parallel all-gather over NCCL (NVLink / NVSwitch) for a job whose heads are
+/// sharded across the GPUs of one box: rank r computes heads [r*H/N, (r+1)*H/N) with
+/// `attention(..., head_begin:, head_count:)` and, where a caller needs every head (a
+/// non-sharded to_out, DiTAttention.swift:402-404), gathers them.  The reference is
+/// single-device; this has no counterpart there.
+public final class HeadGather {
+    private var comm: OpaquePointer?
+    public let ranks: Int
+    public let rank: Int
+
+    /// Rank 0 creates the id and shares its 128 bytes with the other ranks out of band.
+    public static func uniqueId() throws -> [UInt8] {
+        var id = [UInt8](repeating: 0, count: 128)
+        try AttentionBackend.check(ltxattn_comm_unique_id(&id))
+        return id
+    }
+
+    public init(ranks: Int, rank: Int, uniqueId: [UInt8], device: Int) throws {
+        precondition(uniqueId.count == 128, "an NCCL unique id is 128 bytes")
+        self.ranks = ranks
+        self.rank = rank
+        var c: OpaquePointer?
+        try AttentionBackend.check(ltxattn_comm_init(&c, Int32(ranks), Int32(rank), uniqueId, Int32(device)))
+        comm = c
+    }
+
+    deinit {
+        if let comm { _ = ltxattn_comm_destroy(comm) }
+    }
+
+    /// (ranks, rank) as NCCL itself reports them.
+    public func size() throws -> (ranks: Int, rank: Int) {
+        var n: Int32 = 0, r: Int32 = 0
+        try AttentionBackend.check(ltxattn_comm_size(comm, &n, &r))
+        return (Int(n), Int(r))
+    }
+
+    /// send: contiguous [B, headsPerRank, T, D] on this rank; recv: contiguous
+    /// [B, ranks * headsPerRank, T, D] on every rank.
+    public func gather(bf16: Bool, batch: Int32, headsPerRank: Int32, tokens: Int32, headDim: Int32,
+                       send: UnsafeRawPointer, recv: UnsafeMutableRawPointer,
+                       stream: UnsafeMutableRawPointer?) throws {
+        var a = ltxattn_gather_args()
+        a.dtype = bf16 ? Int32(LTXATTN_BF16.rawValue) : Int32(LTXATTN_F32.rawValue)
+        a.batch = batch; a.heads_per_rank = headsPerRank; a.tokens = tokens; a.head_dim = headDim
+        a.send = send
+        a.recv = recv
+        try AttentionBackend.check(ltxattn_allgather_heads(&a, comm, stream))
     }
 }

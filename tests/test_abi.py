@@ -52,6 +52,10 @@ int main(void) {
   printf("ltxattn_rotary_table_args %zu\n", sizeof(ltxattn_rotary_table_args));
   printf("ltxattn_qk_prep_args %zu\n", sizeof(ltxattn_qk_prep_args));
   printf("ltxattn_fwd_plan_info %zu\n", sizeof(ltxattn_fwd_plan_info));
+  printf("ltxattn_memory_plan_args %zu\n", sizeof(ltxattn_memory_plan_args));
+  printf("ltxattn_memory_plan_info %zu\n", sizeof(ltxattn_memory_plan_info));
+  P(ltxattn_memory_plan_args, resident_bytes) P(ltxattn_memory_plan_args, margin_fraction)
+  P(ltxattn_memory_plan_info, fits) P(ltxattn_memory_plan_info, bytes_per_token)
   P(ltxattn_fwd_args, q) P(ltxattn_fwd_args, out) P(ltxattn_fwd_args, scale)
   P(ltxattn_fwd_args, key_mask) P(ltxattn_fwd_args, q_rotary) P(ltxattn_fwd_args, k_rotary)
   P(ltxattn_fwd_args, lse) P(ltxattn_fwd_args, workspace) P(ltxattn_fwd_args, num_splits)
@@ -82,13 +86,15 @@ def test_ctypes_layout_matches_the_header(tmp_path):
              "ltxattn_bwd_args": _lib.BwdArgs, "ltxattn_gather_args": _lib.GatherArgs,
              "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs,
              "ltxattn_rotary_table_args": _lib.RotaryTableArgs, "ltxattn_qk_prep_args": _lib.QkPrepArgs,
-             "ltxattn_fwd_plan_info": _lib.FwdPlanInfo}
+             "ltxattn_fwd_plan_info": _lib.FwdPlanInfo, "ltxattn_memory_plan_args": _lib.MemoryPlanArgs,
+             "ltxattn_memory_plan_info": _lib.MemoryPlanInfo}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
                "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
                "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs,
-               "ltxattn_qk_prep_args": _lib.QkPrepArgs, "ltxattn_fwd_plan_info": _lib.FwdPlanInfo}
+               "ltxattn_qk_prep_args": _lib.QkPrepArgs, "ltxattn_fwd_plan_info": _lib.FwdPlanInfo,
+               "ltxattn_memory_plan_args": _lib.MemoryPlanArgs, "ltxattn_memory_plan_info": _lib.MemoryPlanInfo}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")
@@ -213,3 +219,36 @@ def test_selftest_and_comm_size_refuse_bad_arguments():
     assert "limit_us" in _lib.last_error()
     n = ctypes.c_int32()
     assert L.ltxattn_comm_size(None, ctypes.byref(n), ctypes.byref(n)) == _lib.ERR_ARG
+
+
+def test_memory_plan_counts_the_call_buffers():
+    # config 2 (3120 tokens, 32 heads of 128, bf16, rotary): q, k, v, out are 25.6 MB
+    # each, lse 0.4 MB, and the rotated q / k copies in the workspace another 2 x 25.6 MB
+    L = _lib.load()
+    a = _lib.MemoryPlanArgs(dtype=_lib.BF16, batch=1, heads=32, tokens=3120, head_dim=128, rotary=1,
+                            training=0, resident_bytes=42_060_000_000, available_bytes=180_000_000_000,
+                            margin_fraction=0.15)
+    info = _lib.MemoryPlanInfo()
+    assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK, _lib.last_error()
+    act = 3120 * 32 * 128 * 2
+    assert info.tensor_bytes == 4 * act + 3120 * 32 * 4
+    assert info.workspace_bytes >= 2 * act  # rotated q and k
+    assert info.backward_bytes == 0
+    assert info.peak_bytes == 42_060_000_000 + info.tensor_bytes + info.workspace_bytes
+    want_headroom = 180_000_000_000 - round(info.peak_bytes * 1.15)
+    assert info.headroom_bytes == want_headroom and info.fits == 1
+    assert abs(info.bytes_per_token * 3120 - (info.tensor_bytes + info.workspace_bytes)) < 1.0
+    # training adds dout, dq, dk, dv and the backward's workspace
+    a.training = 1
+    t = _lib.MemoryPlanInfo()
+    assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(t)) == _lib.OK
+    assert t.backward_bytes >= 4 * act
+    # a device too small for the resident weights does not fit
+    a.available_bytes = 40_000_000_000
+    assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(t)) == _lib.OK and t.fits == 0
+    # refusals
+    a.head_dim = 80
+    assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(t)) == _lib.ERR_UNSUPPORTED
+    a.head_dim, a.margin_fraction = 128, -0.1
+    assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(t)) == _lib.ERR_ARG
+    assert L.ltxattn_memory_plan(None, ctypes.byref(t)) == _lib.ERR_ARG
