@@ -49,9 +49,13 @@ EXTRAS = ("c3", "c4a", "c4b", "c4c", "c5")
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's
 # attention kernel, from single-launch ncu captures of the attention call
 # without tables (the kernel-only timing below), L2 flushed before the launch.
-# Filled in from the captures summarised under profiles/ (the summary file named
-# beside each number gives the command); None where no capture exists.
-TRAFFIC = {}
+# Values for all 32 heads, from the capture summarised in the file named beside
+# each number (which gives the command); scaled by heads for a rank's block.
+_TRAFFIC_SRC = "profiles/dram_traffic_attention_launches.md"
+TRAFFIC = {"c2": (79312128, _TRAFFIC_SRC), "c3": (27962368, _TRAFFIC_SRC), "c4a": (1667840, _TRAFFIC_SRC),
+           "c4b": (13873408, _TRAFFIC_SRC), "c4c": (26343168, _TRAFFIC_SRC),
+           # captured on 4 of the 32 heads; scaled by heads
+           "c5": (106580736 * 8, _TRAFFIC_SRC + " (4-head capture x 8)")}
 
 
 class L2Flush:

@@ -101,7 +101,10 @@ int ltxattn_comm_init(ltxattn_comm** comm, int32_t nranks, int32_t rank, const u
     return ltx::set_error_message(LTXATTN_ERR_ARG, "rank out of range");
   if (int rc = need_nccl()) return rc;
   cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // not left behind for a later launch check to find
+    return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  }
   ncclUniqueId u;
   memcpy(u.internal, id, 128);
   ncclComm_t c = nullptr;

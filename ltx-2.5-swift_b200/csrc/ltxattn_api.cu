@@ -33,7 +33,12 @@ int fail(int status, const char* fmt, ...) {
   return status;
 }
 
+// A runtime call of the library failed: report it, and take the failure out of
+// the runtime's per-thread last-error slot so that it is not read again as the
+// result of a later, unrelated kernel launch (ours or the caller's).  Sticky
+// errors stay: the runtime reports those on every call anyway.
 int cuda_fail(cudaError_t e, const char* what) {
+  (void)cudaGetLastError();
   return fail(LTXATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 

@@ -75,7 +75,10 @@ int ltxattn_memory_plan(const ltxattn_memory_plan_args* a, ltxattn_memory_plan_i
   if (avail == 0) {
     size_t free_b = 0, total_b = 0;
     const cudaError_t e = cudaMemGetInfo(&free_b, &total_b);
-    if (e != cudaSuccess) return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // not left behind for a later launch check to find
+      return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+    }
     avail = (int64_t)free_b;
   }
   info->available_bytes = avail;

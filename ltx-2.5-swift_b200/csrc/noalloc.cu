@@ -51,13 +51,17 @@ void* g_scratch_ptr[kMaxDevices] = {};
 int scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // not left behind for a later launch check to find
+    return set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  }
   if (dev < 0 || dev >= kMaxDevices) return set_error_message(LTXATTN_ERR_UNSUPPORTED, "device index out of range");
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
       char buf[256];
       snprintf(buf, sizeof buf, "cudaGetSymbolAddress of the no-alloc scratch failed: %s", cudaGetErrorString(e));
       return set_error_message(LTXATTN_ERR_CUDA, buf);

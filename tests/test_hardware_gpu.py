@@ -8,7 +8,7 @@ import ctypes
 import pytest
 import torch
 
-from ltxattn import _lib, device_info
+from ltxattn import AttentionBackend, _lib, device_info, qk_prep
 
 pytestmark = pytest.mark.gpu
 
@@ -29,9 +29,16 @@ def test_device_query_describes_the_b200():
     assert d["l2_bytes"] >= 100 * 1024 * 1024          # 126 MB L2
     assert d["max_smem_per_block_optin"] >= 227 * 1024
     assert d["sm_clock_khz"] > 1_000_000 and d["mem_bus_width_bits"] >= 4096
-    # an index past the last device is refused, not read
+    # an index past the last device is refused, not read, and the refusal leaves
+    # nothing behind: the next launch's error check does not see it
     info = _lib.DeviceInfo()
     assert _lib.load().ltxattn_device_query(n.value, ctypes.byref(info)) != _lib.OK
+    q = torch.randn((1, 2, 64, 64), device="cuda").to(torch.bfloat16)
+    x = torch.randn((1, 64, 128), device="cuda").to(torch.bfloat16)
+    out, _ = AttentionBackend.attention(q, q, q)
+    qk_prep(x, torch.ones(128, device="cuda", dtype=torch.bfloat16), 2)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
 
 
 def test_memory_plan_reads_the_free_memory_of_the_device():
