@@ -202,6 +202,64 @@ LTXATTN_API int ltxattn_bwd(const ltxattn_bwd_args* args, void* stream);
 /* Device scratch bytes ltxattn_bwd needs for these arguments. */
 LTXATTN_API size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* args);
 
+/* ---- projections ---------------------------------------------------------- */
+
+/* Arguments of ltxattn_linear: out = T(T(x W^T) + bias), the bf16 matmul (fp32
+ * accumulation, one rounding) and then the bias added in bf16.
+ *  - x [m, k] rows of x_stride elements; weight [n, k] (the checkpoint's
+ *    [out, in] layout) rows of weight_stride; out [m, n] rows of out_stride.
+ *  - bias [n] or NULL.
+ *  - n a multiple of 32, k of 64; rows 16-byte aligned. */
+typedef struct ltxattn_linear_args {
+  int32_t dtype; /* LTXATTN_BF16 */
+  int32_t m, n, k;
+  const void* x;
+  int64_t x_stride;
+  const void* weight;
+  int64_t weight_stride;
+  const void* bias;
+  void* out;
+  int64_t out_stride;
+} ltxattn_linear_args;
+
+/* Replaces `DiTAttention.linear` (`DiTAttention.swift:178-188`) without the LoRA
+ * overlay: to_v, to_out.0 and to_gate_logits of the attention module. */
+LTXATTN_API int ltxattn_linear(const ltxattn_linear_args* args, void* stream);
+
+/* Arguments of ltxattn_qk_project: out = split-RoPE(split(rmsNorm(linear(x)))).
+ *  - x [batch, tokens, in_dim] (element strides x_stride_b, x_stride_t; unit
+ *    stride along in_dim); weight [heads * head_dim, in_dim] rows of
+ *    weight_stride; bias [heads * head_dim] or NULL; norm_weight
+ *    [heads * head_dim] and eps: the q_norm / k_norm of the module.
+ *  - rotary: per-head tables as for ltxattn_fwd, or cos = NULL for none.
+ *  - out: the [B, H, T, D] view the attention consumes.
+ *  - heads * head_dim a multiple of 512, at most 4096; in_dim a multiple of 64;
+ *    head_dim 64 or 128; rows and tables 16-byte aligned. */
+typedef struct ltxattn_qk_project_args {
+  int32_t dtype; /* LTXATTN_BF16 */
+  int32_t batch, tokens, heads, head_dim, in_dim;
+  const void* x;
+  int64_t x_stride_b, x_stride_t;
+  const void* weight;
+  int64_t weight_stride;
+  const void* bias;
+  const void* norm_weight;
+  float eps;
+  ltxattn_rotary rotary;
+  ltxattn_tensor out;
+} ltxattn_qk_project_args;
+
+/* Replaces the query / key path of `DiTAttention.callAsFunction` from the
+ * projection to the attention's input (`DiTAttention.swift:341-342,358-367`):
+ * `linear` (`:178-188`), `rmsNorm` over the whole inner dim (`:190-204`), the
+ * head split (`:346-348`) and `applySplitRoPE` (`:206-234`), as one tcgen05
+ * GEMM whose epilogue does everything after the matmul. */
+LTXATTN_API int ltxattn_qk_project(const ltxattn_qk_project_args* args, void* stream);
+
+/* q and k projections (same heads * head_dim) in one launch. */
+LTXATTN_API int ltxattn_qk_project_pair(const ltxattn_qk_project_args* q, const ltxattn_qk_project_args* k,
+                                        void* stream);
+
 /* ---- split RoPE on its own ------------------------------------------------ */
 
 /* Arguments of ltxattn_rope: out = split-RoPE(x, rotary).

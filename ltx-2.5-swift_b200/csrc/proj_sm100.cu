@@ -1,0 +1,677 @@
+// proj_sm100.cu -- the DiT attention module's projections on tcgen05 (sm_100a).
+//
+// Two kernels share one main loop, y = x W^T accumulated in TMEM:
+//
+//  * linear_kernel<BN>: DiTAttention.linear (DiTAttention.swift:178-188) without
+//    the LoRA overlay: out = T(T(x W^T) + b), the matmul's result in the
+//    activation dtype T and then the bias added in T -- the reference's two
+//    roundings (MLX's bf16 matmul accumulates in fp32 and rounds once).
+//    Serves to_v, to_out.0 and to_gate_logits.
+//
+//  * qk_project_kernel: to_q / to_k with everything up to the attention fused
+//    into the epilogue (DiTAttention.swift:341-342,358-367): the projection as
+//    above, rmsNorm over the WHOLE inner dim (:190-204, MLX's arithmetic
+//    y = T(w * T(x * r)), r = 1 / sqrt(mean(x^2) + eps), the mean square in
+//    fp32), the head split (:346-348) and split RoPE with per-head tables
+//    (:206-234, every product and sum rounded to bf16), stored straight into
+//    the [B, H, T, D] view the attention reads.  The norm needs every one of a
+//    row's N = heads * head_dim outputs, so a cluster of N / 512 CTAs covers a
+//    128-row block: each CTA computes 512 columns (two 256-column accumulators
+//    in TMEM), publishes its rows' partial sums of squares in shared memory,
+//    and reads the other CTAs' partials through distributed shared memory
+//    after a cluster barrier.  Every CTA adds the partials in rank order, so
+//    all of them use the same r and the result does not depend on scheduling.
+//
+// CTA: 256 threads.  Warp 0 lane 0 is the TMA producer: 128-row x 64 slices of
+// x and BN-row x 64 slices of W into kStages shared-memory stages (128-byte
+// swizzle, K-major, the UMMA operand layout).  Warp 1 owns TMEM and its lane 0
+// issues the tcgen05.mma (M 128, N BN, K 16: four per stage), freeing a stage
+// with tcgen05.commit once its MMAs complete.  Warps 4-7 are the epilogue:
+// thread i reads TMEM lane i (row i of the tile) in 32-column chunks.  No
+// multicast load anywhere.  Every mbarrier wait is bounded; a wait that gives up
+// records its site in the device error word, and the CTA unwinds (cluster CTAs
+// still reach both cluster barriers, so no CTA is left waiting for another).
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/ltxattn.h"
+#include "ltxattn_internal.h"
+#include "sm100.cuh"
+
+namespace ltx {
+
+int set_error_message(int status, const char* msg);
+
+namespace {
+
+constexpr int kPBM = 128;     // rows per CTA (UMMA M)
+constexpr int kPBK = 64;      // K per stage: one 128-byte swizzle row of bf16
+constexpr int kPStages = 4;
+constexpr int kPThreads = 256;
+
+template <int BN, int NT>
+struct PSmem {
+  static constexpr uint32_t kA = kPBM * kPBK * 2;  // 16 KB
+  static constexpr uint32_t kB = BN * kPBK * 2;
+  static constexpr uint32_t kStage = kA + kB;
+  // full[kPStages], empty[kPStages], acc_full[NT]
+  static constexpr uint32_t kOffBar = kPStages * kStage;
+  static constexpr uint32_t kOffCtl = kOffBar + (2 * kPStages + NT) * 8;  // tmem slot, abort flag
+  static constexpr uint32_t kOffPart = kOffCtl + 16;                      // float[128] partial sums
+  static constexpr uint32_t kBytes = kOffPart + 128 * 4;
+  static constexpr uint32_t kDynamic = kBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = BN * NT < 32 ? 32 : BN * NT;
+  static_assert(kA % 1024 == 0 && kB % 1024 == 0, "stages must keep 1024-byte swizzle atoms aligned");
+  static_assert(BN * NT <= 512, "TMEM holds 512 fp32 columns");
+};
+
+// One projection job of a launch (the q/k kernel can run two: q and k).
+struct ProjJob {
+  CUtensorMap tm_x;  // [K, T, B] bf16, box {64, 128, 1}
+  CUtensorMap tm_w;  // [K, N] bf16, box {64, BN}
+  const __nv_bfloat16* bias;  // [N] or null
+  int T, B, N, K;
+  int tiles_t;     // ceil(T / 128)
+  int col_groups;  // CTAs per row block (the cluster size of the q/k kernel)
+  int ctas;        // tiles_t * B * col_groups
+  // linear: out[b][t][n] at out + b * o_sb + t * o_st + n
+  __nv_bfloat16* out;
+  int64_t o_sb, o_st;
+  // q/k: norm weight, rotary tables [B|1][H|1][T][D/2] (cos null: none), out [B, H, T, D]
+  const __nv_bfloat16* norm_w;
+  float eps;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t r_sb, r_sh, r_st;
+  int64_t h_sb, h_sh, h_st;
+  int D;
+};
+
+struct ProjParams {
+  ProjJob job[2];
+  int n_jobs;
+  int* err;
+};
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// y = T(T(acc) + b) for 32 accumulator columns (b null: T(acc)).
+__device__ __forceinline__ void project_chunk(const uint32_t (&acc)[32], const __nv_bfloat16* bias, float (&y)[32]) {
+  if (bias != nullptr) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(bias);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 bw = b4[q];
+      const uint32_t bb[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float b0 = __uint_as_float(bb[e] << 16), b1 = __uint_as_float(bb[e] & 0xffff0000u);
+        const int c = 8 * q + 2 * e;
+        y[c] = bf16_round(bf16_round(__uint_as_float(acc[c])) + b0);
+        y[c + 1] = bf16_round(bf16_round(__uint_as_float(acc[c + 1])) + b1);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) y[c] = bf16_round(__uint_as_float(acc[c]));
+  }
+}
+
+// The main loop's two roles (producer: warp 0 lane 0; MMA issuer: warp 1 lane
+// 0).  `subtiles` consecutive 256-column (BN-column) accumulators share one
+// row block; accumulator s starts at TMEM column s * BN.
+template <int BN, int NT>
+__device__ __forceinline__ void mainloop_role(const ProjJob& J, int warp, int lane, int t0, int b, int n_base,
+                                              uint8_t* sm, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
+                                              uint32_t tmem, volatile int* abort_flag, int* err) {
+  using S = PSmem<BN, NT>;
+  const int kb_n = J.K / kPBK;
+  if (warp == 0 && lane == 0) {
+    int it = 0;
+    bool ok = true;
+    for (int s = 0; s < NT && ok; ++s) {
+      const int n0 = n_base + s * BN;
+      for (int kb = 0; kb < kb_n; ++kb, ++it) {
+        const int st = it % kPStages, u = it / kPStages;
+        if (it >= kPStages && !mbar_wait(empty + st, (u - 1) & 1, abort_flag, err, 41)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = sm + st * S::kStage;
+        mbar_arrive_expect_tx(full + st, S::kStage);
+        tma_load_3d(&J.tm_x, full + st, sa, kb * kPBK, t0, b);
+        tma_load_2d(&J.tm_w, full + st, sa + S::kA, kb * kPBK, n0);
+      }
+    }
+    // never leave the CTA with a bulk copy still writing its shared memory
+    for (int i = it < kPStages ? 0 : it - kPStages; i < it; ++i) drain_wait(full + i % kPStages, (i / kPStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_bf16_f32(128, BN, 0, 0);
+    const SDesc a0 = sdesc_split(smem_u32(sm), 16, 1024);
+    const SDesc b0 = sdesc_split(smem_u32(sm) + S::kA, 16, 1024);
+    const uint32_t stage_step = S::kStage >> 4;
+    int it = 0;
+    bool ok = true;
+    for (int s = 0; s < NT; ++s) {
+      const uint32_t d = tmem + s * BN;
+      for (int kb = 0; kb < kb_n && ok; ++kb, ++it) {
+        const int st = it % kPStages, u = it / kPStages;
+        if (!mbar_wait(full + st, u & 1, abort_flag, err, 42)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t alo = a0.lo + st * stage_step, blo = b0.lo + st * stage_step;
+#pragma unroll
+        for (int kk = 0; kk < kPBK / 16; ++kk)  // k-step kk: 32 bytes further along each 128-byte row
+          umma_ss2(d, alo + kk * 2, a0.hi, blo + kk * 2, b0.hi, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(empty + st);  // the stage is free once these MMAs have read it
+      }
+      umma_commit(acc_full + s);  // also issued after a timeout, so the epilogue's waits end
+    }
+    drain_wait(acc_full + NT - 1, 0);  // no MMA still running when the CTA tears down
+  }
+}
+
+// ---------------------------------------------------------------------------
+// linear: one CTA per (128-row block, BN columns)
+
+template <int BN>
+__global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_constant__ ProjParams p) {
+  using S = PSmem<BN, 1>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPStages;
+  uint64_t* acc_full = bars + 2 * kPStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+  const ProjJob& J = p.job[0];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const int cg = cta % J.col_groups;
+  const int rb = cta / J.col_groups;
+  const int b = rb / J.tiles_t, t0 = (rb % J.tiles_t) * kPBM;
+  const int n_base = cg * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2 * kPStages + 1; ++i) mbar_init(bars + i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&J.tm_x);
+    tma_prefetch_desc(&J.tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    mainloop_role<BN, 1>(J, warp, lane, t0, b, n_base, sm, full, empty, acc_full, tmem, abort_flag, p.err);
+  } else {
+    const int r = threadIdx.x - 128;  // TMEM lane = tile row
+    const int t = t0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const bool have = warp_wait(acc_full, 0, abort_flag, p.err, 43);
+    tc_fence_after();
+    if (have) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + lane_off + c * 32, acc);
+        tmem_wait_ld();
+        if (t < J.T) {
+          const int n = n_base + c * 32;
+          float y[32];
+          project_chunk(acc, J.bias != nullptr ? J.bias + n : nullptr, y);
+          uint4* dst = reinterpret_cast<uint4*>(J.out + (int64_t)b * J.o_sb + (int64_t)t * J.o_st + n);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                                pack_bf16x2(y[8 * q + 4], y[8 * q + 5]), pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// q / k projection with the fused norm, head split and RoPE: a cluster of
+// col_groups CTAs per 128-row block, 512 columns per CTA (two 256-column
+// accumulators).
+
+constexpr int kQkBN = 256, kQkNT = 2;
+
+// 32 columns starting at `n` of the normalised row: T(w * T(y * r)) as bf16 pairs.
+__device__ __forceinline__ void normalise_chunk(const float (&y)[32], float r, const __nv_bfloat16* w, uint32_t (&z)[16]) {
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  const float2 r2 = make_float2(r, r);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 ww = w4[q];
+    const uint32_t wv[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = 8 * q + 2 * e;
+      const float2 xr = mul2(make_float2(y[c], y[c + 1]), r2);
+      z[4 * q + e] = bmul2(pack_bf16x2(xr.x, xr.y), wv[e]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_constant__ ProjParams p) {
+  using S = PSmem<kQkBN, kQkNT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPStages;
+  uint64_t* acc_full = bars + 2 * kPStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+  float* part = reinterpret_cast<float*>(sm + S::kOffPart);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // job 0 owns CTAs [0, job[0].ctas), job 1 the rest; both are whole clusters
+  const int j = (int)blockIdx.x >= p.job[0].ctas ? 1 : 0;
+  const ProjJob& J = p.job[j];
+  const int cta = (int)blockIdx.x - (j ? p.job[0].ctas : 0);
+  const int C = J.col_groups;
+  const uint32_t rank = cluster_ctarank();  // == cta % C
+  const int rb = cta / C;
+  const int b = rb / J.tiles_t, t0 = (rb % J.tiles_t) * kPBM;
+  const int n_base = (int)rank * kQkBN * kQkNT;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2 * kPStages + kQkNT; ++i) mbar_init(bars + i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&J.tm_x);
+    tma_prefetch_desc(&J.tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    mainloop_role<kQkBN, kQkNT>(J, warp, lane, t0, b, n_base, sm, full, empty, acc_full, tmem, abort_flag, p.err);
+    __syncwarp();
+    cluster_arrive();  // partial sums published (these warps contribute none)
+    cluster_wait();
+    cluster_arrive();  // done reading the other CTAs' partial sums
+    cluster_wait();
+  } else {
+    const int r = threadIdx.x - 128;
+    const int t = t0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    bool have = true;
+    for (int s = 0; s < kQkNT; ++s) have = warp_wait(acc_full + s, 0, abort_flag, p.err, 44) && have;
+    tc_fence_after();
+    // phase 1: this CTA's share of the row's sum of squares of y = T(T(acc) + b)
+    float ss = 0.f;
+    if (have) {
+#pragma unroll 1
+      for (int c = 0; c < kQkBN * kQkNT / 32; ++c) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + lane_off + c * 32, acc);
+        tmem_wait_ld();
+        float y[32];
+        project_chunk(acc, J.bias != nullptr ? J.bias + n_base + c * 32 : nullptr, y);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ss = __fmaf_rn(y[e], y[e], ss);
+      }
+    }
+    part[r] = ss;
+    cluster_arrive();
+    cluster_wait();
+    float tot = 0.f;
+    for (int q = 0; q < C; ++q) tot = __fadd_rn(tot, ld_cluster_f32(part + r, (uint32_t)q));
+    cluster_arrive();  // this CTA's reads of the other CTAs' shared memory are done
+    const float rn = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)J.N), J.eps));
+    // phase 2: normalise, split into heads, rotate, store
+    const int D = J.D, half_chunks = D / 64;  // 32-column chunks per half head
+    if (have && t < J.T) {
+#pragma unroll 1
+      for (int c1 = 0; c1 < kQkBN * kQkNT / 32; ++c1) {
+        if ((c1 % (D / 32)) >= half_chunks) continue;  // c1 walks the lower halves; c2 is its partner
+        const int c2 = c1 + half_chunks;
+        const int n1 = n_base + c1 * 32;
+        const int head = n1 / D, d1 = n1 % D;  // d1 < D / 2
+        uint32_t a1[32], a2[32];
+        tmem_ld32(tmem + lane_off + c1 * 32, a1);
+        tmem_ld32(tmem + lane_off + c2 * 32, a2);
+        tmem_wait_ld();
+        float y1[32], y2[32];
+        project_chunk(a1, J.bias != nullptr ? J.bias + n1 : nullptr, y1);
+        project_chunk(a2, J.bias != nullptr ? J.bias + n1 + D / 2 : nullptr, y2);
+        uint32_t z1[16], z2[16];
+        normalise_chunk(y1, rn, J.norm_w + n1, z1);
+        normalise_chunk(y2, rn, J.norm_w + n1 + D / 2, z2);
+        uint32_t o1[16], o2[16];
+        if (J.cos != nullptr) {
+          const int64_t toff = (int64_t)b * J.r_sb + (int64_t)head * J.r_sh + (int64_t)t * J.r_st + d1;
+          const uint4* c4 = reinterpret_cast<const uint4*>(J.cos + toff);
+          const uint4* s4 = reinterpret_cast<const uint4*>(J.sin + toff);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 cw = c4[q], sw = s4[q];
+            const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w}, sv[4] = {sw.x, sw.y, sw.z, sw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * q + e;
+              o1[i] = bsub2(bmul2(z1[i], cv[e]), bmul2(z2[i], sv[e]));
+              o2[i] = badd2(bmul2(z2[i], cv[e]), bmul2(z1[i], sv[e]));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            o1[i] = z1[i];
+            o2[i] = z2[i];
+          }
+        }
+        __nv_bfloat16* orow = J.out + (int64_t)b * J.h_sb + (int64_t)head * J.h_sh + (int64_t)t * J.h_st;
+        uint4* dst1 = reinterpret_cast<uint4*>(orow + d1);
+        uint4* dst2 = reinterpret_cast<uint4*>(orow + d1 + D / 2);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          dst1[q] = make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]);
+          dst2[q] = make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]);
+        }
+      }
+    }
+    __syncwarp();
+    cluster_wait();  // every CTA has read this CTA's partial sums: its shared memory may go
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+    else
+      (void)cudaGetLastError();
+  });
+  return fn;
+}
+
+int fail_msg(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  return set_error_message(status, buf);
+}
+
+// x: [K, T, B] bf16 (element strides st for T, sb for B), box {64, 128, 1}
+int map_rows(CUtensorMap* m, const void* ptr, int K, int T, int B, int64_t st, int64_t sb, const char* name) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return fail_msg(LTXATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int64_t s2 = B == 1 ? st * T : sb;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)st * 2, (cuuint64_t)s2 * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail_msg(LTXATTN_ERR_ALIGN, "%s: cuTensorMapEncodeTiled rejected the view (CUresult %d)", name, (int)r);
+  return LTXATTN_OK;
+}
+
+// W: [K, N] bf16 (row stride sw elements), box {64, bn}
+int map_weight(CUtensorMap* m, const void* ptr, int K, int N, int64_t sw, int bn, const char* name) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return fail_msg(LTXATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+  cuuint64_t strides[1] = {(cuuint64_t)sw * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)bn};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail_msg(LTXATTN_ERR_ALIGN, "%s: cuTensorMapEncodeTiled rejected the view (CUresult %d)", name, (int)r);
+  return LTXATTN_OK;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_fail(cudaError_t e, const char* what) {
+  (void)cudaGetLastError();
+  return fail_msg(LTXATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Dynamic shared memory above 48 KB is opted into once per device and kernel.
+constexpr int kMaxDev = 64;
+std::mutex g_mu;
+bool g_attr_set[kMaxDev][5] = {};
+
+template <typename K>
+cudaError_t prepare_kernel(K kernel, int slot, size_t smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_attr_set[dev][slot]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    g_attr_set[dev][slot] = true;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace ltx
+
+using namespace ltx;
+
+namespace {
+
+int bn_for(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 128 == 0) return 128;
+  if (n % 64 == 0) return 64;
+  if (n % 32 == 0) return 32;
+  return 0;
+}
+
+template <int BN>
+int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t st) {
+  using S = PSmem<BN, 1>;
+  ProjJob& J = P.job[0];
+  if (int rc = map_weight(&J.tm_w, a->weight, a->k, a->n, a->weight_stride, BN, "weight")) return rc;
+  J.col_groups = a->n / BN;
+  J.ctas = J.tiles_t * J.col_groups;
+  const int slot = BN == 256 ? 0 : BN == 128 ? 1 : BN == 64 ? 2 : 3;
+  cudaError_t e = prepare_kernel(linear_kernel<BN>, slot, S::kDynamic);
+  if (e != cudaSuccess) return launch_fail(e, "linear kernel attributes");
+  linear_kernel<BN><<<J.ctas, kPThreads, S::kDynamic, st>>>(P);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_fail(e, "linear launch");
+  return LTXATTN_OK;
+}
+
+// Fills job j of a q/k projection from the C arguments.
+int qk_job(const ltxattn_qk_project_args* a, ProjJob* J) {
+  if (a == nullptr) return fail_msg(LTXATTN_ERR_ARG, "args is NULL");
+  if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_qk_project: bf16 only");
+  if (a->batch < 1 || a->tokens < 1 || a->heads < 1 || a->in_dim < 1)
+    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: batch, tokens, heads and in_dim must be >= 1");
+  if (a->head_dim != 64 && a->head_dim != 128)
+    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_qk_project: head_dim %d (64 and 128 are supported)", a->head_dim);
+  const int N = a->heads * a->head_dim;
+  if (N % 512 != 0 || N / 512 > 8)
+    return fail_msg(LTXATTN_ERR_UNSUPPORTED,
+                    "ltxattn_qk_project: heads * head_dim = %d must be a multiple of 512 and at most 4096", N);
+  if (a->in_dim % 64 != 0)
+    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_qk_project: in_dim %d must be a multiple of 64", a->in_dim);
+  if (!a->x || !a->weight || !a->norm_weight || !a->out.data)
+    return fail_msg(LTXATTN_ERR_ARG, "ltxattn_qk_project: x, weight, norm_weight and out are required");
+  if (a->x_stride_t < a->in_dim || a->x_stride_b < 0 || a->weight_stride < a->in_dim)
+    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: x / weight strides are shorter than in_dim");
+  if (!al16(a->x) || !al16(a->weight) || (a->x_stride_t % 8) || (a->batch > 1 && a->x_stride_b % 8) ||
+      (a->weight_stride % 8))
+    return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_qk_project: x and weight need 16-byte aligned rows");
+  if ((a->bias && !al16(a->bias)) || !al16(a->norm_weight) || !al16(a->out.data) || (a->out.stride_t % 8) ||
+      (a->out.stride_h % 8) || (a->out.stride_b % 8) || a->out.stride_t < 0 || a->out.stride_h < 0 ||
+      a->out.stride_b < 0)
+    return fail_msg(LTXATTN_ERR_ALIGN,
+                    "ltxattn_qk_project: bias, norm_weight and out rows must be 16-byte aligned (strides multiples of 8)");
+  if (a->rotary.cos != nullptr) {
+    if (!a->rotary.sin) return fail_msg(LTXATTN_ERR_ARG, "ltxattn_qk_project: rotary has cos but no sin");
+    if (a->rotary.tokens < a->tokens)
+      return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: rotary covers %d tokens, expected at least %d",
+                      a->rotary.tokens, a->tokens);
+    if (!al16(a->rotary.cos) || !al16(a->rotary.sin) || (a->rotary.stride_t % 8) || (a->rotary.stride_h % 8) ||
+        (a->rotary.stride_b % 8) || a->rotary.stride_t < 0 || a->rotary.stride_h < 0 || a->rotary.stride_b < 0)
+      return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_qk_project: rotary tables need 16-byte aligned rows");
+  }
+  *J = ProjJob{};
+  if (int rc = map_rows(&J->tm_x, a->x, a->in_dim, a->tokens, a->batch, a->x_stride_t, a->x_stride_b, "x")) return rc;
+  if (int rc = map_weight(&J->tm_w, a->weight, a->in_dim, N, a->weight_stride, kQkBN, "weight")) return rc;
+  J->bias = static_cast<const __nv_bfloat16*>(a->bias);
+  J->T = a->tokens;
+  J->B = a->batch;
+  J->N = N;
+  J->K = a->in_dim;
+  J->tiles_t = (a->tokens + kPBM - 1) / kPBM;
+  J->col_groups = N / (kQkBN * kQkNT);
+  J->ctas = J->tiles_t * J->B * J->col_groups;
+  J->norm_w = static_cast<const __nv_bfloat16*>(a->norm_weight);
+  J->eps = a->eps;
+  J->cos = static_cast<const __nv_bfloat16*>(a->rotary.cos);
+  J->sin = static_cast<const __nv_bfloat16*>(a->rotary.sin);
+  J->r_sb = a->rotary.stride_b;
+  J->r_sh = a->rotary.stride_h;
+  J->r_st = a->rotary.stride_t;
+  J->out = static_cast<__nv_bfloat16*>(a->out.data);
+  J->h_sb = a->out.stride_b;
+  J->h_sh = a->out.stride_h;
+  J->h_st = a->out.stride_t;
+  J->D = a->head_dim;
+  return LTXATTN_OK;
+}
+
+int launch_qk(ProjParams& P, cudaStream_t st) {
+  using S = PSmem<kQkBN, kQkNT>;
+  cudaError_t e = prepare_kernel(qk_project_kernel, 4, S::kDynamic);
+  if (e != cudaSuccess) return launch_fail(e, "q/k projection kernel attributes");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P.job[0].ctas + (P.n_jobs > 1 ? P.job[1].ctas : 0));
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = S::kDynamic;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = P.job[0].col_groups;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, qk_project_kernel, P);
+  if (e != cudaSuccess) return launch_fail(e, "q/k projection launch");
+  return LTXATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
+  if (a == nullptr) return fail_msg(LTXATTN_ERR_ARG, "args is NULL");
+  if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_linear: bf16 only");
+  if (a->m < 1 || a->n < 1 || a->k < 1) return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_linear: m, n and k must be >= 1");
+  const int bn = bn_for(a->n);
+  if (bn == 0 || a->k % 64 != 0)
+    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_linear: n (%d) must be a multiple of 32 and k (%d) of 64", a->n,
+                    a->k);
+  if (!a->x || !a->weight || !a->out) return fail_msg(LTXATTN_ERR_ARG, "ltxattn_linear: x, weight and out are required");
+  if (a->x_stride < a->k || a->weight_stride < a->k || a->out_stride < a->n)
+    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_linear: a row stride is shorter than its row");
+  if (!al16(a->x) || !al16(a->weight) || !al16(a->out) || (a->bias && !al16(a->bias)) || (a->x_stride % 8) ||
+      (a->weight_stride % 8) || (a->out_stride % 8))
+    return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_linear: x, weight, bias and out need 16-byte aligned rows");
+  ProjParams P{};
+  P.n_jobs = 1;
+  P.err = device_error_word();
+  if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
+  ProjJob& J = P.job[0];
+  if (int rc = map_rows(&J.tm_x, a->x, a->k, a->m, 1, a->x_stride, 0, "x")) return rc;
+  J.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  J.T = a->m;
+  J.B = 1;
+  J.N = a->n;
+  J.K = a->k;
+  J.tiles_t = (a->m + kPBM - 1) / kPBM;
+  J.out = static_cast<__nv_bfloat16*>(a->out);
+  J.o_sb = 0;
+  J.o_st = a->out_stride;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 256: return launch_linear_bn<256>(P, a, st);
+    case 128: return launch_linear_bn<128>(P, a, st);
+    case 64: return launch_linear_bn<64>(P, a, st);
+    default: return launch_linear_bn<32>(P, a, st);
+  }
+}
+
+int ltxattn_qk_project(const ltxattn_qk_project_args* a, void* stream) {
+  ProjParams P{};
+  P.n_jobs = 1;
+  P.err = device_error_word();
+  if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
+  if (int rc = qk_job(a, &P.job[0])) return rc;
+  return launch_qk(P, static_cast<cudaStream_t>(stream));
+}
+
+int ltxattn_qk_project_pair(const ltxattn_qk_project_args* q, const ltxattn_qk_project_args* k, void* stream) {
+  ProjParams P{};
+  P.n_jobs = 2;
+  P.err = device_error_word();
+  if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
+  if (int rc = qk_job(q, &P.job[0])) return rc;
+  if (int rc = qk_job(k, &P.job[1])) return rc;
+  if (P.job[0].N != P.job[1].N)
+    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project_pair: q and k must have the same heads * head_dim");
+  return launch_qk(P, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

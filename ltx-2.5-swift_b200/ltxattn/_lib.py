@@ -28,6 +28,7 @@ EXPORTED = (
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
+    "ltxattn_linear", "ltxattn_qk_project", "ltxattn_qk_project_pair",
 )
 
 
@@ -114,6 +115,21 @@ class DeviceInfo(ctypes.Structure):
 _lib = None
 
 
+class LinearArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+                ("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("weight", ctypes.c_void_p),
+                ("weight_stride", ctypes.c_int64), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("out_stride", ctypes.c_int64)]
+
+
+class QkProjectArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("in_dim", ctypes.c_int32),
+                ("x", ctypes.c_void_p), ("x_stride_b", ctypes.c_int64), ("x_stride_t", ctypes.c_int64),
+                ("weight", ctypes.c_void_p), ("weight_stride", ctypes.c_int64), ("bias", ctypes.c_void_p),
+                ("norm_weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("rotary", Rotary), ("out", Tensor)]
+
+
 class MemoryPlanArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("rotary", ctypes.c_int32),
@@ -182,6 +198,12 @@ def load(path: str = LIB_PATH):
     L.ltxattn_selftest_wait_timeout.restype = ctypes.c_int
     L.ltxattn_memory_plan.argtypes = [ctypes.POINTER(MemoryPlanArgs), ctypes.POINTER(MemoryPlanInfo)]
     L.ltxattn_memory_plan.restype = ctypes.c_int
+    L.ltxattn_linear.argtypes = [ctypes.POINTER(LinearArgs), vp]
+    L.ltxattn_linear.restype = ctypes.c_int
+    L.ltxattn_qk_project.argtypes = [ctypes.POINTER(QkProjectArgs), vp]
+    L.ltxattn_qk_project.restype = ctypes.c_int
+    L.ltxattn_qk_project_pair.argtypes = [ctypes.POINTER(QkProjectArgs), ctypes.POINTER(QkProjectArgs), vp]
+    L.ltxattn_qk_project_pair.restype = ctypes.c_int
     L.ltxattn_abi_version.argtypes = []
     L.ltxattn_abi_version.restype = ctypes.c_int
     _lib = L

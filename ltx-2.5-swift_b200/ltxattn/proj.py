@@ -1,0 +1,110 @@
+"""The attention module's projections through libltxattn_cuda's tcgen05 GEMMs.
+
+* ``linear(x, weight, bias)`` is ``DiTAttention.linear`` (DiTAttention.swift:178-188,
+  without the LoRA overlay): ``T(T(x W^T) + b)`` through ``ltxattn_linear``.
+* ``qk_project(x, weight, bias, norm_weight, heads, rotary)`` is the q (or k)
+  path from the projection to the attention's input (:341-342, 358-367) as one
+  kernel (``ltxattn_qk_project``): projection, rmsNorm over the whole inner dim,
+  head split and split RoPE, written as the ``[B, heads, T, D]`` view.
+* ``qk_project_pair`` runs the q and k projections in one launch.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from .backend import Failure, Rotary, _rotary, _stream_ptr, _view
+
+
+def _need_bf16(name: str, t: torch.Tensor):
+    if not t.is_cuda:
+        raise Failure("arg", f"{name} must be a CUDA tensor", _lib.ERR_ARG)
+    if t.dtype != torch.bfloat16:
+        raise Failure("dtype", f"{name} must be bfloat16", _lib.ERR_DTYPE)
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """x [..., k] (rows with one stride, unit stride along k), weight [n, k] -> [..., n]."""
+    _need_bf16("x", x)
+    _need_bf16("weight", weight)
+    k = x.shape[-1]
+    n = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != k or weight.stride(1) != 1:
+        raise Failure.shape("weight", weight.shape, f"[n, {k}] with unit stride along k")
+    x2 = x.reshape(-1, k)  # a view when the leading dims collapse into one row stride
+    if x2.stride(1) != 1:
+        raise Failure("align", "x must have unit stride along its last dim", _lib.ERR_ALIGN)
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (n,), dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, n)
+    a = _lib.LinearArgs()
+    a.dtype, a.m, a.n, a.k = _lib.BF16, m, n, k
+    a.x, a.x_stride = x2.data_ptr(), x2.stride(0) if m > 1 else k
+    a.weight, a.weight_stride = weight.data_ptr(), weight.stride(0)
+    if bias is not None:
+        _need_bf16("bias", bias)
+        if bias.numel() != n or not bias.is_contiguous():
+            raise Failure.shape("bias", bias.shape, f"[{n}] contiguous")
+        a.bias = bias.data_ptr()
+    a.out, a.out_stride = o2.data_ptr(), o2.stride(0) if m > 1 else n
+    rc = _lib.load().ltxattn_linear(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out
+
+
+def _qk_args(x, weight, bias, norm_weight, heads, rotary, eps, out):
+    _need_bf16("x", x)
+    _need_bf16("weight", weight)
+    _need_bf16("norm_weight", norm_weight)
+    if x.dim() != 3 or x.stride(2) != 1:
+        raise Failure.shape("x", x.shape, "[B, tokens, in_dim] with unit stride along in_dim")
+    B, T, k = x.shape
+    n = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != k or n % heads or weight.stride(1) != 1:
+        raise Failure.shape("weight", weight.shape, f"[{heads} * head_dim, {k}]")
+    D = n // heads
+    if out is None:
+        out = torch.empty((B, heads, T, D), dtype=x.dtype, device=x.device)
+    a = _lib.QkProjectArgs()
+    a.dtype, a.batch, a.tokens, a.heads, a.head_dim, a.in_dim = _lib.BF16, B, T, heads, D, k
+    a.x, a.x_stride_b, a.x_stride_t = x.data_ptr(), x.stride(0), x.stride(1)
+    a.weight, a.weight_stride = weight.data_ptr(), weight.stride(0)
+    if bias is not None:
+        _need_bf16("bias", bias)
+        a.bias = bias.data_ptr()
+    if norm_weight.numel() != n or not norm_weight.is_contiguous():
+        raise Failure.shape("norm_weight", norm_weight.shape, f"[{n}] contiguous")
+    a.norm_weight = norm_weight.data_ptr()
+    a.eps = float(eps)
+    a.rotary = _rotary("rotary", rotary, B, heads, T, D, x.dtype)
+    a.out = _view("out", out, (B, heads, T, D))
+    return a, out, (x, weight, bias, norm_weight, rotary)
+
+
+def qk_project(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], norm_weight: torch.Tensor,
+               heads: int, rotary: Optional[Rotary] = None, eps: float = 1e-6,
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """split-RoPE(split(rmsNorm(linear(x)))) -> [B, heads, T, D] (or into ``out``)."""
+    a, out, _keep = _qk_args(x, weight, bias, norm_weight, heads, rotary, eps, out)
+    rc = _lib.load().ltxattn_qk_project(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out
+
+
+def qk_project_pair(xq, wq, bq, nq, xk, wk, bk, nk, heads: int, q_rotary: Optional[Rotary] = None,
+                    k_rotary: Optional[Rotary] = None, eps: float = 1e-6, out_q=None, out_k=None,
+                    stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q and k projections in one launch; each result is what ``qk_project`` gives."""
+    aq, out_q, _kq = _qk_args(xq, wq, bq, nq, heads, q_rotary, eps, out_q)
+    ak, out_k, _kk = _qk_args(xk, wk, bk, nk, heads, k_rotary, eps, out_k)
+    rc = _lib.load().ltxattn_qk_project_pair(ctypes.byref(aq), ctypes.byref(ak), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out_q, out_k

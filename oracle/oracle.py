@@ -279,6 +279,16 @@ def gate_output(out, logits, bf16=True):
     return round_bf16(y) if bf16 else y
 
 
+def linear(x, weight, bias=None):
+    """DiTAttention.linear (DiTAttention.swift:178-188) for bf16 activations: the
+    matmul x W^T (accumulated here in fp64) rounded to bf16, then the bias added
+    and rounded again -- the reference's two roundings."""
+    y = round_bf16(_f32(x).astype(np.float64) @ _f32(weight).astype(np.float64).T)
+    if bias is not None:
+        y = round_bf16(y.astype(np.float64) + _f32(bias).astype(np.float64))
+    return y
+
+
 def dit_attention_module(x, w, heads, cos=None, sin=None, k_cos=None, k_sin=None, context=None):
     """DiTAttention.callAsFunction (DiTAttention.swift:315-404) for bf16
     activations, on the CPU: every projection is an fp64 matmul rounded to bf16
@@ -289,10 +299,7 @@ def dit_attention_module(x, w, heads, cos=None, sin=None, k_cos=None, k_sin=None
     merge and ``to_out.0``.  ``w`` maps checkpoint names without the block
     prefix to float32 arrays holding bf16 values."""
     def lin(a, name):
-        y = round_bf16(a.astype(np.float64) @ w[name + ".weight"].astype(np.float64).T)
-        if name + ".bias" in w:
-            y = round_bf16(y.astype(np.float64) + w[name + ".bias"].astype(np.float64))
-        return y
+        return linear(a, w[name + ".weight"], w.get(name + ".bias"))
     kv = x if context is None else context
     B, T, _ = x.shape
     Tk = kv.shape[1]
