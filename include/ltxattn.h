@@ -209,7 +209,7 @@ LTXATTN_API size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* args);
  *  - x [m, k] rows of x_stride elements; weight [n, k] (the checkpoint's
  *    [out, in] layout) rows of weight_stride; out [m, n] rows of out_stride.
  *  - bias [n] or NULL.
- *  - n a multiple of 32, k of 64; rows 16-byte aligned. */
+ *  - n a multiple of 8, k of 64; rows 16-byte aligned. */
 typedef struct ltxattn_linear_args {
   int32_t dtype; /* LTXATTN_BF16 */
   int32_t m, n, k;
@@ -259,6 +259,23 @@ LTXATTN_API int ltxattn_qk_project(const ltxattn_qk_project_args* args, void* st
 /* q and k projections (same heads * head_dim) in one launch. */
 LTXATTN_API int ltxattn_qk_project_pair(const ltxattn_qk_project_args* q, const ltxattn_qk_project_args* k,
                                         void* stream);
+
+/* Arguments of ltxattn_head_gate: out = T(T(x) * g) per head, g = 2 * T(sigmoid(logit)).
+ *  - x, out: [B, H, T, D] views (out may view the merged [B, T, H * D] buffer).
+ *  - gate: the to_gate_logits output [B, T, H] (element strides), or NULL for a
+ *    plain copy (the merge alone).  head_dim a multiple of 8. */
+typedef struct ltxattn_head_gate_args {
+  int32_t dtype;
+  int32_t batch, heads, tokens, head_dim;
+  ltxattn_tensor x, out;
+  const void* gate;
+  int64_t gate_stride_b, gate_stride_t, gate_stride_h;
+} ltxattn_head_gate_args;
+
+/* Replaces the per-head gate and merge (`DiTAttention.swift:395-403`) for the
+ * STG passthrough (`:349-356`), whose output is the value stream rather than an
+ * attention output (ltxattn_fwd applies the same gate in its own store). */
+LTXATTN_API int ltxattn_head_gate(const ltxattn_head_gate_args* args, void* stream);
 
 /* ---- split RoPE on its own ------------------------------------------------ */
 

@@ -96,9 +96,18 @@ struct ProjParams {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// y = T(T(acc) + b) for 32 accumulator columns (b null: T(acc)).
-__device__ __forceinline__ void project_chunk(const uint32_t (&acc)[32], const __nv_bfloat16* bias, float (&y)[32]) {
-  if (bias != nullptr) {
+// y = T(T(acc) + b) for 32 accumulator columns (b null: T(acc)).  `valid` < 32:
+// only the first `valid` columns exist (a ragged last column tile); the bias is
+// read for those alone.
+__device__ __forceinline__ void project_chunk(const uint32_t (&acc)[32], const __nv_bfloat16* bias, float (&y)[32],
+                                              int valid = 32) {
+  if (bias != nullptr && valid < 32) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const float bc = c < valid ? __bfloat162float(bias[c]) : 0.f;
+      y[c] = bf16_round(bf16_round(__uint_as_float(acc[c])) + bc);
+    }
+  } else if (bias != nullptr) {
     const uint4* b4 = reinterpret_cast<const uint4*>(bias);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -223,18 +232,21 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
     if (have) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
+        const int n = n_base + c * 32;
+        if (n >= J.N) break;  // a ragged last column tile (warp-uniform)
+        const int valid = min(32, J.N - n);  // a multiple of 8
         uint32_t acc[32];
         tmem_ld32(tmem + lane_off + c * 32, acc);
         tmem_wait_ld();
         if (t < J.T) {
-          const int n = n_base + c * 32;
           float y[32];
-          project_chunk(acc, J.bias != nullptr ? J.bias + n : nullptr, y);
+          project_chunk(acc, J.bias != nullptr ? J.bias + n : nullptr, y, valid);
           uint4* dst = reinterpret_cast<uint4*>(J.out + (int64_t)b * J.o_sb + (int64_t)t * J.o_st + n);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
-                                pack_bf16x2(y[8 * q + 4], y[8 * q + 5]), pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+            if (8 * q < valid)
+              dst[q] = make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                                  pack_bf16x2(y[8 * q + 4], y[8 * q + 5]), pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
         }
       }
     }
@@ -505,12 +517,13 @@ using namespace ltx;
 
 namespace {
 
+// Column tile: the widest that divides n; otherwise 32 with a ragged last tile
+// (the weight's missing rows read as zeros, only existing columns are stored).
 int bn_for(int n) {
   if (n % 256 == 0) return 256;
   if (n % 128 == 0) return 128;
   if (n % 64 == 0) return 64;
-  if (n % 32 == 0) return 32;
-  return 0;
+  return 32;
 }
 
 template <int BN>
@@ -518,7 +531,7 @@ int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t s
   using S = PSmem<BN, 1>;
   ProjJob& J = P.job[0];
   if (int rc = map_weight(&J.tm_w, a->weight, a->k, a->n, a->weight_stride, BN, "weight")) return rc;
-  J.col_groups = a->n / BN;
+  J.col_groups = (a->n + BN - 1) / BN;
   J.ctas = J.tiles_t * J.col_groups;
   const int slot = BN == 256 ? 0 : BN == 128 ? 1 : BN == 64 ? 2 : 3;
   cudaError_t e = prepare_kernel(linear_kernel<BN>, slot, S::kDynamic);
@@ -620,8 +633,8 @@ int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
   if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_linear: bf16 only");
   if (a->m < 1 || a->n < 1 || a->k < 1) return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_linear: m, n and k must be >= 1");
   const int bn = bn_for(a->n);
-  if (bn == 0 || a->k % 64 != 0)
-    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_linear: n (%d) must be a multiple of 32 and k (%d) of 64", a->n,
+  if (a->n % 8 != 0 || a->k % 64 != 0)
+    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_linear: n (%d) must be a multiple of 8 and k (%d) of 64", a->n,
                     a->k);
   if (!a->x || !a->weight || !a->out) return fail_msg(LTXATTN_ERR_ARG, "ltxattn_linear: x, weight and out are required");
   if (a->x_stride < a->k || a->weight_stride < a->k || a->out_stride < a->n)

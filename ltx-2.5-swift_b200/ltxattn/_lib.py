@@ -28,7 +28,7 @@ EXPORTED = (
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
-    "ltxattn_linear", "ltxattn_qk_project", "ltxattn_qk_project_pair",
+    "ltxattn_linear", "ltxattn_qk_project", "ltxattn_qk_project_pair", "ltxattn_head_gate",
 )
 
 
@@ -130,6 +130,13 @@ class QkProjectArgs(ctypes.Structure):
                 ("norm_weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("rotary", Rotary), ("out", Tensor)]
 
 
+class HeadGateArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("x", Tensor), ("out", Tensor),
+                ("gate", ctypes.c_void_p), ("gate_stride_b", ctypes.c_int64), ("gate_stride_t", ctypes.c_int64),
+                ("gate_stride_h", ctypes.c_int64)]
+
+
 class MemoryPlanArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("rotary", ctypes.c_int32),
@@ -204,6 +211,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_qk_project.restype = ctypes.c_int
     L.ltxattn_qk_project_pair.argtypes = [ctypes.POINTER(QkProjectArgs), ctypes.POINTER(QkProjectArgs), vp]
     L.ltxattn_qk_project_pair.restype = ctypes.c_int
+    L.ltxattn_head_gate.argtypes = [ctypes.POINTER(HeadGateArgs), vp]
+    L.ltxattn_head_gate.restype = ctypes.c_int
     L.ltxattn_abi_version.argtypes = []
     L.ltxattn_abi_version.restype = ctypes.c_int
     _lib = L

@@ -108,3 +108,27 @@ def qk_project_pair(xq, wq, bq, nq, xk, wk, bk, nk, heads: int, q_rotary: Option
     if rc != _lib.OK:
         raise Failure.from_status(rc)
     return out_q, out_k
+
+
+def head_gate(x: torch.Tensor, logits: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              stream=None) -> torch.Tensor:
+    """x [B, H, T, D] -> T(T(x) * 2 T(sigmoid(logits))) per head (logits [B, T, H]; None:
+    a copy), into ``out`` (may view the merged [B, T, H * D] buffer)."""
+    if x.dim() != 4:
+        raise Failure.shape("x", x.shape, "[B, heads, tokens, headDim]")
+    B, H, T, D = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    a = _lib.HeadGateArgs()
+    a.dtype = _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F32
+    a.batch, a.heads, a.tokens, a.head_dim = B, H, T, D
+    a.x, a.out = _view("x", x, (B, H, T, D)), _view("out", out, (B, H, T, D))
+    if logits is not None:
+        if tuple(logits.shape) != (B, T, H) or logits.dtype != x.dtype:
+            raise Failure.shape("logits", logits.shape, f"[{B}, {T}, {H}] {x.dtype}")
+        a.gate = logits.data_ptr()
+        a.gate_stride_b, a.gate_stride_t, a.gate_stride_h = logits.stride(0), logits.stride(1), logits.stride(2)
+    rc = _lib.load().ltxattn_head_gate(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    if rc != _lib.OK:
+        raise Failure.from_status(rc)
+    return out

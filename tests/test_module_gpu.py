@@ -1,8 +1,9 @@
 """A whole DiT attention module (DiTAttention.callAsFunction,
-DiTAttention.swift:315-404) on the device -- library GEMMs for the
-projections, libltxattn_cuda for rmsNorm + split + RoPE, the attention, the
-gate and the merge -- against the CPU oracle's composition of the same steps
-(``oracle.dit_attention_module``).
+DiTAttention.swift:315-404) on the device -- every step in libltxattn_cuda
+(tcgen05 projections with the norms, split and RoPE fused into the q / k
+projection, the attention, the gate and the merge), and the same module with
+the projections on torch's library GEMM -- against the CPU oracle's
+composition of the same steps (``oracle.dit_attention_module``).
 
 Tolerance: the bf16 bar (max abs <= 2e-2, rel-L2 <= 1e-2) on the module output;
 the projections' fp32-accumulated GEMMs and the oracle's fp64 ones may round a
@@ -46,17 +47,18 @@ def check(got, want, what):
     assert err.max() <= 2e-2 and rel <= 1e-2, f"{what}: max abs {err.max():.3e} rel-L2 {rel:.3e}"
 
 
+@pytest.mark.parametrize("gemm", ["ltxattn", "torch"])
 @pytest.mark.parametrize("gate", [True, False])
-def test_video_self_attention_module(gate):
+def test_video_self_attention_module(gate, gemm):
     B, T, heads, D = 1, 96, 8, 64
     inner = query_dim = heads * D
     w = weights(3, query_dim, inner, query_dim, gate, heads)
     x = inputs.round_bf16(inputs.seeded_tensor(5, (B, T, query_dim)))
     cos, sin = inputs.rope1d(np.arange(T, dtype=np.float64), D)
     want = oracle.dit_attention_module(x, w, heads, cos, sin)
-    mod = DiTAttentionModule({k: dev(v) for k, v in w.items()}, heads)
+    mod = DiTAttentionModule({k: dev(v) for k, v in w.items()}, heads, gemm=gemm)
     got = mod(dev(x), rotary=Rotary(dev(cos), dev(sin)))
-    check(got, want, f"self gate={gate}")
+    check(got, want, f"self gate={gate} gemm={gemm}")
 
 
 def test_cross_modal_module_with_separate_key_tables():
@@ -84,3 +86,21 @@ def test_text_cross_attention_takes_no_rotary():
     cos = torch.ones((16, D // 2), device="cuda", dtype=torch.bfloat16)
     with pytest.raises(Failure):
         mod(x, rotary=Rotary(cos, cos))
+
+
+@pytest.mark.parametrize("gate", [True, False])
+def test_stg_passthrough_gates_and_merges_the_value_stream(gate):
+    # all_perturbed (DiTAttention.swift:349-356): v, split, gated (ltxattn_head_gate), merged, to_out
+    B, T, heads, D = 1, 96, 8, 64
+    inner = query_dim = heads * D
+    w = weights(13, query_dim, inner, query_dim, gate, heads)
+    x = inputs.round_bf16(inputs.seeded_tensor(14, (B, T, query_dim)))
+    v = oracle.linear(x, w["to_v.weight"], w["to_v.bias"])
+    vh = v.reshape(B, T, heads, D).transpose(0, 2, 1, 3)
+    if gate:
+        vh = oracle.gate_output(vh, oracle.linear(x, w["to_gate_logits.weight"], w["to_gate_logits.bias"]))
+    merged = np.ascontiguousarray(vh.transpose(0, 2, 1, 3).reshape(B, T, inner))
+    want = oracle.linear(merged, w["to_out.0.weight"], w["to_out.0.bias"])
+    mod = DiTAttentionModule({k: dev(v) for k, v in w.items()}, heads)
+    got = mod(dev(x), all_perturbed=True)
+    check(got, want, f"passthrough gate={gate}")

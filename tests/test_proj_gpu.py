@@ -61,6 +61,8 @@ def bias(seed, n):
     (3120, 32, 4096, True),     # to_gate_logits: [3120, 4096] -> 32 heads
     (96, 128, 256, True),
     (64, 64, 64, True),
+    (100, 8, 512, True),        # eight heads' gate logits: a ragged 32-column tile
+    (130, 296, 256, True),      # 256 + a ragged tile of 40
 ])
 def test_linear_matches_the_oracle(m, n, k, with_bias):
     x = inputs.seeded_tensor(10 + m, (m, k))
