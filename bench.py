@@ -1,7 +1,7 @@
 """Benchmark of the LTX 2.5 DiT fused attention on B200 (libltxattn_cuda).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4a|c4b|c4c|c5|a101|benchgemm|qkprep|module]
+                    [--workload c2|c3|c4a|c4b|c4c|c5|a101|benchgemm|qkprep|module|outproj]
                     [--no-extras] [--no-cpu-baseline] [--bwd]
 
 Default workload (the metric's configuration): video
@@ -707,6 +707,91 @@ def run_module(args):
     return result
 
 
+def run_outproj(args):
+    """Row-parallel to_out of a head-sharded module at the config-2 shape: rank r
+    holds heads [r*32/N, (r+1)*32/N) of the merged attention output [3120, 4096]
+    and the matching column block of to_out.0.weight [4096, 4096];
+    ltxattn_out_project_allreduce (tcgen05 GEMM to an fp32 partial, NCCL
+    all-reduce, bias and rounding) leaves the whole output on every rank.
+    TFLOP/s of the whole to_out (2 M N K) per step; the GEMM alone and the
+    all-reduce's share are reported beside it, and rank 0 checks sampled rows
+    against the oracle."""
+    import ctypes
+    import torch
+    from ltxattn import _lib
+    from ltxattn import dist as ldist
+    from ltxattn.proj import linear
+    ctx = Ctx()
+    M, N, H, D = 3120, 4096, 32, 128
+    K = H * D
+    if H % ctx.ws:
+        raise SystemExit(f"{H} heads do not shard over {ctx.ws} ranks")
+    k = (H // ctx.ws) * D
+    k0 = ctx.rank * k
+    g = torch.Generator(device="cuda").manual_seed(DEFAULT_SEED)  # the same tensors on every rank
+    bf = torch.bfloat16
+    merged = torch.randn((M, K), generator=g, device="cuda").to(bf)
+    W = (torch.randn((N, K), generator=g, device="cuda") / 64).to(bf)
+    b = (torch.randn(N, generator=g, device="cuda") * 0.1).to(bf)
+    x_local, w_block = merged[:, k0:k0 + k], W[:, k0:k0 + k]
+    if ctx.ws > 1:
+        uid = ldist.exchange_unique_id()
+    else:
+        raw = (ctypes.c_uint8 * 128)()
+        assert _lib.load().ltxattn_comm_unique_id(raw) == _lib.OK
+        uid = bytes(raw)
+    hg = ldist.HeadGather(ctx.ws, ctx.rank, uid, ctx.local)
+    out = torch.empty((M, N), device="cuda", dtype=bf)
+    wsb = torch.empty(M * N * 4, device="cuda", dtype=torch.uint8)
+    try:
+        nranks, _ = hg.size()
+        step = lambda: hg.out_project(x_local, w_block, b, out=out, workspace=wsb, stream=ctx.stream)
+        full_ms = ctx.timed(step, args.steps, warmup=args.warmup)
+        part = torch.empty((M, N), device="cuda", dtype=bf)
+        gemm_ms = ctx.timed(lambda: linear(x_local, w_block, out=part, stream=ctx.stream), args.steps,
+                            warmup=args.warmup)
+        step()
+        torch.cuda.synchronize()
+        parity = None
+        if ctx.rank == 0:
+            orc = _oracle()
+            rows = np.r_[0:32, 1544:1576, 3088:3120]
+            ref = orc.linear(merged[torch.as_tensor(rows, device="cuda")].float().cpu().numpy(),
+                             W.float().cpu().numpy(), b.float().cpu().numpy())
+            got = out[torch.as_tensor(rows, device="cuda")].float().cpu().numpy()
+            err = np.abs(got - ref)
+            rel = float(np.linalg.norm(err) / np.linalg.norm(ref))
+            parity = {"max_abs": round(float(err.max()), 6), "rel_l2": round(rel, 6),
+                      "ok": bool(err.max() <= 2e-2 and rel <= 1e-2),
+                      "checked": f"{len(rows)} rows of the reduced output on rank 0, fp64 oracle of the full to_out"}
+        ms, gms = ctx.max_over_ranks([sum(full_ms) / args.steps, sum(gemm_ms) / args.steps])
+    finally:
+        ctx.barrier()
+        hg.close()
+    flops = 2.0 * M * N * K
+    burst, _, _, src = peaks()
+    result = None
+    if ctx.rank == 0:
+        result = {
+            "metric": "row-parallel to_out TFLOP/s bf16 (tcgen05 GEMM + NCCL all-reduce) @3120 tok, 4096 -> 4096 "
+                      "(aggregate over GPUs)",
+            "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": ctx.ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (N(0,1) merged output, N(0,1)/64 weight, seeded CUDA generator)",
+            "config": {"workload": "outproj: to_out.0 over head shards, [3120, 4096] x [4096, 4096]^T + b",
+                       "parallelism": f"heads x{ctx.ws}", "l2": L2_NOTE, "k_per_rank": k},
+            "gemm_ms": round(gms, 5),
+            "gemm_tflops_per_gpu": round(2.0 * M * N * k / (gms * 1e-3) / 1e12, 2),
+            "gemm_frac_of_burst": round(2.0 * M * N * k / (gms * 1e-3) / 1e12 / burst, 4),
+            "allreduce_and_round_ms": round(max(0.0, ms - gms), 5),
+            "allreduce_bytes_per_rank": M * N * 4, "nccl_nranks": nranks,
+            "parity": parity, "gpu_launches": 2 * args.steps,
+        }
+    ctx.close()
+    return result
+
+
 # ---------------------------------------------------------------------------
 # the CPU arms
 
@@ -851,7 +936,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS) + ["benchgemm", "qkprep", "module"])
+    ap.add_argument("--workload", default="c2",
+                    choices=sorted(WORKLOADS) + ["benchgemm", "qkprep", "module", "outproj"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the chosen workload (no sub-records)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -875,6 +961,8 @@ def main():
         res = run_module(args)
     elif args.workload == "benchgemm":
         res = run_benchgemm(args)
+    elif args.workload == "outproj":
+        res = run_outproj(args)
     else:
         res = run_ours(args)
     if res is not None:

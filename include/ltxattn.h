@@ -395,6 +395,37 @@ typedef struct ltxattn_gather_args {
 
 LTXATTN_API int ltxattn_allgather_heads(const ltxattn_gather_args* args, ltxattn_comm* comm, void* stream);
 
+/* Row-parallel to_out over the head shards (`DiTAttention.swift:401-404` with
+ * heads sharded across ranks): rank r holds its heads' slice of the merged
+ * attention output x [m, k] (k = heads_per_rank * head_dim) and the matching
+ * column block of to_out.0.weight ([n, k] rows of weight_stride, e.g. the full
+ * weight's pointer advanced by r * k with weight_stride = heads * head_dim).
+ * Each rank's GEMM writes its fp32 partial product into the workspace
+ * (m * n floats, ltxattn_out_project_workspace bytes, 256-byte aligned), an
+ * NCCL all-reduce sums the partials over the ranks in place, and every rank
+ * stores out = T(T(sum) + bias), the roundings of DiTAttention.linear
+ * (`:178-188`) applied once to the full sum.  With one rank the result is
+ * bit-identical to ltxattn_linear on the same arguments.  n a multiple of 8,
+ * k of 64.  The reference is single-device; this serves a head-parallel job
+ * whose next layer needs the whole to_out output on every rank. */
+typedef struct ltxattn_out_project_args {
+  int32_t dtype; /* LTXATTN_BF16 */
+  int32_t m, n, k;
+  const void* x;
+  int64_t x_stride;
+  const void* weight;
+  int64_t weight_stride;
+  const void* bias;
+  void* out;
+  int64_t out_stride;
+  void* workspace;
+  size_t workspace_bytes;
+} ltxattn_out_project_args;
+
+LTXATTN_API size_t ltxattn_out_project_workspace(const ltxattn_out_project_args* args);
+LTXATTN_API int ltxattn_out_project_allreduce(const ltxattn_out_project_args* args, ltxattn_comm* comm,
+                                              void* stream);
+
 /* The rank count and this rank's index as NCCL itself reports them
  * (ncclCommCount / ncclCommUserRank), for checking a launch's world size.
  * No counterpart in the reference. */

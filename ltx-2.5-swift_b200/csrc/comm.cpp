@@ -19,6 +19,7 @@
 #include <string>
 
 #include "../../include/ltxattn.h"
+#include "ltxattn_internal.h"
 
 namespace ltx {
 int set_error_message(int status, const char* msg);
@@ -38,6 +39,7 @@ struct NcclApi {
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
   ncclResult_t (*CommDestroy)(ncclComm_t);
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*GroupStart)();
   ncclResult_t (*GroupEnd)();
   const char* (*GetErrorString)(ncclResult_t);
@@ -58,12 +60,13 @@ const NcclApi& nccl() {
     api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
     api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
     api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+    api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
     api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
     api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
     api.CommCount = reinterpret_cast<decltype(api.CommCount)>(dlsym(h, "ncclCommCount"));
     api.CommUserRank = reinterpret_cast<decltype(api.CommUserRank)>(dlsym(h, "ncclCommUserRank"));
-    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GroupStart &&
+    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.AllReduce && api.GroupStart &&
              api.GroupEnd && api.GetErrorString && api.CommCount && api.CommUserRank;
   });
   return api;
@@ -164,6 +167,52 @@ int ltxattn_allgather_heads(const ltxattn_gather_args* a, ltxattn_comm* comm, vo
   r = nccl().GroupEnd();
   if (r != ncclSuccess) return nccl_fail("ncclGroupEnd", r);
   return LTXATTN_OK;
+}
+
+size_t ltxattn_out_project_workspace(const ltxattn_out_project_args* a) {
+  if (!a || a->m < 1 || a->n < 1) return 0;
+  return ((size_t)a->m * a->n * sizeof(float) + 255) & ~size_t(255);
+}
+
+// Row-parallel to_out: this rank's heads' slice of the merged attention output
+// times its column block of to_out.0.weight, as an fp32 partial in the
+// workspace; the partials of all ranks summed in place by ncclAllReduce; then
+// out = T(T(sum) + bias) on every rank.  All three steps are ordered on
+// `stream`.  With one rank the result is bit-identical to ltxattn_linear.
+int ltxattn_out_project_allreduce(const ltxattn_out_project_args* a, ltxattn_comm* comm, void* stream) {
+  if (!a || !comm) return ltx::set_error_message(LTXATTN_ERR_ARG, "args or comm is NULL");
+  if (a->dtype != LTXATTN_BF16)
+    return ltx::set_error_message(LTXATTN_ERR_DTYPE, "ltxattn_out_project_allreduce: bf16 only");
+  const size_t need = ltxattn_out_project_workspace(a);
+  if (need == 0) return ltx::set_error_message(LTXATTN_ERR_SHAPE, "ltxattn_out_project_allreduce: m and n must be >= 1");
+  if (!a->workspace || a->workspace_bytes < need || (reinterpret_cast<uintptr_t>(a->workspace) & 255u)) {
+    char buf[200];
+    snprintf(buf, sizeof buf, "ltxattn_out_project_allreduce: a 256-byte aligned workspace of %zu bytes is needed", need);
+    return ltx::set_error_message(LTXATTN_ERR_WORKSPACE, buf);
+  }
+  if (!a->out || a->out_stride < a->n || (a->out_stride % 8) || (reinterpret_cast<uintptr_t>(a->out) & 15u) ||
+      (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15u)))
+    return ltx::set_error_message(LTXATTN_ERR_ALIGN, "ltxattn_out_project_allreduce: out and bias need 16-byte aligned rows");
+  if (int rc = need_nccl()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(a->workspace);
+  ltxattn_linear_args l{};
+  l.dtype = a->dtype;
+  l.m = a->m;
+  l.n = a->n;
+  l.k = a->k;
+  l.x = a->x;
+  l.x_stride = a->x_stride;
+  l.weight = a->weight;
+  l.weight_stride = a->weight_stride;
+  l.bias = nullptr;
+  l.out = a->out;
+  l.out_stride = a->out_stride;
+  if (int rc = ltx::linear_partial_f32(&l, partial, st)) return rc;
+  const ncclResult_t r =
+      nccl().AllReduce(partial, partial, (size_t)a->m * a->n, ncclFloat32, ncclSum, comm->nccl, st);
+  if (r != ncclSuccess) return nccl_fail("ncclAllReduce", r);
+  return ltx::bias_round(partial, a->bias, a->out, a->out_stride, a->m, a->n, st);
 }
 
 }  // extern "C"

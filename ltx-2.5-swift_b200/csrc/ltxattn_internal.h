@@ -226,3 +226,15 @@ cudaError_t launch_bwd_f32(const BwdParams& p, int D, int Hc, int B, cudaStream_
 int* device_error_word();
 
 }  // namespace ltx
+
+struct ltxattn_linear_args;
+
+namespace ltx {
+
+// The row-parallel to_out's local steps (proj_sm100.cu): the GEMM's fp32
+// accumulator into `partial` [m, n] (no bias, no rounding), and, after the
+// reduction across ranks, out = T(T(sum) + bias).
+int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_t st);
+int bias_round(const float* sum, const void* bias, void* out, int64_t out_stride, int m, int n, cudaStream_t st);
+
+}  // namespace ltx

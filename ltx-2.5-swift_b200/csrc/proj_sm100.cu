@@ -75,8 +75,9 @@ struct ProjJob {
   int tiles_t;     // ceil(T / 128)
   int col_groups;  // CTAs per row block (the cluster size of the q/k kernel)
   int ctas;        // tiles_t * B * col_groups
-  // linear: out[b][t][n] at out + b * o_sb + t * o_st + n
+  // linear: out[b][t][n] at out + b * o_sb + t * o_st + n (bf16), or out_f32 + t * o_st + n
   __nv_bfloat16* out;
+  float* out_f32;
   int64_t o_sb, o_st;
   // q/k: norm weight, rotary tables [B|1][H|1][T][D/2] (cos null: none), out [B, H, T, D]
   const __nv_bfloat16* norm_w;
@@ -186,7 +187,7 @@ __device__ __forceinline__ void mainloop_role(const ProjJob& J, int warp, int la
 // ---------------------------------------------------------------------------
 // linear: one CTA per (128-row block, BN columns)
 
-template <int BN>
+template <int BN, bool kF32Out>
 __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_constant__ ProjParams p) {
   using S = PSmem<BN, 1>;
   extern __shared__ uint8_t smem_raw[];
@@ -238,7 +239,14 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
         uint32_t acc[32];
         tmem_ld32(tmem + lane_off + c * 32, acc);
         tmem_wait_ld();
-        if (t < J.T) {
+        if (t < J.T && kF32Out) {
+          // the fp32 accumulator itself (a partial sum that is reduced across ranks before
+          // the bias and the roundings)
+          uint4* dst = reinterpret_cast<uint4*>(J.out_f32 + (int64_t)t * J.o_st + n);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (4 * q < valid) dst[q] = make_uint4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+        } else if (t < J.T) {
           float y[32];
           project_chunk(acc, J.bias != nullptr ? J.bias + n : nullptr, y, valid);
           uint4* dst = reinterpret_cast<uint4*>(J.out + (int64_t)b * J.o_sb + (int64_t)t * J.o_st + n);
@@ -419,6 +427,26 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
   }
 }
 
+// out[t][n] = T(T(sum[t][n]) + b[n]): the roundings of DiTAttention.linear applied
+// once the row-parallel partial sums have been reduced.  One thread per 8 columns.
+__global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64_t s_st, const __nv_bfloat16* bias,
+                                                         __nv_bfloat16* out, int64_t o_st, int M, int N) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int n8 = N / 8;
+  if (i >= (int64_t)M * n8) return;
+  const int t = (int)(i / n8), n = (int)(i % n8) * 8;
+  const float4* src = reinterpret_cast<const float4*>(sum + (int64_t)t * s_st + n);
+  const float4 a = src[0], c = src[1];
+  float y[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    y[e] = bf16_round(y[e]);
+    if (bias != nullptr) y[e] = bf16_round(y[e] + __bfloat162float(bias[n + e]));
+  }
+  *reinterpret_cast<uint4*>(out + (int64_t)t * o_st + n) =
+      make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+}
+
 // ---------------------------------------------------------------------------
 // host side
 
@@ -493,7 +521,7 @@ int launch_fail(cudaError_t e, const char* what) {
 // Dynamic shared memory above 48 KB is opted into once per device and kernel.
 constexpr int kMaxDev = 64;
 std::mutex g_mu;
-bool g_attr_set[kMaxDev][5] = {};
+bool g_attr_set[kMaxDev][10] = {};
 
 template <typename K>
 cudaError_t prepare_kernel(K kernel, int slot, size_t smem) {
@@ -526,17 +554,17 @@ int bn_for(int n) {
   return 32;
 }
 
-template <int BN>
+template <int BN, bool kF32Out>
 int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t st) {
   using S = PSmem<BN, 1>;
   ProjJob& J = P.job[0];
   if (int rc = map_weight(&J.tm_w, a->weight, a->k, a->n, a->weight_stride, BN, "weight")) return rc;
   J.col_groups = (a->n + BN - 1) / BN;
   J.ctas = J.tiles_t * J.col_groups;
-  const int slot = BN == 256 ? 0 : BN == 128 ? 1 : BN == 64 ? 2 : 3;
-  cudaError_t e = prepare_kernel(linear_kernel<BN>, slot, S::kDynamic);
+  const int slot = (BN == 256 ? 0 : BN == 128 ? 1 : BN == 64 ? 2 : 3) + (kF32Out ? 5 : 0);
+  cudaError_t e = prepare_kernel(linear_kernel<BN, kF32Out>, slot, S::kDynamic);
   if (e != cudaSuccess) return launch_fail(e, "linear kernel attributes");
-  linear_kernel<BN><<<J.ctas, kPThreads, S::kDynamic, st>>>(P);
+  linear_kernel<BN, kF32Out><<<J.ctas, kPThreads, S::kDynamic, st>>>(P);
   e = cudaGetLastError();
   if (e != cudaSuccess) return launch_fail(e, "linear launch");
   return LTXATTN_OK;
@@ -624,11 +652,9 @@ int launch_qk(ProjParams& P, cudaStream_t st) {
   return LTXATTN_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
+// ltxattn_linear, or (f32_out != null) the same GEMM storing its fp32
+// accumulator, without bias or roundings, into f32_out [m, n] (row stride n).
+int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
   if (a == nullptr) return fail_msg(LTXATTN_ERR_ARG, "args is NULL");
   if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_linear: bf16 only");
   if (a->m < 1 || a->n < 1 || a->k < 1) return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_linear: m, n and k must be >= 1");
@@ -655,15 +681,53 @@ int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
   J.K = a->k;
   J.tiles_t = (a->m + kPBM - 1) / kPBM;
   J.out = static_cast<__nv_bfloat16*>(a->out);
+  J.out_f32 = f32_out;
   J.o_sb = 0;
-  J.o_st = a->out_stride;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (bn) {
-    case 256: return launch_linear_bn<256>(P, a, st);
-    case 128: return launch_linear_bn<128>(P, a, st);
-    case 64: return launch_linear_bn<64>(P, a, st);
-    default: return launch_linear_bn<32>(P, a, st);
+  J.o_st = f32_out != nullptr ? a->n : a->out_stride;
+  if (f32_out != nullptr) {
+    switch (bn) {
+      case 256: return launch_linear_bn<256, true>(P, a, st);
+      case 128: return launch_linear_bn<128, true>(P, a, st);
+      case 64: return launch_linear_bn<64, true>(P, a, st);
+      default: return launch_linear_bn<32, true>(P, a, st);
+    }
   }
+  switch (bn) {
+    case 256: return launch_linear_bn<256, false>(P, a, st);
+    case 128: return launch_linear_bn<128, false>(P, a, st);
+    case 64: return launch_linear_bn<64, false>(P, a, st);
+    default: return launch_linear_bn<32, false>(P, a, st);
+  }
+}
+
+}  // namespace
+
+namespace ltx {
+
+// The row-parallel to_out's local steps (the collective between them is in comm.cpp).
+int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_t st) {
+  if (partial == nullptr || (reinterpret_cast<uintptr_t>(partial) & 15u))
+    return fail_msg(LTXATTN_ERR_ALIGN, "the fp32 partial buffer must be 16-byte aligned");
+  return run_linear(a, partial, st);
+}
+
+int bias_round(const float* sum, const void* bias, void* out, int64_t out_stride, int m, int n, cudaStream_t st) {
+  const int64_t threads = (int64_t)m * (n / 8);
+  const int64_t blocks = (threads + 255) / 256;
+  if (blocks > 0x7fffffff) return fail_msg(LTXATTN_ERR_UNSUPPORTED, "output too large");
+  bias_round_kernel<<<(unsigned)blocks, 256, 0, st>>>(sum, n, static_cast<const __nv_bfloat16*>(bias),
+                                                      static_cast<__nv_bfloat16*>(out), out_stride, m, n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return launch_fail(e, "bias and rounding launch");
+  return LTXATTN_OK;
+}
+
+}  // namespace ltx
+
+extern "C" {
+
+int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
+  return run_linear(a, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int ltxattn_qk_project(const ltxattn_qk_project_args* a, void* stream) {

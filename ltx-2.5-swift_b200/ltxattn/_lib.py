@@ -29,6 +29,7 @@ EXPORTED = (
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
     "ltxattn_linear", "ltxattn_qk_project", "ltxattn_qk_project_pair", "ltxattn_head_gate",
+    "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce",
 )
 
 
@@ -137,6 +138,13 @@ class HeadGateArgs(ctypes.Structure):
                 ("gate_stride_h", ctypes.c_int64)]
 
 
+class OutProjectArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+                ("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("weight", ctypes.c_void_p),
+                ("weight_stride", ctypes.c_int64), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("out_stride", ctypes.c_int64), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
 class MemoryPlanArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("rotary", ctypes.c_int32),
@@ -213,6 +221,10 @@ def load(path: str = LIB_PATH):
     L.ltxattn_qk_project_pair.restype = ctypes.c_int
     L.ltxattn_head_gate.argtypes = [ctypes.POINTER(HeadGateArgs), vp]
     L.ltxattn_head_gate.restype = ctypes.c_int
+    L.ltxattn_out_project_workspace.argtypes = [ctypes.POINTER(OutProjectArgs)]
+    L.ltxattn_out_project_workspace.restype = ctypes.c_size_t
+    L.ltxattn_out_project_allreduce.argtypes = [ctypes.POINTER(OutProjectArgs), vp, vp]
+    L.ltxattn_out_project_allreduce.restype = ctypes.c_int
     L.ltxattn_abi_version.argtypes = []
     L.ltxattn_abi_version.restype = ctypes.c_int
     _lib = L

@@ -103,6 +103,38 @@ class HeadGather:
             raise Failure.from_status(rc)
         return out
 
+    def out_project(self, x_local: torch.Tensor, weight_block: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                    out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+                    stream=None) -> torch.Tensor:
+        """Row-parallel to_out (``ltxattn_out_project_allreduce``): this rank's merged
+        head slice x_local [..., k] times its column block of to_out.0.weight
+        ([n, k], any row stride), summed over the ranks, + bias; every rank gets
+        [..., n]."""
+        k = x_local.shape[-1]
+        x2 = x_local.reshape(-1, k)
+        m, n = x2.shape[0], weight_block.shape[0]
+        if weight_block.dim() != 2 or weight_block.shape[1] != k or weight_block.stride(1) != 1:
+            raise Failure.shape("weight_block", weight_block.shape, f"[n, {k}] with unit stride along k")
+        if out is None:
+            out = torch.empty(x_local.shape[:-1] + (n,), dtype=x_local.dtype, device=x_local.device)
+        a = _lib.OutProjectArgs()
+        a.dtype, a.m, a.n, a.k = _lib.BF16, m, n, k
+        a.x, a.x_stride = x2.data_ptr(), x2.stride(0) if m > 1 else k
+        a.weight, a.weight_stride = weight_block.data_ptr(), weight_block.stride(0)
+        a.bias = bias.data_ptr() if bias is not None else None
+        o2 = out.view(-1, n)
+        a.out, a.out_stride = o2.data_ptr(), o2.stride(0) if m > 1 else n
+        L = _lib.load()
+        need = int(L.ltxattn_out_project_workspace(ctypes.byref(a)))
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=x_local.device)
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+        s = stream if stream is not None else torch.cuda.current_stream()
+        rc = L.ltxattn_out_project_allreduce(ctypes.byref(a), self._comm, ctypes.c_void_p(s.cuda_stream))
+        if rc != _lib.OK:
+            raise Failure.from_status(rc)
+        return out
+
     def close(self):
         if self._comm:
             _lib.load().ltxattn_comm_destroy(self._comm)
