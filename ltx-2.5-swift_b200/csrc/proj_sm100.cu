@@ -17,10 +17,11 @@
 //    the [B, H, T, D] view the attention reads.  The norm needs every one of a
 //    row's N = heads * head_dim outputs, so a cluster of N / 512 CTAs covers a
 //    128-row block: each CTA computes 512 columns (two 256-column accumulators
-//    in TMEM), publishes its rows' partial sums of squares in shared memory,
-//    and reads the other CTAs' partials through distributed shared memory
-//    after a cluster barrier.  Every CTA adds the partials in rank order, so
-//    all of them use the same r and the result does not depend on scheduling.
+//    in TMEM), stores its rows' partial sums of squares into every CTA of the
+//    cluster through distributed shared memory and arrives on each CTA's
+//    exchange mbarrier; each CTA waits (bounded) for all arrivals and adds the
+//    partials in rank order, so all of them use the same r and the result does
+//    not depend on scheduling.
 //
 // CTA: 256 threads.  Warp 0 lane 0 is the TMA producer: 128-row x 64 slices of
 // x and BN-row x 64 slices of W into kStages shared-memory stages (128-byte
@@ -58,8 +59,9 @@ struct PSmem {
   // full[kPStages], empty[kPStages], acc_full[NT]
   static constexpr uint32_t kOffBar = kPStages * kStage;
   static constexpr uint32_t kOffCtl = kOffBar + (2 * kPStages + NT) * 8;  // tmem slot, abort flag
-  static constexpr uint32_t kOffPart = kOffCtl + 16;                      // float[128] partial sums
-  static constexpr uint32_t kBytes = kOffPart + 128 * 4;
+  static constexpr uint32_t kOffXbar = kOffCtl + 16;   // the partial-sum exchange's mbarrier
+  static constexpr uint32_t kOffPart = kOffXbar + 16;  // float[8][128]: the cluster's partial sums by rank
+  static constexpr uint32_t kBytes = kOffPart + 8 * 128 * 4;
   static constexpr uint32_t kDynamic = kBytes + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = BN * NT < 32 ? 32 : BN * NT;
   static_assert(kA % 1024 == 0 && kB % 1024 == 0, "stages must keep 1024-byte swizzle atoms aligned");
@@ -302,6 +304,7 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   float* part = reinterpret_cast<float*>(sm + S::kOffPart);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + S::kOffXbar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // job 0 owns CTAs [0, job[0].ctas), job 1 the rest; both are whole clusters
   const int j = (int)blockIdx.x >= p.job[0].ctas ? 1 : 0;
@@ -315,11 +318,16 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2 * kPStages + kQkNT; ++i) mbar_init(bars + i, 1);
+    mbar_init(xbar, 128 * C);  // every epilogue thread of every CTA of the cluster arrives once
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&J.tm_x);
     tma_prefetch_desc(&J.tm_w);
   }
+  // every CTA's barriers are initialised before any CTA arrives on another's
+  __syncwarp();
+  cluster_arrive();
+  cluster_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, S::kTmemCols);
     tmem_relinquish();
@@ -331,11 +339,6 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
 
   if (warp < 4) {
     mainloop_role<kQkBN, kQkNT>(J, warp, lane, t0, b, n_base, sm, full, empty, acc_full, tmem, abort_flag, p.err);
-    __syncwarp();
-    cluster_arrive();  // partial sums published (these warps contribute none)
-    cluster_wait();
-    cluster_arrive();  // done reading the other CTAs' partial sums
-    cluster_wait();
   } else {
     const int r = threadIdx.x - 128;
     const int t = t0 + r;
@@ -357,12 +360,15 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
         for (int e = 0; e < 32; ++e) ss = __fmaf_rn(y[e], y[e], ss);
       }
     }
-    part[r] = ss;
-    cluster_arrive();
-    cluster_wait();
+    // publish this row's partial into slot [rank][r] of every CTA of the cluster,
+    // then arrive on each CTA's exchange barrier; each CTA waits (bounded) for all
+    // 128 * C arrivals on its own barrier and then reads every partial locally
+    for (int q = 0; q < C; ++q) st_cluster_f32(part + rank * 128 + r, (uint32_t)q, ss);
+    for (int q = 0; q < C; ++q) mbar_arrive_cluster(xbar, (uint32_t)q);
+    const bool have_all = mbar_wait_cluster(xbar, 0, abort_flag, p.err, 45);
+    have = __all_sync(0xffffffffu, have_all) && have;
     float tot = 0.f;
-    for (int q = 0; q < C; ++q) tot = __fadd_rn(tot, ld_cluster_f32(part + r, (uint32_t)q));
-    cluster_arrive();  // this CTA's reads of the other CTAs' shared memory are done
+    for (int q = 0; q < C; ++q) tot = __fadd_rn(tot, part[q * 128 + r]);
     const float rn = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)J.N), J.eps));
     // phase 2: normalise, split into heads, rotate, store
     const int D = J.D, half_chunks = D / 64;  // 32-column chunks per half head
@@ -416,8 +422,6 @@ __global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_c
         }
       }
     }
-    __syncwarp();
-    cluster_wait();  // every CTA has read this CTA's partial sums: its shared memory may go
   }
   tc_fence_before();
   __syncthreads();
