@@ -223,42 +223,9 @@ typedef struct ltxattn_linear_args {
 } ltxattn_linear_args;
 
 /* Replaces `DiTAttention.linear` (`DiTAttention.swift:178-188`) without the LoRA
- * overlay: to_v, to_out.0 and to_gate_logits of the attention module. */
+ * overlay: to_q, to_k, to_v, to_out.0 and to_gate_logits of the attention module
+ * (q and k then take ltxattn_qk_prep for the norm, the head split and RoPE). */
 LTXATTN_API int ltxattn_linear(const ltxattn_linear_args* args, void* stream);
-
-/* Arguments of ltxattn_qk_project: out = split-RoPE(split(rmsNorm(linear(x)))).
- *  - x [batch, tokens, in_dim] (element strides x_stride_b, x_stride_t; unit
- *    stride along in_dim); weight [heads * head_dim, in_dim] rows of
- *    weight_stride; bias [heads * head_dim] or NULL; norm_weight
- *    [heads * head_dim] and eps: the q_norm / k_norm of the module.
- *  - rotary: per-head tables as for ltxattn_fwd, or cos = NULL for none.
- *  - out: the [B, H, T, D] view the attention consumes.
- *  - heads * head_dim a multiple of 512, at most 4096; in_dim a multiple of 64;
- *    head_dim 64 or 128; rows and tables 16-byte aligned. */
-typedef struct ltxattn_qk_project_args {
-  int32_t dtype; /* LTXATTN_BF16 */
-  int32_t batch, tokens, heads, head_dim, in_dim;
-  const void* x;
-  int64_t x_stride_b, x_stride_t;
-  const void* weight;
-  int64_t weight_stride;
-  const void* bias;
-  const void* norm_weight;
-  float eps;
-  ltxattn_rotary rotary;
-  ltxattn_tensor out;
-} ltxattn_qk_project_args;
-
-/* Replaces the query / key path of `DiTAttention.callAsFunction` from the
- * projection to the attention's input (`DiTAttention.swift:341-342,358-367`):
- * `linear` (`:178-188`), `rmsNorm` over the whole inner dim (`:190-204`), the
- * head split (`:346-348`) and `applySplitRoPE` (`:206-234`), as one tcgen05
- * GEMM whose epilogue does everything after the matmul. */
-LTXATTN_API int ltxattn_qk_project(const ltxattn_qk_project_args* args, void* stream);
-
-/* q and k projections (same heads * head_dim) in one launch. */
-LTXATTN_API int ltxattn_qk_project_pair(const ltxattn_qk_project_args* q, const ltxattn_qk_project_args* k,
-                                        void* stream);
 
 /* Arguments of ltxattn_head_gate: out = T(T(x) * g) per head, g = 2 * T(sigmoid(logit)).
  *  - x, out: [B, H, T, D] views (out may view the merged [B, T, H * D] buffer).

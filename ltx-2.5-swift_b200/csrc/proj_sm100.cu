@@ -1,37 +1,23 @@
 // proj_sm100.cu -- the DiT attention module's projections on tcgen05 (sm_100a).
 //
-// Two kernels share one main loop, y = x W^T accumulated in TMEM:
+// linear_kernel<BN, kF32Out>: DiTAttention.linear (DiTAttention.swift:178-188)
+// without the LoRA overlay: out = T(T(x W^T) + b), the matmul's result in the
+// activation dtype T and then the bias added in T -- the reference's two
+// roundings (MLX's bf16 matmul accumulates in fp32 and rounds once).  Serves
+// to_q, to_k, to_v, to_out.0 and to_gate_logits.  The kF32Out instance stores
+// the fp32 accumulator itself (no bias, no rounding): the partial product of a
+// row-parallel to_out, which is reduced across ranks before bias_round_kernel
+// applies the bias and the roundings once.
 //
-//  * linear_kernel<BN>: DiTAttention.linear (DiTAttention.swift:178-188) without
-//    the LoRA overlay: out = T(T(x W^T) + b), the matmul's result in the
-//    activation dtype T and then the bias added in T -- the reference's two
-//    roundings (MLX's bf16 matmul accumulates in fp32 and rounds once).
-//    Serves to_v, to_out.0 and to_gate_logits.
-//
-//  * qk_project_kernel: to_q / to_k with everything up to the attention fused
-//    into the epilogue (DiTAttention.swift:341-342,358-367): the projection as
-//    above, rmsNorm over the WHOLE inner dim (:190-204, MLX's arithmetic
-//    y = T(w * T(x * r)), r = 1 / sqrt(mean(x^2) + eps), the mean square in
-//    fp32), the head split (:346-348) and split RoPE with per-head tables
-//    (:206-234, every product and sum rounded to bf16), stored straight into
-//    the [B, H, T, D] view the attention reads.  The norm needs every one of a
-//    row's N = heads * head_dim outputs, so a cluster of N / 512 CTAs covers a
-//    128-row block: each CTA computes 512 columns (two 256-column accumulators
-//    in TMEM), stores its rows' partial sums of squares into every CTA of the
-//    cluster through distributed shared memory and arrives on each CTA's
-//    exchange mbarrier; each CTA waits (bounded) for all arrivals and adds the
-//    partials in rank order, so all of them use the same r and the result does
-//    not depend on scheduling.
-//
-// CTA: 256 threads.  Warp 0 lane 0 is the TMA producer: 128-row x 64 slices of
-// x and BN-row x 64 slices of W into kStages shared-memory stages (128-byte
-// swizzle, K-major, the UMMA operand layout).  Warp 1 owns TMEM and its lane 0
-// issues the tcgen05.mma (M 128, N BN, K 16: four per stage), freeing a stage
-// with tcgen05.commit once its MMAs complete.  Warps 4-7 are the epilogue:
-// thread i reads TMEM lane i (row i of the tile) in 32-column chunks.  No
-// multicast load anywhere.  Every mbarrier wait is bounded; a wait that gives up
-// records its site in the device error word, and the CTA unwinds (cluster CTAs
-// still reach both cluster barriers, so no CTA is left waiting for another).
+// CTA: 256 threads, one (128-row block, BN columns) tile.  Warp 0 lane 0 is the
+// TMA producer: 128-row x 64 slices of x and BN-row x 64 slices of W into
+// kPStages shared-memory stages (128-byte swizzle, K-major, the UMMA operand
+// layout).  Warp 1 owns TMEM and its lane 0 issues the tcgen05.mma (M 128,
+// N BN, K 16: four per stage), freeing a stage with tcgen05.commit once its
+// MMAs complete.  Warps 4-7 are the epilogue: thread i reads TMEM lane i (row
+// i of the tile) in 32-column chunks.  No multicast load anywhere.  Every
+// mbarrier wait is bounded; a wait that gives up records its site in the
+// device error word and the CTA unwinds.
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -59,41 +45,30 @@ struct PSmem {
   // full[kPStages], empty[kPStages], acc_full[NT]
   static constexpr uint32_t kOffBar = kPStages * kStage;
   static constexpr uint32_t kOffCtl = kOffBar + (2 * kPStages + NT) * 8;  // tmem slot, abort flag
-  static constexpr uint32_t kOffXbar = kOffCtl + 16;   // the partial-sum exchange's mbarrier
-  static constexpr uint32_t kOffPart = kOffXbar + 16;  // float[8][128]: the cluster's partial sums by rank
-  static constexpr uint32_t kBytes = kOffPart + 8 * 128 * 4;
+  static constexpr uint32_t kBytes = kOffCtl + 16;
   static constexpr uint32_t kDynamic = kBytes + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = BN * NT < 32 ? 32 : BN * NT;
   static_assert(kA % 1024 == 0 && kB % 1024 == 0, "stages must keep 1024-byte swizzle atoms aligned");
   static_assert(BN * NT <= 512, "TMEM holds 512 fp32 columns");
 };
 
-// One projection job of a launch (the q/k kernel can run two: q and k).
+// The projection of a launch.
 struct ProjJob {
   CUtensorMap tm_x;  // [K, T, B] bf16, box {64, 128, 1}
   CUtensorMap tm_w;  // [K, N] bf16, box {64, BN}
   const __nv_bfloat16* bias;  // [N] or null
   int T, B, N, K;
   int tiles_t;     // ceil(T / 128)
-  int col_groups;  // CTAs per row block (the cluster size of the q/k kernel)
+  int col_groups;  // CTAs per row block
   int ctas;        // tiles_t * B * col_groups
   // linear: out[b][t][n] at out + b * o_sb + t * o_st + n (bf16), or out_f32 + t * o_st + n
   __nv_bfloat16* out;
   float* out_f32;
   int64_t o_sb, o_st;
-  // q/k: norm weight, rotary tables [B|1][H|1][T][D/2] (cos null: none), out [B, H, T, D]
-  const __nv_bfloat16* norm_w;
-  float eps;
-  const __nv_bfloat16* cos;
-  const __nv_bfloat16* sin;
-  int64_t r_sb, r_sh, r_st;
-  int64_t h_sb, h_sh, h_st;
-  int D;
 };
 
 struct ProjParams {
-  ProjJob job[2];
-  int n_jobs;
+  ProjJob job[1];
   int* err;
 };
 
@@ -269,168 +244,6 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
   }
 }
 
-// ---------------------------------------------------------------------------
-// q / k projection with the fused norm, head split and RoPE: a cluster of
-// col_groups CTAs per 128-row block, 512 columns per CTA (two 256-column
-// accumulators).
-
-constexpr int kQkBN = 256, kQkNT = 2;
-
-// 32 columns starting at `n` of the normalised row: T(w * T(y * r)) as bf16 pairs.
-__device__ __forceinline__ void normalise_chunk(const float (&y)[32], float r, const __nv_bfloat16* w, uint32_t (&z)[16]) {
-  const uint4* w4 = reinterpret_cast<const uint4*>(w);
-  const float2 r2 = make_float2(r, r);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 ww = w4[q];
-    const uint32_t wv[4] = {ww.x, ww.y, ww.z, ww.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c = 8 * q + 2 * e;
-      const float2 xr = mul2(make_float2(y[c], y[c + 1]), r2);
-      z[4 * q + e] = bmul2(pack_bf16x2(xr.x, xr.y), wv[e]);
-    }
-  }
-}
-
-__global__ void __launch_bounds__(kPThreads, 1) qk_project_kernel(const __grid_constant__ ProjParams p) {
-  using S = PSmem<kQkBN, kQkNT>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = align1024(smem_raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + kPStages;
-  uint64_t* acc_full = bars + 2 * kPStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
-  float* part = reinterpret_cast<float*>(sm + S::kOffPart);
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + S::kOffXbar);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // job 0 owns CTAs [0, job[0].ctas), job 1 the rest; both are whole clusters
-  const int j = (int)blockIdx.x >= p.job[0].ctas ? 1 : 0;
-  const ProjJob& J = p.job[j];
-  const int cta = (int)blockIdx.x - (j ? p.job[0].ctas : 0);
-  const int C = J.col_groups;
-  const uint32_t rank = cluster_ctarank();  // == cta % C
-  const int rb = cta / C;
-  const int b = rb / J.tiles_t, t0 = (rb % J.tiles_t) * kPBM;
-  const int n_base = (int)rank * kQkBN * kQkNT;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2 * kPStages + kQkNT; ++i) mbar_init(bars + i, 1);
-    mbar_init(xbar, 128 * C);  // every epilogue thread of every CTA of the cluster arrives once
-    *abort_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&J.tm_x);
-    tma_prefetch_desc(&J.tm_w);
-  }
-  // every CTA's barriers are initialised before any CTA arrives on another's
-  __syncwarp();
-  cluster_arrive();
-  cluster_wait();
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, S::kTmemCols);
-    tmem_relinquish();
-    tc_fence_before();
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp < 4) {
-    mainloop_role<kQkBN, kQkNT>(J, warp, lane, t0, b, n_base, sm, full, empty, acc_full, tmem, abort_flag, p.err);
-  } else {
-    const int r = threadIdx.x - 128;
-    const int t = t0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    bool have = true;
-    for (int s = 0; s < kQkNT; ++s) have = warp_wait(acc_full + s, 0, abort_flag, p.err, 44) && have;
-    tc_fence_after();
-    // phase 1: this CTA's share of the row's sum of squares of y = T(T(acc) + b)
-    float ss = 0.f;
-    if (have) {
-#pragma unroll 1
-      for (int c = 0; c < kQkBN * kQkNT / 32; ++c) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + lane_off + c * 32, acc);
-        tmem_wait_ld();
-        float y[32];
-        project_chunk(acc, J.bias != nullptr ? J.bias + n_base + c * 32 : nullptr, y);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) ss = __fmaf_rn(y[e], y[e], ss);
-      }
-    }
-    // publish this row's partial into slot [rank][r] of every CTA of the cluster,
-    // then arrive on each CTA's exchange barrier; each CTA waits (bounded) for all
-    // 128 * C arrivals on its own barrier and then reads every partial locally
-    for (int q = 0; q < C; ++q) st_cluster_f32(part + rank * 128 + r, (uint32_t)q, ss);
-    for (int q = 0; q < C; ++q) mbar_arrive_cluster(xbar, (uint32_t)q);
-    const bool have_all = mbar_wait_cluster(xbar, 0, abort_flag, p.err, 45);
-    have = __all_sync(0xffffffffu, have_all) && have;
-    float tot = 0.f;
-    for (int q = 0; q < C; ++q) tot = __fadd_rn(tot, part[q * 128 + r]);
-    const float rn = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)J.N), J.eps));
-    // phase 2: normalise, split into heads, rotate, store
-    const int D = J.D, half_chunks = D / 64;  // 32-column chunks per half head
-    if (have && t < J.T) {
-#pragma unroll 1
-      for (int c1 = 0; c1 < kQkBN * kQkNT / 32; ++c1) {
-        if ((c1 % (D / 32)) >= half_chunks) continue;  // c1 walks the lower halves; c2 is its partner
-        const int c2 = c1 + half_chunks;
-        const int n1 = n_base + c1 * 32;
-        const int head = n1 / D, d1 = n1 % D;  // d1 < D / 2
-        uint32_t a1[32], a2[32];
-        tmem_ld32(tmem + lane_off + c1 * 32, a1);
-        tmem_ld32(tmem + lane_off + c2 * 32, a2);
-        tmem_wait_ld();
-        float y1[32], y2[32];
-        project_chunk(a1, J.bias != nullptr ? J.bias + n1 : nullptr, y1);
-        project_chunk(a2, J.bias != nullptr ? J.bias + n1 + D / 2 : nullptr, y2);
-        uint32_t z1[16], z2[16];
-        normalise_chunk(y1, rn, J.norm_w + n1, z1);
-        normalise_chunk(y2, rn, J.norm_w + n1 + D / 2, z2);
-        uint32_t o1[16], o2[16];
-        if (J.cos != nullptr) {
-          const int64_t toff = (int64_t)b * J.r_sb + (int64_t)head * J.r_sh + (int64_t)t * J.r_st + d1;
-          const uint4* c4 = reinterpret_cast<const uint4*>(J.cos + toff);
-          const uint4* s4 = reinterpret_cast<const uint4*>(J.sin + toff);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 cw = c4[q], sw = s4[q];
-            const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w}, sv[4] = {sw.x, sw.y, sw.z, sw.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 4 * q + e;
-              o1[i] = bsub2(bmul2(z1[i], cv[e]), bmul2(z2[i], sv[e]));
-              o2[i] = badd2(bmul2(z2[i], cv[e]), bmul2(z1[i], sv[e]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            o1[i] = z1[i];
-            o2[i] = z2[i];
-          }
-        }
-        __nv_bfloat16* orow = J.out + (int64_t)b * J.h_sb + (int64_t)head * J.h_sh + (int64_t)t * J.h_st;
-        uint4* dst1 = reinterpret_cast<uint4*>(orow + d1);
-        uint4* dst2 = reinterpret_cast<uint4*>(orow + d1 + D / 2);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          dst1[q] = make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]);
-          dst2[q] = make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]);
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, S::kTmemCols);
-  }
-}
-
 // out[t][n] = T(T(sum[t][n]) + b[n]): the roundings of DiTAttention.linear applied
 // once the row-parallel partial sums have been reduced.  One thread per 8 columns.
 __global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64_t s_st, const __nv_bfloat16* bias,
@@ -574,88 +387,6 @@ int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t s
   return LTXATTN_OK;
 }
 
-// Fills job j of a q/k projection from the C arguments.
-int qk_job(const ltxattn_qk_project_args* a, ProjJob* J) {
-  if (a == nullptr) return fail_msg(LTXATTN_ERR_ARG, "args is NULL");
-  if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_qk_project: bf16 only");
-  if (a->batch < 1 || a->tokens < 1 || a->heads < 1 || a->in_dim < 1)
-    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: batch, tokens, heads and in_dim must be >= 1");
-  if (a->head_dim != 64 && a->head_dim != 128)
-    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_qk_project: head_dim %d (64 and 128 are supported)", a->head_dim);
-  const int N = a->heads * a->head_dim;
-  if (N % 512 != 0 || N / 512 > 8)
-    return fail_msg(LTXATTN_ERR_UNSUPPORTED,
-                    "ltxattn_qk_project: heads * head_dim = %d must be a multiple of 512 and at most 4096", N);
-  if (a->in_dim % 64 != 0)
-    return fail_msg(LTXATTN_ERR_UNSUPPORTED, "ltxattn_qk_project: in_dim %d must be a multiple of 64", a->in_dim);
-  if (!a->x || !a->weight || !a->norm_weight || !a->out.data)
-    return fail_msg(LTXATTN_ERR_ARG, "ltxattn_qk_project: x, weight, norm_weight and out are required");
-  if (a->x_stride_t < a->in_dim || a->x_stride_b < 0 || a->weight_stride < a->in_dim)
-    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: x / weight strides are shorter than in_dim");
-  if (!al16(a->x) || !al16(a->weight) || (a->x_stride_t % 8) || (a->batch > 1 && a->x_stride_b % 8) ||
-      (a->weight_stride % 8))
-    return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_qk_project: x and weight need 16-byte aligned rows");
-  if ((a->bias && !al16(a->bias)) || !al16(a->norm_weight) || !al16(a->out.data) || (a->out.stride_t % 8) ||
-      (a->out.stride_h % 8) || (a->out.stride_b % 8) || a->out.stride_t < 0 || a->out.stride_h < 0 ||
-      a->out.stride_b < 0)
-    return fail_msg(LTXATTN_ERR_ALIGN,
-                    "ltxattn_qk_project: bias, norm_weight and out rows must be 16-byte aligned (strides multiples of 8)");
-  if (a->rotary.cos != nullptr) {
-    if (!a->rotary.sin) return fail_msg(LTXATTN_ERR_ARG, "ltxattn_qk_project: rotary has cos but no sin");
-    if (a->rotary.tokens < a->tokens)
-      return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project: rotary covers %d tokens, expected at least %d",
-                      a->rotary.tokens, a->tokens);
-    if (!al16(a->rotary.cos) || !al16(a->rotary.sin) || (a->rotary.stride_t % 8) || (a->rotary.stride_h % 8) ||
-        (a->rotary.stride_b % 8) || a->rotary.stride_t < 0 || a->rotary.stride_h < 0 || a->rotary.stride_b < 0)
-      return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_qk_project: rotary tables need 16-byte aligned rows");
-  }
-  *J = ProjJob{};
-  if (int rc = map_rows(&J->tm_x, a->x, a->in_dim, a->tokens, a->batch, a->x_stride_t, a->x_stride_b, "x")) return rc;
-  if (int rc = map_weight(&J->tm_w, a->weight, a->in_dim, N, a->weight_stride, kQkBN, "weight")) return rc;
-  J->bias = static_cast<const __nv_bfloat16*>(a->bias);
-  J->T = a->tokens;
-  J->B = a->batch;
-  J->N = N;
-  J->K = a->in_dim;
-  J->tiles_t = (a->tokens + kPBM - 1) / kPBM;
-  J->col_groups = N / (kQkBN * kQkNT);
-  J->ctas = J->tiles_t * J->B * J->col_groups;
-  J->norm_w = static_cast<const __nv_bfloat16*>(a->norm_weight);
-  J->eps = a->eps;
-  J->cos = static_cast<const __nv_bfloat16*>(a->rotary.cos);
-  J->sin = static_cast<const __nv_bfloat16*>(a->rotary.sin);
-  J->r_sb = a->rotary.stride_b;
-  J->r_sh = a->rotary.stride_h;
-  J->r_st = a->rotary.stride_t;
-  J->out = static_cast<__nv_bfloat16*>(a->out.data);
-  J->h_sb = a->out.stride_b;
-  J->h_sh = a->out.stride_h;
-  J->h_st = a->out.stride_t;
-  J->D = a->head_dim;
-  return LTXATTN_OK;
-}
-
-int launch_qk(ProjParams& P, cudaStream_t st) {
-  using S = PSmem<kQkBN, kQkNT>;
-  cudaError_t e = prepare_kernel(qk_project_kernel, 4, S::kDynamic);
-  if (e != cudaSuccess) return launch_fail(e, "q/k projection kernel attributes");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(P.job[0].ctas + (P.n_jobs > 1 ? P.job[1].ctas : 0));
-  cfg.blockDim = dim3(kPThreads);
-  cfg.dynamicSmemBytes = S::kDynamic;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = P.job[0].col_groups;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, qk_project_kernel, P);
-  if (e != cudaSuccess) return launch_fail(e, "q/k projection launch");
-  return LTXATTN_OK;
-}
-
 // ltxattn_linear, or (f32_out != null) the same GEMM storing its fp32
 // accumulator, without bias or roundings, into f32_out [m, n] (row stride n).
 int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
@@ -673,7 +404,6 @@ int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
       (a->weight_stride % 8) || (a->out_stride % 8))
     return fail_msg(LTXATTN_ERR_ALIGN, "ltxattn_linear: x, weight, bias and out need 16-byte aligned rows");
   ProjParams P{};
-  P.n_jobs = 1;
   P.err = device_error_word();
   if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
   ProjJob& J = P.job[0];
@@ -732,27 +462,6 @@ extern "C" {
 
 int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
   return run_linear(a, nullptr, static_cast<cudaStream_t>(stream));
-}
-
-int ltxattn_qk_project(const ltxattn_qk_project_args* a, void* stream) {
-  ProjParams P{};
-  P.n_jobs = 1;
-  P.err = device_error_word();
-  if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
-  if (int rc = qk_job(a, &P.job[0])) return rc;
-  return launch_qk(P, static_cast<cudaStream_t>(stream));
-}
-
-int ltxattn_qk_project_pair(const ltxattn_qk_project_args* q, const ltxattn_qk_project_args* k, void* stream) {
-  ProjParams P{};
-  P.n_jobs = 2;
-  P.err = device_error_word();
-  if (!P.err) return fail_msg(LTXATTN_ERR_CUDA, "no device error word");
-  if (int rc = qk_job(q, &P.job[0])) return rc;
-  if (int rc = qk_job(k, &P.job[1])) return rc;
-  if (P.job[0].N != P.job[1].N)
-    return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_qk_project_pair: q and k must have the same heads * head_dim");
-  return launch_qk(P, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -141,75 +141,6 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
-// ---------------------------------------------------------------------------
-// thread-block clusters: the cluster-wide barrier (every thread of every CTA
-// of the cluster executes both halves) and a 32-bit load from the shared
-// memory of another CTA of the cluster (distributed shared memory).
-
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// `local` is this CTA's address of a shared variable; returns that variable's
-// value in CTA `rank` of the cluster.
-__device__ __forceinline__ float ld_cluster_f32(const void* local, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-
-// A 32-bit store into CTA `rank`'s copy of a shared variable, and an arrival on
-// CTA `rank`'s copy of an mbarrier, released at cluster scope so that the stores
-// before it are visible to a cluster-scope acquire of that barrier's phase.
-__device__ __forceinline__ void st_cluster_f32(void* local, uint32_t rank, float v) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* local_bar, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_bar)), "r"(rank));
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
-}
-// Bounded wait on this CTA's barrier phase with cluster-scope acquire (arrivals
-// came from other CTAs); same give-up rule as mbar_wait.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* err_word, int site) {
-  auto try_once = [&]() {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-  };
-  if (try_once()) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (try_once()) return true;
-    if ((it & 63u) == 0u) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        if (err_word) atomicCAS(err_word, 0, (site << 8) | kErrTimeout);
-        return false;
-      }
-    }
-  }
-}
-
 // Tiled bulk store shared -> global (same box and swizzle as the map's
 // loads).  Rows past the tensor's extent are not written.  The source may be
 // reused once bulk_wait_read() returns.

@@ -7,7 +7,7 @@ from . import _lib
 from .backend import (AttentionBackend, Failure, Rotary, Variant, apply_split_rope, device_info,
                       device_status, qk_prep, qk_prep_pair, rotary_tables, scaled_dot_product_attention)
 from .module import DiTAttentionModule
-from .proj import linear, qk_project, qk_project_pair
+from .proj import head_gate, linear
 
 __all__ = ["AttentionBackend", "Failure", "Rotary", "Variant", "scaled_dot_product_attention", "apply_split_rope", "rotary_tables", "qk_prep", "qk_prep_pair",
-           "device_info", "device_status", "DiTAttentionModule", "linear", "qk_project", "qk_project_pair", "_lib"]
+           "device_info", "device_status", "DiTAttentionModule", "linear", "head_gate", "_lib"]

@@ -28,7 +28,7 @@ EXPORTED = (
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
-    "ltxattn_linear", "ltxattn_qk_project", "ltxattn_qk_project_pair", "ltxattn_head_gate",
+    "ltxattn_linear", "ltxattn_head_gate",
     "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce",
 )
 
@@ -123,14 +123,6 @@ class LinearArgs(ctypes.Structure):
                 ("out_stride", ctypes.c_int64)]
 
 
-class QkProjectArgs(ctypes.Structure):
-    _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("tokens", ctypes.c_int32),
-                ("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("in_dim", ctypes.c_int32),
-                ("x", ctypes.c_void_p), ("x_stride_b", ctypes.c_int64), ("x_stride_t", ctypes.c_int64),
-                ("weight", ctypes.c_void_p), ("weight_stride", ctypes.c_int64), ("bias", ctypes.c_void_p),
-                ("norm_weight", ctypes.c_void_p), ("eps", ctypes.c_float), ("rotary", Rotary), ("out", Tensor)]
-
-
 class HeadGateArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("x", Tensor), ("out", Tensor),
@@ -215,10 +207,6 @@ def load(path: str = LIB_PATH):
     L.ltxattn_memory_plan.restype = ctypes.c_int
     L.ltxattn_linear.argtypes = [ctypes.POINTER(LinearArgs), vp]
     L.ltxattn_linear.restype = ctypes.c_int
-    L.ltxattn_qk_project.argtypes = [ctypes.POINTER(QkProjectArgs), vp]
-    L.ltxattn_qk_project.restype = ctypes.c_int
-    L.ltxattn_qk_project_pair.argtypes = [ctypes.POINTER(QkProjectArgs), ctypes.POINTER(QkProjectArgs), vp]
-    L.ltxattn_qk_project_pair.restype = ctypes.c_int
     L.ltxattn_head_gate.argtypes = [ctypes.POINTER(HeadGateArgs), vp]
     L.ltxattn_head_gate.restype = ctypes.c_int
     L.ltxattn_out_project_workspace.argtypes = [ctypes.POINTER(OutProjectArgs)]

@@ -2,15 +2,16 @@
 (DiTAttention.swift:315-404), every step in libltxattn_cuda.
 
     v = linear(kv, to_v)                                   # ltxattn_linear, :341
-    qh = split-RoPE(split(rmsNorm(linear(x, to_q))))       # ltxattn_qk_project_pair: q and k
-    kh = split-RoPE(split(rmsNorm(linear(kv, to_k))))      #   in one launch, :342,358-367
+    q, k = linear(x, to_q), linear(kv, to_k)               # ltxattn_linear, :342
+    qh, kh = split-RoPE(split(rmsNorm(q, k)))              # ltxattn_qk_prep_pair, :358-367
     out = SDPA(qh, kh, split(v), 1/sqrt(D))                # ltxattn_fwd, :369-382
     out = out * 2 sigmoid(linear(x, to_gate_logits))       # fused into ltxattn_fwd's store, :395-399
     return linear(merge(out), to_out.0)                    # merge by view, :401-403
 
 The projections run on the library's tcgen05 GEMMs (``gemm="ltxattn"``, the
 default) or, for comparison, on the library GEMM of torch (``gemm="torch"``:
-cuBLAS, then ltxattn_qk_prep_pair for the norms and RoPE).  `linear` keeps the
+cuBLAS).  Either way ltxattn_qk_prep_pair applies the norms, the head split
+and RoPE to q and k in one launch.  `linear` keeps the
 reference's two roundings either way: the matmul's output in the activation
 dtype, then the bias added in that dtype (DiTAttention.swift:178-189).  The STG
 passthrough (all_perturbed, :349-356) gates and merges the value stream with
@@ -86,17 +87,9 @@ class DiTAttentionModule:
             proj.head_gate(vh, logits, out=out_view)
         else:
             k_rot = key_rotary if key_rotary is not None else rotary
-            if g == "ltxattn":
-                dt = w["to_q.weight"].dtype
-                bias = lambda name: w[name].to(dt) if name in w else None
-                qh, kh = proj.qk_project_pair(x.to(dt), w["to_q.weight"], bias("to_q.bias"),
-                                              w["q_norm.weight"].to(dt), kv.to(dt), w["to_k.weight"],
-                                              bias("to_k.bias"), w["k_norm.weight"].to(dt), H, rotary, k_rot,
-                                              eps=NORM_EPS)
-            else:
-                q = linear(x, w, "to_q", g)
-                k = linear(kv, w, "to_k", g)
-                qh, kh = qk_prep_pair(q, w["q_norm.weight"].to(q.dtype), k, w["k_norm.weight"].to(k.dtype), H,
-                                      rotary, k_rot, eps=NORM_EPS)
+            q = linear(x, w, "to_q", g)
+            k = linear(kv, w, "to_k", g)
+            qh, kh = qk_prep_pair(q, w["q_norm.weight"].to(q.dtype), k, w["k_norm.weight"].to(k.dtype), H,
+                                  rotary, k_rot, eps=NORM_EPS)
             AttentionBackend.attention(qh, kh, vh, scale=1.0 / math.sqrt(D), out=out_view, gate=logits)
         return linear(merged, w, "to_out.0", g)

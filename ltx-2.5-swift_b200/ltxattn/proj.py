@@ -2,21 +2,18 @@
 
 * ``linear(x, weight, bias)`` is ``DiTAttention.linear`` (DiTAttention.swift:178-188,
   without the LoRA overlay): ``T(T(x W^T) + b)`` through ``ltxattn_linear``.
-* ``qk_project(x, weight, bias, norm_weight, heads, rotary)`` is the q (or k)
-  path from the projection to the attention's input (:341-342, 358-367) as one
-  kernel (``ltxattn_qk_project``): projection, rmsNorm over the whole inner dim,
-  head split and split RoPE, written as the ``[B, heads, T, D]`` view.
-* ``qk_project_pair`` runs the q and k projections in one launch.
+* ``head_gate(x, logits, out)`` is the per-head gate and merge of the STG
+  passthrough (:349-356, 395-403) through ``ltxattn_head_gate``.
 """
 from __future__ import annotations
 
 import ctypes
-from typing import Optional, Tuple
+from typing import Optional
 
 import torch
 
 from . import _lib
-from .backend import Failure, Rotary, _rotary, _stream_ptr, _view
+from .backend import Failure, _stream_ptr, _view
 
 
 def _need_bf16(name: str, t: torch.Tensor):
@@ -56,58 +53,6 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     if rc != _lib.OK:
         raise Failure.from_status(rc)
     return out
-
-
-def _qk_args(x, weight, bias, norm_weight, heads, rotary, eps, out):
-    _need_bf16("x", x)
-    _need_bf16("weight", weight)
-    _need_bf16("norm_weight", norm_weight)
-    if x.dim() != 3 or x.stride(2) != 1:
-        raise Failure.shape("x", x.shape, "[B, tokens, in_dim] with unit stride along in_dim")
-    B, T, k = x.shape
-    n = weight.shape[0]
-    if weight.dim() != 2 or weight.shape[1] != k or n % heads or weight.stride(1) != 1:
-        raise Failure.shape("weight", weight.shape, f"[{heads} * head_dim, {k}]")
-    D = n // heads
-    if out is None:
-        out = torch.empty((B, heads, T, D), dtype=x.dtype, device=x.device)
-    a = _lib.QkProjectArgs()
-    a.dtype, a.batch, a.tokens, a.heads, a.head_dim, a.in_dim = _lib.BF16, B, T, heads, D, k
-    a.x, a.x_stride_b, a.x_stride_t = x.data_ptr(), x.stride(0), x.stride(1)
-    a.weight, a.weight_stride = weight.data_ptr(), weight.stride(0)
-    if bias is not None:
-        _need_bf16("bias", bias)
-        a.bias = bias.data_ptr()
-    if norm_weight.numel() != n or not norm_weight.is_contiguous():
-        raise Failure.shape("norm_weight", norm_weight.shape, f"[{n}] contiguous")
-    a.norm_weight = norm_weight.data_ptr()
-    a.eps = float(eps)
-    a.rotary = _rotary("rotary", rotary, B, heads, T, D, x.dtype)
-    a.out = _view("out", out, (B, heads, T, D))
-    return a, out, (x, weight, bias, norm_weight, rotary)
-
-
-def qk_project(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], norm_weight: torch.Tensor,
-               heads: int, rotary: Optional[Rotary] = None, eps: float = 1e-6,
-               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """split-RoPE(split(rmsNorm(linear(x)))) -> [B, heads, T, D] (or into ``out``)."""
-    a, out, _keep = _qk_args(x, weight, bias, norm_weight, heads, rotary, eps, out)
-    rc = _lib.load().ltxattn_qk_project(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
-    if rc != _lib.OK:
-        raise Failure.from_status(rc)
-    return out
-
-
-def qk_project_pair(xq, wq, bq, nq, xk, wk, bk, nk, heads: int, q_rotary: Optional[Rotary] = None,
-                    k_rotary: Optional[Rotary] = None, eps: float = 1e-6, out_q=None, out_k=None,
-                    stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """q and k projections in one launch; each result is what ``qk_project`` gives."""
-    aq, out_q, _kq = _qk_args(xq, wq, bq, nq, heads, q_rotary, eps, out_q)
-    ak, out_k, _kk = _qk_args(xk, wk, bk, nk, heads, k_rotary, eps, out_k)
-    rc = _lib.load().ltxattn_qk_project_pair(ctypes.byref(aq), ctypes.byref(ak), ctypes.c_void_p(_stream_ptr(stream)))
-    if rc != _lib.OK:
-        raise Failure.from_status(rc)
-    return out_q, out_k
 
 
 def head_gate(x: torch.Tensor, logits: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,

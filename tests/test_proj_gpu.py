@@ -4,21 +4,18 @@ CPU oracle.
 * ltxattn_linear (DiTAttention.linear, DiTAttention.swift:178-188): the fp64
   matmul rounded to bf16, plus the bias rounded again (oracle.linear); also
   against the library GEMM (cuBLAS through torch) with the same two roundings.
-* ltxattn_qk_project / _pair (the q / k path :341-342,358-367 in one kernel):
-  against oracle.qk_prep(oracle.linear(x)) and against the unfused composition
-  (library GEMM + ltxattn_qk_prep).
 
 Tolerances (bf16): max abs <= 2e-2 and rel-L2 <= 1e-2
-against the oracle.  The fused and unfused paths may differ in the last bit of
-the matmul (fp32 accumulation order), so they are compared in the same terms.
+against the oracle; the fp32-accumulated GEMM and the oracle's fp64 sum round
+to the same bf16 in almost every entry (asserted).
 """
 import numpy as np
 import pytest
 import torch
 
 import oracle
-from ltxattn import Rotary, device_status, inputs, qk_prep
-from ltxattn.proj import linear, qk_project, qk_project_pair
+from ltxattn import device_status, inputs
+from ltxattn.proj import linear
 
 pytestmark = pytest.mark.gpu
 
@@ -107,71 +104,3 @@ def test_linear_views_and_batches():
         ref = oracle.linear(host(x[bi]), host(w))
         check(o, ref, f"strided batch {bi}")
     assert torch.all(wide[:, n:] == 0)  # nothing written past the view
-
-
-def _tables(T, D, H, per_head, seed):
-    ang = np.arange(T, dtype=np.float64)[:, None] * (10000.0 ** (-np.arange(D // 2) / (D // 2)))[None, :]
-    if per_head:
-        ang = ang[None] * (1.0 + 0.01 * np.arange(H))[:, None, None]
-        ang = ang[None]
-    else:
-        ang = ang[None, None]
-    c = inputs.round_bf16(np.cos(ang).astype(np.float32))
-    s = inputs.round_bf16(np.sin(ang).astype(np.float32))
-    return c, s
-
-
-@pytest.mark.parametrize("B,T,heads,D,k,rope,per_head,with_bias", [
-    (1, 300, 32, 128, 4096, True, False, True),   # video: cluster of 8
-    (1, 3120, 32, 128, 4096, True, False, True),  # config 2's q at full size
-    (2, 200, 32, 64, 2048, True, True, True),     # audio: cluster of 4, per-head tables, batch 2
-    (1, 129, 8, 64, 512, False, False, False),    # cluster of 1, no rotary, no bias
-    (1, 64, 16, 128, 1024, True, True, False),
-])
-def test_qk_project_matches_the_oracle(B, T, heads, D, k, rope, per_head, with_bias):
-    n = heads * D
-    x = inputs.seeded_tensor(40 + T, (B, T, k))
-    w = weights(41, n, k)
-    b = bias(42, n) if with_bias else None
-    nw = inputs.round_bf16(0.5 + inputs.seeded_tensor(43, (n,)) ** 2 * np.float32(0.25))
-    c = s = None
-    rot = None
-    if rope:
-        c, s = _tables(T, D, heads, per_head, 44)
-        rot = Rotary(dev(c), dev(s))
-    got = qk_project(dev(x), dev(w), dev(b) if b is not None else None, dev(nw), heads, rot)
-    torch.cuda.synchronize()
-    y = oracle.linear(x.reshape(B * T, k), w, b).reshape(B, T, n)
-    ref = oracle.qk_prep(y, nw, heads, 1e-6, c, s, bf16=True)
-    err = check(got, ref, f"qk_project B{B} T{T} {heads}x{D}")
-    assert np.mean(err == 0) > 0.95
-    # the unfused composition on the device: library GEMM, then ltxattn_qk_prep
-    yd = (dev(x) @ dev(w).t())
-    if b is not None:
-        yd = yd + dev(b)
-    unfused = qk_prep(yd, dev(nw), heads, rot)
-    diff = (got.float() - unfused.float()).abs()
-    assert diff.max().item() <= 2e-2 and (diff == 0).float().mean().item() > 0.95
-
-
-def test_qk_project_pair_is_two_single_calls():
-    # a cross-attention's q (300 query tokens) and k (1024 context tokens) in one launch
-    heads, D, k = 32, 128, 4096
-    n = heads * D
-    xq = dev(inputs.seeded_tensor(50, (1, 300, k)))
-    xk = dev(inputs.seeded_tensor(51, (1, 1024, k)))
-    wq, wk = dev(weights(52, n, k)), dev(weights(53, n, k))
-    bq, bk = dev(bias(54, n)), dev(bias(55, n))
-    nq = dev(inputs.round_bf16(0.5 + inputs.seeded_tensor(56, (n,)) ** 2 * np.float32(0.25)))
-    nk = dev(inputs.round_bf16(0.5 + inputs.seeded_tensor(57, (n,)) ** 2 * np.float32(0.25)))
-    cq, sq = _tables(300, D, heads, False, 0)
-    ck, sk = _tables(1024, D, heads, False, 0)
-    rq, rk = Rotary(dev(cq), dev(sq)), Rotary(dev(ck), dev(sk))
-    pq, pk = qk_project_pair(xq, wq, bq, nq, xk, wk, bk, nk, heads, rq, rk)
-    oq = qk_project(xq, wq, bq, nq, heads, rq)
-    ok = qk_project(xk, wk, bk, nk, heads, rk)
-    torch.cuda.synchronize()
-    assert torch.equal(pq, oq) and torch.equal(pk, ok)
-    # deterministic: a second pair call gives the same bits
-    pq2, pk2 = qk_project_pair(xq, wq, bq, nq, xk, wk, bk, nk, heads, rq, rk)
-    assert torch.equal(pq, pq2) and torch.equal(pk, pk2)
