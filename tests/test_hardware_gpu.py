@@ -34,9 +34,9 @@ def test_device_query_describes_the_b200():
     info = _lib.DeviceInfo()
     assert _lib.load().ltxattn_device_query(n.value, ctypes.byref(info)) != _lib.OK
     q = torch.randn((1, 2, 64, 64), device="cuda").to(torch.bfloat16)
-    x = torch.randn((1, 64, 128), device="cuda").to(torch.bfloat16)
+    x = torch.randn((1, 64, 512), device="cuda").to(torch.bfloat16)
     out, _ = AttentionBackend.attention(q, q, q)
-    qk_prep(x, torch.ones(128, device="cuda", dtype=torch.bfloat16), 2)
+    qk_prep(x, torch.ones(512, device="cuda", dtype=torch.bfloat16), 4)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
 
