@@ -209,7 +209,13 @@ LTXATTN_API size_t ltxattn_bwd_workspace(const ltxattn_bwd_args* args);
  *  - x [m, k] rows of x_stride elements; weight [n, k] (the checkpoint's
  *    [out, in] layout) rows of weight_stride; out [m, n] rows of out_stride.
  *  - bias [n] or NULL.
- *  - n a multiple of 8, k of 64; rows 16-byte aligned. */
+ *  - n a multiple of 8, k of 64; rows 16-byte aligned.
+ *  - workspace: NULL, or device scratch of ltxattn_linear_workspace() bytes
+ *    (256-byte aligned).  That size is non-zero for a narrow output whose
+ *    column tiles would leave most SMs idle (the gate logits: 32 columns);
+ *    with the workspace such a call splits K across CTAs into fp32 partials
+ *    and adds them in a fixed order before the bias and the roundings (the
+ *    same function; only the fp32 summation order differs). */
 typedef struct ltxattn_linear_args {
   int32_t dtype; /* LTXATTN_BF16 */
   int32_t m, n, k;
@@ -220,12 +226,17 @@ typedef struct ltxattn_linear_args {
   const void* bias;
   void* out;
   int64_t out_stride;
+  void* workspace;
+  size_t workspace_bytes;
 } ltxattn_linear_args;
 
 /* Replaces `DiTAttention.linear` (`DiTAttention.swift:178-188`) without the LoRA
  * overlay: to_q, to_k, to_v, to_out.0 and to_gate_logits of the attention module
  * (q and k then take ltxattn_qk_prep for the norm, the head split and RoPE). */
 LTXATTN_API int ltxattn_linear(const ltxattn_linear_args* args, void* stream);
+
+/* Device scratch bytes ltxattn_linear can use for these arguments (0: none). */
+LTXATTN_API size_t ltxattn_linear_workspace(const ltxattn_linear_args* args);
 
 /* Arguments of ltxattn_head_gate: out = T(T(x) * g) per head, g = 2 * T(sigmoid(logit)).
  *  - x, out: [B, H, T, D] views (out may view the merged [B, T, H * D] buffer).

@@ -212,7 +212,7 @@ int ltxattn_out_project_allreduce(const ltxattn_out_project_args* a, ltxattn_com
   const ncclResult_t r =
       nccl().AllReduce(partial, partial, (size_t)a->m * a->n, ncclFloat32, ncclSum, comm->nccl, st);
   if (r != ncclSuccess) return nccl_fail("ncclAllReduce", r);
-  return ltx::bias_round(partial, a->bias, a->out, a->out_stride, a->m, a->n, st);
+  return ltx::bias_round(partial, 1, 0, a->bias, a->out, a->out_stride, a->m, a->n, st);
 }
 
 }  // extern "C"

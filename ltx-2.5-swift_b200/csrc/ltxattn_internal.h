@@ -233,8 +233,10 @@ namespace ltx {
 
 // The row-parallel to_out's local steps (proj_sm100.cu): the GEMM's fp32
 // accumulator into `partial` [m, n] (no bias, no rounding), and, after the
-// reduction across ranks, out = T(T(sum) + bias).
+// reduction across ranks, out = T(T(sum) + bias) (sum: `splits` partial planes
+// split_stride floats apart, added in order).
 int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_t st);
-int bias_round(const float* sum, const void* bias, void* out, int64_t out_stride, int m, int n, cudaStream_t st);
+int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
+               int m, int n, cudaStream_t st);
 
 }  // namespace ltx

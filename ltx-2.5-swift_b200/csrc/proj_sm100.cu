@@ -18,6 +18,7 @@
 // i of the tile) in 32-column chunks.  No multicast load anywhere.  Every
 // mbarrier wait is bounded; a wait that gives up records its site in the
 // device error word and the CTA unwinds.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -60,11 +61,14 @@ struct ProjJob {
   int T, B, N, K;
   int tiles_t;     // ceil(T / 128)
   int col_groups;  // CTAs per row block
-  int ctas;        // tiles_t * B * col_groups
-  // linear: out[b][t][n] at out + b * o_sb + t * o_st + n (bf16), or out_f32 + t * o_st + n
+  int ctas;        // tiles_t * B * col_groups * splits
+  int splits;      // K split into `splits` ranges of kb_per 64-wide blocks (fp32 partials)
+  int kb_per;
+  // linear: out[b][t][n] at out + b * o_sb + t * o_st + n (bf16), or split s's fp32 partial at
+  // out_f32 + s * split_stride + t * o_st + n
   __nv_bfloat16* out;
   float* out_f32;
-  int64_t o_sb, o_st;
+  int64_t o_sb, o_st, split_stride;
 };
 
 struct ProjParams {
@@ -110,10 +114,9 @@ __device__ __forceinline__ void project_chunk(const uint32_t (&acc)[32], const _
 // row block; accumulator s starts at TMEM column s * BN.
 template <int BN, int NT>
 __device__ __forceinline__ void mainloop_role(const ProjJob& J, int warp, int lane, int t0, int b, int n_base,
-                                              uint8_t* sm, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
-                                              uint32_t tmem, volatile int* abort_flag, int* err) {
+                                              int kb0, int kb_n, uint8_t* sm, uint64_t* full, uint64_t* empty,
+                                              uint64_t* acc_full, uint32_t tmem, volatile int* abort_flag, int* err) {
   using S = PSmem<BN, NT>;
-  const int kb_n = J.K / kPBK;
   if (warp == 0 && lane == 0) {
     int it = 0;
     bool ok = true;
@@ -127,8 +130,8 @@ __device__ __forceinline__ void mainloop_role(const ProjJob& J, int warp, int la
         }
         uint8_t* sa = sm + st * S::kStage;
         mbar_arrive_expect_tx(full + st, S::kStage);
-        tma_load_3d(&J.tm_x, full + st, sa, kb * kPBK, t0, b);
-        tma_load_2d(&J.tm_w, full + st, sa + S::kA, kb * kPBK, n0);
+        tma_load_3d(&J.tm_x, full + st, sa, (kb0 + kb) * kPBK, t0, b);
+        tma_load_2d(&J.tm_w, full + st, sa + S::kA, (kb0 + kb) * kPBK, n0);
       }
     }
     // never leave the CTA with a bulk copy still writing its shared memory
@@ -177,11 +180,16 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   const ProjJob& J = p.job[0];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cta = blockIdx.x;
-  const int cg = cta % J.col_groups;
-  const int rb = cta / J.col_groups;
+  // CTA -> (K split, row block, column tile), column tile fastest
+  const int tiles = J.tiles_t * J.B * J.col_groups;
+  const int split = (int)blockIdx.x / tiles;
+  const int tile = (int)blockIdx.x - split * tiles;
+  const int cg = tile % J.col_groups;
+  const int rb = tile / J.col_groups;
   const int b = rb / J.tiles_t, t0 = (rb % J.tiles_t) * kPBM;
   const int n_base = cg * BN;
+  const int kb0 = split * J.kb_per;
+  const int kb_n = min(J.kb_per, J.K / kPBK - kb0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2 * kPStages + 1; ++i) mbar_init(bars + i, 1);
@@ -200,7 +208,8 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
-    mainloop_role<BN, 1>(J, warp, lane, t0, b, n_base, sm, full, empty, acc_full, tmem, abort_flag, p.err);
+    mainloop_role<BN, 1>(J, warp, lane, t0, b, n_base, kb0, kb_n, sm, full, empty, acc_full, tmem, abort_flag,
+                         p.err);
   } else {
     const int r = threadIdx.x - 128;  // TMEM lane = tile row
     const int t = t0 + r;
@@ -219,7 +228,7 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
         if (t < J.T && kF32Out) {
           // the fp32 accumulator itself (a partial sum that is reduced across ranks before
           // the bias and the roundings)
-          uint4* dst = reinterpret_cast<uint4*>(J.out_f32 + (int64_t)t * J.o_st + n);
+          uint4* dst = reinterpret_cast<uint4*>(J.out_f32 + split * J.split_stride + (int64_t)t * J.o_st + n);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             if (4 * q < valid) dst[q] = make_uint4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
@@ -244,17 +253,25 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
   }
 }
 
-// out[t][n] = T(T(sum[t][n]) + b[n]): the roundings of DiTAttention.linear applied
-// once the row-parallel partial sums have been reduced.  One thread per 8 columns.
-__global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64_t s_st, const __nv_bfloat16* bias,
+// out[t][n] = T(T(sum[t][n]) + b[n]) with sum the `splits` fp32 partial planes
+// added in split order: the roundings of DiTAttention.linear applied once the
+// partial sums (K splits of one GPU, or the row-parallel ranks after their
+// all-reduce) are complete.  One thread per 8 columns.
+__global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64_t s_st, int splits,
+                                                         int64_t split_stride, const __nv_bfloat16* bias,
                                                          __nv_bfloat16* out, int64_t o_st, int M, int N) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int n8 = N / 8;
   if (i >= (int64_t)M * n8) return;
   const int t = (int)(i / n8), n = (int)(i % n8) * 8;
-  const float4* src = reinterpret_cast<const float4*>(sum + (int64_t)t * s_st + n);
-  const float4 a = src[0], c = src[1];
-  float y[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  float y[8];
+  for (int s = 0; s < splits; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(sum + s * split_stride + (int64_t)t * s_st + n);
+    const float4 a = src[0], c = src[1];
+    const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = s == 0 ? v[e] : __fadd_rn(y[e], v[e]);
+  }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     y[e] = bf16_round(y[e]);
@@ -377,7 +394,7 @@ int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t s
   ProjJob& J = P.job[0];
   if (int rc = map_weight(&J.tm_w, a->weight, a->k, a->n, a->weight_stride, BN, "weight")) return rc;
   J.col_groups = (a->n + BN - 1) / BN;
-  J.ctas = J.tiles_t * J.col_groups;
+  J.ctas = J.tiles_t * J.col_groups * J.splits;
   const int slot = (BN == 256 ? 0 : BN == 128 ? 1 : BN == 64 ? 2 : 3) + (kF32Out ? 5 : 0);
   cudaError_t e = prepare_kernel(linear_kernel<BN, kF32Out>, slot, S::kDynamic);
   if (e != cudaSuccess) return launch_fail(e, "linear kernel attributes");
@@ -385,6 +402,54 @@ int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t s
   e = cudaGetLastError();
   if (e != cudaSuccess) return launch_fail(e, "linear launch");
   return LTXATTN_OK;
+}
+
+}  // namespace
+
+namespace ltx {
+int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
+               int m, int n, cudaStream_t st);
+}  // namespace ltx
+
+namespace {
+
+int sm_count_cached() {
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    (void)cudaGetLastError();
+    return 148;
+  }
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = 148;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// K splits for a narrow output: when the tiles fill under half the SMs (e.g. the
+// 32 gate logits of 3120 rows: 25 tiles), split the 64-wide K blocks into ranges
+// of at least 4 so the CTAs cover the SMs; 1 = no split.
+void plan_splits(int m, int n, int k, int* splits, int* kb_per) {
+  const int bn = bn_for(n);
+  const int tiles = ((m + kPBM - 1) / kPBM) * ((n + bn - 1) / bn);
+  const int kb_total = k / kPBK;
+  const int sms = sm_count_cached();
+  *splits = 1;
+  *kb_per = kb_total;
+  if (2 * tiles > sms || kb_total < 8) return;
+  const int want = std::min({sms / tiles, kb_total / 4, 16});
+  if (want < 2) return;
+  *kb_per = (kb_total + want - 1) / want;
+  *splits = (kb_total + *kb_per - 1) / *kb_per;
+}
+
+size_t split_workspace(int m, int n, int splits) {
+  return splits > 1 ? ((size_t)splits * m * n * sizeof(float) + 255) & ~size_t(255) : 0;
 }
 
 // ltxattn_linear, or (f32_out != null) the same GEMM storing its fp32
@@ -418,6 +483,33 @@ int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
   J.out_f32 = f32_out;
   J.o_sb = 0;
   J.o_st = f32_out != nullptr ? a->n : a->out_stride;
+  J.splits = 1;
+  J.kb_per = a->k / kPBK;
+  J.split_stride = 0;
+  if (f32_out == nullptr) {
+    // a narrow output with a workspace: K splits into fp32 partials, then one
+    // pass adds them in split order and applies the bias and the roundings
+    int splits = 1, kb_per = 0;
+    plan_splits(a->m, a->n, a->k, &splits, &kb_per);
+    const size_t need = split_workspace(a->m, a->n, splits);
+    if (splits > 1 && a->workspace != nullptr && a->workspace_bytes >= need &&
+        (reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0) {
+      J.splits = splits;
+      J.kb_per = kb_per;
+      J.out_f32 = static_cast<float*>(a->workspace);
+      J.o_st = a->n;
+      J.split_stride = (int64_t)a->m * a->n;
+      int rc;
+      switch (bn) {
+        case 256: rc = launch_linear_bn<256, true>(P, a, st); break;
+        case 128: rc = launch_linear_bn<128, true>(P, a, st); break;
+        case 64: rc = launch_linear_bn<64, true>(P, a, st); break;
+        default: rc = launch_linear_bn<32, true>(P, a, st); break;
+      }
+      if (rc) return rc;
+      return ltx::bias_round(J.out_f32, splits, J.split_stride, a->bias, a->out, a->out_stride, a->m, a->n, st);
+    }
+  }
   if (f32_out != nullptr) {
     switch (bn) {
       case 256: return launch_linear_bn<256, true>(P, a, st);
@@ -445,11 +537,13 @@ int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_
   return run_linear(a, partial, st);
 }
 
-int bias_round(const float* sum, const void* bias, void* out, int64_t out_stride, int m, int n, cudaStream_t st) {
+int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
+               int m, int n, cudaStream_t st) {
   const int64_t threads = (int64_t)m * (n / 8);
   const int64_t blocks = (threads + 255) / 256;
   if (blocks > 0x7fffffff) return fail_msg(LTXATTN_ERR_UNSUPPORTED, "output too large");
-  bias_round_kernel<<<(unsigned)blocks, 256, 0, st>>>(sum, n, static_cast<const __nv_bfloat16*>(bias),
+  bias_round_kernel<<<(unsigned)blocks, 256, 0, st>>>(sum, n, splits, split_stride,
+                                                      static_cast<const __nv_bfloat16*>(bias),
                                                       static_cast<__nv_bfloat16*>(out), out_stride, m, n);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return launch_fail(e, "bias and rounding launch");
@@ -462,6 +556,13 @@ extern "C" {
 
 int ltxattn_linear(const ltxattn_linear_args* a, void* stream) {
   return run_linear(a, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+size_t ltxattn_linear_workspace(const ltxattn_linear_args* a) {
+  if (a == nullptr || a->m < 1 || a->n < 8 || a->k < 64 || a->n % 8 || a->k % 64) return 0;
+  int splits = 1, kb_per = 0;
+  plan_splits(a->m, a->n, a->k, &splits, &kb_per);
+  return split_workspace(a->m, a->n, splits);
 }
 
 }  // extern "C"

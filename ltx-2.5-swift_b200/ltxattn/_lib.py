@@ -28,7 +28,7 @@ EXPORTED = (
     "ltxattn_allgather_heads", "ltxattn_device_count", "ltxattn_device_query",
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
-    "ltxattn_linear", "ltxattn_head_gate",
+    "ltxattn_linear", "ltxattn_linear_workspace", "ltxattn_head_gate",
     "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce",
 )
 
@@ -120,7 +120,7 @@ class LinearArgs(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int32), ("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
                 ("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("weight", ctypes.c_void_p),
                 ("weight_stride", ctypes.c_int64), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
-                ("out_stride", ctypes.c_int64)]
+                ("out_stride", ctypes.c_int64), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
 
 
 class HeadGateArgs(ctypes.Structure):
@@ -207,6 +207,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_memory_plan.restype = ctypes.c_int
     L.ltxattn_linear.argtypes = [ctypes.POINTER(LinearArgs), vp]
     L.ltxattn_linear.restype = ctypes.c_int
+    L.ltxattn_linear_workspace.argtypes = [ctypes.POINTER(LinearArgs)]
+    L.ltxattn_linear_workspace.restype = ctypes.c_size_t
     L.ltxattn_head_gate.argtypes = [ctypes.POINTER(HeadGateArgs), vp]
     L.ltxattn_head_gate.restype = ctypes.c_int
     L.ltxattn_out_project_workspace.argtypes = [ctypes.POINTER(OutProjectArgs)]

@@ -24,8 +24,11 @@ def _need_bf16(name: str, t: torch.Tensor):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """x [..., k] (rows with one stride, unit stride along k), weight [n, k] -> [..., n]."""
+           out: Optional[torch.Tensor] = None, stream=None, split_k: bool = True) -> torch.Tensor:
+    """x [..., k] (rows with one stride, unit stride along k), weight [n, k] -> [..., n].
+
+    A narrow output (few column tiles) gets the workspace ltxattn_linear asks
+    for and splits K across CTAs, unless ``split_k`` is False."""
     _need_bf16("x", x)
     _need_bf16("weight", weight)
     k = x.shape[-1]
@@ -49,7 +52,13 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
             raise Failure.shape("bias", bias.shape, f"[{n}] contiguous")
         a.bias = bias.data_ptr()
     a.out, a.out_stride = o2.data_ptr(), o2.stride(0) if m > 1 else n
-    rc = _lib.load().ltxattn_linear(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
+    L = _lib.load()
+    ws_bytes = int(L.ltxattn_linear_workspace(ctypes.byref(a)))
+    ws = None
+    if ws_bytes and split_k:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)  # a narrow output splits K
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws_bytes
+    rc = L.ltxattn_linear(ctypes.byref(a), ctypes.c_void_p(_stream_ptr(stream)))
     if rc != _lib.OK:
         raise Failure.from_status(rc)
     return out

@@ -53,6 +53,11 @@ int main(void) {
   printf("ltxattn_qk_prep_args %zu\n", sizeof(ltxattn_qk_prep_args));
   printf("ltxattn_fwd_plan_info %zu\n", sizeof(ltxattn_fwd_plan_info));
   printf("ltxattn_memory_plan_args %zu\n", sizeof(ltxattn_memory_plan_args));
+  printf("ltxattn_linear_args %zu\n", sizeof(ltxattn_linear_args));
+  printf("ltxattn_out_project_args %zu\n", sizeof(ltxattn_out_project_args));
+  printf("ltxattn_head_gate_args %zu\n", sizeof(ltxattn_head_gate_args));
+  P(ltxattn_linear_args, out_stride) P(ltxattn_linear_args, workspace_bytes)
+  P(ltxattn_out_project_args, workspace_bytes) P(ltxattn_head_gate_args, gate_stride_h)
   printf("ltxattn_memory_plan_info %zu\n", sizeof(ltxattn_memory_plan_info));
   P(ltxattn_memory_plan_args, resident_bytes) P(ltxattn_memory_plan_args, margin_fraction)
   P(ltxattn_memory_plan_info, fits) P(ltxattn_memory_plan_info, bytes_per_token)
@@ -87,14 +92,17 @@ def test_ctypes_layout_matches_the_header(tmp_path):
              "ltxattn_device_info": _lib.DeviceInfo, "ltxattn_rope_args": _lib.RopeArgs,
              "ltxattn_rotary_table_args": _lib.RotaryTableArgs, "ltxattn_qk_prep_args": _lib.QkPrepArgs,
              "ltxattn_fwd_plan_info": _lib.FwdPlanInfo, "ltxattn_memory_plan_args": _lib.MemoryPlanArgs,
-             "ltxattn_memory_plan_info": _lib.MemoryPlanInfo}
+             "ltxattn_memory_plan_info": _lib.MemoryPlanInfo, "ltxattn_linear_args": _lib.LinearArgs,
+             "ltxattn_out_project_args": _lib.OutProjectArgs, "ltxattn_head_gate_args": _lib.HeadGateArgs}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
                "ltxattn_rotary": _lib.Rotary, "ltxattn_device_info": _lib.DeviceInfo,
                "ltxattn_rope_args": _lib.RopeArgs, "ltxattn_rotary_table_args": _lib.RotaryTableArgs,
                "ltxattn_qk_prep_args": _lib.QkPrepArgs, "ltxattn_fwd_plan_info": _lib.FwdPlanInfo,
-               "ltxattn_memory_plan_args": _lib.MemoryPlanArgs, "ltxattn_memory_plan_info": _lib.MemoryPlanInfo}
+               "ltxattn_memory_plan_args": _lib.MemoryPlanArgs, "ltxattn_memory_plan_info": _lib.MemoryPlanInfo,
+               "ltxattn_linear_args": _lib.LinearArgs, "ltxattn_out_project_args": _lib.OutProjectArgs,
+               "ltxattn_head_gate_args": _lib.HeadGateArgs}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")
@@ -252,3 +260,16 @@ def test_memory_plan_counts_the_call_buffers():
     a.head_dim, a.margin_fraction = 128, -0.1
     assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(t)) == _lib.ERR_ARG
     assert L.ltxattn_memory_plan(None, ctypes.byref(t)) == _lib.ERR_ARG
+
+
+def test_linear_plans_split_k_for_narrow_outputs_only():
+    # 32 gate logits of 3120 rows: 25 tiles fill few SMs, so a workspace for K
+    # splits is asked for; a 4096-wide projection fills the GPU and asks for none
+    L = _lib.load()
+    a = _lib.LinearArgs(dtype=_lib.BF16, m=3120, n=32, k=4096)
+    need = L.ltxattn_linear_workspace(ctypes.byref(a))
+    assert need > 0 and need % 256 == 0 and need >= 2 * 3120 * 32 * 4
+    a.n = 4096
+    assert L.ltxattn_linear_workspace(ctypes.byref(a)) == 0
+    a.n, a.k = 32, 192  # too short a K to split
+    assert L.ltxattn_linear_workspace(ctypes.byref(a)) == 0

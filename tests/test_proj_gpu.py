@@ -104,3 +104,22 @@ def test_linear_views_and_batches():
         ref = oracle.linear(host(x[bi]), host(w))
         check(o, ref, f"strided batch {bi}")
     assert torch.all(wide[:, n:] == 0)  # nothing written past the view
+
+
+@pytest.mark.parametrize("m,n,k", [(3120, 32, 4096), (300, 8, 2048), (200, 64, 1024)])
+def test_split_k_for_narrow_outputs(m, n, k):
+    # narrow outputs split K across CTAs (fp32 partials added in a fixed order,
+    # then the bias and the roundings): against the oracle, against the unsplit
+    # kernel, and bit-identical on a second call
+    x = inputs.seeded_tensor(70 + n, (m, k))
+    w = weights(71 + n, n, k)
+    b = bias(72 + n, n)
+    got = linear(dev(x), dev(w), dev(b))
+    again = linear(dev(x), dev(w), dev(b))
+    unsplit = linear(dev(x), dev(w), dev(b), split_k=False)
+    torch.cuda.synchronize()
+    err = check(got, oracle.linear(x, w, b), f"split-K linear {m}x{n}x{k}")
+    assert np.mean(err == 0) > 0.97
+    assert torch.equal(got, again)
+    diff = (got.float() - unsplit.float()).abs()
+    assert diff.max().item() <= 2e-2 and (diff == 0).float().mean().item() > 0.97
