@@ -121,5 +121,7 @@ def test_split_k_for_narrow_outputs(m, n, k):
     err = check(got, oracle.linear(x, w, b), f"split-K linear {m}x{n}x{k}")
     assert np.mean(err == 0) > 0.97
     assert torch.equal(got, again)
+    # the two fp32 summation orders round to the same bf16 almost everywhere, else one ulp apart
     diff = (got.float() - unsplit.float()).abs()
-    assert diff.max().item() <= 2e-2 and (diff == 0).float().mean().item() > 0.97
+    ulp = torch.clamp(unsplit.float().abs(), min=2.0 ** -126) * 2.0 ** -7
+    assert bool(torch.all(diff <= ulp)) and (diff == 0).float().mean().item() > 0.97
