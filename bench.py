@@ -642,8 +642,9 @@ def run_qkprep(args):
 def run_module(args):
     """One whole video self-attention module (DiTAttention.callAsFunction) at the
     config-2 shape: x [1, 3120, 4096] -> [1, 3120, 4096], 32 heads of 128, biases,
-    q/k norms, the gate, 3D RoPE.  Projections on the library GEMM, the rest in
-    libltxattn_cuda.  TFLOP/s of the module's GEMM + attention FLOPs."""
+    q/k norms, the gate, 3D RoPE.  Every launch is libltxattn_cuda's: the five
+    projections on its tcgen05 GEMM (ltxattn_linear; the narrow gate logits split
+    K and add a second, bias-and-round launch), qk_prep_pair, the attention.  TFLOP/s of the module's GEMM + attention FLOPs."""
     import math
     import torch
     from ltxattn import DiTAttentionModule, Rotary, inputs
@@ -701,10 +702,10 @@ def run_module(args):
                        "flops_per_step": {"gemm": gemm_flops, "attention": attn_flops}},
             "roofline": {"bound": "tensor", "achieved": round(tf / ctx.ws, 1), "peak": burst, "unit": "TFLOP/s",
                          "frac": round(tf / ctx.ws / burst, 4), "peak_source": f"{src} bf16_tflops (burst)",
-                         "kernel": "whole module (cuBLAS GEMMs + qk_prep + fwd_bf16_sm100_kernel)", "traffic": None},
+                         "kernel": "whole module (linear_kernel x5 + bias_round + qk_prep_pair + fwd_bf16_sm100_kernel)", "traffic": None},
             "e2e": {"value": round(flops * ctx.ws / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2},
-            "gpu_launches": 3 * args.steps,  # qk_prep for q and k, the attention (gate fused); GEMMs are cuBLAS
+            "gpu_launches": 8 * args.steps,  # v, gate (split K: 2), q, k, qk_prep_pair, attention, to_out
             "clocks": clk,
         }
     ctx.close()
