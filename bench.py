@@ -328,7 +328,8 @@ def measure(ctx, args, wl, *, main=False, bwd=False):
     plan, kplan = _lib.FwdPlanInfo(), _lib.FwdPlanInfo()
     assert _lib.load().ltxattn_fwd_plan(ctypes.byref(call.args), ctypes.byref(plan)) == 0
     assert _lib.load().ltxattn_fwd_plan(ctypes.byref(kcall.args), ctypes.byref(kplan)) == 0
-    kernel_name = {0: "fwd_f32_kernel", 1: "fwd_bf16_sm100_kernel", 2: "fwd_short_sm100_kernel"}[kplan.kernel]
+    kernel_name = {0: "fwd_f32_kernel", 1: "fwd_bf16_sm100_kernel", 2: "fwd_short_sm100_kernel",
+                   3: "fwd_persist_sm100_kernel"}[kplan.kernel]
     run = lambda: call.run(ctx.stream)
     krun = lambda: kcall.run(ctx.stream)
 
@@ -702,7 +703,7 @@ def run_module(args):
                        "flops_per_step": {"gemm": gemm_flops, "attention": attn_flops}},
             "roofline": {"bound": "tensor", "achieved": round(tf / ctx.ws, 1), "peak": burst, "unit": "TFLOP/s",
                          "frac": round(tf / ctx.ws / burst, 4), "peak_source": f"{src} bf16_tflops (burst)",
-                         "kernel": "whole module (linear_kernel x5 + bias_round + qk_prep_pair + fwd_bf16_sm100_kernel)", "traffic": None},
+                         "kernel": "whole module (linear_kernel x5 + bias_round + qk_prep_pair + fwd_persist_sm100_kernel)", "traffic": None},
             "e2e": {"value": round(flops * ctx.ws / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2},
             "gpu_launches": 8 * args.steps,  # v, gate (split K: 2), q, k, qk_prep_pair, attention, to_out

@@ -51,7 +51,8 @@ def _stale(target: str, deps) -> bool:
 # setmaxnreg.inc that asks for more than the launch provided never returns.
 # ptxas' report is checked against the value the kernel source assumes.
 REGISTER_PINS = {"fwd_sm100.cu": ("fwd_bf16_sm100_kernel", 168),
-                 "fwd_short_sm100.cu": ("fwd_short_sm100_kernel", 128)}
+                 "fwd_short_sm100.cu": ("fwd_short_sm100_kernel", 128),
+                 "fwd_persist_sm100.cu": ("fwd_persist_sm100_kernel", 168)}
 
 
 def _check_register_pin(src: str, ptxas_log: str) -> None:

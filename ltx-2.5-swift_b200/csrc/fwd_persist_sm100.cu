@@ -1,0 +1,458 @@
+// fwd_persist_sm100.cu -- the bf16 forward run persistently: one CTA per SM
+// walks several work units (256-row query block, head, batch) and overlaps
+// the end of one unit with the start of the next.
+//
+// The one-CTA-per-unit forward (fwd_sm100.cu) pays, per unit, a CTA launch,
+// barrier and TMEM setup, the first Q/K/V loads with nothing to overlap
+// them, and an epilogue during which the tensor pipe idles: about 8 us per
+// unit at the 3,120-token video shape, whose 416 units also run as three
+// waves of 148 for 2.81 waves of work.  Here CTA c runs units c, c + G,
+// c + 2G, ... (G = the grid, at most one CTA per SM) and the roles never
+// drain between units:
+//   - the producer loads the next unit's Q tile t as soon as the last
+//     S_t = Q_t K^T of the current unit has completed (q_free), and the K/V
+//     ring runs on across unit boundaries;
+//   - the MMA thread issues across the boundary in the steady-state order,
+//     PV0 of the last tile, S0 of the next unit's first tile, PV1, S1, so
+//     each softmax warpgroup finds its next S ready after its epilogue;
+//   - the softmax warpgroup of tile t writes O_t straight from TMEM to global
+//     memory (no staging: the shared memory holds the next unit's Q/K/V), and
+//     releases the O_t columns (o_free) once it has read them, which is all
+//     the next unit's first P V waits for.
+// Only calls with no key mask and no causal or window band come here, so every
+// unit covers every KV tile (no per-unit tile list).  The arithmetic of a unit
+// is the one-CTA-per-unit kernel's (the same exponentials, lazy rescale, P
+// rounding, row-sum order and normalisation), so both give the same bits.
+//
+// Thread layout, register split and TMEM map are the forward kernel's:
+// warps 0-3 softmax of Q tile 0, warps 4-7 of Q tile 1, warp 8 TMA producer
+// (lane 0), warp 9 TMEM owner and MMA issuer (lane 0), warps 10-11 idle;
+// TMEM S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).  A unit of
+// the ragged last query block with no rows in Q tile 1 runs tile 0 alone.
+//
+// Barrier phases are counted per role: the producer and MMA thread count K/V
+// tiles (ring stage g & 1, use g >> 1) and per-tile Q loads; the softmax
+// warpgroup of tile t counts the S_t tiles and the units it has processed.
+// Every wait is bounded (2 s) and a timeout stops every role.
+#include <mutex>
+
+#include "fwd_common.cuh"
+
+namespace ltx {
+
+namespace {
+
+template <int D>
+struct PSmem {
+  static constexpr int kChunks = D / 64;
+  static constexpr uint32_t kTile = kChunks * kChunkBytes;
+  static constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 4 * kTile;
+  // q_full[2], q_free[2], k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
+  // p_half[2], p_full[2], o_full[2], o_free[2], done
+  static constexpr int kBars = 23;
+  static constexpr uint32_t kOffBar = 6 * kTile;
+  static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
+  static constexpr uint32_t kBytes = kOffCtl + 16;
+};
+
+struct PUnit {
+  int q0, hl, b;
+  bool two;  // Q tile 1 holds rows of the sequence
+};
+
+__device__ __forceinline__ PUnit persist_unit(const FwdParams& p, int unit) {
+  PUnit u;
+  u.q0 = (unit % p.q_blocks) * kBlockM;
+  u.hl = (unit / p.q_blocks) % p.Hc;
+  u.b = unit / (p.q_blocks * p.Hc);
+  u.two = u.q0 + kTileM < p.Lq;
+  return u;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __grid_constant__ FwdParams p) {
+  using S = PSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sQ = sm + S::kOffQ;  // Q tile t at sQ + t * kTile
+  uint8_t* sK = sm + S::kOffK;  // K stage st at sK + st * kTile
+  uint8_t* sV = sm + S::kOffV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
+  uint64_t* bar_qf = bars + 0;   // [2] Q tile t loaded
+  uint64_t* bar_qe = bars + 2;   // [2] the unit's last S_t has read Q tile t
+  uint64_t* bar_kf = bars + 4;   // [2]
+  uint64_t* bar_ke = bars + 6;   // [2]
+  uint64_t* bar_vf = bars + 8;   // [2]
+  uint64_t* bar_ve = bars + 10;  // [2]
+  uint64_t* bar_s = bars + 12;   // [2] S_t in TMEM
+  uint64_t* bar_ph = bars + 14;  // [2] first half of P_t stored (128 arrivals)
+  uint64_t* bar_p = bars + 16;   // [2] all of P_t stored (128 arrivals)
+  uint64_t* bar_of = bars + 18;  // [2] O_t of a unit complete
+  uint64_t* bar_oe = bars + 20;  // [2] O_t read by the epilogue (128 arrivals)
+  uint64_t* bar_done = bars + 22;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int units = p.n_full;
+  const int n = p.n_kv_tiles;
+
+  if (warp == 8 && lane == 0) {
+    for (int i = 0; i < S::kBars; ++i) mbar_init(bars + i, (i >= 14 && i < 18) || i == 20 || i == 21 ? 128 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the kernel that wrote q / k (the RoPE pre-pass) has completed
+
+  if (warp >= 8) {
+    setmaxnreg_dec<kProducerRegs>();
+    if (warp == 8) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        int nq[2] = {0, 0};  // loads issued into Q tile t
+        int gk = 0, gv = 0;  // K and V tiles issued (ring stage i & 1, use i >> 1)
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < units && ok; unit += G) {
+          const PUnit u = persist_unit(p, unit);
+          const int qh = p.q_head_off + u.hl;
+          const int kvh = (p.kv_head_off + u.hl) / p.group;
+          for (int t = 0; t < (u.two ? 2 : 1) && ok; ++t) {
+            // the previous unit's last S_t must have read this buffer
+            if (nq[t] > 0 && !(ok = mbar_wait(bar_qe + t, (nq[t] - 1) & 1, abort_flag, p.err, 40))) break;
+            mbar_arrive_expect_tx(bar_qf + t, S::kTile);
+#pragma unroll
+            for (int c = 0; c < S::kChunks; ++c)
+              tma_load_4d(&p.tm_q, bar_qf + t, sQ + t * S::kTile + c * kChunkBytes, c * 64, u.q0 + t * kTileM, qh,
+                          u.b);
+            ++nq[t];
+          }
+          for (int j = 0; j < n && ok; ++j) {
+            const int kv0 = j * kTileN;
+            int st = gk & 1;
+            if (gk >= 2 && !(ok = mbar_wait(bar_ke + st, ((gk >> 1) - 1) & 1, abort_flag, p.err, 41))) break;
+            mbar_arrive_expect_tx(bar_kf + st, S::kTile);
+#pragma unroll
+            for (int c = 0; c < S::kChunks; ++c)
+              tma_load_4d(&p.tm_k, bar_kf + st, sK + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, u.b);
+            ++gk;
+            st = gv & 1;
+            if (gv >= 2 && !(ok = mbar_wait(bar_ve + st, ((gv >> 1) - 1) & 1, abort_flag, p.err, 42))) break;
+            mbar_arrive_expect_tx(bar_vf + st, S::kTile);
+#pragma unroll
+            for (int c = 0; c < S::kChunks; ++c)
+              tma_load_4d(&p.tm_v, bar_vf + st, sV + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, u.b);
+            ++gv;
+          }
+        }
+        // never leave the CTA with a bulk copy still writing its shared memory:
+        // a load into a buffer is issued only after the one before it into that
+        // buffer was consumed, so only the last load per Q tile and the last
+        // two per ring can still be in flight
+        for (int t = 0; t < 2; ++t)
+          if (nq[t] > 0) drain_wait(bar_qf + t, (nq[t] - 1) & 1);
+        for (int i = gk < 2 ? 0 : gk - 2; i < gk; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
+        for (int i = gv < 2 ? 0 : gv - 2; i < gv; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
+      }
+      __syncwarp();
+    } else if (warp == 9) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        const uint32_t tS[2] = {tmem, tmem + 128};
+        const uint32_t tO[2] = {tmem + 256, tmem + 384};
+        const SDesc dQ[2] = {sdesc_split(smem_u32(sQ), 16, 1024), sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024)};
+        const SDesc dK = sdesc_split(smem_u32(sK), 16, 1024);
+        const SDesc dV = sdesc_split(smem_u32(sV), kChunkBytes, 1024);
+        const uint32_t stage_step = S::kTile >> 4;
+        auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
+        auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
+        int nq[2] = {0, 0};  // units begun on Q tile t (q_full phase count)
+        int np[2] = {0, 0};  // P_t tiles consumed (p_half / p_full phase count)
+        bool go = true;
+        // S_t of (unit, tile j) whose K sits in ring slot g; j == 0 first waits
+        // for the unit's Q tile t, j == n - 1 then releases Q tile t
+        auto issue_s_step = [&](int t, int j, int g) {
+          if (j == 0) {
+            if (!mbar_wait(bar_qf + t, nq[t] & 1, abort_flag, p.err, 43)) return false;
+            ++nq[t];
+          }
+          tc_fence_after();
+          issue_s<D>(tS[t], dQ[t], kdesc(g & 1));
+          umma_commit(bar_s + t);
+          if (j == n - 1) umma_commit(bar_qe + t);
+          return true;
+        };
+        int unit = blockIdx.x;
+        PUnit u = persist_unit(p, unit);
+        int g = 0;  // ring slot of the current tile
+        if (unit < units) {
+          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(0, 0, 0);
+          if (go && u.two) go = issue_s_step(1, 0, 0);
+          if (go) umma_commit(bar_ke + 0);
+        }
+        for (; unit < units && go; unit += G) {
+          const int nxt_unit = unit + G;
+          const bool has_next = nxt_unit < units;
+          const PUnit v = has_next ? persist_unit(p, nxt_unit) : u;
+          for (int j = 0; j < n; ++j, ++g) {
+            const int st = g & 1;
+            // the step after this one: (unit, j + 1) or (next unit, 0)
+            const bool more = j + 1 < n || has_next;
+            const bool nx_two = j + 1 < n ? u.two : v.two;
+            const int nj = j + 1 < n ? j + 1 : 0;
+            const int g1 = g + 1, st1 = g1 & 1;
+            for (int t = 0; t < 2 && go; ++t) {
+              if (t == 0 || u.two) {
+                if (!(go = mbar_wait(bar_ph + t, np[t] & 1, abort_flag, p.err, 45))) break;
+                if (t == 0 && !(go = mbar_wait(bar_vf + st, (g >> 1) & 1, abort_flag, p.err, 46))) break;
+                // the first P V of a unit overwrites O_t: the epilogue of the
+                // previous unit on this tile must have read it
+                if (j == 0 && nq[t] > 1 && !(go = mbar_wait(bar_oe + t, (nq[t] - 2) & 1, abort_flag, p.err, 47)))
+                  break;
+                tc_fence_after();
+                issue_pv_half<D>(tO[t], tS[t], vdesc(st), j > 0, 0);
+                if (!(go = mbar_wait(bar_p + t, np[t] & 1, abort_flag, p.err, 45))) break;
+                tc_fence_after();
+                issue_pv_half<D>(tO[t], tS[t], vdesc(st), true, 1);
+                ++np[t];
+                if (j == n - 1) umma_commit(bar_of + t);
+              }
+              // S_t of the next step right behind P V_t of this one (a unit with
+              // no rows in Q tile 1 issues no S1)
+              if (more && (t == 0 || nx_two)) {
+                if (t == 0 && !(go = mbar_wait(bar_kf + st1, (g1 >> 1) & 1, abort_flag, p.err, 48))) break;
+                go = issue_s_step(t, nj, g1);
+              }
+            }
+            if (!go) break;
+            umma_commit(bar_ve + st);
+            if (more) umma_commit(bar_ke + st1);
+          }
+          u = v;
+        }
+        umma_commit(bar_done);
+        drain_wait(bar_done, 0);  // every issued MMA has completed
+      }
+      __syncwarp();
+    }
+  } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
+    // ---------------- softmax and epilogue of Q tile t ----------------
+    const int t = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+    const float sl2 = p.scale_log2;
+    const int Lk = p.Lk;
+    const bool ragged = Lk % kTileN != 0;
+    int ns = 0;     // S_t tiles consumed
+    int nunit = 0;  // units processed on this tile
+    bool ok = true;
+    for (int unit = blockIdx.x; unit < units && ok; unit += G) {
+      const PUnit u = persist_unit(p, unit);
+      if (t == 1 && !u.two) continue;
+      const int row = u.q0 + t * kTileM + r;
+      float m = -INFINITY;  // running max, log2 domain (lazy)
+      float l = 0.f;
+      for (int i = 0; i < n; ++i, ++ns) {
+        if (!(ok = warp_wait(bar_s + t, ns & 1, abort_flag, p.err, 49))) break;
+        tc_fence_after();
+        float s[128];
+        {
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(tS + 0, r0);
+          tmem_ld32(tS + 32, r1);
+          tmem_ld32(tS + 64, r2);
+          tmem_ld32(tS + 96, r3);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            s[c] = __uint_as_float(r0[c]);
+            s[32 + c] = __uint_as_float(r1[c]);
+            s[64 + c] = __uint_as_float(r2[c]);
+            s[96 + c] = __uint_as_float(r3[c]);
+          }
+        }
+        const bool masked_tile = ragged && i == n - 1;  // the ragged last tile: keys past Lk get -inf
+        if (masked_tile) {
+          const int kv0 = i * kTileN;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            uint32_t bits = 0xffffffffu;
+            const int lim = Lk - (kv0 + 32 * w);
+            if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+          }
+        }
+        float mx;
+        {
+          float pm[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pm[e] = fmaxf(s[e], s[8 + e]);
+#pragma unroll
+          for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) pm[e] = max3(pm[e], s[c + e], s[c + 8 + e]);
+          }
+          mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+        }
+        const float m_cand = mx * sl2;
+        const bool need = m_cand > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need && i > 0)) {
+          const float alpha = need ? fast_exp2(m - m_cand) : 1.f;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        if (need) {
+          l *= fast_exp2(m - m_cand);  // exp2(-inf) = 0 on the first tile
+          m = m_cand;
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        const float2 sl2x2 = make_float2(sl2, sl2), nmx2 = make_float2(neg_m, neg_m);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+          for (int c = 64 * h2; c < 64 * h2 + 64; c += 2) {
+            const float2 x = fma2(make_float2(s[c], s[c + 1]), sl2x2, nmx2);
+            const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            s[c] = e.x;
+            s[c + 1] = e.y;
+            acc[(c >> 1) & 3] = add2(acc[(c >> 1) & 3], e);
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
+          tmem_st32(tS + 32 * h2, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(h2 == 0 ? bar_ph + t : bar_p + t);
+        }
+        {
+          const float2 a01 = add2(acc[0], acc[1]), a23 = add2(acc[2], acc[3]);
+          const float2 tot = add2(a01, a23);
+          l += tot.x + tot.y;
+        }
+      }
+      if (!ok) break;
+
+      // ---- epilogue: O_t / l, gated, straight to global memory ----
+      uint32_t g2 = 0x3f803f80u;  // bf16x2 (1, 1)
+      if (p.gate != nullptr && row < p.Lq) {
+        const float gv = gate_bf16(__bfloat162float(
+            p.gate[(int64_t)u.b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + u.hl) * p.g_sh]));
+        g2 = pack_bf16x2(gv, gv);
+      }
+      if (!(ok = warp_wait(bar_of + t, nunit & 1, abort_flag, p.err, 50))) break;
+      tc_fence_after();
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      uint4 packed[D / 8];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv_l, __uint_as_float(o[8 * e + 1]) * inv_l);
+          v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
+          v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
+          v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
+          if (p.gate != nullptr) {  // T(T(O) * g): one bf16x2 multiply (the product is exact in fp32)
+            v.x = bmul2(v.x, g2);
+            v.y = bmul2(v.y, g2);
+            v.z = bmul2(v.z, g2);
+            v.w = bmul2(v.w, g2);
+          }
+          packed[c * 4 + e] = v;
+        }
+      }
+      // O_t is in registers: the next unit's first P V may overwrite it
+      tc_fence_before();
+      mbar_arrive(bar_oe + t);
+      ++nunit;
+      if (row < p.Lq) {
+        uint4* orow = reinterpret_cast<uint4*>(p.out + (int64_t)u.b * p.o_sb +
+                                               (int64_t)(p.head_begin + u.hl) * p.o_sh + (int64_t)row * p.o_st);
+#pragma unroll
+        for (int e = 0; e < D / 8; ++e) orow[e] = packed[e];
+        if (p.lse != nullptr)
+          p.lse[(int64_t)u.b * p.lse_sb + (int64_t)(p.head_begin + u.hl) * p.lse_sh + row] =
+              (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+      }
+    }
+  }
+
+  // ---------------- teardown ----------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+constexpr int kMaxDev = 64;
+std::mutex g_persist_mu;
+bool g_persist_ready[kMaxDev][2] = {};
+
+}  // namespace
+
+size_t fwd_persist_smem_bytes(int D) {
+  return 1024 /* alignment slack */ + (D == 128 ? PSmem<128>::kBytes : PSmem<64>::kBytes);
+}
+
+// Once per device and head dim: the register count the warpgroup split
+// assumes, and the dynamic shared-memory limit.
+cudaError_t prepare_fwd_persist(int D) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  const int di = D == 128 ? 1 : 0;
+  std::lock_guard<std::mutex> lock(g_persist_mu);
+  if (g_persist_ready[dev][di]) return cudaSuccess;
+  const void* k = D == 128 ? (const void*)fwd_persist_sm100_kernel<128> : (const void*)fwd_persist_sm100_kernel<64>;
+  cudaFuncAttributes fa;
+  if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
+  if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
+  if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_persist_smem_bytes(D))) !=
+      cudaSuccess)
+    return e;
+  g_persist_ready[dev][di] = true;
+  return cudaSuccess;
+}
+
+// p.n_full is the unit count; `ctas` <= units CTAs walk them round-robin.
+cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, cudaStream_t s) {
+  const size_t smem = fwd_persist_smem_bytes(D);
+  if (D == 128) return launch_pdl(fwd_persist_sm100_kernel<128>, dim3(ctas), dim3(kThreads), smem, s, p);
+  return launch_pdl(fwd_persist_sm100_kernel<64>, dim3(ctas), dim3(kThreads), smem, s, p);
+}
+
+}  // namespace ltx

@@ -188,6 +188,7 @@ int check_rotary(const ltxattn_rotary& r, const char* name, int tokens_needed) {
 struct SplitChoice {
   int64_t n_tail;
   int splits;
+  double us;  // the model's time for the choice
 };
 
 SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
@@ -195,7 +196,7 @@ SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
   auto unit_us = [&](int sp) { return kCtaUs + (double)((kv_tiles + sp - 1) / sp) * kTileUs; };
   const int64_t waves = units / sms, rem = units % sms;
   const double whole = (double)((units + sms - 1) / sms) * unit_us(1);
-  SplitChoice best{0, 1};
+  SplitChoice best{0, 1, whole};
   double best_us = whole;
   for (int64_t k = 0; k <= waves; ++k) {
     const int64_t n_tail = rem + k * sms;
@@ -206,11 +207,21 @@ SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
                         combine;
       if (us < best_us) {
         best_us = us;
-        best = {n_tail, sp};
+        best = {n_tail, sp, us};
       }
     }
   }
-  return best_us < 0.985 * whole ? best : SplitChoice{0, 1};
+  return best_us < 0.985 * whole ? best : SplitChoice{0, 1, whole};
+}
+
+// The persistent forward (fwd_persist_sm100.cu) on the same terms: one CTA
+// per SM walks ceil(units / sms) units back to back; the per-CTA setup is paid
+// once, and a unit boundary costs ~1.5 us (the epilogue of one unit on the
+// softmax warps while the next unit's first S runs), not a whole t_cta.
+double persist_us(int64_t units, int sms, int kv_tiles) {
+  constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBoundaryUs = 1.5;
+  const double rounds = (double)((units + sms - 1) / sms);
+  return kCtaUs + rounds * ((double)kv_tiles * kTileUs + kBoundaryUs);
 }
 
 // Uniform split count (every unit split) for masked or banded calls, whose
@@ -248,6 +259,7 @@ struct FwdPlan {
   int q_tiles, kv_tiles, splits;
   int64_t units, n_full, n_tail;  // bf16: n_tail units split `splits` ways after n_full whole ones
   bool short_kv;                  // bf16, one KV tile, more units than SMs: the persistent kernel
+  bool persist;                   // bf16, no mask or band, at least a wave: the persistent multi-tile kernel
   int sms;
   size_t off_q, off_k, off_po, off_pl, total;
 };
@@ -282,6 +294,7 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
   P->units = (int64_t)P->q_tiles * s.Hc * s.B;
   P->n_tail = 0;
   P->short_kv = false;
+  P->persist = false;
   P->sms = 0;
   if (s.dtype == LTXATTN_BF16) {
     const int64_t units = P->units;
@@ -309,9 +322,15 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
         P->splits = uniform_splits(units, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
         P->n_tail = units;
       } else if (units >= sms) {
+        // whole units back to back on persistent CTAs, or one CTA per unit with
+        // the last units' KV ranges split: whichever the model times shorter
         const SplitChoice c = tail_splits(units, sms, P->kv_tiles, s.D);
-        P->splits = c.splits;
-        P->n_tail = c.n_tail;
+        if (P->kv_tiles > 1 && persist_us(units, sms, P->kv_tiles) < c.us) {
+          P->persist = true;
+        } else {
+          P->splits = c.splits;
+          P->n_tail = c.n_tail;
+        }
       }
     } else {
       return fail(LTXATTN_ERR_ARG, "num_splits %d is negative", a->num_splits);
@@ -439,7 +458,7 @@ int ltxattn_fwd_plan(const ltxattn_fwd_args* a, ltxattn_fwd_plan_info* info) {
   const int rc = plan_fwd(a, &P);
   if (rc) return rc;
   const bool bf16 = P.s.dtype == LTXATTN_BF16;
-  info->kernel = !bf16 ? 0 : (P.short_kv ? 2 : 1);
+  info->kernel = !bf16 ? 0 : (P.short_kv ? 2 : (P.persist ? 3 : 1));
   info->splits = P.splits;
   info->units = P.units;
   info->split_units = P.n_tail;
@@ -610,6 +629,15 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "fwd_short setup");
     e = launch_fwd_short(p, s.D, (int)P.units, P.sms, st);
     if (e != cudaSuccess) return cuda_fail(e, "fwd_short launch");
+    return LTXATTN_OK;
+  }
+  if (P.persist) {
+    e = prepare_fwd_persist(s.D);
+    if (e == cudaErrorInvalidConfiguration)
+      return fail(LTXATTN_ERR_CUDA, "fwd_persist: the loaded kernel's register count differs from its warpgroup split");
+    if (e != cudaSuccess) return cuda_fail(e, "fwd_persist setup");
+    e = launch_fwd_persist(p, s.D, (int)std::min<int64_t>(P.units, P.sms), st);
+    if (e != cudaSuccess) return cuda_fail(e, "fwd_persist launch");
     return LTXATTN_OK;
   }
   e = launch_fwd_bf16(p, s.D, smem, st);

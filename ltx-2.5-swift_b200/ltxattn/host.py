@@ -8,9 +8,12 @@ output back, one after the other.  Heads are independent, so ``HostAttention``
 splits the call into head blocks (the C ABI's ``head_begin`` / ``head_count``)
 and runs three streams: the host-to-device copy of block i+1, the attention of
 block i (``ltxattn_fwd``) and the device-to-host copy of block i-1 overlap.
-The result is bit-identical to one call over all heads: every head is computed
-by the same kernel on the same inputs, and only the order in which heads are
-computed and copied changes.
+Each block is an ordinary ``ltxattn_fwd`` call over its heads, so the result is
+bit-identical to the same head-block calls made on device buffers.  Against one
+call over all heads it is bit-identical whenever neither splits a unit's KV
+range (``num_splits=1`` guarantees that); otherwise the planner may split the
+smaller block calls differently, and the two agree within the bf16 tolerance
+of a split (partials combined in fp32).
 """
 from __future__ import annotations
 
@@ -26,13 +29,14 @@ class HostAttention:
     """Device staging buffers and per-block prepared calls for one shape.
 
     ``q``, ``k``, ``v``: the device tensors ([B, H, T, D], contiguous) that the
-    host data is copied into; ``chunks``: how many head blocks to pipeline.
+    host data is copied into; ``chunks``: how many head blocks to pipeline;
+    ``num_splits``: passed to every block call (0 lets the planner choose).
     Rotary tables, key mask and gate stay on the device (they are small and
     reused across calls)."""
 
     def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
                  key_mask: Optional[torch.Tensor] = None, q_rotary: Optional[Rotary] = None,
-                 k_rotary: Optional[Rotary] = None, chunks: int = 4):
+                 k_rotary: Optional[Rotary] = None, chunks: int = 4, num_splits: int = 0):
         for name, t in (("q", q), ("k", k), ("v", v)):
             if not t.is_cuda or not t.is_contiguous() or t.dim() != 4:
                 raise Failure.shape(name, t.shape, "a contiguous CUDA [B, H, T, D]")
@@ -48,7 +52,7 @@ class HostAttention:
         self.blocks = [(h, min(per, H - h)) for h in range(0, H, per)]
         self.calls: List[PreparedAttention] = [
             AttentionBackend.prepare(q, k, v, scale, key_mask=key_mask, q_rotary=q_rotary, k_rotary=k_rotary,
-                                     head_begin=h0, head_count=hc, out=self.out)
+                                     head_begin=h0, head_count=hc, num_splits=num_splits, out=self.out)
             for h0, hc in self.blocks]
         self.h2d = torch.cuda.Stream()
         self.comp = torch.cuda.Stream()
