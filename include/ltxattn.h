@@ -178,7 +178,7 @@ LTXATTN_API size_t ltxattn_fwd_workspace(const ltxattn_fwd_args* args);
 typedef struct ltxattn_fwd_plan_info {
   int32_t kernel;       /* 0: fp32 path; 1: tiled bf16 forward (one CTA per unit); 2: persistent bf16
                            forward for kv_len <= 128; 3: persistent bf16 forward over whole units
-                           (no key mask, no causal or window band, at least one wave of units) */
+                           (no causal or window band, at least one wave of units) */
   int32_t splits;       /* KV splits of the split units (1: none) */
   int64_t units;        /* 256-row query blocks x heads x batch (bf16) or 128-row blocks (fp32) */
   int64_t split_units;  /* how many of them run split */

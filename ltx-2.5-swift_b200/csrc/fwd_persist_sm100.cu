@@ -19,10 +19,15 @@
 //     memory (no staging: the shared memory holds the next unit's Q/K/V), and
 //     releases the O_t columns (o_free) once it has read them, which is all
 //     the next unit's first P V waits for.
-// Only calls with no key mask and no causal or window band come here, so every
-// unit covers every KV tile (no per-unit tile list).  The arithmetic of a unit
-// is the one-CTA-per-unit kernel's (the same exponentials, lazy rescale, P
-// rounding, row-sum order and normalisation), so both give the same bits.
+// Calls with a causal or window band do not come here: a unit's KV tiles depend
+// only on its batch row.  With a key mask the prologue reads every batch row's
+// mask once into shared memory (one bit per key) and lists the tiles holding a
+// valid key; a unit then walks its batch row's list (the text cross-attention's
+// 1024 slots with 94 valid keys: one tile), masking keys per column, and a row
+// with no valid key attends every key (GemmaTextEncoder.swift:306-319).  The
+// arithmetic of a unit is the one-CTA-per-unit kernel's (the same tiles, masks,
+// exponentials, lazy rescale, P rounding, row-sum order and normalisation), so
+// both give the same bits.
 //
 // Thread layout, register split and TMEM map are the forward kernel's:
 // warps 0-3 softmax of Q tile 0, warps 4-7 of Q tile 1, warp 8 TMA producer
@@ -52,20 +57,48 @@ struct PSmem {
   static constexpr int kBars = 23;
   static constexpr uint32_t kOffBar = 6 * kTile;
   static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
-  static constexpr uint32_t kBytes = kOffCtl + 16;
+  static constexpr uint32_t kOffMeta = kOffCtl + 16;        // key-mask tables (masked calls only)
+  static constexpr uint32_t kBytes = kOffMeta;
 };
+
+// Key-mask tables after kOffMeta, for B batch rows of nt KV tiles: the live tile
+// count and the "mask applies" flag per row (int [B] each), the live tiles
+// (uint16 [B][nt]) and the mask bits (uint32 [B][4 nt], bit i of word w = key
+// 32 w + i valid).
+__host__ __device__ constexpr uint32_t align16u(uint32_t x) { return (x + 15u) & ~15u; }
+__host__ __device__ constexpr uint32_t meta_off_tiles(int B) { return align16u(8u * (uint32_t)B); }
+__host__ __device__ constexpr uint32_t meta_off_bits(int B, int nt) {
+  return meta_off_tiles(B) + align16u(2u * (uint32_t)B * (uint32_t)nt);
+}
+__host__ __device__ constexpr uint32_t meta_bytes(int B, int nt) { return meta_off_bits(B, nt) + 16u * B * nt; }
 
 struct PUnit {
   int q0, hl, b;
-  bool two;  // Q tile 1 holds rows of the sequence
+  bool two;   // Q tile 1 holds rows of the sequence
+  int n;      // KV tiles the unit walks
+  bool mask;  // per-key mask bits apply
 };
 
-__device__ __forceinline__ PUnit persist_unit(const FwdParams& p, int unit) {
+// The key-mask tables of the prologue (meta == null when the call has no mask).
+struct MaskTables {
+  const uint8_t* meta;
+  int B, nt;
+  __device__ __forceinline__ int tile(int b, int j) const {
+    return meta == nullptr ? j : reinterpret_cast<const uint16_t*>(meta + meta_off_tiles(B))[b * nt + j];
+  }
+  __device__ __forceinline__ uint32_t word(int b, int w) const {
+    return reinterpret_cast<const uint32_t*>(meta + meta_off_bits(B, nt))[b * 4 * nt + w];
+  }
+};
+
+__device__ __forceinline__ PUnit persist_unit(const FwdParams& p, const MaskTables& mt, int unit) {
   PUnit u;
   u.q0 = (unit % p.q_blocks) * kBlockM;
   u.hl = (unit / p.q_blocks) % p.Hc;
   u.b = unit / (p.q_blocks * p.Hc);
   u.two = u.q0 + kTileM < p.Lq;
+  u.n = mt.meta == nullptr ? p.n_kv_tiles : reinterpret_cast<const int*>(mt.meta)[u.b];
+  u.mask = mt.meta != nullptr && reinterpret_cast<const int*>(mt.meta)[mt.B + u.b] != 0;
   return u;
 }
 
@@ -97,7 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   const int lane = threadIdx.x & 31;
   const int G = gridDim.x;
   const int units = p.n_full;
-  const int n = p.n_kv_tiles;
+  const int nt = p.n_kv_tiles;
+  const MaskTables mt{p.mask != nullptr ? sm + S::kOffMeta : nullptr, units / (p.q_blocks * p.Hc), nt};
 
   if (warp == 8 && lane == 0) {
     for (int i = 0; i < S::kBars; ++i) mbar_init(bars + i, (i >= 14 && i < 18) || i == 20 || i == 21 ? 128 : 1);
@@ -117,6 +151,61 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   const uint32_t tmem = *tmem_slot;
   grid_dep_wait();  // the kernel that wrote q / k (the RoPE pre-pass) has completed
 
+  if (p.mask != nullptr) {
+    // every batch row's mask bits (one 32-key word per thread per pass: two
+    // 16-byte loads when the rows are aligned, else byte loads; keys past Lk
+    // read as masked), then one warp per row lists the tiles holding a valid key
+    const int B = units / (p.q_blocks * p.Hc);
+    uint8_t* meta = sm + S::kOffMeta;
+    int* count = reinterpret_cast<int*>(meta);
+    int* on = count + B;
+    uint16_t* tiles = reinterpret_cast<uint16_t*>(meta + meta_off_tiles(B));
+    uint32_t* bits = reinterpret_cast<uint32_t*>(meta + meta_off_bits(B, nt));
+    const int nwords = 4 * nt;
+    const int Lk = p.Lk;
+    for (int idx = threadIdx.x; idx < B * nwords; idx += kThreads) {
+      const int b = idx / nwords, k0 = (idx - b * nwords) * 32;
+      const uint8_t* mrow = p.mask + (int64_t)b * p.mask_sb;
+      uint32_t w = 0;
+      if (p.mask_vec && k0 + 32 <= Lk) {
+        const uint4 lo = *reinterpret_cast<const uint4*>(mrow + k0);
+        const uint4 hi = *reinterpret_cast<const uint4*>(mrow + k0 + 16);
+        const uint32_t wd[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t m = __vcmpne4(wd[i], 0u);  // 0xff in each nonzero byte
+          w |= (((m >> 7) & 1u) | ((m >> 14) & 2u) | ((m >> 21) & 4u) | ((m >> 28) & 8u)) << (4 * i);
+        }
+      } else {
+        for (int i = 0; i < 32; ++i)
+          if (k0 + i < Lk && mrow[k0 + i] != 0) w |= 1u << i;
+      }
+      bits[idx] = w;
+    }
+    __syncthreads();
+    for (int b = warp; b < B; b += kThreads / 32) {
+      const uint32_t* wb = bits + b * nwords;
+      int cnt = 0;
+      for (int j0 = 0; j0 < nt; j0 += 32) {
+        const int j = j0 + lane;
+        const bool act = j < nt && (wb[4 * j] | wb[4 * j + 1] | wb[4 * j + 2] | wb[4 * j + 3]) != 0u;
+        const unsigned bal = __ballot_sync(0xffffffffu, act);
+        if (act) tiles[b * nt + cnt + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint16_t>(j);
+        cnt += __popc(bal);
+      }
+      const bool free_row = cnt == 0;  // no valid key: every key, unmasked
+      if (free_row) {
+        for (int j = lane; j < nt; j += 32) tiles[b * nt + j] = static_cast<uint16_t>(j);
+        cnt = nt;
+      }
+      if (lane == 0) {
+        count[b] = cnt;
+        on[b] = free_row ? 0 : 1;
+      }
+    }
+    __syncthreads();
+  }
+
   if (warp >= 8) {
     setmaxnreg_dec<kProducerRegs>();
     if (warp == 8) {
@@ -126,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         int gk = 0, gv = 0;  // K and V tiles issued (ring stage i & 1, use i >> 1)
         bool ok = true;
         for (int unit = blockIdx.x; unit < units && ok; unit += G) {
-          const PUnit u = persist_unit(p, unit);
+          const PUnit u = persist_unit(p, mt, unit);
           const int qh = p.q_head_off + u.hl;
           const int kvh = (p.kv_head_off + u.hl) / p.group;
           for (int t = 0; t < (u.two ? 2 : 1) && ok; ++t) {
@@ -139,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
                           u.b);
             ++nq[t];
           }
-          for (int j = 0; j < n && ok; ++j) {
-            const int kv0 = j * kTileN;
+          for (int j = 0; j < u.n && ok; ++j) {
+            const int kv0 = mt.tile(u.b, j) * kTileN;
             int st = gk & 1;
             if (gk >= 2 && !(ok = mbar_wait(bar_ke + st, ((gk >> 1) - 1) & 1, abort_flag, p.err, 41))) break;
             mbar_arrive_expect_tx(bar_kf + st, S::kTile);
@@ -182,8 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         int np[2] = {0, 0};  // P_t tiles consumed (p_half / p_full phase count)
         bool go = true;
         // S_t of (unit, tile j) whose K sits in ring slot g; j == 0 first waits
-        // for the unit's Q tile t, j == n - 1 then releases Q tile t
-        auto issue_s_step = [&](int t, int j, int g) {
+        // for the unit's Q tile t, j == n - 1 (n: the unit's tile count) then
+        // releases Q tile t
+        auto issue_s_step = [&](int t, int j, int n, int g) {
           if (j == 0) {
             if (!mbar_wait(bar_qf + t, nq[t] & 1, abort_flag, p.err, 43)) return false;
             ++nq[t];
@@ -195,23 +285,25 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
           return true;
         };
         int unit = blockIdx.x;
-        PUnit u = persist_unit(p, unit);
+        PUnit u = persist_unit(p, mt, unit);
         int g = 0;  // ring slot of the current tile
         if (unit < units) {
-          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(0, 0, 0);
-          if (go && u.two) go = issue_s_step(1, 0, 0);
+          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(0, 0, u.n, 0);
+          if (go && u.two) go = issue_s_step(1, 0, u.n, 0);
           if (go) umma_commit(bar_ke + 0);
         }
         for (; unit < units && go; unit += G) {
           const int nxt_unit = unit + G;
           const bool has_next = nxt_unit < units;
-          const PUnit v = has_next ? persist_unit(p, nxt_unit) : u;
+          const PUnit v = has_next ? persist_unit(p, mt, nxt_unit) : u;
+          const int n = u.n;
           for (int j = 0; j < n; ++j, ++g) {
             const int st = g & 1;
             // the step after this one: (unit, j + 1) or (next unit, 0)
             const bool more = j + 1 < n || has_next;
             const bool nx_two = j + 1 < n ? u.two : v.two;
             const int nj = j + 1 < n ? j + 1 : 0;
+            const int nn = j + 1 < n ? n : v.n;
             const int g1 = g + 1, st1 = g1 & 1;
             for (int t = 0; t < 2 && go; ++t) {
               if (t == 0 || u.two) {
@@ -233,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
               // no rows in Q tile 1 issues no S1)
               if (more && (t == 0 || nx_two)) {
                 if (t == 0 && !(go = mbar_wait(bar_kf + st1, (g1 >> 1) & 1, abort_flag, p.err, 48))) break;
-                go = issue_s_step(t, nj, g1);
+                go = issue_s_step(t, nj, nn, g1);
               }
             }
             if (!go) break;
@@ -257,13 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     const uint32_t tO = tmem + 256 + t * 128 + lane_off;
     const float sl2 = p.scale_log2;
     const int Lk = p.Lk;
-    const bool ragged = Lk % kTileN != 0;
     int ns = 0;     // S_t tiles consumed
     int nunit = 0;  // units processed on this tile
     bool ok = true;
     for (int unit = blockIdx.x; unit < units && ok; unit += G) {
-      const PUnit u = persist_unit(p, unit);
+      const PUnit u = persist_unit(p, mt, unit);
       if (t == 1 && !u.two) continue;
+      const int n = u.n;
       const int row = u.q0 + t * kTileM + r;
       float m = -INFINITY;  // running max, log2 domain (lazy)
       float l = 0.f;
@@ -286,12 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
             s[96 + c] = __uint_as_float(r3[c]);
           }
         }
-        const bool masked_tile = ragged && i == n - 1;  // the ragged last tile: keys past Lk get -inf
+        // masked keys and keys past Lk get -inf logits
+        const int kv0 = mt.tile(u.b, i) * kTileN;
+        const bool masked_tile = u.mask || kv0 + kTileN > Lk;
         if (masked_tile) {
-          const int kv0 = i * kTileN;
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
-            uint32_t bits = 0xffffffffu;
+            uint32_t bits = u.mask ? mt.word(u.b, kv0 / 32 + w) : 0xffffffffu;
             const int lim = Lk - (kv0 + 32 * w);
             if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
 #pragma unroll
@@ -419,38 +512,42 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
 
 constexpr int kMaxDev = 64;
 std::mutex g_persist_mu;
-bool g_persist_ready[kMaxDev][2] = {};
+bool g_persist_regs_ok[kMaxDev][2] = {};
+size_t g_persist_smem_set[kMaxDev][2] = {};
 
 }  // namespace
 
-size_t fwd_persist_smem_bytes(int D) {
-  return 1024 /* alignment slack */ + (D == 128 ? PSmem<128>::kBytes : PSmem<64>::kBytes);
+size_t fwd_persist_smem_bytes(int D, int batch, int kv_tiles, bool has_mask) {
+  return 1024 /* alignment slack */ + (D == 128 ? PSmem<128>::kBytes : PSmem<64>::kBytes) +
+         (has_mask ? meta_bytes(batch, kv_tiles) : 0);
 }
 
 // Once per device and head dim: the register count the warpgroup split
-// assumes, and the dynamic shared-memory limit.
-cudaError_t prepare_fwd_persist(int D) {
+// assumes; and the dynamic shared-memory limit whenever a larger size is needed.
+cudaError_t prepare_fwd_persist(int D, size_t smem) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
   const int di = D == 128 ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_persist_mu);
-  if (g_persist_ready[dev][di]) return cudaSuccess;
   const void* k = D == 128 ? (const void*)fwd_persist_sm100_kernel<128> : (const void*)fwd_persist_sm100_kernel<64>;
-  cudaFuncAttributes fa;
-  if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
-  if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
-  if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_persist_smem_bytes(D))) !=
-      cudaSuccess)
-    return e;
-  g_persist_ready[dev][di] = true;
+  if (!g_persist_regs_ok[dev][di]) {
+    cudaFuncAttributes fa;
+    if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
+    if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
+    g_persist_regs_ok[dev][di] = true;
+  }
+  if (smem > g_persist_smem_set[dev][di]) {
+    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
+    g_persist_smem_set[dev][di] = smem;
+  }
   return cudaSuccess;
 }
 
-// p.n_full is the unit count; `ctas` <= units CTAs walk them round-robin.
-cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, cudaStream_t s) {
-  const size_t smem = fwd_persist_smem_bytes(D);
+// p.n_full is the unit count; `ctas` <= units CTAs walk them round-robin
+// (prepare_fwd_persist must have succeeded for D and at least smem).
+cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, size_t smem, cudaStream_t s) {
   if (D == 128) return launch_pdl(fwd_persist_sm100_kernel<128>, dim3(ctas), dim3(kThreads), smem, s, p);
   return launch_pdl(fwd_persist_sm100_kernel<64>, dim3(ctas), dim3(kThreads), smem, s, p);
 }

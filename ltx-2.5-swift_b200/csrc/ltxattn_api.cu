@@ -259,7 +259,7 @@ struct FwdPlan {
   int q_tiles, kv_tiles, splits;
   int64_t units, n_full, n_tail;  // bf16: n_tail units split `splits` ways after n_full whole ones
   bool short_kv;                  // bf16, one KV tile, more units than SMs: the persistent kernel
-  bool persist;                   // bf16, no mask or band, at least a wave: the persistent multi-tile kernel
+  bool persist;                   // bf16, no band, at least a wave: the persistent multi-tile kernel
   int sms;
   size_t off_q, off_k, off_po, off_pl, total;
 };
@@ -308,6 +308,11 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
       // its units (fwd_short_sm100.cu); no split
       P->short_kv = P->kv_tiles == 1 && !P->causal && P->window == 0 && units > sms;
       const bool opaque = a->key_mask != nullptr || P->causal || P->window > 0;  // per-unit work unknown
+      const bool banded = P->causal || P->window > 0;
+      // a key mask but no band: units of one batch row walk the same live tiles,
+      // which the persistent kernel lists once per row (shared memory permitting)
+      const bool persist_masked = a->key_mask != nullptr && !banded && units >= sms && P->kv_tiles > 1 &&
+                                  fwd_persist_smem_bytes(s.D, s.B, P->kv_tiles, true) <= kMaxDynamicSmem;
       if (units < sms && P->kv_tiles > 1 && opaque) {
         // fewer units than SMs: as many splits as keep one wave
         P->splits = std::max(1, std::min({(int)(sms / units), P->kv_tiles, kMaxSplits}));
@@ -318,6 +323,8 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
         const SplitChoice c = tail_splits(units, sms, P->kv_tiles, s.D);
         P->splits = c.splits;
         P->n_tail = c.n_tail;
+      } else if (persist_masked) {
+        P->persist = true;
       } else if (units >= sms && opaque) {
         P->splits = uniform_splits(units, sms, P->kv_tiles, (double)s.B * s.Hc * s.Lq * s.D);
         P->n_tail = units;
@@ -632,11 +639,12 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     return LTXATTN_OK;
   }
   if (P.persist) {
-    e = prepare_fwd_persist(s.D);
+    const size_t psmem = fwd_persist_smem_bytes(s.D, s.B, P.kv_tiles, a->key_mask != nullptr);
+    e = prepare_fwd_persist(s.D, psmem);
     if (e == cudaErrorInvalidConfiguration)
       return fail(LTXATTN_ERR_CUDA, "fwd_persist: the loaded kernel's register count differs from its warpgroup split");
     if (e != cudaSuccess) return cuda_fail(e, "fwd_persist setup");
-    e = launch_fwd_persist(p, s.D, (int)std::min<int64_t>(P.units, P.sms), st);
+    e = launch_fwd_persist(p, s.D, (int)std::min<int64_t>(P.units, P.sms), psmem, st);
     if (e != cudaSuccess) return cuda_fail(e, "fwd_persist launch");
     return LTXATTN_OK;
   }

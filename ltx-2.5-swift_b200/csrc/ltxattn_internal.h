@@ -209,10 +209,13 @@ size_t fwd_bf16_smem_bytes(int D, int Lk, bool has_mask);
 // Persistent forward for kv_len <= 128 (one KV tile); see fwd_short_sm100.cu.
 cudaError_t prepare_fwd_short(int D);
 cudaError_t launch_fwd_short(const FwdParams& p, int D, int units, int sms, cudaStream_t s);
-// Persistent forward for unmasked, unbanded calls of at least one wave: `ctas`
-// CTAs walk the p.n_full units round-robin; see fwd_persist_sm100.cu.
-cudaError_t prepare_fwd_persist(int D);
-cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, cudaStream_t s);
+// Persistent forward for unbanded calls of at least one wave: `ctas` CTAs walk
+// the p.n_full units round-robin; see fwd_persist_sm100.cu.  With a key mask the
+// shared memory holds every batch row's mask bits and live-tile list.
+size_t fwd_persist_smem_bytes(int D, int batch, int kv_tiles, bool has_mask);
+constexpr size_t kMaxDynamicSmem = 232448;  // sm_100 per-block opt-in limit (227 KB)
+cudaError_t prepare_fwd_persist(int D, size_t smem);
+cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, size_t smem, cudaStream_t s);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_fwd_f32(const F32Params& p, int D, int Hc, int B, cudaStream_t s);
 // Rotate one tensor (b == nullptr) or two in one launch.

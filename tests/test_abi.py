@@ -177,15 +177,18 @@ def test_grouped_kv_heads_take_no_rotary():
     # (B, H, Lq, Lk, D), (kernel, splits, split_units, launches); 148 SMs (no device here)
     ((1, 32, 3120, 3120, 128), (3, 1, 0, 1)),     # config 2: 416 units on 148 persistent CTAs
     ((1, 32, 29760, 29760, 128), (1, 3, 44, 2)),  # config 5 on 1 GPU: 25 waves + 44 units split 3 ways
+    ((1, 32, 3120, 1024, 128, "mask"), (3, 1, 0, 1)),  # config 3: masked, 416 units, persistent
     ((1, 32, 3120, 126, 64), (2, 1, 0, 1)),       # config 4b: one KV tile -> persistent kernel
     ((1, 32, 126, 3120, 64), (1, 4, 32, 2)),      # config 4c: one wave of 4-way splits + combine
     ((1, 4, 29760, 29760, 128), (1, 6, 24, 2)),   # config 5 on 8 GPUs: the last 24 units split 6 ways
     ((1, 32, 126, 126, 64), (1, 1, 0, 1)),        # config 4a: 32 units, one KV tile, nothing to split
 ])
 def test_forward_plan(shape, want):
-    B, H, Lq, Lk, D = shape
+    B, H, Lq, Lk, D = shape[:5]
     a = _lib.FwdArgs()
     a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, B, H, Lq, Lk, D
+    if "mask" in shape:
+        a.key_mask, a.key_mask_stride_b = 4096, Lk
     info = _lib.FwdPlanInfo()
     assert _lib.load().ltxattn_fwd_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK, _lib.last_error()
     assert (info.kernel, info.splits, info.split_units, info.launches) == want

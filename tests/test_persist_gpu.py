@@ -2,9 +2,10 @@
 SM walks units c, c + G, c + 2G, ... and overlaps the end of one unit with the
 start of the next.
 
-The planner chooses it (ltxattn_fwd_plan kernel 3) for unmasked, unbanded bf16
-calls of at least a wave of units when its cost model beats the one-CTA-per-unit
-kernel; num_splits=1 forces the one-CTA-per-unit kernel over whole units.  Both
+The planner chooses it (ltxattn_fwd_plan kernel 3) for unbanded bf16 calls of at
+least a wave of units (masked ones always; unmasked ones when its cost model
+beats the one-CTA-per-unit kernel); num_splits=1 forces the one-CTA-per-unit
+kernel over whole units.  Both
 compute each unit with the same arithmetic, so their outputs and LSEs must agree
 bit for bit; the persistent result is also checked against the CPU oracle (bf16
 bar: max abs <= 2e-2, rel-L2 <= 1e-2).
@@ -118,3 +119,34 @@ def test_head_block_of_a_larger_tensor():
     hs = [h0, h0 + hc - 1]
     ref, _ = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs])
     check(out[:, hs], ref, "head block")
+
+
+@pytest.mark.parametrize("B,H,Lq,Lk,D,valid", [
+    (1, 32, 3120, 1024, 128, 94),   # config 3: text cross-attention, 94 of 1024 slots valid (one live tile)
+    (2, 80, 600, 1000, 64, None),   # batch 0 a random mask, batch 1 no valid key (every key)
+])
+def test_key_masks_match_bit_for_bit_and_the_oracle(B, H, Lq, Lk, D, valid):
+    assert device_info()["sm_count"] == 148
+    q = inputs.seeded_tensor(231 + D, (B, H, Lq, D), rmsnorm=True, bf16=True)
+    k = inputs.seeded_tensor(232 + D, (B, H, Lk, D), rmsnorm=True, bf16=True)
+    v = inputs.seeded_tensor(233 + D, (B, H, Lk, D), bf16=True)
+    m = np.zeros((B, Lk), np.uint8)
+    if valid is not None:
+        m[:, :valid] = 1
+    else:
+        m[0] = np.random.default_rng(5).random(Lk) < 0.3
+    a = _lib.FwdArgs()
+    a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, B, H, Lq, Lk, D
+    a.key_mask, a.key_mask_stride_b = 4096, Lk
+    info = _lib.FwdPlanInfo()
+    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK
+    assert info.kernel == 3
+    qd, kd, vd, md = dev(q), dev(k), dev(v), torch.from_numpy(m).cuda()
+    out, lse = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True)
+    one, lse1 = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True, num_splits=1)
+    assert same_bits(out, one)
+    assert torch.equal(lse, lse1)
+    hs = [0, H - 1]
+    ref, ref_lse = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs], mask=m)
+    check(out[:, hs], ref, f"mask B={B} D={D}")
+    assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS

@@ -2,8 +2,8 @@
 requests and masks through ltxattn_fwd_plan / ltxattn_fwd_workspace must never
 crash and must stay self-consistent -- a split plan always has scratch for its
 partials, every launch fits the 1-D grid, and the persistent kernel is chosen
-only for one-tile key sequences (kernel 2) or for unmasked, unbanded calls of at
-least a wave of units (kernel 3).  148 SMs are assumed (no device here)."""
+only for one-tile key sequences (kernel 2) or for unbanded calls of at least a
+wave of units (kernel 3).  148 SMs are assumed (no device here)."""
 import ctypes
 
 from hypothesis import given, settings, strategies as st
@@ -48,7 +48,7 @@ def test_plan_is_self_consistent(B, H, Lq, Lk, D, splits, masked, causal, window
         assert info.split_units == 0 and ws == 0 and info.launches == 1
     if info.kernel == 2:
         assert kv_tiles == 1 and not causal and window == 0 and splits == 0 and info.units > 148
-    if info.kernel == 3:  # persistent whole units: unmasked, unbanded, at least a wave, more than one KV tile
-        assert not masked and not causal and window == 0 and splits == 0
+    if info.kernel == 3:  # persistent whole units: unbanded, at least a wave, more than one KV tile
+        assert not causal and window == 0 and splits == 0
         assert info.units >= 148 and kv_tiles > 1 and info.splits == 1 and info.launches == 1
     assert info.units - info.split_units + info.split_units * info.splits < 2 ** 31
