@@ -5,10 +5,9 @@ start of the next.
 The planner chooses it (ltxattn_fwd_plan kernel 3) for unbanded bf16 calls of at
 least a wave of units (masked ones always; unmasked ones when its cost model
 beats the one-CTA-per-unit kernel); num_splits=1 forces the one-CTA-per-unit
-kernel over whole units.  Both
-compute each unit with the same arithmetic, so their outputs and LSEs must agree
-bit for bit; the persistent result is also checked against the CPU oracle (bf16
-bar: max abs <= 2e-2, rel-L2 <= 1e-2).
+kernel over whole units.  Both compute each unit with the same arithmetic, so
+their outputs and LSEs must agree bit for bit; the persistent result is also
+checked against the CPU oracle (bf16 bar: max abs <= 2e-2, rel-L2 <= 1e-2).
 """
 import ctypes
 
