@@ -15,10 +15,14 @@
 //   - the MMA thread issues across the boundary in the steady-state order,
 //     PV0 of the last tile, S0 of the next unit's first tile, PV1, S1, so
 //     each softmax warpgroup finds its next S ready after its epilogue;
-//   - the softmax warpgroup of tile t writes O_t straight from TMEM to global
-//     memory (no staging: the shared memory holds the next unit's Q/K/V), and
-//     releases the O_t columns (o_free) once it has read them, which is all
-//     the next unit's first P V waits for.
+//   - the softmax warpgroup of tile t reads O_t from TMEM into registers and
+//     releases the O_t columns (o_free), which is all the next unit's first
+//     P V waits for; it then stores the normalised rows with TMA through a
+//     16 KB staging tile of its own, one 64-column chunk at a time (the rest
+//     of shared memory holds the next unit's Q/K/V).  Full-line TMA stores
+//     matter here: per-row 16-byte stores write partial sectors, and at the
+//     3,120-token shape they made the kernel 6% slower than the one-CTA-per-
+//     unit kernel, whose epilogue stages in an idle K stage.
 // Calls with a causal or window band do not come here: a unit's KV tiles depend
 // only on its batch row.  With a key mask the prologue reads every batch row's
 // mask once into shared memory (one bit per key) and lists the tiles holding a
@@ -52,10 +56,11 @@ struct PSmem {
   static constexpr int kChunks = D / 64;
   static constexpr uint32_t kTile = kChunks * kChunkBytes;
   static constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 4 * kTile;
+  static constexpr uint32_t kOffStg = 6 * kTile;  // [2] epilogue staging, one 64-column chunk per tile
   // q_full[2], q_free[2], k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
   // p_half[2], p_full[2], o_full[2], o_free[2], done
   static constexpr int kBars = 23;
-  static constexpr uint32_t kOffBar = 6 * kTile;
+  static constexpr uint32_t kOffBar = kOffStg + 2 * kChunkBytes;
   static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kOffMeta = kOffCtl + 16;        // key-mask tables (masked calls only)
   static constexpr uint32_t kBytes = kOffMeta;
@@ -110,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   uint8_t* sQ = sm + S::kOffQ;  // Q tile t at sQ + t * kTile
   uint8_t* sK = sm + S::kOffK;  // K stage st at sK + st * kTile
   uint8_t* sV = sm + S::kOffV;
+  uint8_t* sStg = sm + S::kOffStg;  // staging tile t at sStg + t * kChunkBytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* bar_qf = bars + 0;   // [2] Q tile t loaded
   uint64_t* bar_qe = bars + 2;   // [2] the unit's last S_t has read Q tile t
@@ -140,6 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    tma_prefetch_desc(&p.tm_o);
   }
   if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
@@ -305,7 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
             const int nj = j + 1 < n ? j + 1 : 0;
             const int nn = j + 1 < n ? n : v.n;
             const int g1 = g + 1, st1 = g1 & 1;
-            for (int t = 0; t < 2 && go; ++t) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              if (!go) break;
               if (t == 0 || u.two) {
                 if (!(go = mbar_wait(bar_ph + t, np[t] & 1, abort_flag, p.err, 45))) break;
                 if (t == 0 && !(go = mbar_wait(bar_vf + st, (g >> 1) & 1, abort_flag, p.err, 46))) break;
@@ -489,16 +498,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
       tc_fence_before();
       mbar_arrive(bar_oe + t);
       ++nunit;
-      if (row < p.Lq) {
-        uint4* orow = reinterpret_cast<uint4*>(p.out + (int64_t)u.b * p.o_sb +
-                                               (int64_t)(p.head_begin + u.hl) * p.o_sh + (int64_t)row * p.o_st);
+      // one 64-column chunk at a time through this tile's staging tile (128-byte
+      // swizzled like the loads), stored by one thread with TMA; rows past Lq
+      // are clipped by the tensor map
+      uint8_t* srow = sStg + t * kChunkBytes + r * 128;
 #pragma unroll
-        for (int e = 0; e < D / 8; ++e) orow[e] = packed[e];
-        if (p.lse != nullptr)
-          p.lse[(int64_t)u.b * p.lse_sb + (int64_t)(p.head_begin + u.hl) * p.lse_sh + row] =
-              (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+      for (int ch = 0; ch < S::kChunks; ++ch) {
+        if (r == 0) bulk_wait_read();  // the previous store has read the staging tile
+        named_barrier(1 + t, 128);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(srow + ((j ^ (r & 7)) << 4)) = packed[ch * 8 + j];
+        fence_proxy_async_smem();  // the bulk copy reads these rows through the async proxy
+        named_barrier(1 + t, 128);
+        if (r == 0) {
+          tma_store_4d(&p.tm_o, sStg + t * kChunkBytes, ch * 64, u.q0 + t * kTileM, p.head_begin + u.hl, u.b);
+          bulk_commit();
+        }
       }
+      if (p.lse != nullptr && row < p.Lq)
+        p.lse[(int64_t)u.b * p.lse_sb + (int64_t)(p.head_begin + u.hl) * p.lse_sh + row] =
+            (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
     }
+    if (r == 0) bulk_wait_read();  // the CTA's shared memory must outlive the stores' reads
   }
 
   // ---------------- teardown ----------------

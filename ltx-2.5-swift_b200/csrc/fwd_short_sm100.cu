@@ -26,10 +26,21 @@
 // 12-15 the epilogue of both tiles (thread r owns row r of each; warps 10-11
 // idle).  Registers: launched at 128 per thread, the softmax warpgroups take
 // 184 and the other two 72 (2*128*184 + 2*128*72 = 512*128).  TMEM: S0
-// [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D); P_t overwrites the
-// first 64 columns of S_t.  The softmax hands each row's max and sum to the
-// epilogue through shared memory, double-buffered by unit.  Both Q tiles of a
-// unit are always computed; a tile past q_len reads zeros and is not stored.
+// [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).  The softmax hands
+// each row's max and sum to the epilogue through shared memory,
+// double-buffered by unit.  Both Q tiles of a unit are always computed; a
+// tile past q_len reads zeros and is not stored.
+//
+// Where P_t lives.  With D = 64, O_t takes 64 columns and P_t (bf16, two per
+// column) gets the other 64 of its 128-column block: P0 [320,384), P1
+// [448,512).  The softmax then frees the S_t columns as soon as it has loaded
+// S_t into registers (s_read), and the MMA thread issues S_t of the next unit
+// right away, before P V_t of this one: while the softmax exponentiates unit
+// i, the tensor pipe already computes unit i + 1's scores, so the softmax
+// warps go from one unit to the next without waiting for P V and S.  Before
+// writing P_t of unit i + 1 the softmax waits for P V_t of unit i (pv_done).
+// With D = 128 the O tiles fill TMEM and P_t overwrites the first 64 columns
+// of S_t: S_t of the next unit then follows P V_t of this one.
 //
 // Every wait is bounded.  A warpgroup decides to stop only at a reducing named
 // barrier that all four of its warps reach each unit, so a timeout seen by one
@@ -59,8 +70,9 @@ struct ShortSmem {
   static constexpr int kQBuf = D == 64 ? 2 : 1;
   static constexpr uint32_t kOffQ = 0, kOffK = 2 * kQBuf * kTile, kOffV = kOffK + kTile, kOffO = kOffV + kTile;
   // q_full[2], q_free[2], kv_full, kv_free, s_full[2], p_half[2], p_full[2], o_full, o_free[2],
-  // mma_done, stat[2 unit parities][2 tiles]
-  static constexpr int kBars = 20;
+  // mma_done, stat[2 unit parities][2 tiles], s_read[2], pv_done[2]
+  static constexpr int kBars = 24;
+  static constexpr bool kSplitP = D == 64;  // P_t in its own TMEM columns (see above)
   static constexpr uint32_t kOffBar = kOffO + 2 * kTile;
   static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kOffRow = kOffCtl + 16;         // float2 (max, sum) [2 units][2 tiles][128 rows]
@@ -105,6 +117,8 @@ __global__ void __launch_bounds__(kShortThreads, 1)
   // phase every second unit, so the epilogue (which must release O of unit i
   // before the softmax can reach unit i + 2) never sees it two phases ahead
   uint64_t* bar_stat = bars + 16;
+  uint64_t* bar_sread = bars + 20;  // [2] S_t of a unit loaded by its softmax (128 arrivals; kSplitP)
+  uint64_t* bar_pvd = bars + 22;    // [2] P V_t of a unit complete (kSplitP)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
   float2* rowstat = reinterpret_cast<float2*>(sm + S::kOffRow);  // [(i & 1) * 2 + t][row]
@@ -116,7 +130,7 @@ __global__ void __launch_bounds__(kShortThreads, 1)
 
   if (warp == 8 && lane == 0) {
     for (int i = 0; i < S::kBars; ++i)
-      mbar_init(bars + i, (i >= 8 && i <= 11) || i == 13 || i == 14 || i >= 16 ? 128 : 1);
+      mbar_init(bars + i, (i >= 8 && i <= 11) || i == 13 || i == 14 || (i >= 16 && i <= 21) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
@@ -274,16 +288,27 @@ __global__ void __launch_bounds__(kShortThreads, 1)
           return true;
         };
         // P V of tile t of unit i (after its P halves, and after the epilogue
-        // has read O_t of unit i - 1)
+        // has read O_t of unit i - 1); P_t from its own columns (kSplitP) or
+        // from the first 64 columns of S_t
         auto pv = [&](int i, int t) {
-          const uint32_t tS = t ? tS1 : tS0, tO = t ? tO1 : tO0;
+          const uint32_t tO = t ? tO1 : tO0;
+          const uint32_t tP = S::kSplitP ? tO + 64 : (t ? tS1 : tS0);
           if (!mbar_wait(bar_ph + t, i & 1, abort_flag, p.err, 24)) return false;
           if (i > 0 && !mbar_wait(bar_ofree + t, (i - 1) & 1, abort_flag, p.err, 25)) return false;
           tc_fence_after();
-          issue_pv_half<D>(tO, tS, dV, false, 0);
+          issue_pv_half<D>(tO, tP, dV, false, 0);
           if (!mbar_wait(bar_p + t, i & 1, abort_flag, p.err, 24)) return false;
           tc_fence_after();
-          issue_pv_half<D>(tO, tS, dV, true, 1);
+          issue_pv_half<D>(tO, tP, dV, true, 1);
+          if (S::kSplitP) umma_commit(bar_pvd + t);
+          return true;
+        };
+        // kSplitP: S_t of unit i + 1 once the softmax has loaded S_t of unit i
+        auto s_next = [&](int i, int t) {
+          if (!mbar_wait(bar_sread + t, i & 1, abort_flag, p.err, 29)) return false;
+          tc_fence_after();
+          issue_s<D>(t ? tS1 : tS0, qdesc(i + 1, t), dK);
+          umma_commit(bar_s + t);
           return true;
         };
         ShortUnit cur = short_unit(p, u0);
@@ -299,7 +324,27 @@ __global__ void __launch_bounds__(kShortThreads, 1)
         // K/V and its Q has its own buffer, so the two tiles' softmaxes
         // alternate; otherwise both P V first (a K/V reload needs P V of
         // unit i done, and a single Q buffer fills only after S_i).
-        for (int i = 0; i < cnt && go; ++i) {
+        for (int i = 0; i < cnt && go && S::kSplitP; ++i) {
+          // S of unit i + 1 first when it reuses K/V (its Q has its own
+          // buffer), then both P V of unit i; a K/V reload waits for P V of
+          // unit i and so comes after it
+          const bool more = i + 1 < cnt;
+          const ShortUnit nxt = more ? short_unit(p, u0 + i + 1) : cur;
+          const bool same_kv = more && nxt.kv_key == cur.kv_key;
+          if (same_kv) {
+            if (!(go = inputs_ready(i + 1, nxt) && s_next(i, 0) && s_next(i, 1))) break;
+            umma_commit(bar_qfree + (i + 1) % S::kQBuf);
+          }
+          if (!(go = pv(i, 0) && pv(i, 1))) break;
+          umma_commit(bar_o);
+          if (more && !same_kv) {
+            umma_commit(bar_kvfree);  // the next unit reloads K/V
+            if (!(go = inputs_ready(i + 1, nxt) && s_next(i, 0) && s_next(i, 1))) break;
+            umma_commit(bar_qfree + (i + 1) % S::kQBuf);
+          }
+          cur = nxt;
+        }
+        for (int i = 0; i < cnt && go && !S::kSplitP; ++i) {
           const bool more = i + 1 < cnt;
           const ShortUnit nxt = more ? short_unit(p, u0 + i + 1) : cur;
           const bool pingpong = S::kQBuf == 2 && more && nxt.kv_key == cur.kv_key;
@@ -336,6 +381,7 @@ __global__ void __launch_bounds__(kShortThreads, 1)
     const int r = threadIdx.x & 127;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tP = S::kSplitP ? tmem + 256 + t * 128 + 64 + lane_off : tS;  // where P_t goes
     const float sl2 = p.scale_log2;
     const int Lk = p.Lk;
     int mask_b = -1;
@@ -375,6 +421,10 @@ __global__ void __launch_bounds__(kShortThreads, 1)
           s[64 + c] = __uint_as_float(r2[c]);
           s[96 + c] = __uint_as_float(r3[c]);
         }
+      }
+      if (S::kSplitP) {  // S_t is in registers: the next unit's S_t may overwrite its columns
+        tc_fence_before();
+        mbar_arrive(bar_sread + t);
       }
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
@@ -422,7 +472,11 @@ __global__ void __launch_bounds__(kShortThreads, 1)
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
-        tmem_st32(tS + 32 * h2, pk);
+        if (S::kSplitP && h2 == 0 && i > 0) {  // P V_t of the previous unit has read the P_t columns
+          ok = ok && warp_wait(bar_pvd + t, (i - 1) & 1, abort_flag, p.err, 30);
+          tc_fence_after();
+        }
+        tmem_st32(tP + 32 * h2, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(h2 == 0 ? bar_ph + t : bar_p + t);
