@@ -44,6 +44,7 @@
 // warpgroup of tile t counts the S_t tiles and the units it has processed.
 // Every wait is bounded (2 s) and a timeout stops every role.
 #include <mutex>
+#include <type_traits>
 
 #include "fwd_common.cuh"
 
@@ -96,6 +97,14 @@ struct MaskTables {
   }
 };
 
+// A copy of x the compiler cannot see through, so values derived from it are
+// recomputed instead of kept live in registers.
+__device__ __forceinline__ int fresh_int(int x) {
+  int y;
+  asm volatile("mov.b32 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __device__ __forceinline__ PUnit persist_unit(const FwdParams& p, const MaskTables& mt, int unit) {
   PUnit u;
   u.q0 = (unit % p.q_blocks) * kBlockM;
@@ -107,7 +116,9 @@ __device__ __forceinline__ PUnit persist_unit(const FwdParams& p, const MaskTabl
   return u;
 }
 
-template <int D>
+// kMasked: the call has a key mask (the prologue builds the per-row tables); the
+// unmasked instance carries none of that state through its loops.
+template <int D, bool kMasked>
 __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __grid_constant__ FwdParams p) {
   using S = PSmem<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -137,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   const int G = gridDim.x;
   const int units = p.n_full;
   const int nt = p.n_kv_tiles;
-  const MaskTables mt{p.mask != nullptr ? sm + S::kOffMeta : nullptr, units / (p.q_blocks * p.Hc), nt};
+  const MaskTables mt{kMasked ? sm + S::kOffMeta : nullptr, units / (p.q_blocks * p.Hc), nt};
 
   if (warp == 8 && lane == 0) {
     for (int i = 0; i < S::kBars; ++i) mbar_init(bars + i, (i >= 14 && i < 18) || i == 20 || i == 21 ? 128 : 1);
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   const uint32_t tmem = *tmem_slot;
   grid_dep_wait();  // the kernel that wrote q / k (the RoPE pre-pass) has completed
 
-  if (p.mask != nullptr) {
+  if (kMasked) {
     // every batch row's mask bits (one 32-key word per thread per pass: two
     // 16-byte loads when the rows are aligned, else byte loads; keys past Lk
     // read as masked), then one warp per row lists the tiles holding a valid key
@@ -218,23 +229,27 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     if (warp == 8) {
       // ---------------- TMA producer ----------------
       if (lane == 0) {
-        int nq[2] = {0, 0};  // loads issued into Q tile t
-        int gk = 0, gv = 0;  // K and V tiles issued (ring stage i & 1, use i >> 1)
+        int nq0 = 0, nq1 = 0;  // loads issued into Q tile 0 / 1
+        int gk = 0, gv = 0;    // K and V tiles issued (ring stage i & 1, use i >> 1)
         bool ok = true;
+        // Q tile t of a unit; the previous unit's last S_t must have read the buffer
+        auto load_q = [&](auto tc, const PUnit& u, int qh) -> bool {
+          constexpr int t = decltype(tc)::value;
+          int& nq = t == 0 ? nq0 : nq1;
+          if (nq > 0 && !mbar_wait(bar_qe + t, (nq - 1) & 1, abort_flag, p.err, 40)) return false;
+          mbar_arrive_expect_tx(bar_qf + t, S::kTile);
+#pragma unroll
+          for (int c = 0; c < S::kChunks; ++c)
+            tma_load_4d(&p.tm_q, bar_qf + t, sQ + t * S::kTile + c * kChunkBytes, c * 64, u.q0 + t * kTileM, qh, u.b);
+          ++nq;
+          return true;
+        };
         for (int unit = blockIdx.x; unit < units && ok; unit += G) {
           const PUnit u = persist_unit(p, mt, unit);
           const int qh = p.q_head_off + u.hl;
           const int kvh = (p.kv_head_off + u.hl) / p.group;
-          for (int t = 0; t < (u.two ? 2 : 1) && ok; ++t) {
-            // the previous unit's last S_t must have read this buffer
-            if (nq[t] > 0 && !(ok = mbar_wait(bar_qe + t, (nq[t] - 1) & 1, abort_flag, p.err, 40))) break;
-            mbar_arrive_expect_tx(bar_qf + t, S::kTile);
-#pragma unroll
-            for (int c = 0; c < S::kChunks; ++c)
-              tma_load_4d(&p.tm_q, bar_qf + t, sQ + t * S::kTile + c * kChunkBytes, c * 64, u.q0 + t * kTileM, qh,
-                          u.b);
-            ++nq[t];
-          }
+          ok = load_q(std::integral_constant<int, 0>{}, u, qh) &&
+               (!u.two || load_q(std::integral_constant<int, 1>{}, u, qh));
           for (int j = 0; j < u.n && ok; ++j) {
             const int kv0 = mt.tile(u.b, j) * kTileN;
             int st = gk & 1;
@@ -257,8 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         // a load into a buffer is issued only after the one before it into that
         // buffer was consumed, so only the last load per Q tile and the last
         // two per ring can still be in flight
-        for (int t = 0; t < 2; ++t)
-          if (nq[t] > 0) drain_wait(bar_qf + t, (nq[t] - 1) & 1);
+        if (nq0 > 0) drain_wait(bar_qf + 0, (nq0 - 1) & 1);
+        if (nq1 > 0) drain_wait(bar_qf + 1, (nq1 - 1) & 1);
         for (int i = gk < 2 ? 0 : gk - 2; i < gk; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
         for (int i = gv < 2 ? 0 : gv - 2; i < gv; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
       }
@@ -266,37 +281,59 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     } else if (warp == 9) {
       // ---------------- MMA issuer ----------------
       if (lane == 0) {
-        const uint32_t tS[2] = {tmem, tmem + 128};
-        const uint32_t tO[2] = {tmem + 256, tmem + 384};
-        const SDesc dQ[2] = {sdesc_split(smem_u32(sQ), 16, 1024), sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024)};
+        // per-tile work as generic lambdas over a compile-time tile index, so
+        // no per-tile state lives in an indexed (local-memory) array
+        using T0 = std::integral_constant<int, 0>;
+        using T1 = std::integral_constant<int, 1>;
+        const SDesc dQ0 = sdesc_split(smem_u32(sQ), 16, 1024);
+        const SDesc dQ1 = sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024);
         const SDesc dK = sdesc_split(smem_u32(sK), 16, 1024);
         const SDesc dV = sdesc_split(smem_u32(sV), kChunkBytes, 1024);
         const uint32_t stage_step = S::kTile >> 4;
-        auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
-        auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
-        int nq[2] = {0, 0};  // units begun on Q tile t (q_full phase count)
-        int np[2] = {0, 0};  // P_t tiles consumed (p_half / p_full phase count)
-        bool go = true;
+        int nq0 = 0, nq1 = 0;  // units begun on Q tile t (q_full phase count)
+        int np0 = 0, np1 = 0;  // P_t tiles consumed (p_half / p_full phase count)
         // S_t of (unit, tile j) whose K sits in ring slot g; j == 0 first waits
         // for the unit's Q tile t, j == n - 1 (n: the unit's tile count) then
         // releases Q tile t
-        auto issue_s_step = [&](int t, int j, int n, int g) {
+        auto issue_s_step = [&](auto tc, int j, int n, int g) -> bool {
+          constexpr int t = decltype(tc)::value;
+          int& nq = t == 0 ? nq0 : nq1;
           if (j == 0) {
-            if (!mbar_wait(bar_qf + t, nq[t] & 1, abort_flag, p.err, 43)) return false;
-            ++nq[t];
+            if (!mbar_wait(bar_qf + t, nq & 1, abort_flag, p.err, 43)) return false;
+            ++nq;
           }
           tc_fence_after();
-          issue_s<D>(tS[t], dQ[t], kdesc(g & 1));
+          issue_s<D>(tmem + 128 * t, t == 0 ? dQ0 : dQ1, SDesc{dK.lo + (g & 1) * stage_step, dK.hi});
           umma_commit(bar_s + t);
           if (j == n - 1) umma_commit(bar_qe + t);
           return true;
         };
+        // P V_t of (unit, tile j) with V in ring stage st; the first P V of a
+        // unit overwrites O_t, so it waits for the previous unit's epilogue on
+        // this tile to have read O_t
+        auto pv_step = [&](auto tc, int j, int n, int st) -> bool {
+          constexpr int t = decltype(tc)::value;
+          int& np = t == 0 ? np0 : np1;
+          const int nq = t == 0 ? nq0 : nq1;
+          const SDesc vd{dV.lo + st * stage_step, dV.hi};
+          if (!mbar_wait(bar_ph + t, np & 1, abort_flag, p.err, 45)) return false;
+          if (j == 0 && nq > 1 && !mbar_wait(bar_oe + t, (nq - 2) & 1, abort_flag, p.err, 47)) return false;
+          tc_fence_after();
+          issue_pv_half<D>(tmem + 256 + 128 * t, tmem + 128 * t, vd, j > 0, 0);
+          if (!mbar_wait(bar_p + t, np & 1, abort_flag, p.err, 45)) return false;
+          tc_fence_after();
+          issue_pv_half<D>(tmem + 256 + 128 * t, tmem + 128 * t, vd, true, 1);
+          ++np;
+          if (j == n - 1) umma_commit(bar_of + t);
+          return true;
+        };
+        bool go = true;
         int unit = blockIdx.x;
         PUnit u = persist_unit(p, mt, unit);
         int g = 0;  // ring slot of the current tile
         if (unit < units) {
-          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(0, 0, u.n, 0);
-          if (go && u.two) go = issue_s_step(1, 0, u.n, 0);
+          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(T0{}, 0, u.n, 0);
+          if (go && u.two) go = issue_s_step(T1{}, 0, u.n, 0);
           if (go) umma_commit(bar_ke + 0);
         }
         for (; unit < units && go; unit += G) {
@@ -306,37 +343,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
           const int n = u.n;
           for (int j = 0; j < n; ++j, ++g) {
             const int st = g & 1;
-            // the step after this one: (unit, j + 1) or (next unit, 0)
+            // the step after this one: (unit, j + 1) or (next unit, 0); S_t of
+            // it right behind P V_t of this one (a unit with no rows in Q tile
+            // 1 issues neither P V1 nor S1)
             const bool more = j + 1 < n || has_next;
             const bool nx_two = j + 1 < n ? u.two : v.two;
             const int nj = j + 1 < n ? j + 1 : 0;
             const int nn = j + 1 < n ? n : v.n;
             const int g1 = g + 1, st1 = g1 & 1;
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              if (!go) break;
-              if (t == 0 || u.two) {
-                if (!(go = mbar_wait(bar_ph + t, np[t] & 1, abort_flag, p.err, 45))) break;
-                if (t == 0 && !(go = mbar_wait(bar_vf + st, (g >> 1) & 1, abort_flag, p.err, 46))) break;
-                // the first P V of a unit overwrites O_t: the epilogue of the
-                // previous unit on this tile must have read it
-                if (j == 0 && nq[t] > 1 && !(go = mbar_wait(bar_oe + t, (nq[t] - 2) & 1, abort_flag, p.err, 47)))
-                  break;
-                tc_fence_after();
-                issue_pv_half<D>(tO[t], tS[t], vdesc(st), j > 0, 0);
-                if (!(go = mbar_wait(bar_p + t, np[t] & 1, abort_flag, p.err, 45))) break;
-                tc_fence_after();
-                issue_pv_half<D>(tO[t], tS[t], vdesc(st), true, 1);
-                ++np[t];
-                if (j == n - 1) umma_commit(bar_of + t);
-              }
-              // S_t of the next step right behind P V_t of this one (a unit with
-              // no rows in Q tile 1 issues no S1)
-              if (more && (t == 0 || nx_two)) {
-                if (t == 0 && !(go = mbar_wait(bar_kf + st1, (g1 >> 1) & 1, abort_flag, p.err, 48))) break;
-                go = issue_s_step(t, nj, nn, g1);
-              }
-            }
+            go = mbar_wait(bar_vf + st, (g >> 1) & 1, abort_flag, p.err, 46) && pv_step(T0{}, j, n, st);
+            if (go && more)
+              go = mbar_wait(bar_kf + st1, (g1 >> 1) & 1, abort_flag, p.err, 48) && issue_s_step(T0{}, nj, nn, g1);
+            if (go && u.two) go = pv_step(T1{}, j, n, st);
+            if (go && more && nx_two) go = issue_s_step(T1{}, nj, nn, g1);
             if (!go) break;
             umma_commit(bar_ve + st);
             if (more) umma_commit(bar_ke + st1);
@@ -362,10 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     int nunit = 0;  // units processed on this tile
     bool ok = true;
     for (int unit = blockIdx.x; unit < units && ok; unit += G) {
-      const PUnit u = persist_unit(p, mt, unit);
-      if (t == 1 && !u.two) continue;
-      const int n = u.n;
-      const int row = u.q0 + t * kTileM + r;
+      // only the tile count, the mask flag and the batch row stay live through
+      // the tile loop; the epilogue decodes the unit again
+      int n, ub;
+      bool umask;
+      {
+        const PUnit u = persist_unit(p, mt, unit);
+        if (t == 1 && !u.two) continue;
+        n = u.n;
+        ub = u.b;
+        umask = kMasked && u.mask;
+      }
       float m = -INFINITY;  // running max, log2 domain (lazy)
       float l = 0.f;
       for (int i = 0; i < n; ++i, ++ns) {
@@ -388,12 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
           }
         }
         // masked keys and keys past Lk get -inf logits
-        const int kv0 = mt.tile(u.b, i) * kTileN;
-        const bool masked_tile = u.mask || kv0 + kTileN > Lk;
+        const int kv0 = (kMasked ? mt.tile(ub, i) : i) * kTileN;
+        const bool masked_tile = umask || kv0 + kTileN > Lk;
         if (masked_tile) {
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
-            uint32_t bits = u.mask ? mt.word(u.b, kv0 / 32 + w) : 0xffffffffu;
+            uint32_t bits = umask ? mt.word(ub, kv0 / 32 + w) : 0xffffffffu;
             const int lim = Lk - (kv0 + 32 * w);
             if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
 #pragma unroll
@@ -462,7 +488,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
       }
       if (!ok) break;
 
-      // ---- epilogue: O_t / l, gated, straight to global memory ----
+      // ---- epilogue: O_t / l, gated, stored with TMA ----
+      const PUnit u = persist_unit(p, mt, fresh_int(unit));
+      const int row = u.q0 + t * kTileM + r;
       uint32_t g2 = 0x3f803f80u;  // bf16x2 (1, 1)
       if (p.gate != nullptr && row < p.Lq) {
         const float gv = gate_bf16(__bfloat162float(
@@ -552,15 +580,21 @@ cudaError_t prepare_fwd_persist(int D, size_t smem) {
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
   const int di = D == 128 ? 1 : 0;
   std::lock_guard<std::mutex> lock(g_persist_mu);
-  const void* k = D == 128 ? (const void*)fwd_persist_sm100_kernel<128> : (const void*)fwd_persist_sm100_kernel<64>;
+  const void* ks[2] = {
+      D == 128 ? (const void*)fwd_persist_sm100_kernel<128, false> : (const void*)fwd_persist_sm100_kernel<64, false>,
+      D == 128 ? (const void*)fwd_persist_sm100_kernel<128, true> : (const void*)fwd_persist_sm100_kernel<64, true>};
   if (!g_persist_regs_ok[dev][di]) {
-    cudaFuncAttributes fa;
-    if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
-    if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
+    for (const void* k : ks) {
+      cudaFuncAttributes fa;
+      if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
+      if (fa.numRegs != (int)kLaunchRegs) return cudaErrorInvalidConfiguration;
+    }
     g_persist_regs_ok[dev][di] = true;
   }
   if (smem > g_persist_smem_set[dev][di]) {
-    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
+    for (const void* k : ks)
+      if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+        return e;
     g_persist_smem_set[dev][di] = smem;
   }
   return cudaSuccess;
@@ -569,8 +603,11 @@ cudaError_t prepare_fwd_persist(int D, size_t smem) {
 // p.n_full is the unit count; `ctas` <= units CTAs walk them round-robin
 // (prepare_fwd_persist must have succeeded for D and at least smem).
 cudaError_t launch_fwd_persist(const FwdParams& p, int D, int ctas, size_t smem, cudaStream_t s) {
-  if (D == 128) return launch_pdl(fwd_persist_sm100_kernel<128>, dim3(ctas), dim3(kThreads), smem, s, p);
-  return launch_pdl(fwd_persist_sm100_kernel<64>, dim3(ctas), dim3(kThreads), smem, s, p);
+  const bool m = p.mask != nullptr;
+  if (D == 128 && m) return launch_pdl(fwd_persist_sm100_kernel<128, true>, dim3(ctas), dim3(kThreads), smem, s, p);
+  if (D == 128) return launch_pdl(fwd_persist_sm100_kernel<128, false>, dim3(ctas), dim3(kThreads), smem, s, p);
+  if (m) return launch_pdl(fwd_persist_sm100_kernel<64, true>, dim3(ctas), dim3(kThreads), smem, s, p);
+  return launch_pdl(fwd_persist_sm100_kernel<64, false>, dim3(ctas), dim3(kThreads), smem, s, p);
 }
 
 }  // namespace ltx
