@@ -192,7 +192,7 @@ struct SplitChoice {
 };
 
 SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
-  constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBytesPerUs = 5.0e6, kLaunchUs = 3.0;
+  constexpr double kTileUs = 1.83, kCtaUs = 9.0, kBytesPerUs = 5.0e6, kLaunchUs = 3.0;
   auto unit_us = [&](int sp) { return kCtaUs + (double)((kv_tiles + sp - 1) / sp) * kTileUs; };
   const int64_t waves = units / sms, rem = units % sms;
   const double whole = (double)((units + sms - 1) / sms) * unit_us(1);
@@ -214,14 +214,20 @@ SplitChoice tail_splits(int64_t units, int sms, int kv_tiles, int D) {
   return best_us < 0.985 * whole ? best : SplitChoice{0, 1, whole};
 }
 
-// The persistent forward (fwd_persist_sm100.cu) on the same terms: one CTA
-// per SM walks ceil(units / sms) units back to back; the per-CTA setup is paid
-// once, and a unit boundary costs ~1.5 us (the epilogue of one unit on the
-// softmax warps while the next unit's first S runs), not a whole t_cta.
+// The persistent forward (fwd_persist_sm100.cu) against one CTA per unit, with
+// constants fitted to CUDA-event timings on a B200 (32 heads x 3,120 queries,
+// D = 128, 2 to 25 KV tiles per unit, L2 flushed):
+//   one CTA per unit:  ceil(units / sms) * (1.83 us * kv_tiles + 9.0 us)
+//   persistent:        4.6 us + ceil(units / sms) * (2.07 us * kv_tiles + 4.6 us)
+// A unit boundary costs the persistent kernel less than a CTA does the other
+// (4.6 against 9.0 us), but its KV step is ~13% slower, so it wins for short
+// KV ranges (below ~12 tiles at three rounds: 30.8 against 37.8 us at 2 tiles)
+// and loses at the 3,120-token self-attention (173.5 against 163.8 us).
+double tiled_us(int64_t units, int sms, int kv_tiles) {
+  return (double)((units + sms - 1) / sms) * (1.83 * kv_tiles + 9.0);
+}
 double persist_us(int64_t units, int sms, int kv_tiles) {
-  constexpr double kTileUs = 1.8, kCtaUs = 8.0, kBoundaryUs = 1.5;
-  const double rounds = (double)((units + sms - 1) / sms);
-  return kCtaUs + rounds * ((double)kv_tiles * kTileUs + kBoundaryUs);
+  return 4.6 + (double)((units + sms - 1) / sms) * (2.07 * kv_tiles + 4.6);
 }
 
 // Uniform split count (every unit split) for masked or banded calls, whose
@@ -310,9 +316,11 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
       const bool opaque = a->key_mask != nullptr || P->causal || P->window > 0;  // per-unit work unknown
       const bool banded = P->causal || P->window > 0;
       // a key mask but no band: units of one batch row walk the same live tiles,
-      // which the persistent kernel lists once per row (shared memory permitting)
+      // which the persistent kernel lists once per row (shared memory permitting);
+      // the live count is unknown here, so the model is evaluated at kv_tiles
       const bool persist_masked = a->key_mask != nullptr && !banded && units >= sms && P->kv_tiles > 1 &&
-                                  fwd_persist_smem_bytes(s.D, s.B, P->kv_tiles, true) <= kMaxDynamicSmem;
+                                  fwd_persist_smem_bytes(s.D, s.B, P->kv_tiles, true) <= kMaxDynamicSmem &&
+                                  persist_us(units, sms, P->kv_tiles) < tiled_us(units, sms, P->kv_tiles);
       if (units < sms && P->kv_tiles > 1 && opaque) {
         // fewer units than SMs: as many splits as keep one wave
         P->splits = std::max(1, std::min({(int)(sms / units), P->kv_tiles, kMaxSplits}));

@@ -175,7 +175,8 @@ def test_grouped_kv_heads_take_no_rotary():
 
 @pytest.mark.parametrize("shape,want", [
     # (B, H, Lq, Lk, D), (kernel, splits, split_units, launches); 148 SMs (no device here)
-    ((1, 32, 3120, 3120, 128), (3, 1, 0, 1)),     # config 2: 416 units on 148 persistent CTAs
+    ((1, 32, 3120, 3120, 128), (1, 1, 0, 1)),     # config 2: 416 units, one CTA each
+    ((1, 32, 3120, 512, 128), (3, 1, 0, 1)),      # 4 KV tiles: the persistent kernel's cheaper unit boundary wins
     ((1, 32, 29760, 29760, 128), (1, 3, 44, 2)),  # config 5 on 1 GPU: 25 waves + 44 units split 3 ways
     ((1, 32, 3120, 1024, 128, "mask"), (3, 1, 0, 1)),  # config 3: masked, 416 units, persistent
     ((1, 32, 3120, 126, 64), (2, 1, 0, 1)),       # config 4b: one KV tile -> persistent kernel
