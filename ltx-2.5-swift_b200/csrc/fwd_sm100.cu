@@ -39,17 +39,6 @@
 // quarter of them (exp2_poly2; kPolyCols keeps the option, at 0) and paired
 // f16 exponentials (ex2.approx.f16x2; the widening conversions share the MUFU pipe).
 //
-// Query RoPE in the kernel.  When the call gives a bf16 rotary table for q
-// (FwdParams.q_cos != null), the TMA loads the caller's un-rotated Q tile and
-// its softmax warpgroup rotates it in shared memory before the first S: thread
-// r pairs the 16-byte unit j of row r with its partner D/2 elements on (the
-// same swizzled position in the next 64-column chunk for D = 128, unit j + 4
-// of the same chunk for D = 64), applies rope_bf16x8 -- the pre-pass's
-// arithmetic, so the bits are the pre-pass's -- writes both back, and arrives
-// on q_rot[t], which the MMA thread waits for instead of the TMA barrier.  The
-// table rows are loaded while the tile is in flight.  Only K is then rotated by
-// the pre-pass: at the 3,120-token shape that halves its traffic.
-//
 // Keys: a tile whose keys are all masked is skipped outright (its weight is
 // exactly zero); partial tiles and the ragged tail get -inf logits per
 // column.  A batch row whose mask has no valid key attends to all keys
@@ -86,8 +75,7 @@ struct Smem {
                             kOffV0 = 4 * kTile, kOffV1 = 5 * kTile;
   // q0_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_full, p_half[2], q1_full
   static constexpr uint32_t kOffBar = 6 * kTile;
-  // ... q_rot[2] (barriers 17, 18)
-  static constexpr uint32_t kOffCtl = kOffBar + 19 * 8;  // tmem slot, abort, n_tiles
+  static constexpr uint32_t kOffCtl = kOffBar + 17 * 8;  // tmem slot, abort, n_tiles
   static constexpr uint32_t kOffTiles = kOffCtl + 16;    // uint16 [kMaxKvTiles]
   static constexpr uint32_t kOffBits = kOffTiles + 2 * kMaxKvTiles;  // uint32 mask bits
 };
@@ -125,46 +113,6 @@ __device__ __forceinline__ int ctaid_x_fresh() {
   return x;
 }
 
-// Rotate row r of a Q tile in shared memory (see "Query RoPE in the kernel"):
-// table units first (they overlap the tile's TMA load), then the tile, then the
-// rotation in place; arrives on `done` in every case so the MMA thread never
-// waits on a row that gave up.  Rows past Lq (zero-filled) are left as loaded.
-template <int D>
-__device__ __forceinline__ bool rotate_q_row(const FwdParams& p, uint8_t* tile, uint64_t* loaded, uint64_t* done,
-                                             int row, int r, int b, int h, volatile int* abort_flag) {
-  constexpr int kUnits = D / 16;  // 16-byte units of x1 per row (8 rotary pairs each)
-  const bool live = row < p.Lq;
-  uint4 c[kUnits], s[kUnits];
-  if (live) {
-    const int64_t toff = (int64_t)b * p.qt_sb + (int64_t)h * p.qt_sh + (int64_t)row * p.qt_st;
-    const uint4* cp = reinterpret_cast<const uint4*>(p.q_cos + toff);
-    const uint4* sp = reinterpret_cast<const uint4*>(p.q_sin + toff);
-#pragma unroll
-    for (int j = 0; j < kUnits; ++j) {
-      c[j] = __ldg(cp + j);
-      s[j] = __ldg(sp + j);
-    }
-  }
-  const bool ok = warp_wait(loaded, 0, abort_flag, p.err, 11);
-  if (ok && live) {
-    uint8_t* rowp = tile + r * 128;
-#pragma unroll
-    for (int j = 0; j < kUnits; ++j) {
-      // x1: unit j of chunk 0; x2: D = 128 the same unit of chunk 1, D = 64 unit j + 4
-      uint4* a1 = reinterpret_cast<uint4*>(rowp + ((j ^ (r & 7)) << 4));
-      uint4* a2 = D == 128 ? reinterpret_cast<uint4*>(rowp + kChunkBytes + ((j ^ (r & 7)) << 4))
-                           : reinterpret_cast<uint4*>(rowp + (((j + 4) ^ (r & 7)) << 4));
-      uint4 o1, o2;
-      rope_bf16x8(*a1, *a2, c[j], s[j], o1, o2);
-      *a1 = o1;
-      *a2 = o2;
-    }
-    fence_proxy_async_smem();  // the MMA reads the tile through the async proxy
-  }
-  mbar_arrive(done);
-  return ok;
-}
-
 // kBanded: causal / sliding-window rows and the free-row rule (the Gemma
 // encoder's self-attention); the DiT's attention runs the kBanded = false
 // instance, which carries none of that per-row state.
@@ -180,7 +128,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kOffBar);
   uint64_t* bar_q = bars + 0;   // Q tile 0 loaded
   uint64_t* bar_q1 = bars + 16; // Q tile 1 loaded
-  uint64_t* bar_qrot = bars + 17;  // [2] Q tile t rotated in shared memory (128 arrivals; q_cos != null)
   uint64_t* bar_kf = bars + 1;   // [2]
   uint64_t* bar_ke = bars + 3;   // [2]
   uint64_t* bar_vf = bars + 5;   // [2]
@@ -210,8 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
   // barrier after the __syncthreads below.)
   const int qh = p.q_head_off + hl;
   if (warp == 8 && lane == 0) {
-    for (int i = 0; i < 19; ++i)
-      mbar_init(bars + i, (i == 11 || i == 12 || i == 14 || i == 15 || i == 17 || i == 18) ? 128 : 1);
+    for (int i = 0; i < 17; ++i) mbar_init(bars + i, (i == 11 || i == 12 || i == 14 || i == 15) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
@@ -373,16 +319,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
       const uint32_t stage_step = S::kTile >> 4;
       auto kdesc = [&](int st) { return SDesc{dK.lo + st * stage_step, dK.hi}; };
       auto vdesc = [&](int st) { return SDesc{dV.lo + st * stage_step, dV.hi}; };
-      const bool qrope = p.q_cos != nullptr;
-      bool go = mbar_wait(qrope ? bar_qrot : bar_q, 0, abort_flag, p.err, 3) &&
-                mbar_wait(bar_kf, 0, abort_flag, p.err, 4);
+      bool go = mbar_wait(bar_q, 0, abort_flag, p.err, 3) && mbar_wait(bar_kf, 0, abort_flag, p.err, 4);
       if (go) {
         tc_fence_after();
         issue_s<D>(tS0, dQ0, kdesc(0));
         umma_commit(bar_s + 0);
       }
       if (go && two) {
-        go = mbar_wait(qrope ? bar_qrot + 1 : bar_q1, 0, abort_flag, p.err, 3);
+        go = mbar_wait(bar_q1, 0, abort_flag, p.err, 3);
         if (go) {
           tc_fence_after();
           issue_s<D>(tS1, dQ1, kdesc(0));
@@ -446,8 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     float m = -INFINITY;  // running max, log2 domain (lazy)
     float l = 0.f;
     bool ok = true;
-    if (p.q_cos != nullptr) ok = rotate_q_row<D>(p, sQ + t * S::kTile, t == 0 ? bar_q : bar_q1, bar_qrot + t, row,
-                                                  threadIdx.x & 127, b, p.head_begin + hl, abort_flag);
     for (int i = 0; i < n; ++i) {
       if (!warp_wait(my_s, i & 1, abort_flag, p.err, 9)) { ok = false; break; }
       tc_fence_after();

@@ -259,7 +259,6 @@ int uniform_splits(int64_t units, int sms, int kv_tiles, double out_elems) {
 struct FwdPlan {
   Shape s;
   bool rope_q, rope_k;
-  bool q_fused;              // q is rotated inside the one-CTA-per-unit kernel (no workspace copy)
   const ltxattn_rotary* kr;  // table used for k
   int kv_heads, group;        // grouped KV heads: query head h reads kv head h / group
   int causal, window;
@@ -353,24 +352,12 @@ int plan_fwd(const ltxattn_fwd_args* a, FwdPlan* P) {
     }
     if (P->splits == 1) P->n_tail = 0;
   }
-  // q's rotation moves into the one-CTA-per-unit bf16 kernel when its table can
-  // be read as 16-byte rows and q itself can be loaded by TMA (fwd_sm100.cu); k
-  // is still rotated by the pre-pass
-  {
-    const ltxattn_rotary& qr = a->q_rotary;
-    const ltxattn_tensor& qt = a->q;
-    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    P->q_fused = s.dtype == LTXATTN_BF16 && P->rope_q && !P->short_kv && !P->persist && al16(qr.cos) &&
-                 al16(qr.sin) && qr.stride_b % 8 == 0 && qr.stride_h % 8 == 0 && qr.stride_t % 8 == 0 &&
-                 al16(qt.data) && (s.B == 1 || qt.stride_b % 8 == 0) && (s.H == 1 || qt.stride_h % 8 == 0) &&
-                 qt.stride_t % 8 == 0 && qt.stride_b >= 0 && qt.stride_h >= 0 && qt.stride_t >= 0;
-  }
   P->n_full = P->units - P->n_tail;
   if (P->n_full + P->n_tail * P->splits > (int64_t)INT32_MAX)
     return fail(LTXATTN_ERR_UNSUPPORTED, "%lld query blocks exceed one launch", (long long)P->units);
   size_t off = 0;
   P->off_q = off;
-  if (P->rope_q && !P->q_fused) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
+  if (P->rope_q) off += align256((size_t)s.B * s.Hc * s.Lq * s.D * s.esize);
   P->off_k = off;
   if (P->rope_k) off += align256((size_t)s.B * s.Hc * s.Lk * s.D * s.esize);
   P->off_po = off;
@@ -501,7 +488,7 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   const Shape& s = P.s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = s.dtype == LTXATTN_BF16;
-  if ((rc = check_tensor(a->q, "q", s, bf16 && (!P.rope_q || P.q_fused)))) return rc;
+  if ((rc = check_tensor(a->q, "q", s, bf16 && !P.rope_q))) return rc;
   if ((rc = check_tensor(a->k, "k", s, bf16 && !P.rope_k))) return rc;
   if ((rc = check_tensor(a->v, "v", s, bf16))) return rc;
   if ((rc = check_tensor(a->out, "out", s, bf16))) return rc;
@@ -531,14 +518,12 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     // k is always rotated with q (with its own table or q's); one launch
     // rotates both into the workspace
     rope_k = rope_params(a->k, *P.kr, s, s.Lk, ws + P.off_k);
-    if (!P.q_fused) {
-      rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
-      q.data = ws + P.off_q;
-      q.stride_t = s.D;
-      q.stride_h = (int64_t)s.Lq * s.D;
-      q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
-      q_head_off = 0;
-    }
+    rope_q = rope_params(a->q, a->q_rotary, s, s.Lq, ws + P.off_q);
+    q.data = ws + P.off_q;
+    q.stride_t = s.D;
+    q.stride_h = (int64_t)s.Lq * s.D;
+    q.stride_b = (int64_t)s.Hc * s.Lq * s.D;
+    q_head_off = 0;
   }
   ltxattn_tensor v = a->v;
   if (P.rope_k) {
@@ -552,7 +537,7 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
 
   auto launch_pre_pass = [&]() -> int {
     if (!P.rope_q) return LTXATTN_OK;
-    const cudaError_t er = P.q_fused ? launch_rope(&rope_k, nullptr, bf16, st) : launch_rope(&rope_q, &rope_k, bf16, st);
+    const cudaError_t er = launch_rope(&rope_q, &rope_k, bf16, st);
     return er == cudaSuccess ? LTXATTN_OK : cuda_fail(er, "rope launch");
   };
   if (!bf16) {
@@ -592,16 +577,9 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
   }
 
   FwdParams p{};
-  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, (P.rope_q && !P.q_fused) ? s.Hc : s.H, s.B, q.stride_t,
+  if ((rc = make_tmap(&p.tm_q, q.data, s.D, s.Lq, P.rope_q ? s.Hc : s.H, s.B, q.stride_t,
                       q.stride_h, q.stride_b, "q")))
     return rc;
-  if (P.q_fused) {
-    p.q_cos = static_cast<const __nv_bfloat16*>(a->q_rotary.cos);
-    p.q_sin = static_cast<const __nv_bfloat16*>(a->q_rotary.sin);
-    p.qt_sb = a->q_rotary.stride_b;
-    p.qt_sh = a->q_rotary.stride_h;
-    p.qt_st = a->q_rotary.stride_t;
-  }
   if ((rc = make_tmap(&p.tm_k, k.data, s.D, s.Lk, P.rope_k ? s.Hc : P.kv_heads, s.B, k.stride_t, k.stride_h,
                       k.stride_b, "k")))
     return rc;

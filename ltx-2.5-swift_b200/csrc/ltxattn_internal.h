@@ -54,12 +54,6 @@ struct FwdParams {
   float* part_lse;   // [splits][n_tail][256] log2 domain (n_tail > 0)
   const __nv_bfloat16* gate;  // [B, Lq, H] gate logits or null (global head index)
   int64_t g_sb, g_st, g_sh;
-  // bf16 rotary table of q, applied in the kernel (null: q arrives rotated or
-  // needs no rotation); element (b, global head h, token t, pair i) at
-  // b * qt_sb + h * qt_sh + t * qt_st + i, rows 16-byte aligned
-  const __nv_bfloat16* q_cos;
-  const __nv_bfloat16* q_sin;
-  int64_t qt_sb, qt_sh, qt_st;
   int* err;
 };
 

@@ -236,8 +236,7 @@ def test_selftest_and_comm_size_refuse_bad_arguments():
 
 def test_memory_plan_counts_the_call_buffers():
     # config 2 (3120 tokens, 32 heads of 128, bf16, rotary): q, k, v, out are 25.6 MB
-    # each, lse 0.4 MB, and the rotated k copy in the workspace another 25.6 MB (q is
-    # rotated inside the attention kernel)
+    # each, lse 0.4 MB, and the rotated q / k copies in the workspace another 2 x 25.6 MB
     L = _lib.load()
     a = _lib.MemoryPlanArgs(dtype=_lib.BF16, batch=1, heads=32, tokens=3120, head_dim=128, rotary=1,
                             training=0, resident_bytes=42_060_000_000, available_bytes=180_000_000_000,
@@ -246,7 +245,7 @@ def test_memory_plan_counts_the_call_buffers():
     assert L.ltxattn_memory_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK, _lib.last_error()
     act = 3120 * 32 * 128 * 2
     assert info.tensor_bytes == 4 * act + 3120 * 32 * 4
-    assert info.workspace_bytes >= act  # rotated k
+    assert info.workspace_bytes >= 2 * act  # rotated q and k
     assert info.backward_bytes == 0
     assert info.peak_bytes == 42_060_000_000 + info.tensor_bytes + info.workspace_bytes
     want_headroom = 180_000_000_000 - round(info.peak_bytes * 1.15)

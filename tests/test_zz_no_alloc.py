@@ -65,7 +65,7 @@ def _check(got, ref):
 
 @pytest.mark.parametrize("shape,rope", [
     ((1, 8, 126, 3120, 64), True),     # short queries: split-KV partials live in the scratch
-    ((1, 4, 300, 300, 128), True),     # the rotated k copy lives in the scratch (q rotates in the kernel)
+    ((1, 4, 300, 300, 128), True),     # rotated q / k copies live in the scratch
     ((2, 4, 200, 1000, 64), False),    # split-KV without rotary tables
 ])
 def test_noalloc_matches_fwd_on_two_calls(shape, rope):
@@ -95,7 +95,7 @@ def test_noalloc_against_the_oracle():
 
 
 def test_noalloc_refuses_scratch_beyond_its_array():
-    B, H, Lq, Lk, D = 1, 64, 4096, 4096, 128  # the rotated k copy alone needs 64 MiB
+    B, H, Lq, Lk, D = 1, 64, 4096, 4096, 128  # rotated q and k copies alone need 128 MiB
     q, k, v, qr, kr = _case(1, 1, 8, 8, D, seed=1, rope=True)
     a = _lib.FwdArgs()
     a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, B, H, Lq, Lk, D
