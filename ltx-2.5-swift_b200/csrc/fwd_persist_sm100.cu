@@ -155,6 +155,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
+    // the first unit's Q does not depend on the key mask: its load overlaps
+    // the rest of the prologue (TMEM allocation, the mask tables)
+    if ((int)blockIdx.x < units) {
+      grid_dep_wait();  // the kernel that wrote q (the RoPE pre-pass) has completed
+      const PUnit u0 = persist_unit(p, MaskTables{nullptr, 0, nt}, blockIdx.x);
+      for (int t = 0; t < (u0.two ? 2 : 1); ++t) {
+        mbar_arrive_expect_tx(bar_qf + t, S::kTile);
+#pragma unroll
+        for (int c = 0; c < S::kChunks; ++c)
+          tma_load_4d(&p.tm_q, bar_qf + t, sQ + t * S::kTile + c * kChunkBytes, c * 64, u0.q0 + t * kTileM,
+                      p.q_head_off + u0.hl, u0.b);
+      }
+    }
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
     tma_prefetch_desc(&p.tm_o);
@@ -248,8 +261,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
           const PUnit u = persist_unit(p, mt, unit);
           const int qh = p.q_head_off + u.hl;
           const int kvh = (p.kv_head_off + u.hl) / p.group;
-          ok = load_q(std::integral_constant<int, 0>{}, u, qh) &&
-               (!u.two || load_q(std::integral_constant<int, 1>{}, u, qh));
+          if (unit == (int)blockIdx.x) {  // loaded in the prologue
+            nq0 = 1;
+            nq1 = u.two ? 1 : 0;
+          } else {
+            ok = load_q(std::integral_constant<int, 0>{}, u, qh) &&
+                 (!u.two || load_q(std::integral_constant<int, 1>{}, u, qh));
+          }
           for (int j = 0; j < u.n && ok; ++j) {
             const int kv0 = mt.tile(u.b, j) * kTileN;
             int st = gk & 1;
