@@ -52,10 +52,10 @@ EXTRAS = ("c3", "c4a", "c4b", "c4c", "c5")
 # Values for all 32 heads, from the capture summarised in the file named beside
 # each number (which gives the command); scaled by heads for a rank's block.
 _TRAFFIC_SRC = "profiles/dram_traffic_attention_launches.md"
-TRAFFIC = {"c2": (79312128, _TRAFFIC_SRC), "c3": (27962368, _TRAFFIC_SRC), "c4a": (1667840, _TRAFFIC_SRC),
-           "c4b": (13873408, _TRAFFIC_SRC), "c4c": (26343168, _TRAFFIC_SRC),
+TRAFFIC = {"c2": (78838016, _TRAFFIC_SRC), "c3": (27749120, _TRAFFIC_SRC), "c4a": (1667840, _TRAFFIC_SRC),
+           "c4b": (13884672, _TRAFFIC_SRC), "c4c": (26344704, _TRAFFIC_SRC),
            # captured on 4 of the 32 heads; scaled by heads
-           "c5": (106580736 * 8, _TRAFFIC_SRC + " (4-head capture x 8)")}
+           "c5": (107117824 * 8, _TRAFFIC_SRC + " (4-head capture x 8)")}
 
 
 class L2Flush:
