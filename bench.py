@@ -431,7 +431,11 @@ def measure_e2e(ctx, args, case):
     q, k, v = case["q"], case["k"], case["v"]
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    chunks = min(4, q.shape[1])
+    # head blocks pay off when the output copy is large enough to overlap the
+    # input copies (configs 2, 3, 4b, 5); a small output (config 4a, or 4c's 126
+    # query rows) leaves nothing to overlap, and more blocks only add copies and
+    # launches
+    chunks = min(4, q.shape[1]) if hout.numel() * hout.element_size() >= (4 << 20) else 1
     ha = HostAttention(q, k, v, key_mask=case["mask"], q_rotary=case["qrot"], k_rotary=case["krot"], chunks=chunks)
     ha.run(hq, hk, hv, hout, stream=ctx.stream)  # warm
     steps = max(1, min(args.steps, 10))
@@ -447,7 +451,8 @@ def measure_e2e(ctx, args, case):
     return {"value": round(w.flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
             "d2h_bytes_per_step": hout.numel() * 2,
-            "pipeline": f"{chunks} head blocks, H2D / attention / D2H overlapped on three streams"}
+            "pipeline": (f"{chunks} head blocks, H2D / attention / D2H overlapped on three streams" if chunks > 1
+                         else "one block: H2D, attention, D2H on three streams in sequence")}
 
 
 def measure_gather(ctx, args, case):
