@@ -39,15 +39,6 @@
 // TMEM S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).  A unit of
 // the ragged last query block with no rows in Q tile 1 runs tile 0 alone.
 //
-// One-tile units (a masked call whose every batch row has one live KV tile: the
-// text cross-attention) would otherwise serialise a CTA's units on its single
-// Q buffer per tile: the next unit's Q could only be requested once this
-// unit's S had read the buffer, on all SMs at once, and DRAM ran in bursts.
-// Such units need one K/V stage, so the K/V ring stays on stage 0 and units
-// alternate between two Q buffers, the second in the idle stage-1 slots (Q
-// tile 0 in the K slot, tile 1 in the V slot): unit k + 1's Q streams in while
-// unit k computes.  The mode is chosen in the prologue from the mask tables.
-//
 // Barrier phases are counted per role: the producer and MMA thread count K/V
 // tiles (ring stage g & 1, use g >> 1) and per-tile Q loads; the softmax
 // warpgroup of tile t counts the S_t tiles and the units it has processed.
@@ -68,11 +59,10 @@ struct PSmem {
   static constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 4 * kTile;
   static constexpr uint32_t kOffStg = 6 * kTile;  // [2] epilogue staging, one 64-column chunk per tile
   // q_full[2], q_free[2], k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
-  // p_half[2], p_full[2], o_full[2], o_free[2], done, then q_full / q_free of the
-  // second Q buffer (one-tile mode) [2] each
-  static constexpr int kBars = 27;
+  // p_half[2], p_full[2], o_full[2], o_free[2], done
+  static constexpr int kBars = 23;
   static constexpr uint32_t kOffBar = kOffStg + 2 * kChunkBytes;
-  static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag, one-tile mode
+  static constexpr uint32_t kOffCtl = kOffBar + kBars * 8;  // tmem slot, abort flag
   static constexpr uint32_t kOffMeta = kOffCtl + 16;        // key-mask tables (masked calls only)
   static constexpr uint32_t kBytes = kOffMeta;
 };
@@ -150,11 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   uint64_t* bar_of = bars + 18;  // [2] O_t of a unit complete
   uint64_t* bar_oe = bars + 20;  // [2] O_t read by the epilogue (128 arrivals)
   uint64_t* bar_done = bars + 22;
-  uint64_t* bar_qfB = bars + 23;  // [2] second Q buffer's q_full (one-tile mode)
-  uint64_t* bar_qeB = bars + 25;  // [2] second Q buffer's q_free
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::kOffCtl + 4);
-  int* one_tile_slot = reinterpret_cast<int*>(sm + S::kOffCtl + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -166,7 +153,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
   if (warp == 8 && lane == 0) {
     for (int i = 0; i < S::kBars; ++i) mbar_init(bars + i, (i >= 14 && i < 18) || i == 20 || i == 21 ? 128 : 1);
     *abort_flag = 0;
-    *one_tile_slot = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tm_q);
     // the first unit's Q does not depend on the key mask: its load overlaps
@@ -249,76 +235,50 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int all_one = 1;
-      for (int b = 0; b < B; ++b) all_one &= count[b] == 1;
-      *one_tile_slot = all_one;
-    }
-    __syncthreads();
   }
-  // one-tile mode (masked calls only): K/V on stage 0, Q alternating between
-  // two buffers by the CTA's unit index
-  const bool one_tile = kMasked && *one_tile_slot != 0;
 
   if (warp >= 8) {
     setmaxnreg_dec<kProducerRegs>();
     if (warp == 8) {
       // ---------------- TMA producer ----------------
       if (lane == 0) {
-        int nqA0 = 0, nqA1 = 0;  // loads issued into Q tile 0 / 1 of buffer A (every unit in two-stage mode)
-        int nqB0 = 0, nqB1 = 0;  // ... of buffer B (odd units of the CTA in one-tile mode)
-        int gk = 0, gv = 0;      // K and V tiles issued
+        int nq0 = 0, nq1 = 0;  // loads issued into Q tile 0 / 1
+        int gk = 0, gv = 0;    // K and V tiles issued (ring stage i & 1, use i >> 1)
         bool ok = true;
-        // ring slot of the i-th K or V tile: stage i & 1, use i >> 1; one-tile mode stage 0, use i
-        const int ring_min = one_tile ? 1 : 2;
-        auto ring_stage = [&](int i) { return one_tile ? 0 : (i & 1); };
-        auto ring_use = [&](int i) { return one_tile ? i : (i >> 1); };
-        // Q tile t of a unit into buffer buf; the last S_t of the unit that used
-        // the buffer before must have read it
-        auto load_q = [&](auto tc, int buf, const PUnit& u, int qh) -> bool {
+        // Q tile t of a unit; the previous unit's last S_t must have read the buffer
+        auto load_q = [&](auto tc, const PUnit& u, int qh) -> bool {
           constexpr int t = decltype(tc)::value;
-          const int nq = buf ? (t ? nqB1 : nqB0) : (t ? nqA1 : nqA0);
-          uint64_t* qf = (buf ? bar_qfB : bar_qf) + t;
-          uint64_t* qe = (buf ? bar_qeB : bar_qe) + t;
-          if (nq > 0 && !mbar_wait(qe, (nq - 1) & 1, abort_flag, p.err, 40)) return false;
-          uint8_t* dst = buf ? (t == 0 ? sK : sV) + S::kTile : sQ + t * S::kTile;
-          mbar_arrive_expect_tx(qf, S::kTile);
+          int& nq = t == 0 ? nq0 : nq1;
+          if (nq > 0 && !mbar_wait(bar_qe + t, (nq - 1) & 1, abort_flag, p.err, 40)) return false;
+          mbar_arrive_expect_tx(bar_qf + t, S::kTile);
 #pragma unroll
           for (int c = 0; c < S::kChunks; ++c)
-            tma_load_4d(&p.tm_q, qf, dst + c * kChunkBytes, c * 64, u.q0 + t * kTileM, qh, u.b);
-          if (buf) {
-            if (t) ++nqB1; else ++nqB0;
-          } else {
-            if (t) ++nqA1; else ++nqA0;
-          }
+            tma_load_4d(&p.tm_q, bar_qf + t, sQ + t * S::kTile + c * kChunkBytes, c * 64, u.q0 + t * kTileM, qh, u.b);
+          ++nq;
           return true;
         };
-        int k_idx = 0;  // this CTA's unit index
-        for (int unit = blockIdx.x; unit < units && ok; unit += G, ++k_idx) {
+        for (int unit = blockIdx.x; unit < units && ok; unit += G) {
           const PUnit u = persist_unit(p, mt, unit);
           const int qh = p.q_head_off + u.hl;
           const int kvh = (p.kv_head_off + u.hl) / p.group;
-          const int buf = one_tile ? (k_idx & 1) : 0;
-          if (k_idx == 0) {  // loaded in the prologue (buffer A)
-            nqA0 = 1;
-            nqA1 = u.two ? 1 : 0;
+          if (unit == (int)blockIdx.x) {  // loaded in the prologue
+            nq0 = 1;
+            nq1 = u.two ? 1 : 0;
           } else {
-            ok = load_q(std::integral_constant<int, 0>{}, buf, u, qh) &&
-                 (!u.two || load_q(std::integral_constant<int, 1>{}, buf, u, qh));
+            ok = load_q(std::integral_constant<int, 0>{}, u, qh) &&
+                 (!u.two || load_q(std::integral_constant<int, 1>{}, u, qh));
           }
           for (int j = 0; j < u.n && ok; ++j) {
             const int kv0 = mt.tile(u.b, j) * kTileN;
-            int st = ring_stage(gk);
-            if (gk >= ring_min && !(ok = mbar_wait(bar_ke + st, (ring_use(gk) - 1) & 1, abort_flag, p.err, 41)))
-              break;
+            int st = gk & 1;
+            if (gk >= 2 && !(ok = mbar_wait(bar_ke + st, ((gk >> 1) - 1) & 1, abort_flag, p.err, 41))) break;
             mbar_arrive_expect_tx(bar_kf + st, S::kTile);
 #pragma unroll
             for (int c = 0; c < S::kChunks; ++c)
               tma_load_4d(&p.tm_k, bar_kf + st, sK + st * S::kTile + c * kChunkBytes, c * 64, kv0, kvh, u.b);
             ++gk;
-            st = ring_stage(gv);
-            if (gv >= ring_min && !(ok = mbar_wait(bar_ve + st, (ring_use(gv) - 1) & 1, abort_flag, p.err, 42)))
-              break;
+            st = gv & 1;
+            if (gv >= 2 && !(ok = mbar_wait(bar_ve + st, ((gv >> 1) - 1) & 1, abort_flag, p.err, 42))) break;
             mbar_arrive_expect_tx(bar_vf + st, S::kTile);
 #pragma unroll
             for (int c = 0; c < S::kChunks; ++c)
@@ -328,16 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         }
         // never leave the CTA with a bulk copy still writing its shared memory:
         // a load into a buffer is issued only after the one before it into that
-        // buffer was consumed, so only the last load per Q buffer and tile and
-        // the last ring_min per ring can still be in flight
-        if (nqA0 > 0) drain_wait(bar_qf + 0, (nqA0 - 1) & 1);
-        if (nqA1 > 0) drain_wait(bar_qf + 1, (nqA1 - 1) & 1);
-        if (nqB0 > 0) drain_wait(bar_qfB + 0, (nqB0 - 1) & 1);
-        if (nqB1 > 0) drain_wait(bar_qfB + 1, (nqB1 - 1) & 1);
-        for (int i = gk < ring_min ? 0 : gk - ring_min; i < gk; ++i)
-          drain_wait(bar_kf + ring_stage(i), ring_use(i) & 1);
-        for (int i = gv < ring_min ? 0 : gv - ring_min; i < gv; ++i)
-          drain_wait(bar_vf + ring_stage(i), ring_use(i) & 1);
+        // buffer was consumed, so only the last load per Q tile and the last
+        // two per ring can still be in flight
+        if (nq0 > 0) drain_wait(bar_qf + 0, (nq0 - 1) & 1);
+        if (nq1 > 0) drain_wait(bar_qf + 1, (nq1 - 1) & 1);
+        for (int i = gk < 2 ? 0 : gk - 2; i < gk; ++i) drain_wait(bar_kf + (i & 1), (i >> 1) & 1);
+        for (int i = gv < 2 ? 0 : gv - 2; i < gv; ++i) drain_wait(bar_vf + (i & 1), (i >> 1) & 1);
       }
       __syncwarp();
     } else if (warp == 9) {
@@ -347,40 +303,27 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         // no per-tile state lives in an indexed (local-memory) array
         using T0 = std::integral_constant<int, 0>;
         using T1 = std::integral_constant<int, 1>;
-        const SDesc dQA0 = sdesc_split(smem_u32(sQ), 16, 1024);
-        const SDesc dQA1 = sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024);
-        const SDesc dQB0 = sdesc_split(smem_u32(sK) + S::kTile, 16, 1024);  // one-tile mode's second buffer
-        const SDesc dQB1 = sdesc_split(smem_u32(sV) + S::kTile, 16, 1024);
+        const SDesc dQ0 = sdesc_split(smem_u32(sQ), 16, 1024);
+        const SDesc dQ1 = sdesc_split(smem_u32(sQ) + S::kTile, 16, 1024);
         const SDesc dK = sdesc_split(smem_u32(sK), 16, 1024);
         const SDesc dV = sdesc_split(smem_u32(sV), kChunkBytes, 1024);
         const uint32_t stage_step = S::kTile >> 4;
-        // ring slot of K/V tile g: stage g & 1, use g >> 1; one-tile mode stage 0, use g
-        auto ring_stage = [&](int i) { return one_tile ? 0 : (i & 1); };
-        auto ring_use = [&](int i) { return one_tile ? i : (i >> 1); };
-        int nq0 = 0, nq1 = 0;      // units begun on Q tile t (both buffers)
-        int nqA0 = 0, nqA1 = 0;    // ... on buffer A (q_full phase count)
-        int nqB0 = 0, nqB1 = 0;    // ... on buffer B
-        int np0 = 0, np1 = 0;      // P_t tiles consumed (p_half / p_full phase count)
-        // S_t of (unit, tile j) with Q in buffer buf and K in ring slot g; j == 0
-        // first waits for the unit's Q tile t, j == n - 1 (n: the unit's tile
-        // count) then releases it
-        auto issue_s_step = [&](auto tc, int j, int n, int g, int buf) -> bool {
+        int nq0 = 0, nq1 = 0;  // units begun on Q tile t (q_full phase count)
+        int np0 = 0, np1 = 0;  // P_t tiles consumed (p_half / p_full phase count)
+        // S_t of (unit, tile j) whose K sits in ring slot g; j == 0 first waits
+        // for the unit's Q tile t, j == n - 1 (n: the unit's tile count) then
+        // releases Q tile t
+        auto issue_s_step = [&](auto tc, int j, int n, int g) -> bool {
           constexpr int t = decltype(tc)::value;
+          int& nq = t == 0 ? nq0 : nq1;
           if (j == 0) {
-            const int nqb = buf ? (t ? nqB1 : nqB0) : (t ? nqA1 : nqA0);
-            if (!mbar_wait((buf ? bar_qfB : bar_qf) + t, nqb & 1, abort_flag, p.err, 43)) return false;
-            if (buf) {
-              if (t) ++nqB1; else ++nqB0;
-            } else {
-              if (t) ++nqA1; else ++nqA0;
-            }
-            if (t) ++nq1; else ++nq0;
+            if (!mbar_wait(bar_qf + t, nq & 1, abort_flag, p.err, 43)) return false;
+            ++nq;
           }
           tc_fence_after();
-          const SDesc dq = buf ? (t == 0 ? dQB0 : dQB1) : (t == 0 ? dQA0 : dQA1);
-          issue_s<D>(tmem + 128 * t, dq, SDesc{dK.lo + ring_stage(g) * stage_step, dK.hi});
+          issue_s<D>(tmem + 128 * t, t == 0 ? dQ0 : dQ1, SDesc{dK.lo + (g & 1) * stage_step, dK.hi});
           umma_commit(bar_s + t);
-          if (j == n - 1) umma_commit((buf ? bar_qeB : bar_qe) + t);
+          if (j == n - 1) umma_commit(bar_qe + t);
           return true;
         };
         // P V_t of (unit, tile j) with V in ring stage st; the first P V of a
@@ -405,21 +348,19 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
         bool go = true;
         int unit = blockIdx.x;
         PUnit u = persist_unit(p, mt, unit);
-        int g = 0;      // ring slot of the current tile
-        int k_idx = 0;  // this CTA's unit index (Q buffer k_idx & 1 in one-tile mode)
+        int g = 0;  // ring slot of the current tile
         if (unit < units) {
-          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(T0{}, 0, u.n, 0, 0);
-          if (go && u.two) go = issue_s_step(T1{}, 0, u.n, 0, 0);
+          go = mbar_wait(bar_kf, 0, abort_flag, p.err, 44) && issue_s_step(T0{}, 0, u.n, 0);
+          if (go && u.two) go = issue_s_step(T1{}, 0, u.n, 0);
           if (go) umma_commit(bar_ke + 0);
         }
-        for (; unit < units && go; unit += G, ++k_idx) {
+        for (; unit < units && go; unit += G) {
           const int nxt_unit = unit + G;
           const bool has_next = nxt_unit < units;
           const PUnit v = has_next ? persist_unit(p, mt, nxt_unit) : u;
           const int n = u.n;
-          const int buf = one_tile ? (k_idx & 1) : 0, nbuf = one_tile ? ((k_idx + 1) & 1) : 0;
           for (int j = 0; j < n; ++j, ++g) {
-            const int st = ring_stage(g);
+            const int st = g & 1;
             // the step after this one: (unit, j + 1) or (next unit, 0); S_t of
             // it right behind P V_t of this one (a unit with no rows in Q tile
             // 1 issues neither P V1 nor S1)
@@ -427,14 +368,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
             const bool nx_two = j + 1 < n ? u.two : v.two;
             const int nj = j + 1 < n ? j + 1 : 0;
             const int nn = j + 1 < n ? n : v.n;
-            const int nb = j + 1 < n ? buf : nbuf;
-            const int g1 = g + 1, st1 = ring_stage(g1);
-            go = mbar_wait(bar_vf + st, ring_use(g) & 1, abort_flag, p.err, 46) && pv_step(T0{}, j, n, st);
+            const int g1 = g + 1, st1 = g1 & 1;
+            go = mbar_wait(bar_vf + st, (g >> 1) & 1, abort_flag, p.err, 46) && pv_step(T0{}, j, n, st);
             if (go && more)
-              go = mbar_wait(bar_kf + st1, ring_use(g1) & 1, abort_flag, p.err, 48) &&
-                   issue_s_step(T0{}, nj, nn, g1, nb);
+              go = mbar_wait(bar_kf + st1, (g1 >> 1) & 1, abort_flag, p.err, 48) && issue_s_step(T0{}, nj, nn, g1);
             if (go && u.two) go = pv_step(T1{}, j, n, st);
-            if (go && more && nx_two) go = issue_s_step(T1{}, nj, nn, g1, nb);
+            if (go && more && nx_two) go = issue_s_step(T1{}, nj, nn, g1);
             if (!go) break;
             umma_commit(bar_ve + st);
             if (more) umma_commit(bar_ke + st1);

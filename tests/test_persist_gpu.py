@@ -151,34 +151,3 @@ def test_key_masks_match_bit_for_bit_and_the_oracle(B, H, Lq, Lk, D, valid):
     ref, ref_lse = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs], mask=m)
     check(out[:, hs], ref, f"mask B={B} D={D}")
     assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS
-
-
-@pytest.mark.parametrize("D", [64, 128])
-def test_one_live_tile_per_row_alternates_q_buffers(D):
-    # every batch row has exactly one live KV tile, at a different tile per row:
-    # the kernel keeps K/V on one stage and alternates the units' Q between two
-    # buffers (the second in the idle stage-1 slots)
-    B, H, Lq, Lk = 2, 80, 700, 1024
-    q = inputs.seeded_tensor(241 + D, (B, H, Lq, D), rmsnorm=True, bf16=True)
-    k = inputs.seeded_tensor(242 + D, (B, H, Lk, D), rmsnorm=True, bf16=True)
-    v = inputs.seeded_tensor(243 + D, (B, H, Lk, D), bf16=True)
-    m = np.zeros((B, Lk), np.uint8)
-    m[0, :94] = 1          # tile 0
-    m[1, 300:350] = 1      # tile 2
-    a = _lib.FwdArgs()
-    a.dtype, a.batch, a.heads, a.q_len, a.kv_len, a.head_dim = _lib.BF16, B, H, Lq, Lk, D
-    a.key_mask, a.key_mask_stride_b = 4096, Lk
-    info = _lib.FwdPlanInfo()
-    assert _lib.load().ltxattn_fwd_plan(ctypes.byref(a), ctypes.byref(info)) == _lib.OK
-    assert info.kernel == 3 and info.units == 3 * H * B
-    qd, kd, vd, md = dev(q), dev(k), dev(v), torch.from_numpy(m).cuda()
-    out, lse = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True)
-    one, lse1 = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True, num_splits=1)
-    assert same_bits(out, one)
-    assert torch.equal(lse, lse1)
-    again, _ = AttentionBackend.attention(qd, kd, vd, key_mask=md, save_lse=True)
-    assert same_bits(again, out)
-    hs = [0, H - 1]
-    ref, ref_lse = oracle.attn_fwd(q[:, hs], k[:, hs], v[:, hs], mask=m)
-    check(out[:, hs], ref, f"one live tile D={D}")
-    assert np.abs(lse[:, hs].cpu().numpy() - ref_lse).max() < LSE_ABS
