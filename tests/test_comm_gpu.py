@@ -31,7 +31,8 @@ def test_single_rank_gather_is_identity_layout():
 
 def test_single_rank_row_parallel_to_out_is_the_plain_linear():
     # ltxattn_out_project_allreduce on a one-rank communicator: the fp32 partial, the
-    # (identity) all-reduce and the bias / rounding pass give ltxattn_linear's bits
+    # (identity) all-reduce and the bias / rounding pass give the bits of ltxattn_linear
+    # without K splitting (the same single fp32 sum per output)
     raw = (ctypes.c_uint8 * 128)()
     assert _lib.load().ltxattn_comm_unique_id(raw) == _lib.OK, _lib.last_error()
     g = HeadGather(1, 0, bytes(raw), torch.cuda.current_device())
@@ -43,7 +44,7 @@ def test_single_rank_row_parallel_to_out_is_the_plain_linear():
         b = torch.from_numpy(inputs.round_bf16(inputs.seeded_tensor(63, (n,)) * np.float32(0.1))).to(
             "cuda", torch.bfloat16)
         got = g.out_project(x, w, b)
-        want = linear(x, w, b)
+        want = linear(x, w, b, split_k=False)
         torch.cuda.synchronize()
         assert torch.equal(got, want)
         ref = oracle.linear(x.float().cpu().numpy(), w.float().cpu().numpy(), b.float().cpu().numpy())
