@@ -51,7 +51,7 @@ EXTRAS = ("c3", "c4a", "c4b", "c4c", "c5")
 # without tables (the kernel-only timing below), L2 flushed before the launch.
 # Values for all 32 heads, from the capture summarised in the file named beside
 # each number (which gives the command); scaled by heads for a rank's block.
-_TRAFFIC_SRC = "profiles/dram_traffic_attention_launches.md"
+_TRAFFIC_SRC = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one L2-flushed launch (bench.py --traffic-launches)"
 TRAFFIC = {"c2": (78838016, _TRAFFIC_SRC), "c3": (27749120, _TRAFFIC_SRC), "c4a": (1667840, _TRAFFIC_SRC),
            "c4b": (13884672, _TRAFFIC_SRC), "c4c": (26344704, _TRAFFIC_SRC),
            # captured on 4 of the 32 heads; scaled by heads
