@@ -413,7 +413,7 @@ def measure_backward(ctx, args, case, out, lse):
     value = 2.5 * w.flops / (ms * 1e-3) / 1e12
     rec = {"ms_per_step": round(ms, 4), "value": round(value, 2), "unit": "TFLOP/s",
            "flop_convention": "2.5 x forward (dQ, dK, dV)",
-           "kernels": "bwd_prep_kernel, bwd_dq_kernel, bwd_dkdv_kernel",
+           "kernels": "bwd_prep_kernel, bwd_sm100_kernel (dK/dV and dQ passes in one launch)",
            "frac_of_burst": round(value / ctx.ws / burst, 4), "peak_source": f"{src} bf16_tflops (burst)"}
     if "host" in case:
         rec["parity"] = bwd_parity_check(ctx, case, out, lse, grads)
