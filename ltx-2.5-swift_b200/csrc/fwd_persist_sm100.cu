@@ -440,9 +440,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_persist_sm100_kernel(const __
             uint32_t bits = umask ? mt.word(ub, kv0 / 32 + w) : 0xffffffffu;
             const int lim = Lk - (kv0 + 32 * w);
             if (lim < 32) bits &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
+            if (bits != 0xffffffffu) {  // a word whose keys are all valid needs no per-column select
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+              for (int c = 0; c < 32; ++c)
+                if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+            }
           }
         }
         float mx;

@@ -136,6 +136,25 @@ __global__ void __launch_bounds__(kShortThreads, 1)
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    // the first unit's Q and K/V loads start here, overlapping TMEM allocation
+    // and the rest of the prologue (the producer loop skips them)
+    if (cnt > 0) {
+      grid_dep_wait();  // the kernel that wrote q / k (the RoPE pre-pass) has completed
+      const ShortUnit u = short_unit(p, u0);
+      const int qh = p.q_head_off + u.hl, kvh = (p.kv_head_off + u.hl) / p.group;
+      mbar_arrive_expect_tx(bar_qfull, 2 * S::kTile);
+#pragma unroll
+      for (int c = 0; c < S::kChunks; ++c) {
+        tma_load_4d(&p.tm_q, bar_qfull, sQ + c * kChunkBytes, c * 64, u.q0, qh, u.b);
+        tma_load_4d(&p.tm_q, bar_qfull, sQ + S::kTile + c * kChunkBytes, c * 64, u.q0 + kTileM, qh, u.b);
+      }
+      mbar_arrive_expect_tx(bar_kvfull, 2 * S::kTile);
+#pragma unroll
+      for (int c = 0; c < S::kChunks; ++c) {
+        tma_load_4d(&p.tm_k, bar_kvfull, sK + c * kChunkBytes, c * 64, 0, kvh, u.b);
+        tma_load_4d(&p.tm_v, bar_kvfull, sV + c * kChunkBytes, c * 64, 0, kvh, u.b);
+      }
+    }
     tma_prefetch_desc(&p.tm_o);
   }
   if (warp == 9) {
@@ -226,8 +245,10 @@ __global__ void __launch_bounds__(kShortThreads, 1)
     if (warp == 8) {
       // ---------------- TMA producer ----------------
       if (lane == 0) {
-        int q_issued = 0, kv_issued = 0, kv_prev = -1;
-        for (int i = 0; i < cnt; ++i) {
+        // the first unit's Q and K/V were issued in the prologue
+        int q_issued = cnt > 0 ? 1 : 0, kv_issued = cnt > 0 ? 1 : 0;
+        int kv_prev = cnt > 0 ? short_unit(p, u0).kv_key : -1;
+        for (int i = 1; i < cnt; ++i) {
           const ShortUnit u = short_unit(p, u0 + i);
           const int qh = p.q_head_off + u.hl;
           const int qb = i % S::kQBuf, qn = i / S::kQBuf;  // buffer, and its use count

@@ -429,9 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
               bits &= skip <= 0 ? ~0u : (skip >= 32 ? 0u : (~0u << skip));
             }
           }
+          if (bits != 0xffffffffu) {  // a word whose keys are all valid needs no per-column select
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+            for (int c = 0; c < 32; ++c)
+              if (!((bits >> c) & 1u)) s[32 * w + c] = -INFINITY;
+          }
         }
       }
       // row max: eight independent 3-input-max chains, then a short tree
