@@ -112,9 +112,32 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
   }
 }
 
-// Transpose rotation of one row held as D fp32 values in registers.
+// Transpose rotation of one row held as D fp32 values in registers.  The table
+// row is read 8 entries (16 bytes) at a time when `vec` (row 16-byte aligned),
+// else entry by entry: each thread reads a different row, so scalar loads cost
+// a cache line per lane per entry (at config 2 that was 117 us of the
+// backward's 810).
 template <int D>
-__device__ __forceinline__ void rope_inverse_row(float (&g)[D], const __nv_bfloat16* c, const __nv_bfloat16* s) {
+__device__ __forceinline__ void rope_inverse_row(float (&g)[D], const __nv_bfloat16* c, const __nv_bfloat16* s,
+                                                 bool vec) {
+  if (vec) {
+#pragma unroll
+    for (int u = 0; u < D / 16; ++u) {
+      const uint4 cv = __ldg(reinterpret_cast<const uint4*>(c) + u);
+      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(s) + u);
+      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * u + e;
+        const float cc = __uint_as_float((e & 1) ? (cw[e >> 1] & 0xffff0000u) : (cw[e >> 1] << 16));
+        const float ss = __uint_as_float((e & 1) ? (sw[e >> 1] & 0xffff0000u) : (sw[e >> 1] << 16));
+        const float g1 = g[i], g2 = g[i + D / 2];
+        g[i] = __fadd_rn(__fmul_rn(g1, cc), __fmul_rn(g2, ss));
+        g[i + D / 2] = __fsub_rn(__fmul_rn(g2, cc), __fmul_rn(g1, ss));
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < D / 2; ++i) {
     const float cc = __bfloat162float(c[i]), ss = __bfloat162float(s[i]);
@@ -396,7 +419,8 @@ __device__ __forceinline__ void bwd_dq_body(const BwdParams& p, int tile, int hl
         for (int e = 0; e < D; ++e) g[e] *= p.scale;
         if (p.qcos != nullptr)
           rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.qcos) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
-                              static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st);
+                              static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
+                              p.rope_vec != 0);
         store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
       }
     }
@@ -646,7 +670,8 @@ __device__ __forceinline__ void bwd_dkdv_body(const BwdParams& p, int tile, int 
         for (int e = 0; e < D; ++e) g[e] *= p.scale;
         if (p.kcos != nullptr)
           rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.kcos) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
-                              static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st);
+                              static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
+                              p.rope_vec != 0);
         store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
       }
     }

@@ -903,6 +903,11 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
     p.kcos = static_cast<const uint8_t*>(kr.cos) + h0 * kr.stride_h * (int64_t)es;
     p.ksin = static_cast<const uint8_t*>(kr.sin) + h0 * kr.stride_h * (int64_t)es;
     p.kt_sb = kr.stride_b; p.kt_sh = kr.stride_h; p.kt_st = kr.stride_t;
+    const int64_t per16 = 16 / (int64_t)es;  // elements per 16 bytes
+    auto al = [&](const void* ptr) { return aligned16(ptr); };
+    auto m = [&](int64_t st) { return st % per16 == 0; };
+    p.rope_vec = al(p.qcos) && al(p.qsin) && al(p.kcos) && al(p.ksin) && m(qr.stride_b) && m(qr.stride_h) &&
+                 m(qr.stride_t) && m(kr.stride_b) && m(kr.stride_h) && m(kr.stride_t);
   }
   p.Lq = s.Lq;
   p.Lk = s.Lk;

@@ -156,6 +156,7 @@ struct BwdParams {
   const void* kcos;  // transpose rotation of dk
   const void* ksin;
   int64_t kt_sb, kt_sh, kt_st;
+  int rope_vec;  // both tables' rows are 16-byte aligned (bf16 path: vector table reads)
   // fp32 path: plain strided inputs (no tensor maps)
   const float* q;
   const float* k;
