@@ -112,61 +112,77 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
   }
 }
 
-// Transpose rotation of one row held as D fp32 values in registers.  The table
-// row is read 8 entries (16 bytes) at a time when `vec` (row 16-byte aligned),
-// else entry by entry: each thread reads a different row, so scalar loads cost
-// a cache line per lane per entry (at config 2 that was 117 us of the
-// backward's 810).
+// One gradient row out of TMEM: g = scale * (TMEM columns), then, with a table
+// (c, s non-null), the transpose rotation of RoPE (g1 c + g2 s, g2 c - g1 s for
+// the pair (i, i + D/2), each product and sum rounded once in fp32), then bf16
+// to dst.  It works on 32-column pieces of each half of the row, so at most 64
+// values and one piece of the table are live in registers.  The table is read
+// 16 bytes at a time when `vec` (rows 16-byte aligned), else entry by entry
+// (each thread reads its own row, so scalar reads cost a cache line per lane
+// per entry: at config 2 that was 117 us of the backward's 810).  `have`
+// (warp-uniform: TMEM loads are warp-collective) false writes zeros; `live`
+// false skips the store.
 template <int D>
-__device__ __forceinline__ void rope_inverse_row(float (&g)[D], const __nv_bfloat16* c, const __nv_bfloat16* s,
-                                                 bool vec) {
-  if (vec) {
+__device__ __forceinline__ void grad_row_out(uint32_t taddr, bool have, bool live, float scale,
+                                             const __nv_bfloat16* c, const __nv_bfloat16* s, bool vec,
+                                             __nv_bfloat16* dst) {
+  constexpr int H = D / 2;
 #pragma unroll
-    for (int u = 0; u < D / 16; ++u) {
-      const uint4 cv = __ldg(reinterpret_cast<const uint4*>(c) + u);
-      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(s) + u);
-      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+  for (int piece = 0; piece < H / 32; ++piece) {
+    uint32_t r1[32], r2[32];
+    if (have) {
+      tmem_ld32(taddr + piece * 32, r1);
+      tmem_ld32(taddr + H + piece * 32, r2);
+      tmem_wait_ld();
+    } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int i = 8 * u + e;
-        const float cc = __uint_as_float((e & 1) ? (cw[e >> 1] & 0xffff0000u) : (cw[e >> 1] << 16));
-        const float ss = __uint_as_float((e & 1) ? (sw[e >> 1] & 0xffff0000u) : (sw[e >> 1] << 16));
-        const float g1 = g[i], g2 = g[i + D / 2];
-        g[i] = __fadd_rn(__fmul_rn(g1, cc), __fmul_rn(g2, ss));
-        g[i + D / 2] = __fsub_rn(__fmul_rn(g2, cc), __fmul_rn(g1, ss));
+      for (int e = 0; e < 32; ++e) r1[e] = r2[e] = 0u;
+    }
+    if (!live) continue;
+    float g1[32], g2[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      g1[e] = __uint_as_float(r1[e]) * scale;
+      g2[e] = __uint_as_float(r2[e]) * scale;
+    }
+    if (c != nullptr) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // table entries piece*32 + 8u .. + 7
+        float cc[8], ss[8];
+        if (vec) {
+          const uint4 cv = __ldg(reinterpret_cast<const uint4*>(c + piece * 32) + u);
+          const uint4 sv = __ldg(reinterpret_cast<const uint4*>(s + piece * 32) + u);
+          const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {  // bf16 -> fp32 is exact: the bits move to the top half
+            cc[e] = __uint_as_float((e & 1) ? (cw[e >> 1] & 0xffff0000u) : (cw[e >> 1] << 16));
+            ss[e] = __uint_as_float((e & 1) ? (sw[e >> 1] & 0xffff0000u) : (sw[e >> 1] << 16));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            cc[e] = __bfloat162float(c[piece * 32 + 8 * u + e]);
+            ss[e] = __bfloat162float(s[piece * 32 + 8 * u + e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 8 * u + e;
+          const float a1 = g1[i], a2 = g2[i];
+          g1[i] = __fadd_rn(__fmul_rn(a1, cc[e]), __fmul_rn(a2, ss[e]));
+          g2[i] = __fsub_rn(__fmul_rn(a2, cc[e]), __fmul_rn(a1, ss[e]));
+        }
       }
     }
-    return;
-  }
 #pragma unroll
-  for (int i = 0; i < D / 2; ++i) {
-    const float cc = __bfloat162float(c[i]), ss = __bfloat162float(s[i]);
-    const float g1 = g[i], g2 = g[i + D / 2];
-    g[i] = __fadd_rn(__fmul_rn(g1, cc), __fmul_rn(g2, ss));
-    g[i + D / 2] = __fsub_rn(__fmul_rn(g2, cc), __fmul_rn(g1, ss));
-  }
-}
-
-// Load D fp32 columns of this thread's TMEM lane starting at taddr.
-template <int D>
-__device__ __forceinline__ void tmem_row(uint32_t taddr, float (&g)[D]) {
-#pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(taddr + c * 32, r);
-    tmem_wait_ld();
-#pragma unroll
-    for (int e = 0; e < 32; ++e) g[c * 32 + e] = __uint_as_float(r[e]);
-  }
-}
-
-template <int D>
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&g)[D], float mul) {
-#pragma unroll
-  for (int c = 0; c < D / 8; ++c) {
-    uint4 v = make_uint4(pack_bf16x2(g[8 * c] * mul, g[8 * c + 1] * mul), pack_bf16x2(g[8 * c + 2] * mul, g[8 * c + 3] * mul),
-                         pack_bf16x2(g[8 * c + 4] * mul, g[8 * c + 5] * mul), pack_bf16x2(g[8 * c + 6] * mul, g[8 * c + 7] * mul));
-    reinterpret_cast<uint4*>(dst)[c] = v;
+    for (int u = 0; u < 4; ++u) {
+      reinterpret_cast<uint4*>(dst + piece * 32)[u] =
+          make_uint4(pack_bf16x2(g1[8 * u], g1[8 * u + 1]), pack_bf16x2(g1[8 * u + 2], g1[8 * u + 3]),
+                     pack_bf16x2(g1[8 * u + 4], g1[8 * u + 5]), pack_bf16x2(g1[8 * u + 6], g1[8 * u + 7]));
+      reinterpret_cast<uint4*>(dst + H + piece * 32)[u] =
+          make_uint4(pack_bf16x2(g2[8 * u], g2[8 * u + 1]), pack_bf16x2(g2[8 * u + 2], g2[8 * u + 3]),
+                     pack_bf16x2(g2[8 * u + 4], g2[8 * u + 5]), pack_bf16x2(g2[8 * u + 6], g2[8 * u + 7]));
+    }
   }
 }
 
@@ -407,22 +423,11 @@ __device__ __forceinline__ void bwd_dq_body(const BwdParams& p, int tile, int hl
     if (half == 0) {
       const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
       tc_fence_after();
-      float g[D];
-      if (have) {
-        tmem_row<D>(tQ, g);
-      } else {
-#pragma unroll
-        for (int e = 0; e < D; ++e) g[e] = 0.f;
-      }
-      if (row < p.Lq) {
-#pragma unroll
-        for (int e = 0; e < D; ++e) g[e] *= p.scale;
-        if (p.qcos != nullptr)
-          rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.qcos) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
-                              static_cast<const __nv_bfloat16*>(p.qsin) + (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st,
-                              p.rope_vec != 0);
-        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st, g, 1.f);
-      }
+      const int64_t toff = (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
+      grad_row_out<D>(tQ, have, row < p.Lq, p.scale,
+                      p.qcos ? static_cast<const __nv_bfloat16*>(p.qcos) + toff : nullptr,
+                      p.qcos ? static_cast<const __nv_bfloat16*>(p.qsin) + toff : nullptr, p.rope_vec != 0,
+                      static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st);
     }
   }
   tc_fence_before();
@@ -655,25 +660,15 @@ __device__ __forceinline__ void bwd_dkdv_body(const BwdParams& p, int tile, int 
     }
     const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 37);
     tc_fence_after();
-    float g[D];
-    if (have) {
-      tmem_row<D>(half == 0 ? tV : tK, g);
+    if (half == 0) {
+      grad_row_out<D>(tV, have, key < p.Lk, 1.f, nullptr, nullptr, false,
+                      static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st);
     } else {
-#pragma unroll
-      for (int e = 0; e < D; ++e) g[e] = 0.f;
-    }
-    if (key < p.Lk) {
-      if (half == 0) {
-        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st, g, 1.f);
-      } else {
-#pragma unroll
-        for (int e = 0; e < D; ++e) g[e] *= p.scale;
-        if (p.kcos != nullptr)
-          rope_inverse_row<D>(g, static_cast<const __nv_bfloat16*>(p.kcos) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
-                              static_cast<const __nv_bfloat16*>(p.ksin) + (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st,
-                              p.rope_vec != 0);
-        store_row_bf16<D>(static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st, g, 1.f);
-      }
+      const int64_t toff = (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st;
+      grad_row_out<D>(tK, have, key < p.Lk, p.scale,
+                      p.kcos ? static_cast<const __nv_bfloat16*>(p.kcos) + toff : nullptr,
+                      p.kcos ? static_cast<const __nv_bfloat16*>(p.ksin) + toff : nullptr, p.rope_vec != 0,
+                      static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st);
     }
   }
   tc_fence_before();
