@@ -121,13 +121,11 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
 // (each thread reads its own row, so scalar reads cost a cache line per lane
 // per entry: at config 2 that was 117 us of the backward's 810).  `have`
 // (warp-uniform: TMEM loads are warp-collective) false writes zeros; `live`
-// false skips the row.  With `stg` the row goes to row r of a 128-row staging
-// tile (64-column chunks kChunkBytes apart, 128-byte swizzle, the layout of a
-// TMA box) for a TMA store, else straight to dst.
+// false skips the store.
 template <int D>
 __device__ __forceinline__ void grad_row_out(uint32_t taddr, bool have, bool live, float scale,
                                              const __nv_bfloat16* c, const __nv_bfloat16* s, bool vec,
-                                             __nv_bfloat16* dst, uint8_t* stg, int r) {
+                                             __nv_bfloat16* dst) {
   constexpr int H = D / 2;
 #pragma unroll
   for (int piece = 0; piece < H / 32; ++piece) {
@@ -178,36 +176,13 @@ __device__ __forceinline__ void grad_row_out(uint32_t taddr, bool have, bool liv
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const uint4 v1 = make_uint4(pack_bf16x2(g1[8 * u], g1[8 * u + 1]), pack_bf16x2(g1[8 * u + 2], g1[8 * u + 3]),
-                                  pack_bf16x2(g1[8 * u + 4], g1[8 * u + 5]), pack_bf16x2(g1[8 * u + 6], g1[8 * u + 7]));
-      const uint4 v2 = make_uint4(pack_bf16x2(g2[8 * u], g2[8 * u + 1]), pack_bf16x2(g2[8 * u + 2], g2[8 * u + 3]),
-                                  pack_bf16x2(g2[8 * u + 4], g2[8 * u + 5]), pack_bf16x2(g2[8 * u + 6], g2[8 * u + 7]));
-      if (stg != nullptr) {
-        const int c1 = piece * 32 + 8 * u, c2 = c1 + H;  // first column of each 16-byte unit
-        *reinterpret_cast<uint4*>(stg + (c1 >> 6) * kChunkBytes + r * 128 + ((((c1 & 63) >> 3) ^ (r & 7)) << 4)) = v1;
-        *reinterpret_cast<uint4*>(stg + (c2 >> 6) * kChunkBytes + r * 128 + ((((c2 & 63) >> 3) ^ (r & 7)) << 4)) = v2;
-      } else {
-        reinterpret_cast<uint4*>(dst + piece * 32)[u] = v1;
-        reinterpret_cast<uint4*>(dst + H + piece * 32)[u] = v2;
-      }
+      reinterpret_cast<uint4*>(dst + piece * 32)[u] =
+          make_uint4(pack_bf16x2(g1[8 * u], g1[8 * u + 1]), pack_bf16x2(g1[8 * u + 2], g1[8 * u + 3]),
+                     pack_bf16x2(g1[8 * u + 4], g1[8 * u + 5]), pack_bf16x2(g1[8 * u + 6], g1[8 * u + 7]));
+      reinterpret_cast<uint4*>(dst + H + piece * 32)[u] =
+          make_uint4(pack_bf16x2(g2[8 * u], g2[8 * u + 1]), pack_bf16x2(g2[8 * u + 2], g2[8 * u + 3]),
+                     pack_bf16x2(g2[8 * u + 4], g2[8 * u + 5]), pack_bf16x2(g2[8 * u + 6], g2[8 * u + 7]));
     }
-  }
-}
-
-// Store a staged 128-row gradient tile with TMA: every thread of the
-// warpgroup (barrier id, 128 threads) has written its row; thread 0 issues
-// the copies and waits until they have read the tile (rows past the length
-// are clipped by the tensor map).
-template <int D>
-__device__ __forceinline__ void store_staged_tile(const CUtensorMap* map, uint8_t* stg, int row0, int hl, int b,
-                                                  uint32_t bar_id, int r) {
-  fence_proxy_async_smem();  // the bulk copy reads the rows through the async proxy
-  named_barrier(bar_id, 128);
-  if (r == 0) {
-#pragma unroll
-    for (int ch = 0; ch < D / 64; ++ch) tma_store_4d(map, stg + ch * kChunkBytes, ch * 64, row0, hl, b);
-    bulk_commit();
-    bulk_wait_read();
   }
 }
 
@@ -449,14 +424,10 @@ __device__ __forceinline__ void bwd_dq_body(const BwdParams& p, int tile, int hl
       const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
       tc_fence_after();
       const int64_t toff = (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
-      // staging: K/V stage 0, idle once every MMA has completed
-      uint8_t* stg = p.tma_out ? sK0 : nullptr;
       grad_row_out<D>(tQ, have, row < p.Lq, p.scale,
                       p.qcos ? static_cast<const __nv_bfloat16*>(p.qcos) + toff : nullptr,
                       p.qcos ? static_cast<const __nv_bfloat16*>(p.qsin) + toff : nullptr, p.rope_vec != 0,
-                      static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st,
-                      stg, r);
-      if (p.tma_out) store_staged_tile<D>(&p.tm_dq, stg, q0, hl, b, 1, r);
+                      static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st);
     }
   }
   tc_fence_before();
@@ -689,23 +660,15 @@ __device__ __forceinline__ void bwd_dkdv_body(const BwdParams& p, int tile, int 
     }
     const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 37);
     tc_fence_after();
-    // staging: the Q / dO stage-0 tiles, idle once every MMA has completed
-    const int rr = key - kv0;
     if (half == 0) {
-      uint8_t* stg = p.tma_out ? sm + S::kOffQ0 : nullptr;
       grad_row_out<D>(tV, have, key < p.Lk, 1.f, nullptr, nullptr, false,
-                      static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st,
-                      stg, rr);
-      if (p.tma_out) store_staged_tile<D>(&p.tm_dv, stg, kv0, hl, b, 1, rr);
+                      static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st);
     } else {
       const int64_t toff = (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st;
-      uint8_t* stg = p.tma_out ? sm + S::kOffDO0 : nullptr;
       grad_row_out<D>(tK, have, key < p.Lk, p.scale,
                       p.kcos ? static_cast<const __nv_bfloat16*>(p.kcos) + toff : nullptr,
                       p.kcos ? static_cast<const __nv_bfloat16*>(p.ksin) + toff : nullptr, p.rope_vec != 0,
-                      static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st,
-                      stg, rr);
-      if (p.tma_out) store_staged_tile<D>(&p.tm_dk, stg, kv0, hl, b, 2, rr);
+                      static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st);
     }
   }
   tc_fence_before();

@@ -937,24 +937,6 @@ int ltxattn_bwd(const ltxattn_bwd_args* a, void* stream) {
   if ((rc = make_tmap(&p.tm_do, at(a->dout), s.D, s.Lq, s.Hc, s.B, a->dout.stride_t, a->dout.stride_h,
                       a->dout.stride_b, "dout")))
     return rc;
-  // the gradients leave through TMA stores when all three views can be TMA
-  // targets (16-byte aligned base and strides), else as per-thread row stores
-  {
-    auto tma_view = [&](const ltxattn_tensor& t) {
-      return aligned16(at(t)) && (s.B == 1 || t.stride_b % 8 == 0) && (s.Hc == 1 || t.stride_h % 8 == 0) &&
-             t.stride_t % 8 == 0;
-    };
-    p.tma_out = tma_view(a->dq) && tma_view(a->dk) && tma_view(a->dv);
-    if (p.tma_out) {
-      if ((rc = make_tmap(&p.tm_dq, at(a->dq), s.D, s.Lq, s.Hc, s.B, a->dq.stride_t, a->dq.stride_h, a->dq.stride_b,
-                          "dq")) ||
-          (rc = make_tmap(&p.tm_dk, at(a->dk), s.D, s.Lk, s.Hc, s.B, a->dk.stride_t, a->dk.stride_h, a->dk.stride_b,
-                          "dk")) ||
-          (rc = make_tmap(&p.tm_dv, at(a->dv), s.D, s.Lk, s.Hc, s.B, a->dv.stride_t, a->dv.stride_h, a->dv.stride_b,
-                          "dv")))
-        return rc;
-    }
-  }
   const bool has_mask = a->key_mask != nullptr;
   const size_t smem_dq = bwd_dq_smem_bytes(s.D, s.Lk, has_mask), smem_kv = bwd_dkdv_smem_bytes(s.D, s.Lk, has_mask);
   e = prepare_bwd_bf16(s.D, smem_dq, smem_kv);

@@ -139,8 +139,6 @@ struct CombineParams {
 // heads by blockIdx.y directly.
 struct BwdParams {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;  // [D, T, Hc, B] box {64, 128, 1, 1}
-  CUtensorMap tm_dq, tm_dk, tm_dv;      // the gradients, same form (valid when tma_out)
-  int tma_out;                          // gradient rows leave through shared memory and TMA stores
   const float* lse2;                    // [B][Hc][Lq_pad]: lse*log2(e) (bf16) or lse (f32); +inf pad
   const float* delta;                   // [B][Hc][Lq_pad]: rowsum(dO o O); 0 pad
   int Lq_pad;
