@@ -122,27 +122,10 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdPrepParams p) {
 // per entry: at config 2 that was 117 us of the backward's 810).  `have`
 // (warp-uniform: TMEM loads are warp-collective) false writes zeros; `live`
 // false skips the store.
-// The table row as 16-byte units (vector path), loaded before the wait for the
-// last MMAs so its latency overlaps them.
-template <int D>
-struct TableRow {
-  uint4 c[D / 16], s[D / 16];
-};
-template <int D>
-__device__ __forceinline__ void load_table_row(const __nv_bfloat16* c, const __nv_bfloat16* s, bool vec, bool live,
-                                               TableRow<D>& t) {
-  if (c == nullptr || !vec || !live) return;
-#pragma unroll
-  for (int u = 0; u < D / 16; ++u) {
-    t.c[u] = __ldg(reinterpret_cast<const uint4*>(c) + u);
-    t.s[u] = __ldg(reinterpret_cast<const uint4*>(s) + u);
-  }
-}
-
 template <int D>
 __device__ __forceinline__ void grad_row_out(uint32_t taddr, bool have, bool live, float scale,
                                              const __nv_bfloat16* c, const __nv_bfloat16* s, bool vec,
-                                             const TableRow<D>& tab, __nv_bfloat16* dst) {
+                                             __nv_bfloat16* dst) {
   constexpr int H = D / 2;
 #pragma unroll
   for (int piece = 0; piece < H / 32; ++piece) {
@@ -167,8 +150,8 @@ __device__ __forceinline__ void grad_row_out(uint32_t taddr, bool have, bool liv
       for (int u = 0; u < 4; ++u) {  // table entries piece*32 + 8u .. + 7
         float cc[8], ss[8];
         if (vec) {
-          const uint4 cv = tab.c[piece * 4 + u];
-          const uint4 sv = tab.s[piece * 4 + u];
+          const uint4 cv = __ldg(reinterpret_cast<const uint4*>(c + piece * 32) + u);
+          const uint4 sv = __ldg(reinterpret_cast<const uint4*>(s + piece * 32) + u);
           const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {  // bf16 -> fp32 is exact: the bits move to the top half
@@ -438,14 +421,12 @@ __device__ __forceinline__ void bwd_dq_body(const BwdParams& p, int tile, int hl
       mbar_arrive(half == 0 ? bar_ph : bar_p);
     }
     if (half == 0) {
-      const int64_t toff = (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
-      const __nv_bfloat16* tcos = p.qcos ? static_cast<const __nv_bfloat16*>(p.qcos) + toff : nullptr;
-      const __nv_bfloat16* tsin = p.qcos ? static_cast<const __nv_bfloat16*>(p.qsin) + toff : nullptr;
-      TableRow<D> tab;
-      load_table_row<D>(tcos, tsin, p.rope_vec != 0, row < p.Lq, tab);
       const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 26);
       tc_fence_after();
-      grad_row_out<D>(tQ, have, row < p.Lq, p.scale, tcos, tsin, p.rope_vec != 0, tab,
+      const int64_t toff = (int64_t)b * p.qt_sb + (int64_t)hl * p.qt_sh + (int64_t)row * p.qt_st;
+      grad_row_out<D>(tQ, have, row < p.Lq, p.scale,
+                      p.qcos ? static_cast<const __nv_bfloat16*>(p.qcos) + toff : nullptr,
+                      p.qcos ? static_cast<const __nv_bfloat16*>(p.qsin) + toff : nullptr, p.rope_vec != 0,
                       static_cast<__nv_bfloat16*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)hl * p.dq_sh + (int64_t)row * p.dq_st);
     }
   }
@@ -677,19 +658,16 @@ __device__ __forceinline__ void bwd_dkdv_body(const BwdParams& p, int tile, int 
       tc_fence_before();
       mbar_arrive(half == 0 ? bar_ph : bar_p);  // queries 0-63 feed the first half of dV and dK
     }
-    // dK's table row (half 1), loaded while the last MMAs run
-    const int64_t toff = (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st;
-    const __nv_bfloat16* tcos = (half == 1 && p.kcos) ? static_cast<const __nv_bfloat16*>(p.kcos) + toff : nullptr;
-    const __nv_bfloat16* tsin = (half == 1 && p.kcos) ? static_cast<const __nv_bfloat16*>(p.ksin) + toff : nullptr;
-    TableRow<D> tab;
-    load_table_row<D>(tcos, tsin, p.rope_vec != 0, key < p.Lk, tab);
     const bool have = ok && n > 0 && warp_wait(bar_o, 0, abort_flag, p.err, 37);
     tc_fence_after();
     if (half == 0) {
-      grad_row_out<D>(tV, have, key < p.Lk, 1.f, nullptr, nullptr, false, tab,
+      grad_row_out<D>(tV, have, key < p.Lk, 1.f, nullptr, nullptr, false,
                       static_cast<__nv_bfloat16*>(p.dv) + (int64_t)b * p.dv_sb + (int64_t)hl * p.dv_sh + (int64_t)key * p.dv_st);
     } else {
-      grad_row_out<D>(tK, have, key < p.Lk, p.scale, tcos, tsin, p.rope_vec != 0, tab,
+      const int64_t toff = (int64_t)b * p.kt_sb + (int64_t)hl * p.kt_sh + (int64_t)key * p.kt_st;
+      grad_row_out<D>(tK, have, key < p.Lk, p.scale,
+                      p.kcos ? static_cast<const __nv_bfloat16*>(p.kcos) + toff : nullptr,
+                      p.kcos ? static_cast<const __nv_bfloat16*>(p.ksin) + toff : nullptr, p.rope_vec != 0,
                       static_cast<__nv_bfloat16*>(p.dk) + (int64_t)b * p.dk_sb + (int64_t)hl * p.dk_sh + (int64_t)key * p.dk_st);
     }
   }
