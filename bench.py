@@ -458,16 +458,17 @@ def measure_e2e(ctx, args, case):
     and overlaps each block's host-to-device copy, attention and device-to-host
     copy on three streams (the result is bit-identical to one call)."""
     torch = ctx.torch
-    from ltxattn.host import HostAttention
+    from ltxattn.host import HostAttention, tapered_blocks
     q, k, v = case["q"], case["k"], case["v"]
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     # head blocks pay off when the output copy is large enough to overlap the
     # input copies (configs 2, 3, 4b, 5); a small output (config 4a, or 4c's 126
     # query rows) leaves nothing to overlap, and more blocks only add copies and
-    # launches
-    chunks = min(8, q.shape[1]) if hout.numel() * hout.element_size() >= (4 << 20) else 1
-    ha = HostAttention(q, k, v, key_mask=case["mask"], q_rotary=case["qrot"], k_rotary=case["krot"], chunks=chunks)
+    # launches.  The blocks taper (32 heads: 16, 8, 4, 2, 2): few copies, and a
+    # small last block whose attention and output copy follow the input copies
+    blocks = tapered_blocks(q.shape[1]) if hout.numel() * hout.element_size() >= (4 << 20) else [q.shape[1]]
+    ha = HostAttention(q, k, v, key_mask=case["mask"], q_rotary=case["qrot"], k_rotary=case["krot"], blocks=blocks)
     ha.run(hq, hk, hv, hout, stream=ctx.stream)  # warm
     steps = max(1, min(args.steps, 10))
     ctx.barrier()
@@ -482,7 +483,8 @@ def measure_e2e(ctx, args, case):
     return {"value": round(w.flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
             "d2h_bytes_per_step": hout.numel() * 2,
-            "pipeline": (f"{chunks} head blocks, H2D / attention / D2H overlapped on three streams" if chunks > 1
+            "pipeline": (f"head blocks of {','.join(map(str, blocks))} heads, H2D / attention / D2H overlapped on "
+                         "three streams" if len(blocks) > 1
                          else "one block: H2D, attention, D2H on three streams in sequence")}
 
 

@@ -25,18 +25,36 @@ import torch
 from .backend import AttentionBackend, Failure, PreparedAttention, Rotary
 
 
+def tapered_blocks(heads: int, smallest: int = 2) -> List[int]:
+    """Head-block sizes that halve down to ``smallest``: 32 heads -> 16, 8, 4, 2, 2.
+
+    Only the last block's attention and output copy run after the input copies
+    end, so a small last block shortens that tail, while large early blocks keep
+    the number of copies (each with a fixed cost on the copy engine) low."""
+    sizes, left = [], heads
+    while left > smallest:
+        b = max(smallest, left // 2)
+        sizes.append(b)
+        left -= b
+    if left > 0:
+        sizes.append(left)
+    return sizes
+
+
 class HostAttention:
     """Device staging buffers and per-block prepared calls for one shape.
 
     ``q``, ``k``, ``v``: the device tensors ([B, H, T, D], contiguous) that the
-    host data is copied into; ``chunks``: how many head blocks to pipeline;
-    ``num_splits``: passed to every block call (0 lets the planner choose).
-    Rotary tables, key mask and gate stay on the device (they are small and
-    reused across calls)."""
+    host data is copied into; ``chunks``: how many equal head blocks to
+    pipeline, or ``blocks``: the head-block sizes in order (summing to H; see
+    ``tapered_blocks``); ``num_splits``: passed to every block call (0 lets the
+    planner choose).  Rotary tables, key mask and gate stay on the device (they
+    are small and reused across calls)."""
 
     def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
                  key_mask: Optional[torch.Tensor] = None, q_rotary: Optional[Rotary] = None,
-                 k_rotary: Optional[Rotary] = None, chunks: int = 4, num_splits: int = 0):
+                 k_rotary: Optional[Rotary] = None, chunks: int = 4, num_splits: int = 0,
+                 blocks: Optional[List[int]] = None):
         for name, t in (("q", q), ("k", k), ("v", v)):
             if not t.is_cuda or not t.is_contiguous() or t.dim() != 4:
                 raise Failure.shape(name, t.shape, "a contiguous CUDA [B, H, T, D]")
@@ -47,9 +65,15 @@ class HostAttention:
             raise Failure.shape("k", k.shape, f"{H} heads (grouped KV heads are not pipelined)")
         self.q, self.k, self.v = q, k, v
         self.out = torch.empty_like(q)
-        n = max(1, min(chunks, H))
-        per = math.ceil(H / n)
-        self.blocks = [(h, min(per, H - h)) for h in range(0, H, per)]
+        if blocks is not None:
+            if any(b < 1 for b in blocks) or sum(blocks) != H:
+                raise Failure.shape("blocks", tuple(blocks), f"positive head counts summing to {H}")
+            starts = [sum(blocks[:i]) for i in range(len(blocks))]
+            self.blocks = list(zip(starts, blocks))
+        else:
+            n = max(1, min(chunks, H))
+            per = math.ceil(H / n)
+            self.blocks = [(h, min(per, H - h)) for h in range(0, H, per)]
         self.calls: List[PreparedAttention] = [
             AttentionBackend.prepare(q, k, v, scale, key_mask=key_mask, q_rotary=q_rotary, k_rotary=k_rotary,
                                      head_begin=h0, head_count=hc, num_splits=num_splits, out=self.out)

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from ltxattn import AttentionBackend, Rotary, device_status, inputs
-from ltxattn.host import HostAttention
+from ltxattn.host import HostAttention, tapered_blocks
 
 pytestmark = pytest.mark.gpu
 
@@ -84,3 +84,26 @@ def test_host_pipeline_with_a_key_mask():
     ha.run(host(q), host(k), host(v), hout)
     torch.cuda.synchronize()
     assert torch.equal(hout, want.cpu())
+
+
+def test_host_pipeline_with_tapered_blocks():
+    # explicit head-block sizes (the tapered schedule the benchmark uses: large
+    # blocks first, a small last block): bit-identical to the same block calls
+    q, k, v, rot = _case()
+    dq, dk, dv = dev(q), dev(k), dev(v)
+    sizes = tapered_blocks(8)
+    assert sizes == [4, 2, 2]
+    want = torch.empty_like(dq)
+    h0 = 0
+    for hc in sizes:
+        AttentionBackend.attention(dq, dk, dv, q_rotary=rot, head_begin=h0, head_count=hc, out=want)
+        h0 += hc
+    hout = torch.empty(q.shape, dtype=torch.bfloat16).pin_memory()
+    ha = HostAttention(torch.empty_like(dq), torch.empty_like(dq), torch.empty_like(dq), q_rotary=rot, blocks=sizes)
+    assert [(b0, bc) for b0, bc in ha.blocks] == [(0, 4), (4, 2), (6, 2)]
+    ha.run(host(q), host(k), host(v), hout)
+    torch.cuda.synchronize()
+    assert torch.equal(hout, want.cpu())
+    with pytest.raises(Exception):
+        HostAttention(torch.empty_like(dq), torch.empty_like(dq), torch.empty_like(dq), blocks=[4, 2])  # sums to 6
+    assert device_status(clear=True) == 0
