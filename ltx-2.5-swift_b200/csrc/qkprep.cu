@@ -164,7 +164,7 @@ __device__ __forceinline__ float warp_sumsq(const Raw16<T>& xc) {
 template <typename T>
 __global__ void __launch_bounds__(512, sizeof(T) == 2 ? LTX_QK_MIN_BLOCKS_BF16 : 1) qk_prep_kernel(const QkPrepParams p) {
   grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
-  __shared__ float wsum[2][16];  // per-warp partials, alternating by row
+  __shared__ __align__(16) float wsum[2][16];  // per-warp partials, alternating by row
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int rows = p.B * p.tokens;
   const int e0 = tid * 16;
@@ -256,8 +256,15 @@ __device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int sta
   load16<T>(wr, static_cast<const T*>(p.w) + e0, true);
 
   int i = 0, par = 0;
+  int b = blk / p.tokens, t = blk - b * p.tokens;  // (batch, token) of `row`, advanced without a division
   for (int row = blk; row < rows; row += G, ++i, par ^= 1) {
-    const int b = row / p.tokens, t = row - b * p.tokens;
+    if (i > 0) {
+      t += G;
+      while (t >= p.tokens) {
+        t -= p.tokens;
+        ++b;
+      }
+    }
     Raw16<T> cr, sr;
     if (rope) {
       const int64_t toff = (int64_t)b * p.t_sb + (int64_t)h * p.t_sh + (int64_t)t * p.t_st + j0;
@@ -284,8 +291,20 @@ __device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int sta
       bulk_load(ring + (size_t)s * p.inner, row_src(blk + issued * G), row_bytes, full + s);
       ++issued;
     }
+    // the warp partials in warp order (16-byte reads, the same sums)
     float tot = 0.f;
-    for (int k = 0; k < nwarps; ++k) tot += wsum[par][k];
+    {
+      const float4* w4 = reinterpret_cast<const float4*>(wsum[par]);
+      int k = 0;
+      for (; k + 4 <= nwarps; k += 4) {
+        const float4 a = w4[k >> 2];
+        tot += a.x;
+        tot += a.y;
+        tot += a.z;
+        tot += a.w;
+      }
+      for (; k < nwarps; ++k) tot += wsum[par][k];
+    }
     const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)p.inner), p.eps));
     T* out = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)t * p.o_st + d0;
     finish_row<T>(xc, wr, r, rope, cr, sr, lower, partner, out, true);
@@ -300,7 +319,7 @@ template <typename T>
 __global__ void __launch_bounds__(512) qk_prep_bulk_kernel(const QkPrepParams p, int stages) {
   grid_dep_launch_dependents();  // the attention kernel after this one may start its prologue
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float wsum[2][16];
+  __shared__ __align__(16) float wsum[2][16];
   __shared__ int abort_flag;
   qk_prep_bulk_body<T>(p, stages, blockIdx.x, gridDim.x, smem_raw, wsum, abort_flag);
 }
@@ -311,7 +330,7 @@ __global__ void __launch_bounds__(512) qk_prep_bulk_pair_kernel(const QkPrepPara
                                                                  int stages, int g0) {
   grid_dep_launch_dependents();
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float wsum[2][16];
+  __shared__ __align__(16) float wsum[2][16];
   __shared__ int abort_flag;
   if ((int)blockIdx.x < g0)
     qk_prep_bulk_body<T>(p0, stages, blockIdx.x, g0, smem_raw, wsum, abort_flag);
