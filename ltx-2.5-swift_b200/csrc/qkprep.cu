@@ -255,14 +255,24 @@ __device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int sta
   Raw16<T> wr;
   load16<T>(wr, static_cast<const T*>(p.w) + e0, true);
 
+  // mean = tot / inner: for a power-of-two width the product with 1 / inner is
+  // the same correctly rounded value (the exact quotient is a scaling by 2^-k)
+  const bool inner_pow2 = (p.inner & (p.inner - 1)) == 0;
+  const float inv_inner = 1.0f / (float)p.inner;
   int i = 0, par = 0;
   int b = blk / p.tokens, t = blk - b * p.tokens;  // (batch, token) of `row`, advanced without a division
+  int s = 0;                                       // ring stage of slot i (i % stages) ...
+  uint32_t ph = 0;                                 // ... and its phase parity ((i / stages) & 1)
   for (int row = blk; row < rows; row += G, ++i, par ^= 1) {
     if (i > 0) {
       t += G;
       while (t >= p.tokens) {
         t -= p.tokens;
         ++b;
+      }
+      if (++s == stages) {
+        s = 0;
+        ph ^= 1u;
       }
     }
     Raw16<T> cr, sr;
@@ -271,8 +281,7 @@ __device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int sta
       load16<T>(cr, static_cast<const T*>(p.cos) + toff, true);
       load16<T>(sr, static_cast<const T*>(p.sin) + toff, true);
     }
-    const int s = i % stages;
-    const bool ok = mbar_wait(full + s, (uint32_t)(i / stages) & 1u, (volatile int*)&abort_flag, p.err, 40);
+    const bool ok = mbar_wait(full + s, ph, (volatile int*)&abort_flag, p.err, 40);
     Raw16<T> xc;
     if (ok) {
       const uint4* src = reinterpret_cast<const uint4*>(ring + (size_t)s * p.inner + e0);
@@ -305,7 +314,8 @@ __device__ __forceinline__ void qk_prep_bulk_body(const QkPrepParams& p, int sta
       }
       for (; k < nwarps; ++k) tot += wsum[par][k];
     }
-    const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)p.inner), p.eps));
+    const float mean = inner_pow2 ? __fmul_rn(tot, inv_inner) : __fdiv_rn(tot, (float)p.inner);
+    const float r = 1.0f / sqrtf(__fadd_rn(mean, p.eps));
     T* out = static_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)t * p.o_st + d0;
     finish_row<T>(xc, wr, r, rope, cr, sr, lower, partner, out, true);
   }
