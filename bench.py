@@ -628,11 +628,30 @@ def run_qkprep(args):
     rot = Rotary(torch.from_numpy(c).to("cuda", torch.bfloat16), torch.from_numpy(sn).to("cuda", torch.bfloat16))
     outs = [torch.empty((B, H, T, D), device="cuda", dtype=torch.bfloat16) for _ in range(2)]
 
-    def step():  # q and k in one launch (ltxattn_qk_prep_pair)
-        qk_prep_pair(xs[0], w, xs[1], w, H, rot, rot, eps=1e-6, out_q=outs[0], out_k=outs[1], stream=ctx.stream)
+    def call(stream):  # q and k in one launch (ltxattn_qk_prep_pair)
+        qk_prep_pair(xs[0], w, xs[1], w, H, rot, rot, eps=1e-6, out_q=outs[0], out_k=outs[1], stream=stream)
+
+    # captured once and replayed per step, as the attention workloads are, so the
+    # wrapper's host work between the start event and the launch is not timed
+    call(ctx.stream)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        call(side)
+    torch.cuda.current_stream().wait_stream(side)
+    step = graph.replay
 
     clocks = Clocks(ctx.local)
     clocks.start()
+    # keep the GPU loaded for ~0.5 s first: the sampler process starts meanwhile,
+    # so its start-up does not land inside a timed step
+    t_end = time.perf_counter() + 0.5
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
     step_ms = ctx.timed(step, args.steps, warmup=args.warmup)
     clk = clocks.stop()
     hx = [x.cpu().pin_memory() for x in xs]
@@ -712,6 +731,10 @@ def run_module(args):
     flops = gemm_flops + attn_flops
     clocks = Clocks(ctx.local)
     clocks.start()
+    t_end = time.perf_counter() + 0.5  # the sampler starts while the GPU is loaded, not inside a timed step
+    while time.perf_counter() < t_end:
+        mod(x, rotary=rot)
+        torch.cuda.synchronize()
     step_ms = ctx.timed(lambda: mod(x, rotary=rot), args.steps, warmup=args.warmup)
     clk = clocks.stop()
     hx = x.cpu().pin_memory()
