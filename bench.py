@@ -479,8 +479,19 @@ def measure_e2e(ctx, args, case):
     e1.record(ctx.stream)
     ctx.barrier()
     ms = ctx.max_over_ranks([e0.elapsed_time(e1) / steps])[0]
+    # the host output against the device call's output (same inputs and tables):
+    # the head-block calls may split KV ranges differently from one call, so the
+    # two agree within the bf16 tolerance of a split, not bit for bit
+    torch.cuda.synchronize()
+    ref = case["call"].out.float().cpu()
+    err = (hout.float() - ref).abs()
+    max_abs = float(err.max())
+    rel = float(err.norm() / max(float(ref.norm()), 1e-30))
+    max_abs, rel = ctx.max_over_ranks([max_abs, rel])
     w = case["w"]
     return {"value": round(w.flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "check": {"against": "the device call's output", "max_abs": round(max_abs, 6), "rel_l2": round(rel, 6),
+                      "ok": bool(max_abs <= 2e-2 and rel <= 1e-2)},
             "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
             "d2h_bytes_per_step": hout.numel() * 2,
             "pipeline": (f"head blocks of {','.join(map(str, blocks))} heads, H2D / attention / D2H overlapped on "
