@@ -217,7 +217,8 @@ def device_case(ctx, wl, h0, hc):
     from ltxattn import Rotary
     w = WORKLOADS[wl]
     dt = torch.bfloat16
-    case = {"w": w, "h0": h0, "hc": hc, "qrot": None, "krot": None, "mask": None, "tabs": None, "mask_np": None}
+    case = {"w": w, "wl": wl, "h0": h0, "hc": hc, "qrot": None, "krot": None, "mask": None, "tabs": None,
+            "mask_np": None}
     if wl == "c5":
         # 29,760 tokens x 32 heads would take minutes on the host generator: draw
         # N(0,1) on the device, one generator per head so every rank's block is
@@ -524,10 +525,38 @@ def measure_gather(ctx, args, case):
         hg.close()
     w = case["w"]
     total = full.numel() * full.element_size()
-    return {"gather_ms": round(g, 5), "bytes_gathered_per_rank": total,
+    fused = measure_fused_gather(ctx, args, case, full) if args.fused_gather else None
+    return {"gather_ms": round(g, 5), "bytes_gathered_per_rank": total, "fused": fused,
             "algbw_gbs": round(total / (g * 1e-3) / 1e9, 1),
             "value_with_gather": round(w.flops / (b * 1e-3) / 1e12, 3), "ms_per_step_with_gather": round(b, 5),
             "nccl_nranks": nranks, "nccl_rank": nrank, "nccl_nranks_ok": nranks == ctx.ws}
+
+
+def measure_fused_gather(ctx, args, case, gathered):
+    """N > 1, --fused-gather: ltxattn_fwd_gather (the attention's epilogue stores
+    every output tile into every rank's output over NVLink) on the same job, timed
+    like "with gather", and its output checked against the call + NCCL gather."""
+    torch = ctx.torch
+    from ltxattn.dist import FusedHeadGather
+    wl = case["wl"]
+    w = case["w"]
+    full_case = device_case(ctx, wl, 0, w.H)  # every head's inputs; each rank reads its block
+    fg = FusedHeadGather(tuple(full_case["q"].shape))
+    try:
+        def run():
+            fg.run(full_case["q"], full_case["k"], full_case["v"], q_rotary=full_case["qrot"],
+                   k_rotary=full_case["krot"], stream=ctx.stream)
+        f_ms = ctx.timed(run, args.steps, warmup=args.warmup)
+        torch.cuda.synchronize()
+        err = (fg.out.float() - gathered.float()).abs()
+        max_abs = float(err.max())
+        f, max_abs = ctx.max_over_ranks([sum(f_ms) / args.steps, max_abs])
+    finally:
+        fg.close()
+    return {"ms_per_step": round(f, 5), "value": round(w.flops / (f * 1e-3) / 1e12, 3),
+            "max_abs_vs_nccl_gather": round(max_abs, 6),
+            "how": "ltxattn_fwd_gather: KV ranges unsplit, peer stores of every output tile in the epilogue, "
+                   "bounded entry and arrival handshakes"}
 
 
 def run_ours(args):
@@ -1018,6 +1047,8 @@ def main():
                     choices=sorted(WORKLOADS) + ["benchgemm", "qkprep", "module", "outproj"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the chosen workload (no sub-records)")
+    ap.add_argument("--fused-gather", action="store_true",
+                    help="N > 1: also time ltxattn_fwd_gather (the all-gather fused into the attention)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--bwd", action="store_true", help="also time the training backward")
     ap.add_argument("--traffic-launches", action="store_true",

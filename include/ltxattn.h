@@ -198,6 +198,36 @@ LTXATTN_API int ltxattn_fwd_plan(const ltxattn_fwd_args* args, ltxattn_fwd_plan_
  * ordered (one stream, or explicit events). */
 LTXATTN_API int ltxattn_fwd_noalloc(const ltxattn_fwd_args* args, void* stream);
 
+/* ---- head-sharded forward with the all-gather fused into its epilogue ---- */
+
+/* Every rank's full output tensor and signal words, mapped on the calling
+ * device (CUDA IPC over NVLink).  signals[d] is rank d's array of 16 uint32
+ * words, zero at allocation: [0, 8) count the output tiles that arrived from
+ * each source rank, [8, 16) hold the last call each rank has entered. */
+typedef struct ltxattn_gather_peers {
+  int32_t world;          /* ranks, 2 to 8 */
+  int32_t rank;           /* this rank */
+  void* out[8];           /* rank d's output [B, H, T, D] (out[rank] == args->out.data) */
+  uint32_t* signals[8];   /* rank d's 16 signal words */
+  uint32_t epoch;         /* 1, 2, 3, ...: one per call, the same on every rank */
+  int32_t reserved;
+} ltxattn_gather_peers;
+
+/* ltxattn_fwd of this rank's head block (args->head_begin / head_count; every
+ * rank passes the same shape and head_count), whose epilogue also stores each
+ * output tile into every other rank's output with peer stores over NVLink, so
+ * the all-gather overlaps the attention tile by tile (the head-parallel
+ * counterpart of the call followed by ltxattn_allgather_heads; no counterpart in
+ * the reference, which runs one device).  Stream-ordered: the work queued after
+ * it sees every rank's heads in args->out.  Before storing into the peers'
+ * outputs the call waits until every rank has entered the same epoch (so a
+ * rank's earlier work on its output has completed); every cross-device wait is
+ * bounded and reports LTXATTN_ERR_TIMEOUT through ltxattn_device_status.  bf16
+ * only; KV ranges are not split (num_splits is taken as 1); the output must be
+ * 16-byte aligned with strides that are multiples of 8 elements; not for
+ * stream capture (the epoch is a launch argument). */
+LTXATTN_API int ltxattn_fwd_gather(const ltxattn_fwd_args* args, const ltxattn_gather_peers* peers, void* stream);
+
 /* Replaces the autodiff VJP of the SDPA core (LoRA training backward). */
 LTXATTN_API int ltxattn_bwd(const ltxattn_bwd_args* args, void* stream);
 

@@ -563,9 +563,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
         for (int ch = 0; ch < S::kChunks; ++ch)
           tma_store_4d(&p.tm_o, stg + ch * kChunkBytes, ch * 64, ue.q_block * kBlockM + t * kTileM,
                        p.head_begin + ue.hl, ue.b);
+        // fused all-gather: the same tile into every other rank's output (the
+        // copies read shared memory and leave; the transfer over NVLink overlaps
+        // whatever runs next on this SM)
+        for (int i = 0; i < p.peer_n; ++i)
+#pragma unroll
+          for (int ch = 0; ch < S::kChunks; ++ch)
+            tma_store_4d(&p.tm_peer[i], stg + ch * kChunkBytes, ch * 64, ue.q_block * kBlockM + t * kTileM,
+                         p.head_begin + ue.hl, ue.b);
         bulk_commit();
-        bulk_wait_read();  // the CTA's shared memory must outlive the copy's reads
       }
+      if (r == 0) bulk_wait_read();  // the CTA's shared memory must outlive the copy's reads
     } else {
       // fp32 partial of this split: staged like the bf16 output (128 rows x D fp32
       // = two K/V tiles' worth, so tile t uses 2 * kTile bytes from sK + 2t * kTile),
@@ -612,6 +620,56 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_bf16_sm100_kernel(const __gri
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Entry handshake of the fused all-gather: tell every peer that this rank has
+// entered call `epoch` (its earlier work on its own output is complete: this
+// kernel follows it in stream order), then wait until every peer has entered
+// it too, so no peer store lands in an output that its rank still reads.
+// Bounded: on timeout the error word records site 60 and the kernel returns.
+__global__ void gather_enter_kernel(const GatherSync g) {
+  const int d = threadIdx.x;
+  const bool peer = d < g.n && d != g.rank;
+  if (peer) {
+    __threadfence_system();
+    atomicMax_system(g.sig[d] + 8 + g.rank, g.epoch);
+  }
+  if (peer) {
+    volatile unsigned int* f = g.sig[g.rank] + 8 + d;
+    const uint64_t t0 = globaltimer_ns();
+    while (*f < g.epoch) {
+      if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) {
+        atomicCAS(g.err, 0, (60 << 8) | kErrTimeout);
+        break;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+// Completion of the fused all-gather, after the attention kernel: every store of
+// that kernel (its tiles in the other ranks' outputs included) has been performed
+// when this kernel starts, so tell every peer that this rank's tiles of `epoch`
+// have landed, then wait until every peer has said the same here.  Bounded
+// (site 61).
+__global__ void gather_done_kernel(const GatherSync g) {
+  const int d = threadIdx.x;
+  const bool peer = d < g.n && d != g.rank;
+  if (peer) {
+    __threadfence_system();
+    atomicMax_system(g.sig[d] + g.rank, g.epoch);
+  }
+  if (peer) {
+    volatile unsigned int* f = g.sig[g.rank] + d;
+    const uint64_t t0 = globaltimer_ns();
+    while (*f < g.epoch) {
+      if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) {
+        atomicCAS(g.err, 0, (61 << 8) | kErrTimeout);
+        break;
+      }
+    }
+  }
+  __threadfence_system();
 }
 
 // Merge split partials: lse = log2-sum-exp2 of the splits' lse, O = sum_s w_s O_s.
@@ -729,6 +787,16 @@ cudaError_t launch_fwd_bf16(const FwdParams& p, int D, size_t smem, cudaStream_t
   if (D == 128) return launch_pdl(fwd_bf16_sm100_kernel<128, false>, grid, dim3(kThreads), smem, s, p);
   if (banded) return launch_pdl(fwd_bf16_sm100_kernel<64, true>, grid, dim3(kThreads), smem, s, p);
   return launch_pdl(fwd_bf16_sm100_kernel<64, false>, grid, dim3(kThreads), smem, s, p);
+}
+
+cudaError_t launch_gather_enter(const GatherSync& g, cudaStream_t s) {
+  gather_enter_kernel<<<1, 32, 0, s>>>(g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_done(const GatherSync& g, cudaStream_t s) {
+  gather_done_kernel<<<1, 32, 0, s>>>(g);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s) {

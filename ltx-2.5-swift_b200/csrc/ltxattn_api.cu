@@ -481,7 +481,18 @@ int ltxattn_fwd_plan(const ltxattn_fwd_args* a, ltxattn_fwd_plan_info* info) {
   return LTXATTN_OK;
 }
 
-int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
+}  // extern "C"
+
+// ltxattn_fwd, and ltxattn_fwd_gather when g is set (validated by the caller):
+// the same call with KV ranges unsplit and the epilogue's peer stores.
+static int fwd_impl(const ltxattn_fwd_args* a_in, void* stream, const ltxattn_gather_peers* g) {
+  ltxattn_fwd_args a_unsplit;
+  const ltxattn_fwd_args* a = a_in;
+  if (g != nullptr) {
+    a_unsplit = *a_in;
+    a_unsplit.num_splits = 1;
+    a = &a_unsplit;
+  }
   FwdPlan P;
   int rc = plan_fwd(a, &P);
   if (rc) return rc;
@@ -631,6 +642,22 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     return rc;
   p.part_lse = P.splits > 1 ? reinterpret_cast<float*>(ws + P.off_pl) : nullptr;
   p.err = err;
+  GatherSync gs{};
+  if (g != nullptr) {
+    gs.n = g->world;
+    gs.rank = g->rank;
+    gs.epoch = g->epoch;
+    gs.err = err;
+    for (int d = 0; d < g->world; ++d) {
+      gs.sig[d] = g->signals[d];
+      if (d == g->rank) continue;
+      // rank d's output, same geometry as this rank's (every rank passes the same shape)
+      if ((rc = make_tmap(&p.tm_peer[p.peer_n], g->out[d], s.D, s.Lq, s.H, s.B, a->out.stride_t, a->out.stride_h,
+                          a->out.stride_b, "peer out")))
+        return rc;
+      ++p.peer_n;
+    }
+  }
   const size_t smem = fwd_bf16_smem_bytes(s.D, s.Lk, a->key_mask != nullptr);
   e = prepare_fwd_bf16(s.D, smem);
   if (e == cudaErrorInvalidConfiguration)
@@ -656,8 +683,10 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "fwd_persist launch");
     return LTXATTN_OK;
   }
+  if (g != nullptr && (e = launch_gather_enter(gs, st)) != cudaSuccess) return cuda_fail(e, "gather entry launch");
   e = launch_fwd_bf16(p, s.D, smem, st);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
+  if (g != nullptr && (e = launch_gather_done(gs, st)) != cudaSuccess) return cuda_fail(e, "gather completion launch");
   if (P.splits > 1) {
     CombineParams c{};
     c.part_o = reinterpret_cast<const float*>(ws + P.off_po);
@@ -685,6 +714,29 @@ int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
   return LTXATTN_OK;
+}
+
+extern "C" {
+
+int ltxattn_fwd(const ltxattn_fwd_args* a, void* stream) { return fwd_impl(a, stream, nullptr); }
+
+int ltxattn_fwd_gather(const ltxattn_fwd_args* a, const ltxattn_gather_peers* g, void* stream) {
+  if (a == nullptr || g == nullptr) return fail(LTXATTN_ERR_ARG, "args or peers is NULL");
+  if (a->dtype != LTXATTN_BF16) return fail(LTXATTN_ERR_DTYPE, "ltxattn_fwd_gather: bf16 only");
+  if (g->world < 2 || g->world > 8 || g->rank < 0 || g->rank >= g->world)
+    return fail(LTXATTN_ERR_ARG, "ltxattn_fwd_gather: rank %d of world %d (2 to 8 ranks)", g->rank, g->world);
+  if (g->epoch == 0) return fail(LTXATTN_ERR_ARG, "ltxattn_fwd_gather: epochs start at 1");
+  if (g->out[g->rank] != a->out.data)
+    return fail(LTXATTN_ERR_ARG, "ltxattn_fwd_gather: peers->out[rank] must be args->out.data");
+  for (int d = 0; d < g->world; ++d) {
+    if (g->out[d] == nullptr || g->signals[d] == nullptr)
+      return fail(LTXATTN_ERR_ARG, "ltxattn_fwd_gather: rank %d's output or signal words are NULL", d);
+    if ((reinterpret_cast<uintptr_t>(g->out[d]) & 15u) || (reinterpret_cast<uintptr_t>(g->signals[d]) & 3u))
+      return fail(LTXATTN_ERR_ALIGN, "ltxattn_fwd_gather: rank %d's output must be 16-byte aligned", d);
+  }
+  if ((a->out.stride_b % 8) || (a->out.stride_h % 8) || (a->out.stride_t % 8))
+    return fail(LTXATTN_ERR_ALIGN, "ltxattn_fwd_gather: output strides must be multiples of 8 elements");
+  return fwd_impl(a, stream, g);
 }
 
 }  // extern "C"

@@ -54,8 +54,25 @@ struct FwdParams {
   float* part_lse;   // [splits][n_tail][256] log2 domain (n_tail > 0)
   const __nv_bfloat16* gate;  // [B, Lq, H] gate logits or null (global head index)
   int64_t g_sb, g_st, g_sh;
+  // Fused all-gather (ltxattn_fwd_gather): peer_n > 0 makes the epilogue also
+  // store each output tile with TMA into the outputs of the other ranks
+  // (tm_peer[i]: the output of the i-th other rank, same geometry as tm_o).
+  int peer_n;
+  int* err;
+  CUtensorMap tm_peer[7];
+};
+
+// Cross-device entry / arrival handshakes of ltxattn_fwd_gather (signal words:
+// [0, 8) "rank d's tiles of this epoch have landed here", [8, 16) "rank d has
+// entered this epoch").
+struct GatherSync {
+  unsigned int* sig[8];
+  int n, rank;
+  unsigned int epoch;
   int* err;
 };
+cudaError_t launch_gather_enter(const GatherSync& g, cudaStream_t s);
+cudaError_t launch_gather_done(const GatherSync& g, cudaStream_t s);
 
 // Forward, fp32 SIMT path (parity path for the float32 dtype).
 struct F32Params {

@@ -29,7 +29,7 @@ EXPORTED = (
     "ltxattn_last_error", "ltxattn_device_status", "ltxattn_abi_version",
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
     "ltxattn_linear", "ltxattn_linear_workspace", "ltxattn_head_gate",
-    "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce",
+    "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce", "ltxattn_fwd_gather",
 )
 
 
@@ -57,6 +57,11 @@ class FwdArgs(ctypes.Structure):
                 ("causal", ctypes.c_int32), ("window", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
                 ("gate", ctypes.c_void_p), ("gate_stride_b", ctypes.c_int64), ("gate_stride_t", ctypes.c_int64),
                 ("gate_stride_h", ctypes.c_int64)]
+
+
+class GatherPeers(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("out", ctypes.c_void_p * 8),
+                ("signals", ctypes.c_void_p * 8), ("epoch", ctypes.c_uint32), ("reserved", ctypes.c_int32)]
 
 
 class FwdPlanInfo(ctypes.Structure):
@@ -166,6 +171,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_fwd.restype = ctypes.c_int
     L.ltxattn_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), vp]
     L.ltxattn_fwd_noalloc.restype = ctypes.c_int
+    L.ltxattn_fwd_gather.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(GatherPeers), vp]
+    L.ltxattn_fwd_gather.restype = ctypes.c_int
     L.ltxattn_fwd_workspace.argtypes = [ctypes.POINTER(FwdArgs)]
     L.ltxattn_fwd_workspace.restype = ctypes.c_size_t
     L.ltxattn_fwd_plan.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(FwdPlanInfo)]

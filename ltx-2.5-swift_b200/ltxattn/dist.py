@@ -151,3 +151,115 @@ def gather_layout(blocks):
     """The layout contract of ltxattn_allgather_heads, for host-side checks: rank r's
     [B, H/N, T, D] block lands at heads [r*H/N, (r+1)*H/N) of [B, H, T, D]."""
     return torch.cat(list(blocks), dim=1)
+
+
+class FusedHeadGather:
+    """Buffers and calls of ``ltxattn_fwd_gather``: the head-sharded attention
+    whose epilogue stores each output tile into every rank's output over NVLink
+    (the all-gather fused into the attention).
+
+    Each rank allocates one device block (cudaMalloc): 16 signal words, then its
+    full output ``out`` [B, H, T, D] bf16.  The blocks' CUDA IPC handles are
+    exchanged through ``torch.distributed`` and opened on this rank's device
+    with lazy peer access, so every rank holds device pointers to every rank's
+    output and signal words.  ``run`` computes this rank's head block
+    (``head_block``) and returns with every rank's heads in ``out`` (stream
+    ordered).  Every rank must call ``run`` the same number of times with the
+    same shapes; ``close`` releases the mappings (collective: every rank calls
+    it)."""
+
+    _SIG_BYTES = 256  # 16 uint32 words, padded so the output starts 256-byte aligned
+
+    def __init__(self, shape, group=None):
+        from cuda.bindings import runtime as cudart
+        self._rt = cudart
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise Failure("arg", f"world {self.world}: ltxattn_fwd_gather joins 2 to 8 ranks", _lib.ERR_ARG)
+        B, H, T, D = (int(x) for x in shape)
+        self.shape = (B, H, T, D)
+        self.device = torch.cuda.current_device()
+        self._ok(cudart.cudaSetDevice(self.device))
+        nbytes = self._SIG_BYTES + B * H * T * D * 2
+        self._base = int(self._ok(cudart.cudaMalloc(nbytes)))
+        self._ok(cudart.cudaMemset(self._base, 0, self._SIG_BYTES))
+        self._ok(cudart.cudaDeviceSynchronize())
+        handle = self._ok(cudart.cudaIpcGetMemHandle(self._base))
+        mine = bytes(handle.reserved)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        self._opened = []
+        self.peer_base = []
+        for d, h in enumerate(handles):
+            if d == self.rank:
+                self.peer_base.append(self._base)
+                continue
+            ph = cudart.cudaIpcMemHandle_t()
+            ph.reserved = h
+            ptr = int(self._ok(cudart.cudaIpcOpenMemHandle(ph, cudart.cudaIpcMemLazyEnablePeerAccess)))
+            self._opened.append(ptr)
+            self.peer_base.append(ptr)
+        self.epoch = 0
+        self.out = torch.as_tensor(_DeviceArray(self._base + self._SIG_BYTES, (B, H, T, D)),
+                                   device=torch.device("cuda", self.device)).view(torch.bfloat16)
+        self.signals = torch.as_tensor(_DeviceArray(self._base, (self._SIG_BYTES // 2,)),
+                                       device=torch.device("cuda", self.device)).view(torch.int32)[:16]
+        self._peers = _lib.GatherPeers()
+        self._peers.world, self._peers.rank = self.world, self.rank
+        for d, b in enumerate(self.peer_base):
+            self._peers.out[d] = b + self._SIG_BYTES
+            self._peers.signals[d] = b
+        dist.barrier(group=group)  # every rank has mapped every block before any call stores into it
+
+    def _ok(self, res):
+        err = res[0]
+        if int(err) != 0:
+            raise Failure("cuda", f"CUDA runtime call failed: {err}", _lib.ERR_CUDA)
+        return res[1] if len(res) > 1 else None
+
+    def run(self, q, k, v, scale: Optional[float] = None, q_rotary=None, k_rotary=None, stream=None):
+        """This rank's head block of attention(q, k, v) (full [B, H, T, D] inputs on
+        this device; only the block's heads are read), gathered into ``out`` on
+        every rank."""
+        from .backend import AttentionBackend, _stream_ptr
+        H, D = self.shape[1], self.shape[3]
+        h0, hc = head_block(H, self.world, self.rank)
+        if scale is None:
+            scale = 1.0 / float(D) ** 0.5
+        a, _ = AttentionBackend.make_fwd_args(q, k, v, scale, q_rotary=q_rotary, k_rotary=k_rotary, out=self.out,
+                                              head_begin=h0, head_count=hc, num_splits=1)
+        L = _lib.load()
+        n = int(L.ltxattn_fwd_workspace(ctypes.byref(a)))
+        ws = None
+        if n > 0:
+            ws = torch.empty(n + 256, dtype=torch.uint8, device=q.device)
+            a.workspace = (ws.data_ptr() + 255) // 256 * 256
+            a.workspace_bytes = n
+        self.epoch += 1
+        self._peers.epoch = self.epoch
+        rc = L.ltxattn_fwd_gather(ctypes.byref(a), ctypes.byref(self._peers), ctypes.c_void_p(_stream_ptr(stream)))
+        if rc != _lib.OK:
+            raise Failure.from_status(rc)
+        self._ws = ws  # the workspace lives until the next call (stream-ordered use)
+        return self.out
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still stores into a block about to be unmapped
+        for ptr in self._opened:
+            self._ok(self._rt.cudaIpcCloseMemHandle(ptr))
+        self._opened = []
+        dist.barrier(group=self.group)
+        if self._base:
+            self._ok(self._rt.cudaFree(self._base))
+            self._base = 0
+
+
+class _DeviceArray:
+    """A device pointer with a shape, for torch.as_tensor (int16 elements)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": "<i2",
+                                         "version": 3, "strides": None}
