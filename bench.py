@@ -555,8 +555,8 @@ def measure_fused_gather(ctx, args, case, gathered):
         fg.close()
     return {"ms_per_step": round(f, 5), "value": round(w.flops / (f * 1e-3) / 1e12, 3),
             "max_abs_vs_nccl_gather": round(max_abs, 6),
-            "how": "ltxattn_fwd_gather: KV ranges unsplit, peer stores of every output tile in the epilogue, "
-                   "bounded entry and arrival handshakes"}
+            "how": "ltxattn_fwd_gather: TMA stores of every output tile into the other ranks' outputs in the "
+                   "epilogue (split rows from the combine), bounded entry and completion handshakes"}
 
 
 def run_ours(args):

@@ -223,9 +223,11 @@ typedef struct ltxattn_gather_peers {
  * outputs the call waits until every rank has entered the same epoch (so a
  * rank's earlier work on its output has completed); every cross-device wait is
  * bounded and reports LTXATTN_ERR_TIMEOUT through ltxattn_device_status.  bf16
- * only; KV ranges are not split (num_splits is taken as 1); the output must be
- * 16-byte aligned with strides that are multiples of 8 elements; not for
- * stream capture (the epoch is a launch argument). */
+ * only; the call runs the tiled kernel (KV splits as planned, their combine
+ * storing to the peers too; a call planned for a persistent kernel runs tiled
+ * and unsplit); the output must be 16-byte aligned with strides that are
+ * multiples of 8 elements; not for stream capture (the epoch is a launch
+ * argument). */
 LTXATTN_API int ltxattn_fwd_gather(const ltxattn_fwd_args* args, const ltxattn_gather_peers* peers, void* stream);
 
 /* Replaces the autodiff VJP of the SDPA core (LoRA training backward). */

@@ -704,17 +704,22 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     }
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  __nv_bfloat16* orow = p.out + (int64_t)b * p.o_sb + (int64_t)(p.head_begin + hl) * p.o_sh + (int64_t)row * p.o_st;
+  const int64_t ooff = (int64_t)b * p.o_sb + (int64_t)(p.head_begin + hl) * p.o_sh + (int64_t)row * p.o_st;
+  __nv_bfloat16 ov[kPer];
   if (p.gate != nullptr) {  // T(T(O) * g)
     const float g = gate_bf16(
         __bfloat162float(p.gate[(int64_t)b * p.g_sb + (int64_t)row * p.g_st + (int64_t)(p.head_begin + hl) * p.g_sh]));
 #pragma unroll
-    for (int e = 0; e < kPer; ++e)
-      orow[lane + 32 * e] = __float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(acc[e] * inv)) * g);
+    for (int e = 0; e < kPer; ++e) ov[e] = __float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(acc[e] * inv)) * g);
   } else {
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) orow[lane + 32 * e] = __float2bfloat16_rn(acc[e] * inv);
+    for (int e = 0; e < kPer; ++e) ov[e] = __float2bfloat16_rn(acc[e] * inv);
   }
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) p.out[ooff + lane + 32 * e] = ov[e];
+  for (int i = 0; i < p.peer_n; ++i)  // fused all-gather: the row in every other rank's output
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) p.peer_out[i][ooff + lane + 32 * e] = ov[e];
   if (p.lse != nullptr && lane == 0)
     p.lse[(int64_t)b * p.lse_sb + (int64_t)(p.head_begin + hl) * p.lse_sh + row] =
         (wsum > 0.f) ? (mx + log2f(wsum)) * kLn2 : -INFINITY;

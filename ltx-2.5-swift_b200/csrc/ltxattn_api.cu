@@ -488,14 +488,17 @@ int ltxattn_fwd_plan(const ltxattn_fwd_args* a, ltxattn_fwd_plan_info* info) {
 static int fwd_impl(const ltxattn_fwd_args* a_in, void* stream, const ltxattn_gather_peers* g) {
   ltxattn_fwd_args a_unsplit;
   const ltxattn_fwd_args* a = a_in;
-  if (g != nullptr) {
-    a_unsplit = *a_in;
-    a_unsplit.num_splits = 1;
-    a = &a_unsplit;
-  }
   FwdPlan P;
   int rc = plan_fwd(a, &P);
   if (rc) return rc;
+  if (g != nullptr && (P.persist || P.short_kv)) {
+    // the fused all-gather lives in the tiled kernel and the combine: a call the
+    // planner gives to a persistent kernel runs tiled with unsplit KV ranges
+    a_unsplit = *a_in;
+    a_unsplit.num_splits = 1;
+    a = &a_unsplit;
+    if ((rc = plan_fwd(a, &P))) return rc;
+  }
   const Shape& s = P.s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = s.dtype == LTXATTN_BF16;
@@ -686,7 +689,6 @@ static int fwd_impl(const ltxattn_fwd_args* a_in, void* stream, const ltxattn_ga
   if (g != nullptr && (e = launch_gather_enter(gs, st)) != cudaSuccess) return cuda_fail(e, "gather entry launch");
   e = launch_fwd_bf16(p, s.D, smem, st);
   if (e != cudaSuccess) return cuda_fail(e, "fwd_bf16 launch");
-  if (g != nullptr && (e = launch_gather_done(gs, st)) != cudaSuccess) return cuda_fail(e, "gather completion launch");
   if (P.splits > 1) {
     CombineParams c{};
     c.part_o = reinterpret_cast<const float*>(ws + P.off_po);
@@ -710,9 +712,13 @@ static int fwd_impl(const ltxattn_fwd_args* a_in, void* stream, const ltxattn_ga
     c.g_sb = p.g_sb;
     c.g_st = p.g_st;
     c.g_sh = p.g_sh;
+    if (g != nullptr)
+      for (int d = 0; d < g->world; ++d)
+        if (d != g->rank) c.peer_out[c.peer_n++] = static_cast<__nv_bfloat16*>(g->out[d]);
     e = launch_combine(c, st);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
+  if (g != nullptr && (e = launch_gather_done(gs, st)) != cudaSuccess) return cuda_fail(e, "gather completion launch");
   return LTXATTN_OK;
 }
 

@@ -149,6 +149,8 @@ struct CombineParams {
   int q_blocks, n_full, n_tail;  // the forward's unit split (FwdParams)
   const __nv_bfloat16* gate;     // as FwdParams
   int64_t g_sb, g_st, g_sh;
+  int peer_n;                    // fused all-gather: the rows also go to these outputs (same strides)
+  __nv_bfloat16* peer_out[7];
 };
 
 // Backward.  Every pointer and tensor map is based at local head 0 (the

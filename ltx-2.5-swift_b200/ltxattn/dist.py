@@ -229,7 +229,7 @@ class FusedHeadGather:
         if scale is None:
             scale = 1.0 / float(D) ** 0.5
         a, _ = AttentionBackend.make_fwd_args(q, k, v, scale, q_rotary=q_rotary, k_rotary=k_rotary, out=self.out,
-                                              head_begin=h0, head_count=hc, num_splits=1)
+                                              head_begin=h0, head_count=hc)
         L = _lib.load()
         n = int(L.ltxattn_fwd_workspace(ctypes.byref(a)))
         ws = None

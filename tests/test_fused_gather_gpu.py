@@ -4,8 +4,10 @@ all-gather fused into the attention), with bounded entry and arrival
 handshakes between the devices.
 
 Every rank's gathered output must equal, bit for bit, the same head-block calls
-made on one device (ltxattn_fwd with head_begin / head_count and unsplit KV
-ranges), across several calls (the epoch handshake) with changing data.  Runs as
+made on one device (ltxattn_fwd with head_begin / head_count: the same plan, so
+split KV ranges and their combine, which stores the split rows to the peers,
+are exercised: 6 and 52 units per rank here), across several calls (the epoch
+handshake) with changing data.  Runs as
 two spawned processes (gloo for the host exchange); skipped with fewer than two
 GPUs."""
 import os
@@ -53,8 +55,7 @@ def _rank_main(rank, world, port, shape, results):
             ref = torch.empty_like(out)
             for r in range(world):
                 h0, hc = head_block(H, world, r)
-                AttentionBackend.attention(q, k, vv, q_rotary=rot, head_begin=h0, head_count=hc, num_splits=1,
-                                           out=ref)
+                AttentionBackend.attention(q, k, vv, q_rotary=rot, head_begin=h0, head_count=hc, out=ref)
             torch.cuda.synchronize()
             ok = ok and torch.equal(out, ref)
             dist.barrier()  # both ranks compared before the next call overwrites
