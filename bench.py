@@ -872,6 +872,23 @@ def run_outproj(args):
                       "ok": bool(err.max() <= 2e-2 and rel <= 1e-2),
                       "checked": f"{len(rows)} rows of the reduced output on rank 0, fp64 oracle of the full to_out"}
         ms, gms = ctx.max_over_ranks([sum(full_ms) / args.steps, sum(gemm_ms) / args.steps])
+        fused = None
+        if args.fused_gather and ctx.ws > 1:
+            # ltxattn_out_project_fused: the reduction over peer memory instead of NCCL
+            fo = ldist.FusedOutProject(M, N)
+            try:
+                f_ms = ctx.timed(lambda: fo.run(x_local, w_block, b, stream=ctx.stream), args.steps,
+                                 warmup=args.warmup)
+                torch.cuda.synchronize()
+                same = float((fo.out.float() - out.float()).abs().max())
+                fms, same = ctx.max_over_ranks([sum(f_ms) / args.steps, same])
+            finally:
+                fo.close()
+            fused = {"ms_per_step": round(fms, 5), "value": round(2.0 * M * N * K / (fms * 1e-3) / 1e12, 2),
+                     "max_abs_vs_nccl_path": round(same, 6),
+                     "how": "ltxattn_out_project_fused: fp32 partial rows stored into their owners' planes by the "
+                            "GEMM epilogue, owners reduce in rank order and store into every output, bounded "
+                            "handshakes"}
     finally:
         ctx.barrier()
         hg.close()
@@ -893,7 +910,7 @@ def run_outproj(args):
             "gemm_frac_of_burst": round(2.0 * M * N * k / (gms * 1e-3) / 1e12 / burst, 4),
             "allreduce_and_round_ms": round(max(0.0, ms - gms), 5),
             "allreduce_bytes_per_rank": M * N * 4, "nccl_nranks": nranks,
-            "parity": parity, "gpu_launches": 2 * args.steps,
+            "parity": parity, "gpu_launches": 2 * args.steps, "fused": fused,
         }
     ctx.close()
     return result
@@ -1048,7 +1065,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the chosen workload (no sub-records)")
     ap.add_argument("--fused-gather", action="store_true",
-                    help="N > 1: also time ltxattn_fwd_gather (the all-gather fused into the attention)")
+                    help="N > 1: also time ltxattn_fwd_gather (the all-gather fused into the attention) and, "
+                         "with --workload outproj, ltxattn_out_project_fused")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--bwd", action="store_true", help="also time the training backward")
     ap.add_argument("--traffic-launches", action="store_true",

@@ -435,6 +435,36 @@ typedef struct ltxattn_out_project_args {
 } ltxattn_out_project_args;
 
 LTXATTN_API size_t ltxattn_out_project_workspace(const ltxattn_out_project_args* args);
+
+/* Every rank's receive planes, output and signal words for
+ * ltxattn_out_project_fused, mapped on the calling device (CUDA IPC over
+ * NVLink).  recv[d]: rank d's `world` fp32 planes of [m, n] (plane s holds the
+ * partial from rank s); out[d]: rank d's [m, n] bf16 output (row stride
+ * args->out_stride); signals[d]: rank d's 16 signal words, zero at
+ * allocation. */
+typedef struct ltxattn_reduce_peers {
+  int32_t world;
+  int32_t rank;
+  float* recv[8];
+  void* out[8];
+  uint32_t* signals[8];
+  uint32_t epoch;         /* 1, 2, 3, ...: one per call, the same on every rank */
+  int32_t reserved;
+} ltxattn_reduce_peers;
+
+/* The row-parallel to_out with its reduction done over peer memory instead of
+ * an NCCL all-reduce (no counterpart in the reference, which runs one device).
+ * Rows are owned in blocks of 128 (rank t / rows_per_owner); the GEMM's
+ * epilogue stores each fp32 partial row straight into its owner's receive plane
+ * for this rank; after a bounded handshake each owner adds its rows' planes in
+ * rank order, applies the bias and the roundings of DiTAttention.linear, and
+ * stores the bf16 rows into every rank's output; a second bounded handshake
+ * ends the call with the whole output on every rank.  Same arithmetic as
+ * ltxattn_out_project_allreduce (fp32 partials added in rank order, then
+ * T(T(sum) + b)).  args->workspace is unused; args->out must be
+ * peers->out[rank]; not for stream capture (the epoch is a launch argument). */
+LTXATTN_API int ltxattn_out_project_fused(const ltxattn_out_project_args* args, const ltxattn_reduce_peers* peers,
+                                          void* stream);
 LTXATTN_API int ltxattn_out_project_allreduce(const ltxattn_out_project_args* args, ltxattn_comm* comm,
                                               void* stream);
 

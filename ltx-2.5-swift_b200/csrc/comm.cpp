@@ -12,6 +12,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -213,6 +214,70 @@ int ltxattn_out_project_allreduce(const ltxattn_out_project_args* a, ltxattn_com
       nccl().AllReduce(partial, partial, (size_t)a->m * a->n, ncclFloat32, ncclSum, comm->nccl, st);
   if (r != ncclSuccess) return nccl_fail("ncclAllReduce", r);
   return ltx::bias_round(partial, 1, 0, a->bias, a->out, a->out_stride, a->m, a->n, st);
+}
+
+int ltxattn_out_project_fused(const ltxattn_out_project_args* a, const ltxattn_reduce_peers* g, void* stream) {
+  if (!a || !g) return ltx::set_error_message(LTXATTN_ERR_ARG, "args or peers is NULL");
+  if (a->dtype != LTXATTN_BF16)
+    return ltx::set_error_message(LTXATTN_ERR_DTYPE, "ltxattn_out_project_fused: bf16 only");
+  if (a->m < 1 || a->n < 8 || a->n % 8)
+    return ltx::set_error_message(LTXATTN_ERR_SHAPE, "ltxattn_out_project_fused: m >= 1 and n a multiple of 8");
+  if (g->world < 2 || g->world > 8 || g->rank < 0 || g->rank >= g->world || g->epoch == 0)
+    return ltx::set_error_message(LTXATTN_ERR_ARG, "ltxattn_out_project_fused: 2 to 8 ranks, a valid rank, epochs from 1");
+  if (g->out[g->rank] != a->out)
+    return ltx::set_error_message(LTXATTN_ERR_ARG, "ltxattn_out_project_fused: peers->out[rank] must be args->out");
+  for (int d = 0; d < g->world; ++d)
+    if (!g->recv[d] || !g->out[d] || !g->signals[d] || (reinterpret_cast<uintptr_t>(g->recv[d]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(g->out[d]) & 15u))
+      return ltx::set_error_message(LTXATTN_ERR_ALIGN, "ltxattn_out_project_fused: 16-byte aligned peer buffers needed");
+  if (a->out_stride < a->n || (a->out_stride % 8) || (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15u)))
+    return ltx::set_error_message(LTXATTN_ERR_ALIGN, "ltxattn_out_project_fused: out and bias need 16-byte aligned rows");
+  int* err = ltx::device_error_word();
+  if (!err) return ltx::set_error_message(LTXATTN_ERR_CUDA, "no device error word");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int blocks = (a->m + 127) / 128;
+  const int rows_per_owner = (blocks + g->world - 1) / g->world * 128;
+  const int64_t slot = (int64_t)a->m * a->n;
+  ltxattn_linear_args l{};
+  l.dtype = a->dtype;
+  l.m = a->m;
+  l.n = a->n;
+  l.k = a->k;
+  l.x = a->x;
+  l.x_stride = a->x_stride;
+  l.weight = a->weight;
+  l.weight_stride = a->weight_stride;
+  l.out = a->out;
+  l.out_stride = a->out_stride;
+  // 1. every partial row into its owner's plane for this rank
+  if (int rc = ltx::linear_partial_f32_to_owners(&l, g->recv, g->world, g->rank, rows_per_owner, slot, st)) return rc;
+  ltx::GatherSync gs{};
+  gs.n = g->world;
+  gs.rank = g->rank;
+  gs.epoch = g->epoch;
+  gs.err = err;
+  for (int d = 0; d < g->world; ++d) gs.sig[d] = g->signals[d];
+  // 2. every rank's partials have landed at their owners
+  gs.word = 0;
+  cudaError_t e = ltx::launch_gather_done(gs, st);
+  if (e != cudaSuccess) return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  // 3. this rank's rows: planes added in rank order, bias and roundings, stored in every output
+  const int r0 = g->rank * rows_per_owner;
+  const int rows = std::max(0, std::min(a->m, r0 + rows_per_owner) - r0);
+  void* peer_rows[7];
+  int np = 0;
+  for (int d = 0; d < g->world; ++d)
+    if (d != g->rank) peer_rows[np++] = static_cast<__nv_bfloat16*>(g->out[d]) + (int64_t)r0 * a->out_stride;
+  if (rows > 0)
+    if (int rc = ltx::bias_round(g->recv[g->rank] + (int64_t)r0 * a->n, g->world, slot, a->bias,
+                                 static_cast<__nv_bfloat16*>(a->out) + (int64_t)r0 * a->out_stride, a->out_stride, rows,
+                                 a->n, st, np, peer_rows))
+      return rc;
+  // 4. every rank's rows have landed in every output
+  gs.word = 8;
+  e = ltx::launch_gather_done(gs, st);
+  if (e != cudaSuccess) return ltx::set_error_message(LTXATTN_ERR_CUDA, cudaGetErrorString(e));
+  return LTXATTN_OK;
 }
 
 }  // extern "C"

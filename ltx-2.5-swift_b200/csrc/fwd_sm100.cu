@@ -657,10 +657,10 @@ __global__ void gather_done_kernel(const GatherSync g) {
   const bool peer = d < g.n && d != g.rank;
   if (peer) {
     __threadfence_system();
-    atomicMax_system(g.sig[d] + g.rank, g.epoch);
+    atomicMax_system(g.sig[d] + g.word + g.rank, g.epoch);
   }
   if (peer) {
-    volatile unsigned int* f = g.sig[g.rank] + d;
+    volatile unsigned int* f = g.sig[g.rank] + g.word + d;
     const uint64_t t0 = globaltimer_ns();
     while (*f < g.epoch) {
       if (globaltimer_ns() - t0 > LTX_WAIT_LIMIT_NS) {

@@ -69,6 +69,7 @@ struct GatherSync {
   unsigned int* sig[8];
   int n, rank;
   unsigned int epoch;
+  int word;  // gather_done's words: [word, word + 8) (0, or 8 for a second handshake of one call)
   int* err;
 };
 cudaError_t launch_gather_enter(const GatherSync& g, cudaStream_t s);
@@ -264,6 +265,16 @@ namespace ltx {
 // split_stride floats apart, added in order).
 int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_t st);
 int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
-               int m, int n, cudaStream_t st);
+               int m, int n, cudaStream_t st, int n_peer_out = 0, void* const* peer_out = nullptr);
+// The fused reduce-scatter's GEMM (ltxattn_out_project_fused): row t's fp32
+// partial goes to plane `rank` of the receive planes of rank t / rows_per_owner
+// (planes[d]: rank d's [world][m][n] planes, slot_stride floats apart).
+struct OwnerPlanes {
+  int world, rank, rows_per_owner;
+  int64_t slot_stride;
+  float* planes[8];
+};
+int linear_partial_f32_to_owners(const ltxattn_linear_args* a, float* const* planes, int world, int rank,
+                                 int rows_per_owner, int64_t slot_stride, cudaStream_t st);
 
 }  // namespace ltx

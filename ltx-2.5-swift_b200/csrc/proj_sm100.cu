@@ -69,6 +69,15 @@ struct ProjJob {
   __nv_bfloat16* out;
   float* out_f32;
   int64_t o_sb, o_st, split_stride;
+  // fused reduce-scatter (ltxattn_out_project_fused): peer_n > 0 sends the fp32
+  // partial of row t to the receive planes of its owner, rank t / rows_per_owner,
+  // at plane my_rank (peer_f32[d]: rank d's planes, slot_stride floats apart)
+  int peer_n, my_rank, rows_per_owner;
+  int64_t slot_stride;
+  float* peer_f32[8];
+  // rank d's plane for this rank as an fp32 [n, m] tensor map, box {32, 128}:
+  // the owner-directed partials leave through shared memory with TMA stores
+  CUtensorMap tm_owner[8];
 };
 
 struct ProjParams {
@@ -216,7 +225,39 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const bool have = warp_wait(acc_full, 0, abort_flag, p.err, 43);
     tc_fence_after();
-    if (have) {
+    if (kF32Out && J.peer_n > 0) {
+      // fused reduce-scatter: the tile's rows all belong to one owner (owners hold
+      // whole 128-row blocks); each 32-column chunk is staged row-major in the
+      // idle pipeline stages (128 rows x 128 bytes) and stored with TMA into the
+      // owner's plane for this rank, so the NVLink writes go out as bulk copies
+      const CUtensorMap* dst_map = &J.tm_owner[t0 / J.rows_per_owner];
+      float* stg = reinterpret_cast<float*>(sm);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n = n_base + c * 32;
+        if (n >= J.N) break;  // warp-uniform
+        uint32_t acc[32];
+        if (have) {
+          tmem_ld32(tmem + lane_off + c * 32, acc);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[e] = 0u;
+        }
+        if (r == 0) bulk_wait_read();  // the previous chunk's copy has read the staging rows
+        named_barrier(1, 128);
+        uint4* row = reinterpret_cast<uint4*>(stg + r * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) row[q] = make_uint4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+        fence_proxy_async_smem();
+        named_barrier(1, 128);
+        if (r == 0) {
+          tma_store_4d(dst_map, stg, n, t0, 0, 0);
+          bulk_commit();
+        }
+      }
+      if (r == 0) bulk_wait_read();  // the CTA's shared memory must outlive the copies' reads
+    } else if (have) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int n = n_base + c * 32;
@@ -228,7 +269,9 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
         if (t < J.T && kF32Out) {
           // the fp32 accumulator itself (a partial sum that is reduced across ranks before
           // the bias and the roundings)
-          uint4* dst = reinterpret_cast<uint4*>(J.out_f32 + split * J.split_stride + (int64_t)t * J.o_st + n);
+          float* plane = J.out_f32 + split * J.split_stride;
+          if (J.peer_n > 0) plane = J.peer_f32[t / J.rows_per_owner] + (int64_t)J.my_rank * J.slot_stride;
+          uint4* dst = reinterpret_cast<uint4*>(plane + (int64_t)t * J.o_st + n);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             if (4 * q < valid) dst[q] = make_uint4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
@@ -257,9 +300,15 @@ __global__ void __launch_bounds__(kPThreads, 1) linear_kernel(const __grid_const
 // added in split order: the roundings of DiTAttention.linear applied once the
 // partial sums (K splits of one GPU, or the row-parallel ranks after their
 // all-reduce) are complete.  One thread per 8 columns.
+struct PeerRows {  // the same rows in other ranks' outputs (fused all-gather of the reduced rows)
+  int n;
+  __nv_bfloat16* out[7];
+};
+
 __global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64_t s_st, int splits,
                                                          int64_t split_stride, const __nv_bfloat16* bias,
-                                                         __nv_bfloat16* out, int64_t o_st, int M, int N) {
+                                                         __nv_bfloat16* out, int64_t o_st, int M, int N,
+                                                         const PeerRows peers) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int n8 = N / 8;
   if (i >= (int64_t)M * n8) return;
@@ -277,8 +326,10 @@ __global__ void __launch_bounds__(256) bias_round_kernel(const float* sum, int64
     y[e] = bf16_round(y[e]);
     if (bias != nullptr) y[e] = bf16_round(y[e] + __bfloat162float(bias[n + e]));
   }
-  *reinterpret_cast<uint4*>(out + (int64_t)t * o_st + n) =
+  const uint4 packed =
       make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+  *reinterpret_cast<uint4*>(out + (int64_t)t * o_st + n) = packed;
+  for (int d = 0; d < peers.n; ++d) *reinterpret_cast<uint4*>(peers.out[d] + (int64_t)t * o_st + n) = packed;
 }
 
 // ---------------------------------------------------------------------------
@@ -326,6 +377,21 @@ int map_rows(CUtensorMap* m, const void* ptr, int K, int T, int B, int64_t st, i
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail_msg(LTXATTN_ERR_ALIGN, "%s: cuTensorMapEncodeTiled rejected the view (CUresult %d)", name, (int)r);
+  return LTXATTN_OK;
+}
+
+// An fp32 [m, n] plane (row stride n) as a 4-D [n, m, 1, 1] tensor map, box
+// {32, 128, 1, 1}, no swizzle: the owner-directed partial stores.
+int map_plane_f32(CUtensorMap* mp, float* ptr, int n, int m) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return fail_msg(LTXATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[4] = {(cuuint64_t)n, (cuuint64_t)m, 1, 1};
+  cuuint64_t strides[3] = {(cuuint64_t)n * 4, (cuuint64_t)n * m * 4, (cuuint64_t)n * m * 4};
+  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail_msg(LTXATTN_ERR_ALIGN, "receive plane: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
   return LTXATTN_OK;
 }
 
@@ -406,10 +472,6 @@ int launch_linear_bn(ProjParams& P, const ltxattn_linear_args* a, cudaStream_t s
 
 }  // namespace
 
-namespace ltx {
-int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
-               int m, int n, cudaStream_t st);
-}  // namespace ltx
 
 namespace {
 
@@ -454,7 +516,7 @@ size_t split_workspace(int m, int n, int splits) {
 
 // ltxattn_linear, or (f32_out != null) the same GEMM storing its fp32
 // accumulator, without bias or roundings, into f32_out [m, n] (row stride n).
-int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
+int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st, const ltx::OwnerPlanes* owners = nullptr) {
   if (a == nullptr) return fail_msg(LTXATTN_ERR_ARG, "args is NULL");
   if (a->dtype != LTXATTN_BF16) return fail_msg(LTXATTN_ERR_DTYPE, "ltxattn_linear: bf16 only");
   if (a->m < 1 || a->n < 1 || a->k < 1) return fail_msg(LTXATTN_ERR_SHAPE, "ltxattn_linear: m, n and k must be >= 1");
@@ -486,6 +548,18 @@ int run_linear(const ltxattn_linear_args* a, float* f32_out, cudaStream_t st) {
   J.splits = 1;
   J.kb_per = a->k / kPBK;
   J.split_stride = 0;
+  if (owners != nullptr) {
+    J.peer_n = owners->world;
+    J.my_rank = owners->rank;
+    J.rows_per_owner = owners->rows_per_owner;
+    J.slot_stride = owners->slot_stride;
+    for (int d = 0; d < owners->world; ++d) {
+      J.peer_f32[d] = owners->planes[d];
+      if (int rc = map_plane_f32(&J.tm_owner[d], owners->planes[d] + (int64_t)owners->rank * owners->slot_stride,
+                                 a->n, a->m))
+        return rc;
+    }
+  }
   if (f32_out == nullptr) {
     // a narrow output with a workspace: K splits into fp32 partials, then one
     // pass adds them in split order and applies the bias and the roundings
@@ -537,14 +611,27 @@ int linear_partial_f32(const ltxattn_linear_args* a, float* partial, cudaStream_
   return run_linear(a, partial, st);
 }
 
+int linear_partial_f32_to_owners(const ltxattn_linear_args* a, float* const* planes, int world, int rank,
+                                 int rows_per_owner, int64_t slot_stride, cudaStream_t st) {
+  for (int d = 0; d < world; ++d)
+    if (planes[d] == nullptr || (reinterpret_cast<uintptr_t>(planes[d]) & 15u))
+      return fail_msg(LTXATTN_ERR_ALIGN, "rank %d's receive planes must be 16-byte aligned", d);
+  OwnerPlanes o{world, rank, rows_per_owner, slot_stride, {}};
+  for (int d = 0; d < world; ++d) o.planes[d] = planes[d];
+  return run_linear(a, planes[rank], st, &o);
+}
+
 int bias_round(const float* sum, int splits, int64_t split_stride, const void* bias, void* out, int64_t out_stride,
-               int m, int n, cudaStream_t st) {
+               int m, int n, cudaStream_t st, int n_peer_out, void* const* peer_out) {
   const int64_t threads = (int64_t)m * (n / 8);
   const int64_t blocks = (threads + 255) / 256;
   if (blocks > 0x7fffffff) return fail_msg(LTXATTN_ERR_UNSUPPORTED, "output too large");
+  if (blocks == 0) return LTXATTN_OK;
+  PeerRows pr{};
+  for (int d = 0; d < n_peer_out && d < 7; ++d) pr.out[pr.n++] = static_cast<__nv_bfloat16*>(peer_out[d]);
   bias_round_kernel<<<(unsigned)blocks, 256, 0, st>>>(sum, n, splits, split_stride,
                                                       static_cast<const __nv_bfloat16*>(bias),
-                                                      static_cast<__nv_bfloat16*>(out), out_stride, m, n);
+                                                      static_cast<__nv_bfloat16*>(out), out_stride, m, n, pr);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return launch_fail(e, "bias and rounding launch");
   return LTXATTN_OK;

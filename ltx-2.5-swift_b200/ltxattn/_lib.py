@@ -30,6 +30,7 @@ EXPORTED = (
     "ltxattn_comm_size", "ltxattn_selftest_wait_timeout", "ltxattn_memory_plan",
     "ltxattn_linear", "ltxattn_linear_workspace", "ltxattn_head_gate",
     "ltxattn_out_project_workspace", "ltxattn_out_project_allreduce", "ltxattn_fwd_gather",
+    "ltxattn_out_project_fused",
 )
 
 
@@ -62,6 +63,12 @@ class FwdArgs(ctypes.Structure):
 class GatherPeers(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("out", ctypes.c_void_p * 8),
                 ("signals", ctypes.c_void_p * 8), ("epoch", ctypes.c_uint32), ("reserved", ctypes.c_int32)]
+
+
+class ReducePeers(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("recv", ctypes.c_void_p * 8),
+                ("out", ctypes.c_void_p * 8), ("signals", ctypes.c_void_p * 8), ("epoch", ctypes.c_uint32),
+                ("reserved", ctypes.c_int32)]
 
 
 class FwdPlanInfo(ctypes.Structure):
@@ -173,6 +180,8 @@ def load(path: str = LIB_PATH):
     L.ltxattn_fwd_noalloc.restype = ctypes.c_int
     L.ltxattn_fwd_gather.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(GatherPeers), vp]
     L.ltxattn_fwd_gather.restype = ctypes.c_int
+    L.ltxattn_out_project_fused.argtypes = [ctypes.POINTER(OutProjectArgs), ctypes.POINTER(ReducePeers), vp]
+    L.ltxattn_out_project_fused.restype = ctypes.c_int
     L.ltxattn_fwd_workspace.argtypes = [ctypes.POINTER(FwdArgs)]
     L.ltxattn_fwd_workspace.restype = ctypes.c_size_t
     L.ltxattn_fwd_plan.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(FwdPlanInfo)]

@@ -15,6 +15,7 @@ from __future__ import annotations
 import ctypes
 from typing import Optional, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -153,71 +154,94 @@ def gather_layout(blocks):
     return torch.cat(list(blocks), dim=1)
 
 
-class FusedHeadGather:
-    """Buffers and calls of ``ltxattn_fwd_gather``: the head-sharded attention
-    whose epilogue stores each output tile into every rank's output over NVLink
-    (the all-gather fused into the attention).
+class _IpcBlock:
+    """One cudaMalloc block per rank (zeroed), mapped on every rank's device: the
+    blocks' CUDA IPC handles are exchanged through ``torch.distributed`` and opened
+    with lazy peer access, so ``peer_base[d]`` is rank d's block on this device
+    (``peer_base[rank]`` the own one).  Collective: every rank builds and closes
+    its block together."""
 
-    Each rank allocates one device block (cudaMalloc): 16 signal words, then its
-    full output ``out`` [B, H, T, D] bf16.  The blocks' CUDA IPC handles are
-    exchanged through ``torch.distributed`` and opened on this rank's device
-    with lazy peer access, so every rank holds device pointers to every rank's
-    output and signal words.  ``run`` computes this rank's head block
-    (``head_block``) and returns with every rank's heads in ``out`` (stream
-    ordered).  Every rank must call ``run`` the same number of times with the
-    same shapes; ``close`` releases the mappings (collective: every rank calls
-    it)."""
-
-    _SIG_BYTES = 256  # 16 uint32 words, padded so the output starts 256-byte aligned
-
-    def __init__(self, shape, group=None):
+    def __init__(self, nbytes: int, group=None):
         from cuda.bindings import runtime as cudart
         self._rt = cudart
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if not 2 <= self.world <= 8:
-            raise Failure("arg", f"world {self.world}: ltxattn_fwd_gather joins 2 to 8 ranks", _lib.ERR_ARG)
-        B, H, T, D = (int(x) for x in shape)
-        self.shape = (B, H, T, D)
+            raise Failure("arg", f"world {self.world}: peer-memory collectives join 2 to 8 ranks", _lib.ERR_ARG)
         self.device = torch.cuda.current_device()
         self._ok(cudart.cudaSetDevice(self.device))
-        nbytes = self._SIG_BYTES + B * H * T * D * 2
-        self._base = int(self._ok(cudart.cudaMalloc(nbytes)))
-        self._ok(cudart.cudaMemset(self._base, 0, self._SIG_BYTES))
+        self.base = int(self._ok(cudart.cudaMalloc(nbytes)))
+        self._ok(cudart.cudaMemset(self.base, 0, nbytes))
         self._ok(cudart.cudaDeviceSynchronize())
-        handle = self._ok(cudart.cudaIpcGetMemHandle(self._base))
-        mine = bytes(handle.reserved)
+        mine = bytes(self._ok(cudart.cudaIpcGetMemHandle(self.base)).reserved)
         handles = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
         self._opened = []
         self.peer_base = []
         for d, h in enumerate(handles):
             if d == self.rank:
-                self.peer_base.append(self._base)
+                self.peer_base.append(self.base)
                 continue
             ph = cudart.cudaIpcMemHandle_t()
             ph.reserved = h
             ptr = int(self._ok(cudart.cudaIpcOpenMemHandle(ph, cudart.cudaIpcMemLazyEnablePeerAccess)))
             self._opened.append(ptr)
             self.peer_base.append(ptr)
-        self.epoch = 0
-        self.out = torch.as_tensor(_DeviceArray(self._base + self._SIG_BYTES, (B, H, T, D)),
-                                   device=torch.device("cuda", self.device)).view(torch.bfloat16)
-        self.signals = torch.as_tensor(_DeviceArray(self._base, (self._SIG_BYTES // 2,)),
-                                       device=torch.device("cuda", self.device)).view(torch.int32)[:16]
-        self._peers = _lib.GatherPeers()
-        self._peers.world, self._peers.rank = self.world, self.rank
-        for d, b in enumerate(self.peer_base):
-            self._peers.out[d] = b + self._SIG_BYTES
-            self._peers.signals[d] = b
         dist.barrier(group=group)  # every rank has mapped every block before any call stores into it
 
-    def _ok(self, res):
+    @staticmethod
+    def _ok(res):
         err = res[0]
         if int(err) != 0:
             raise Failure("cuda", f"CUDA runtime call failed: {err}", _lib.ERR_CUDA)
         return res[1] if len(res) > 1 else None
+
+    def tensor(self, offset: int, shape, dtype):
+        """A torch view of this rank's block at byte `offset` (bf16 / int32 / float32)."""
+        elems = {torch.bfloat16: 1, torch.int32: 2, torch.float32: 2}[dtype]
+        n16 = int(np.prod(shape)) * elems
+        t = torch.as_tensor(_DeviceArray(self.base + offset, (n16,)), device=torch.device("cuda", self.device))
+        return t.view(dtype).view(tuple(shape))
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still stores into a block about to be unmapped
+        for ptr in self._opened:
+            self._ok(self._rt.cudaIpcCloseMemHandle(ptr))
+        self._opened = []
+        dist.barrier(group=self.group)
+        if self.base:
+            self._ok(self._rt.cudaFree(self.base))
+            self.base = 0
+
+
+_SIG_BYTES = 256  # 16 uint32 signal words, padded so what follows is 256-byte aligned
+
+
+class FusedHeadGather:
+    """Buffers and calls of ``ltxattn_fwd_gather``: the head-sharded attention
+    whose epilogue stores each output tile into every rank's output over NVLink
+    (the all-gather fused into the attention).
+
+    Each rank's IPC block (``_IpcBlock``) holds 16 signal words, then its full
+    output ``out`` [B, H, T, D] bf16.  ``run`` computes this rank's head block
+    (``head_block``) and returns with every rank's heads in ``out`` (stream
+    ordered).  Every rank must call ``run`` the same number of times with the
+    same shapes; ``close`` releases the mappings (collective)."""
+
+    def __init__(self, shape, group=None):
+        B, H, T, D = (int(x) for x in shape)
+        self.shape = (B, H, T, D)
+        self.block = _IpcBlock(_SIG_BYTES + B * H * T * D * 2, group)
+        self.world, self.rank = self.block.world, self.block.rank
+        self.out = self.block.tensor(_SIG_BYTES, (B, H, T, D), torch.bfloat16)
+        self.epoch = 0
+        self._peers = _lib.GatherPeers()
+        self._peers.world, self._peers.rank = self.world, self.rank
+        for d, b in enumerate(self.block.peer_base):
+            self._peers.out[d] = b + _SIG_BYTES
+            self._peers.signals[d] = b
 
     def run(self, q, k, v, scale: Optional[float] = None, q_rotary=None, k_rotary=None, stream=None):
         """This rank's head block of attention(q, k, v) (full [B, H, T, D] inputs on
@@ -246,15 +270,63 @@ class FusedHeadGather:
         return self.out
 
     def close(self):
-        torch.cuda.synchronize()
-        dist.barrier(group=self.group)  # no rank still stores into a block about to be unmapped
-        for ptr in self._opened:
-            self._ok(self._rt.cudaIpcCloseMemHandle(ptr))
-        self._opened = []
-        dist.barrier(group=self.group)
-        if self._base:
-            self._ok(self._rt.cudaFree(self._base))
-            self._base = 0
+        self.block.close()
+
+
+class FusedOutProject:
+    """Buffers and calls of ``ltxattn_out_project_fused``: the row-parallel to_out
+    whose reduction runs over peer memory (the GEMM's epilogue stores each fp32
+    partial row into its owner's receive plane, owners add the planes in rank order
+    and store the rounded rows into every rank's output).
+
+    Each rank's IPC block holds 16 signal words, ``world`` fp32 receive planes of
+    [m, n], then its output ``out`` [m, n] bf16.  Collective like
+    ``FusedHeadGather``."""
+
+    def __init__(self, m: int, n: int, group=None):
+        self.m, self.n = int(m), int(n)
+        world = dist.get_world_size(group)
+        recv_bytes = world * self.m * self.n * 4
+        self._off_out = _SIG_BYTES + (recv_bytes + 255) // 256 * 256
+        self.block = _IpcBlock(self._off_out + self.m * self.n * 2, group)
+        self.world, self.rank = self.block.world, self.block.rank
+        self.out = self.block.tensor(self._off_out, (self.m, self.n), torch.bfloat16)
+        self.epoch = 0
+        self._peers = _lib.ReducePeers()
+        self._peers.world, self._peers.rank = self.world, self.rank
+        for d, b in enumerate(self.block.peer_base):
+            self._peers.recv[d] = b + _SIG_BYTES
+            self._peers.out[d] = b + self._off_out
+            self._peers.signals[d] = b
+
+    def run(self, x_local: torch.Tensor, weight_block: torch.Tensor, bias: Optional[torch.Tensor] = None,
+            stream=None) -> torch.Tensor:
+        """to_out of this rank's merged head slice x_local [m, k] with its column block
+        of to_out.0.weight [n, k]; returns ``out`` [m, n] holding the whole sum on every
+        rank (stream ordered)."""
+        from .backend import _stream_ptr
+        k = x_local.shape[-1]
+        x2 = x_local.reshape(-1, k)
+        if x2.shape[0] != self.m or weight_block.shape[0] != self.n or weight_block.shape[1] != k or \
+                weight_block.stride(1) != 1:
+            raise Failure.shape("x_local / weight_block", tuple(x2.shape) + tuple(weight_block.shape),
+                                f"[{self.m}, k] and [{self.n}, k]")
+        a = _lib.OutProjectArgs()
+        a.dtype, a.m, a.n, a.k = _lib.BF16, self.m, self.n, k
+        a.x, a.x_stride = x2.data_ptr(), x2.stride(0) if self.m > 1 else k
+        a.weight, a.weight_stride = weight_block.data_ptr(), weight_block.stride(0)
+        a.bias = bias.data_ptr() if bias is not None else None
+        a.out, a.out_stride = self.out.data_ptr(), self.n
+        self.epoch += 1
+        self._peers.epoch = self.epoch
+        rc = _lib.load().ltxattn_out_project_fused(ctypes.byref(a), ctypes.byref(self._peers),
+                                                   ctypes.c_void_p(_stream_ptr(stream)))
+        if rc != _lib.OK:
+            raise Failure.from_status(rc)
+        return self.out
+
+    def close(self):
+        self.block.close()
 
 
 class _DeviceArray:

@@ -58,6 +58,9 @@ int main(void) {
   printf("ltxattn_head_gate_args %zu\n", sizeof(ltxattn_head_gate_args));
   printf("ltxattn_gather_peers %zu\n", sizeof(ltxattn_gather_peers));
   P(ltxattn_gather_peers, out) P(ltxattn_gather_peers, signals) P(ltxattn_gather_peers, epoch)
+  printf("ltxattn_reduce_peers %zu\n", sizeof(ltxattn_reduce_peers));
+  P(ltxattn_reduce_peers, recv) P(ltxattn_reduce_peers, out) P(ltxattn_reduce_peers, signals)
+  P(ltxattn_reduce_peers, epoch)
   P(ltxattn_linear_args, out_stride) P(ltxattn_linear_args, workspace_bytes)
   P(ltxattn_out_project_args, workspace_bytes) P(ltxattn_head_gate_args, gate_stride_h)
   printf("ltxattn_memory_plan_info %zu\n", sizeof(ltxattn_memory_plan_info));
@@ -96,7 +99,7 @@ def test_ctypes_layout_matches_the_header(tmp_path):
              "ltxattn_fwd_plan_info": _lib.FwdPlanInfo, "ltxattn_memory_plan_args": _lib.MemoryPlanArgs,
              "ltxattn_memory_plan_info": _lib.MemoryPlanInfo, "ltxattn_linear_args": _lib.LinearArgs,
              "ltxattn_out_project_args": _lib.OutProjectArgs, "ltxattn_head_gate_args": _lib.HeadGateArgs,
-             "ltxattn_gather_peers": _lib.GatherPeers}
+             "ltxattn_gather_peers": _lib.GatherPeers, "ltxattn_reduce_peers": _lib.ReducePeers}
     for cname, py in sizes.items():
         assert int(got[cname]) == ctypes.sizeof(py), cname
     structs = {"ltxattn_fwd_args": _lib.FwdArgs, "ltxattn_bwd_args": _lib.BwdArgs,
@@ -105,7 +108,8 @@ def test_ctypes_layout_matches_the_header(tmp_path):
                "ltxattn_qk_prep_args": _lib.QkPrepArgs, "ltxattn_fwd_plan_info": _lib.FwdPlanInfo,
                "ltxattn_memory_plan_args": _lib.MemoryPlanArgs, "ltxattn_memory_plan_info": _lib.MemoryPlanInfo,
                "ltxattn_linear_args": _lib.LinearArgs, "ltxattn_out_project_args": _lib.OutProjectArgs,
-               "ltxattn_head_gate_args": _lib.HeadGateArgs, "ltxattn_gather_peers": _lib.GatherPeers}
+               "ltxattn_head_gate_args": _lib.HeadGateArgs, "ltxattn_gather_peers": _lib.GatherPeers,
+               "ltxattn_reduce_peers": _lib.ReducePeers}
     for key, val in got.items():
         if "." in key:
             s, f = key.split(".")

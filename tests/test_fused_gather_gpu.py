@@ -88,3 +88,67 @@ def test_fused_gather_matches_the_block_calls_on_two_gpus(shape):
         assert p.exitcode == 0
     for r in range(world):
         assert got[r] == (True, 0), f"rank {r}: bit-identical {got[r][0]}, device status {got[r][1]}"
+
+
+def _outproj_rank_main(rank, world, port, shape, results):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from ltxattn import device_status
+    from ltxattn import dist as ldist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    reported = False
+    try:
+        m, n, K = shape
+        k = K // world
+        g = torch.Generator(device="cuda").manual_seed(11)  # the same tensors on every rank
+        merged = torch.randn((m, K), generator=g, device="cuda").to(torch.bfloat16)
+        W = (torch.randn((n, K), generator=g, device="cuda") / 64).to(torch.bfloat16)
+        b = (torch.randn(n, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+        w_block = W[:, rank * k:(rank + 1) * k]
+        uid = ldist.exchange_unique_id()
+        hg = ldist.HeadGather(world, rank, uid, rank)
+        fo = ldist.FusedOutProject(m, n)
+        ok = True
+        for call in range(3):
+            x_local = (merged[:, rank * k:(rank + 1) * k] * (call + 1)).contiguous()
+            ref = hg.out_project(x_local, w_block, b)  # GEMM, NCCL all-reduce, bias and rounding
+            fo.out.fill_(3.0)
+            got = fo.run(x_local, w_block, b)
+            torch.cuda.synchronize()
+            # two ranks: the fp32 sum of two partials is the same in either order
+            ok = ok and torch.equal(got, ref)
+        status = device_status(clear=True)
+        fo.close()
+        hg.close()
+        results.put((rank, bool(ok), int(status)))
+        reported = True
+    finally:
+        if not reported:
+            results.put((rank, False, -1))
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("shape", [(300, 512, 1024), (3120, 4096, 4096)])
+def test_fused_out_project_matches_the_nccl_all_reduce_on_two_gpus(shape):
+    # ltxattn_out_project_fused (partial rows stored into their owners' planes by the
+    # GEMM's epilogue, owners reduce in rank order and store into every output)
+    # against ltxattn_out_project_allreduce on the same inputs: bit-identical
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_outproj_rank_main, args=(r, world, port, shape, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, ok, status = results.get(timeout=300)
+        got[r] = (ok, status)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert got[r] == (True, 0), f"rank {r}: bit-identical {got[r][0]}, device status {got[r][1]}"
