@@ -285,3 +285,72 @@ def test_linear_plans_split_k_for_narrow_outputs_only():
     assert L.ltxattn_linear_workspace(ctypes.byref(a)) == 0
     a.n, a.k = 32, 192  # too short a K to split
     assert L.ltxattn_linear_workspace(ctypes.byref(a)) == 0
+
+
+def _peers(world=2, rank=0, epoch=1, out=None):
+    g = _lib.GatherPeers()
+    g.world, g.rank, g.epoch = world, rank, epoch
+    for d in range(8):
+        g.out[d] = 4096 * (d + 1)
+        g.signals[d] = 4096 * (d + 9)
+    if out is not None:
+        g.out[rank] = out
+    return g
+
+
+@pytest.mark.parametrize("kw,peers,status", [
+    (dict(dtype=_lib.F32), dict(), _lib.ERR_DTYPE),
+    (dict(), dict(world=1), _lib.ERR_ARG),           # 2 to 8 ranks
+    (dict(), dict(world=9), _lib.ERR_ARG),
+    (dict(), dict(rank=2), _lib.ERR_ARG),            # rank outside the world
+    (dict(), dict(epoch=0), _lib.ERR_ARG),           # epochs start at 1
+    (dict(), dict(out=8192), _lib.ERR_ARG),          # peers.out[rank] must be args.out
+])
+def test_fused_gather_validation_refuses_before_any_device_work(kw, peers, status):
+    # ltxattn_fwd_gather checks its peer description on the host first
+    L = _lib.load()
+    a = _args(**kw)
+    a.out.data = 4096  # == _peers().out[0]
+    rc = L.ltxattn_fwd_gather(ctypes.byref(a), ctypes.byref(_peers(**peers)), None)
+    assert rc == status, (_lib.last_error(), rc)
+    assert "ltxattn_fwd_gather" in _lib.last_error()
+
+
+def test_fused_gather_refuses_unaligned_peer_outputs():
+    L = _lib.load()
+    a = _args()
+    a.out.data = 4096
+    g = _peers()
+    g.out[1] = 4096 * 2 + 8  # rank 1's output not 16-byte aligned
+    assert L.ltxattn_fwd_gather(ctypes.byref(a), ctypes.byref(g), None) == _lib.ERR_ALIGN
+
+
+def _reduce_peers(world=2, rank=0, epoch=1):
+    g = _lib.ReducePeers()
+    g.world, g.rank, g.epoch = world, rank, epoch
+    for d in range(8):
+        g.recv[d] = 4096 * (d + 1)
+        g.out[d] = 4096 * (d + 17)
+        g.signals[d] = 4096 * (d + 33)
+    return g
+
+
+@pytest.mark.parametrize("field,value,peers,status", [
+    ("dtype", _lib.F32, dict(), _lib.ERR_DTYPE),
+    ("n", 12, dict(), _lib.ERR_SHAPE),               # n a multiple of 8
+    ("m", 0, dict(), _lib.ERR_SHAPE),
+    (None, None, dict(world=1), _lib.ERR_ARG),
+    (None, None, dict(rank=5), _lib.ERR_ARG),
+    (None, None, dict(epoch=0), _lib.ERR_ARG),
+    ("out", 8192, dict(), _lib.ERR_ARG),             # peers.out[rank] must be args.out
+])
+def test_fused_out_project_validation_refuses_before_any_device_work(field, value, peers, status):
+    L = _lib.load()
+    a = _lib.OutProjectArgs()
+    a.dtype, a.m, a.n, a.k = _lib.BF16, 300, 512, 1024
+    a.out, a.out_stride = 4096 * 17, 512
+    if field is not None:
+        setattr(a, field, value)
+    rc = L.ltxattn_out_project_fused(ctypes.byref(a), ctypes.byref(_reduce_peers(**peers)), None)
+    assert rc == status, (_lib.last_error(), rc)
+    assert "ltxattn_out_project_fused" in _lib.last_error()
